@@ -1,0 +1,151 @@
+/*
+ * sdb.h -- the C ABI of the B200 (sm_100a) kernels that stand in for
+ * stable-diffusion.assembly's CPU operations.
+ *
+ * The reference's op layer (sources/ops.h:26-62) hands each operation a ggml
+ * node: its sources, its output and the chain of element-wise nodes fused after
+ * it (sources/fusion.h:51-91).  These entry points take the same things as
+ * plain structs -- sdb_tensor mirrors the fields of ggml_tensor an operation
+ * reads (type, ne, nb, data), sdb_chain mirrors sdasm::Epilogue -- with DEVICE
+ * addresses, and enqueue the work on a CUDA stream.  Every entry point returns
+ * an sdb_status; none aborts the process.  "Not supported" is the reference's
+ * "not taken" (hooks.cc:29-55): the caller computes the node some other way.
+ *
+ * Threading: the entry points may be called from any host thread; the weight
+ * store is shared and locked.  Work is stream-ordered; results are ready when
+ * the stream is.
+ */
+#ifndef SDB_H
+#define SDB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types, numbered as ggml's (GGML_TYPE_F32 = 0, GGML_TYPE_F16 = 1). */
+enum { SDB_TYPE_F32 = 0, SDB_TYPE_F16 = 1 };
+
+/* A tensor as ggml describes one: ne[k] elements along dimension k (0 is the
+ * fastest), nb[k] bytes between neighbours along it, data a device address. */
+typedef struct sdb_tensor {
+    int32_t type;
+    int64_t ne[4];
+    int64_t nb[4];
+    void *data;
+} sdb_tensor;
+
+/* One step of an epilogue chain (sdasm::Epilogue_step, fusion.h:51-59): an
+ * in-place addition or multiplication by an FP32 operand whose element for the
+ * output element (i0, i1, i2, i3) is operand[i0*nb[0] + i1*nb[1] + i2*nb[2] +
+ * i3*nb[3]] (nb in ELEMENTS, 0 along a broadcast dimension), or SiLU. */
+enum { SDB_STEP_ADD = 0, SDB_STEP_MUL = 1, SDB_STEP_SILU = 2 };
+#define SDB_MAX_STEPS 6
+typedef struct sdb_step {
+    int32_t kind;
+    const float *operand;
+    int64_t nb[4];
+} sdb_step;
+
+/* The chain after an operation (sdasm::Epilogue, fusion.h:61-91).  With
+ * redirect set, the operation writes its result there instead of into its own
+ * output (same extents and strides), and with from_redirect the sum begins
+ * from what redirect holds (the residual in its own memory); the steps before
+ * are then additions only. */
+typedef struct sdb_chain {
+    int32_t count;
+    sdb_step steps[SDB_MAX_STEPS];
+    float *redirect;
+    int32_t from_redirect;
+} sdb_chain;
+
+typedef enum sdb_status {
+    SDB_OK = 0,
+    SDB_NOT_SUPPORTED = 1, /* not taken: the caller computes it */
+    SDB_INVALID = 2,       /* arguments that describe no valid operation */
+    SDB_CUDA_ERROR = 3,    /* a CUDA call failed; sdb_last_error() says which */
+    SDB_OUT_OF_MEMORY = 4,
+    SDB_DEVICE_ERROR = 5   /* a kernel reported an error word (sdb_device_status) */
+} sdb_status;
+
+/* ---- linear layers: GGML_OP_MUL_MAT of a weight matrix ------------------
+ * dst[m][n] = sum_k x[m][k] * w[n][k] (+ chain), for w FP16 or FP32 [K, N]
+ * and x, dst FP32 with rows m over dimensions 1..3 (mul_mat.cc:9-18).
+ * Replaces sdasm::mul_mat_supported / mul_mat_compute (ops.h:124-126,
+ * mul_mat.cc:181-194, 1175-1196). */
+int sdb_mul_mat_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst);
+int sdb_mul_mat(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_chain *chain,
+                void *stream);
+
+/* The linear layer with the gated GELU after it (GEGLU): out[m][j] =
+ * y[m][j] * GELU(y[m][half + j]), y the product with its chain, half = N/2.
+ * Replaces sdasm::mul_mat_gated_supported / mul_mat_compute_gated (ops.h:127-131,
+ * fusion.h:110-129, mul_mat.cc:934-1058). */
+int sdb_mul_mat_gated_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *out);
+int sdb_mul_mat_gated(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *out, const sdb_chain *chain,
+                      void *stream);
+
+/* ---- convolutions: GGML_OP_CONV_2D (direct) ------------------------------
+ * w [KW, KH, IC, OC] FP16 or FP32, x [W, H, IC, N] FP32, dst [OW, OH, OC, N]
+ * FP32; params = {s0, s1, p0, p1, d0, d1} as ggml_conv_2d_direct's op_params.
+ * 3x3 stride-1 cases go to Winograd when the tuning allows.  Replaces
+ * sdasm::conv2d_* and winograd_* (ops.h:110-120, conv2d.cc:837-858,
+ * winograd.cc:2107-2272). */
+int sdb_conv2d_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const int32_t params[6]);
+int sdb_conv2d(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const int32_t params[6],
+               const sdb_chain *chain, void *stream);
+
+/* ---- attention: GGML_OP_FLASH_ATTN_EXT without a mask --------------------
+ * q [D, LQ, H, B], k [D, LK, HK, B], v [DV, LK, HK, B] (FP32, or FP16 k/v),
+ * dst [DV, H, LQ, B] FP32: softmax(scale q k^T) v per head, H % HK == 0.
+ * Replaces sdasm::attention_supported / attention_compute (ops.h:133-138,
+ * attention.cc:828-1064).  With a chain (residual add: an extension of the
+ * reference, which fuses nothing into attention) the chain is applied to dst. */
+int sdb_attention_supported(const sdb_tensor *q, const sdb_tensor *k, const sdb_tensor *v, const sdb_tensor *dst);
+int sdb_attention(const sdb_tensor *q, const sdb_tensor *k, const sdb_tensor *v, const sdb_tensor *dst, float scale,
+                  const sdb_chain *chain, void *stream);
+
+/* ---- normalisation: GGML_OP_GROUP_NORM and GGML_OP_NORM -----------------
+ * Mean and variance in double precision, two passes, then the chain
+ * (norm.cc:100-175).  Replaces sdasm::group_norm_* / norm_* (ops.h:140-146). */
+int sdb_group_norm(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps, const sdb_chain *chain,
+                   void *stream);
+int sdb_norm(const sdb_tensor *x, const sdb_tensor *dst, float eps, const sdb_chain *chain, void *stream);
+
+/* ---- the weight store (store.h:58-120, store.cc:202-266) ----------------
+ * Weights are repacked once into the layout the kernels read and kept on the
+ * device, keyed by address, shape, strides and layout.  sdb_forget() drops
+ * every entry packed from memory overlapping [begin, begin + size): call it
+ * before changing weights in place (ggml patch 0004 calls sdasm_forget on
+ * every buffer write).  Replaces sdasm_forget (sdasm.h:56-59). */
+void sdb_forget(const void *begin, size_t size);
+/* Entries and bytes the store holds on the current device. */
+void sdb_store_stats(int64_t *entries, int64_t *bytes);
+
+/* ToDo K/V downsampling factor of a token grid (sdasm.h:61-67, hooks.cc:166-172). */
+int sdb_token_downsampling(int64_t width, int64_t height);
+
+/* ---- tuning and diagnostics ----------------------------------------------
+ * sdb_set_tuning parses "name=value,..." as SDASM_TUNE does (cpu.cc:166-220):
+ * fuse, fuse_residual, winograd (0 direct, 1 F(2x2), 2 F(4x4)), store (0 repack
+ * every call), todo, todo_tokens, bits (0 or 8), group, block_n.  Returns
+ * SDB_INVALID on an unknown name or value. */
+int sdb_set_tuning(const char *spec);
+int sdb_get_tuning(const char *name, int64_t *value);
+/* The device error word of the current device (kernel-reported: bit 0 a
+ * bounded wait ran out, bit 1 an activation beyond the FP16 range of the
+ * split, bit 2 an index out of bounds); with clear != 0 it is reset.  Waits
+ * for the device first. */
+unsigned sdb_device_status(int clear);
+/* The last host-side error of this thread, as text. */
+const char *sdb_last_error(void);
+/* Kernel launches this library made on this process (for accounting). */
+uint64_t sdb_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

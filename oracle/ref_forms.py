@@ -1,0 +1,126 @@
+"""ctypes binding of ref_forms.c -- TEST INFRASTRUCTURE ONLY (the CPU baseline and a checker).
+
+build() compiles ref_forms.c with gcc (-O3 -march=native -fopenmp) into a
+directory of its own, per host CPU (a library built for one CPU may not run on
+another's), and loads it.  The functions take and return numpy arrays.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import platform
+import subprocess
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+SRC = HERE / "ref_forms.c"
+
+_lib = None
+
+
+def _cpu_tag() -> str:
+    info = platform.processor() or ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags") or line.startswith("model name"):
+                    info += line
+    except OSError:
+        pass
+    return hashlib.sha1(info.encode()).hexdigest()[:12]
+
+
+def build(march: str = "native") -> Path:
+    out_dir = Path(os.environ.get("SDB_ORACLE_BUILD", Path(tempfile.gettempdir()) / f"sdb_oracle_{_cpu_tag()}"))
+    out_dir.mkdir(parents=True, exist_ok=True)
+    lib = out_dir / f"libref_forms_{march.replace('-', '_')}.so"
+    if not lib.exists() or lib.stat().st_mtime < SRC.stat().st_mtime:
+        cmd = ["gcc", "-O3", f"-march={march}", "-fopenmp", "-shared", "-fPIC", "-o", str(lib), str(SRC), "-lm"]
+        subprocess.run(cmd, check=True, capture_output=True)
+    return lib
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(str(build()))
+        P = ctypes.c_void_p
+        i, f = ctypes.c_int, ctypes.c_float
+        lib.rf_mul_mat.argtypes = [P, i, i, P, i, P]
+        lib.rf_conv2d.argtypes = [P, i, i, i, i, P, i, i, i, i, i, i, i, i, i, P, i, i]
+        lib.rf_attention.argtypes = [P, P, P, P, i, i, i, i, i, i, i, f, i, i]
+        lib.rf_group_norm.argtypes = [P, P, i, i, ctypes.c_long, i, f, P, P, i]
+        lib.rf_threads.restype = i
+        lib.rf_set_threads.argtypes = [i]
+        _lib = lib
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def threads() -> int:
+    return load().rf_threads()
+
+
+def set_threads(n: int) -> None:
+    load().rf_set_threads(n)
+
+
+def mul_mat(w16: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """w16 (N, K) float16, x (M, K) float32 -> (M, N) float32 (mul_mat.cc's form)."""
+    w16 = np.ascontiguousarray(w16, dtype=np.float16)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, k = w16.shape
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    load().rf_mul_mat(_p(w16), n, k, _p(x), m, _p(y))
+    return y
+
+
+def conv2d(w16, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1), oc_range=None) -> np.ndarray:
+    """w16 (OC, IC, KH, KW) float16, x (N, IC, H, W) float32 -> (N, OC, OH, OW) (conv2d.cc's form)."""
+    w16 = np.ascontiguousarray(w16, dtype=np.float16)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    oc, ic, kh, kw = w16.shape
+    n, _, h, wd = x.shape
+    oh = (h + 2 * padding[1] - dilation[1] * (kh - 1) - 1) // stride[1] + 1
+    ow = (wd + 2 * padding[0] - dilation[0] * (kw - 1) - 1) // stride[0] + 1
+    out = np.zeros((n, oc, oh, ow), dtype=np.float32)
+    lo, hi = oc_range if oc_range else (0, oc)
+    load().rf_conv2d(_p(w16), oc, ic, kh, kw, _p(x), n, h, wd, stride[0], stride[1], padding[0], padding[1],
+                     dilation[0], dilation[1], _p(out), lo, hi)
+    return out
+
+
+def attention(q, k, v, heads: int, kv_heads: int, scale: float, q_range=None) -> np.ndarray:
+    """q (B, LQ, H*D), k/v (B, LK, HK*D) float32 -> (B, LQ, H*DV) (attention.cc's form)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    b, lq, hd = q.shape
+    lk = k.shape[1]
+    d = hd // heads
+    dv = v.shape[2] // kv_heads
+    out = np.zeros((b, lq, heads * dv), dtype=np.float32)
+    lo, hi = q_range if q_range else (0, lq)
+    load().rf_attention(_p(q), _p(k), _p(v), _p(out), b, lq, lk, heads, kv_heads, d, dv, scale, lo, hi)
+    return out
+
+
+def group_norm(x, groups: int, eps: float, gamma=None, beta=None, silu=False) -> np.ndarray:
+    """x (N, C, H, W) float32 -> normalised, with gamma/beta per channel and SiLU (norm.cc's form)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, c = x.shape[:2]
+    hw = int(np.prod(x.shape[2:]))
+    y = np.empty_like(x)
+    g = np.ascontiguousarray(gamma, dtype=np.float32) if gamma is not None else None
+    b = np.ascontiguousarray(beta, dtype=np.float32) if beta is not None else None
+    load().rf_group_norm(_p(x), _p(y), n, c, hw, groups, eps, _p(g) if g is not None else None,
+                         _p(b) if b is not None else None, 1 if silu else 0)
+    return y

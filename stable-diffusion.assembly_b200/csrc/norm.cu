@@ -1,0 +1,274 @@
+// GGML_OP_GROUP_NORM and GGML_OP_NORM with the chain after them.
+//
+// The reference (norm.cc:100-175) reads the tensor three times -- for the
+// mean, for the variance, for the output -- sums in double precision, and
+// applies the chain (scale, shift, SiLU) to each row as it writes it:
+//   mean = float(sum(x) / n), var = float(sum(float(x - mean)^2) / n),
+//   y = (x - mean) * float(1 / sqrt(var + eps)), then the chain.
+// Here one CTA (or a cluster of CTAs for large groups) owns one (image,
+// group) or a block of rows; the sums are double, reduced by warp shuffles
+// and across warps in shared memory; the mean and variance are rounded to
+// float exactly as the reference rounds them.  A group larger than what one
+// CTA should stream alone is split over several CTAs that combine their
+// double partial sums through global memory: the first pass writes per-CTA
+// partials, the second kernel finishes the statistics and normalises.  No CTA
+// waits on another (two launches instead of a grid barrier).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "../../include/sdb.h"
+#include "chain.cuh"
+#include "runtime.cuh"
+
+namespace sdb {
+
+namespace {
+
+constexpr int kNormThreads = 512;
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Sum over the CTA; every thread gets the total.
+__device__ double block_sum(double v, double* scratch) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    const int nw = blockDim.x >> 5;
+    for (int i = 0; i < nw; ++i) t += scratch[i];
+    return t;
+}
+
+struct GroupArgs {
+    const float* x;
+    float* y;
+    long long ne0, ne1, ne2, ne3;
+    long long xnb[4], ynb[4];   // element strides
+    int groups, per_group;
+    float eps;
+    int split;                  // CTAs per (image, group)
+    double* partial;            // [items][split][2]
+    Chain chain;
+};
+
+// Element e of the group's contiguous run (channels c0.. are contiguous: the
+// tensor is contiguous, as group_norm_supported requires).
+__device__ __forceinline__ float load_group(const GroupArgs& a, const float* base, long long e) {
+    return __ldg(base + e);
+}
+
+// Pass 1 of a split group: this CTA's slice sums (of x), then (x - mean)^2
+// after the mean is known -- done in two kernels, see group_stats_kernel.
+__global__ void __launch_bounds__(kNormThreads) group_sum_kernel(const GroupArgs a, int phase) {
+    __shared__ double scratch[32];
+    __shared__ float mean_s;
+    const int item = blockIdx.x / a.split;
+    const int part = blockIdx.x % a.split;
+    const int i3 = item / a.groups, g = item % a.groups;
+    const long long c0 = static_cast<long long>(g) * a.per_group;
+    const long long c1 = min(a.ne2, c0 + a.per_group);
+    if (c0 >= c1) return;
+    const long long count = a.ne0 * a.ne1 * (c1 - c0);
+    const float* base = a.x + i3 * a.xnb[3] + c0 * a.xnb[2];
+    const long long per = (count + a.split - 1) / a.split;
+    const long long e0 = part * per, e1 = min(count, e0 + per);
+    double s = 0.0;
+    if (phase == 0) {
+        for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) s += static_cast<double>(load_group(a, base, e));
+    } else {
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int p = 0; p < a.split; ++p) t += a.partial[(static_cast<long long>(item) * a.split + p) * 2];
+            mean_s = static_cast<float>(t / static_cast<double>(count));
+        }
+        __syncthreads();
+        const float mean = mean_s;
+        for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+            const float v = load_group(a, base, e) - mean;
+            s += static_cast<double>(v * v);
+        }
+    }
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) a.partial[(static_cast<long long>(item) * a.split + part) * 2 + phase] = s;
+}
+
+__global__ void __launch_bounds__(kNormThreads) group_apply_kernel(const GroupArgs a) {
+    __shared__ float stats[2];
+    const int item = blockIdx.x / a.split;
+    const int part = blockIdx.x % a.split;
+    const int i3 = item / a.groups, g = item % a.groups;
+    const long long c0 = static_cast<long long>(g) * a.per_group;
+    const long long c1 = min(a.ne2, c0 + a.per_group);
+    if (c0 >= c1) return;
+    const long long count = a.ne0 * a.ne1 * (c1 - c0);
+    if (threadIdx.x == 0) {
+        double s = 0.0, q = 0.0;
+        for (int p = 0; p < a.split; ++p) {
+            s += a.partial[(static_cast<long long>(item) * a.split + p) * 2];
+            q += a.partial[(static_cast<long long>(item) * a.split + p) * 2 + 1];
+        }
+        const float mean = static_cast<float>(s / static_cast<double>(count));
+        const float var = static_cast<float>(q / static_cast<double>(count));
+        stats[0] = mean;
+        stats[1] = 1.0f / sqrtf(var + a.eps);
+    }
+    __syncthreads();
+    const float mean = stats[0], scale = stats[1];
+    const float* xb = a.x + i3 * a.xnb[3] + c0 * a.xnb[2];
+    const long long per = (count + a.split - 1) / a.split;
+    const long long e0 = part * per, e1 = min(count, e0 + per);
+    const long long plane = a.ne0 * a.ne1;
+    for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+        const long long c = c0 + e / plane;
+        const long long r = (e % plane) / a.ne0;
+        const long long i0 = e % a.ne0;
+        float v = (__ldg(xb + e) - mean) * scale;
+        v = apply_chain(a.chain, v, i0, r, c, i3);
+        a.y[i0 * a.ynb[0] + r * a.ynb[1] + c * a.ynb[2] + i3 * a.ynb[3]] = v;
+    }
+}
+
+struct RowArgs {
+    const float* x;
+    float* y;
+    long long ne0, ne1, ne2;
+    long long rows;
+    long long xnb[4], ynb[4];
+    float eps;
+    Chain chain;
+};
+
+// One warp per row (rows of up to a few thousand elements: LayerNorm over
+// channels); each row is read three times from L1/L2, written once.
+__global__ void __launch_bounds__(256) norm_rows_kernel(const RowArgs a) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= a.rows) return;
+    const long long i1 = row % a.ne1;
+    const long long i2 = (row / a.ne1) % a.ne2;
+    const long long i3 = row / (a.ne1 * a.ne2);
+    const float* xr = a.x + i1 * a.xnb[1] + i2 * a.xnb[2] + i3 * a.xnb[3];
+    float* yr = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3];
+    double s = 0.0;
+    for (long long i = lane; i < a.ne0; i += 32) s += static_cast<double>(__ldg(xr + i * a.xnb[0]));
+    s = warp_sum(s);
+    const float mean = static_cast<float>(s / static_cast<double>(a.ne0));
+    double q = 0.0;
+    for (long long i = lane; i < a.ne0; i += 32) {
+        const float v = __ldg(xr + i * a.xnb[0]) - mean;
+        q += static_cast<double>(v * v);
+    }
+    q = warp_sum(q);
+    const float var = static_cast<float>(q / static_cast<double>(a.ne0));
+    const float scale = 1.0f / sqrtf(var + a.eps);
+    for (long long i = lane; i < a.ne0; i += 32) {
+        const float v = (__ldg(xr + i * a.xnb[0]) - mean) * scale;
+        yr[i * a.ynb[0]] = apply_chain(a.chain, v, i, i1, i2, i3);
+    }
+}
+
+bool f32(const sdb_tensor* t) { return t && t->type == SDB_TYPE_F32 && t->data; }
+
+bool contiguous(const sdb_tensor* t) {
+    int64_t expect = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (t->ne[d] <= 0) return false;
+        if (t->ne[d] > 1 && t->nb[d] != expect) return false;
+        expect *= t->ne[d];
+    }
+    return true;
+}
+
+bool same_shape(const sdb_tensor* a, const sdb_tensor* b) {
+    for (int d = 0; d < 4; ++d)
+        if (a->ne[d] != b->ne[d]) return false;
+    return true;
+}
+
+// Double partial sums of split groups (2 per CTA slice), grown on demand.
+double* partial_buffer(size_t count) {
+    static thread_local double* buf = nullptr;
+    static thread_local size_t cap = 0;
+    static thread_local int dev = -1;
+    int d = 0;
+    cudaGetDevice(&d);
+    if (count > cap || d != dev) {
+        if (buf && d == dev) cudaFree(buf);
+        buf = nullptr;
+        cap = 0;
+        if (cudaMalloc(&buf, count * sizeof(double)) != cudaSuccess) return nullptr;
+        cap = count;
+        dev = d;
+    }
+    return buf;
+}
+
+}  // namespace
+
+}  // namespace sdb
+
+using namespace sdb;
+
+extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps,
+                              const sdb_chain* chain, void* stream) {
+    if (!f32(x) || !f32(dst) || !contiguous(x) || !same_shape(x, dst) || groups <= 0)
+        return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: not supported");
+    if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))
+        return fail(SDB_INVALID, "sdb_group_norm: invalid chain");
+    for (int d = 0; d < 4; ++d)
+        if (dst->nb[d] % 4) return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: misaligned output");
+    const auto st = static_cast<cudaStream_t>(stream);
+    GroupArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.y = static_cast<float*>(dst->data);
+    a.ne0 = x->ne[0]; a.ne1 = x->ne[1]; a.ne2 = x->ne[2]; a.ne3 = x->ne[3];
+    for (int d = 0; d < 4; ++d) { a.xnb[d] = x->nb[d] / 4; a.ynb[d] = dst->nb[d] / 4; }
+    a.groups = groups;
+    a.per_group = static_cast<int>((a.ne2 + groups - 1) / groups);
+    a.eps = eps;
+    a.chain = make_chain(chain);
+    const long long items = static_cast<long long>(groups) * a.ne3;
+    const long long group_elems = a.ne0 * a.ne1 * a.per_group;
+    // Enough CTAs for every SM several times over, each slice at least 8K elements.
+    const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
+    a.split = static_cast<int>(std::min<long long>(want, std::max<long long>(1, group_elems / 8192)));
+    a.partial = partial_buffer(static_cast<size_t>(items * a.split * 2));
+    if (!a.partial) return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: partial sums");
+    const unsigned grid = static_cast<unsigned>(items * a.split);
+    group_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 0);
+    group_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 1);
+    group_apply_kernel<<<grid, kNormThreads, 0, st>>>(a);
+    count_launch(3);
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+extern "C" int sdb_norm(const sdb_tensor* x, const sdb_tensor* dst, float eps, const sdb_chain* chain, void* stream) {
+    if (!f32(x) || !f32(dst) || !same_shape(x, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_norm: not supported");
+    if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))
+        return fail(SDB_INVALID, "sdb_norm: invalid chain");
+    for (int d = 0; d < 4; ++d)
+        if (x->nb[d] % 4 || dst->nb[d] % 4) return fail(SDB_NOT_SUPPORTED, "sdb_norm: misaligned");
+    const auto st = static_cast<cudaStream_t>(stream);
+    RowArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.y = static_cast<float*>(dst->data);
+    a.ne0 = x->ne[0]; a.ne1 = x->ne[1]; a.ne2 = x->ne[2];
+    a.rows = x->ne[1] * x->ne[2] * x->ne[3];
+    for (int d = 0; d < 4; ++d) { a.xnb[d] = x->nb[d] / 4; a.ynb[d] = dst->nb[d] / 4; }
+    a.eps = eps;
+    a.chain = make_chain(chain);
+    const long long threads = a.rows * 32;
+    norm_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}

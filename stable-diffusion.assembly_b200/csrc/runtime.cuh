@@ -1,0 +1,55 @@
+// Host-side runtime shared by the entry points: per-thread error text, the
+// per-device error word, tuning, launch accounting, CUDA-call checking.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <string>
+
+#include "../../include/sdb.h"
+
+namespace sdb {
+
+// The knobs of sdb_set_tuning (the GPU analogue of the reference's Tuning,
+// kernels.h:91-135).
+struct Tuning {
+    int64_t fuse = 1;            // match chains after operations (shim)
+    int64_t fuse_residual = 1;   // and residual additions not in place
+    int64_t winograd = 2;        // 0 direct, 1 F(2x2,3x3), 2 F(4x4,3x3) where it fits
+    int64_t store = 1;           // keep packed weights between calls
+    int64_t todo = 1;            // ToDo K/V downsampling factor (1 = none)
+    int64_t todo_tokens = 4096;  // least tokens of a grid downsampled
+    int64_t bits = 0;            // 8: the int8 path
+    int64_t group = 64;          // quantisation group along K
+    int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
+};
+
+Tuning& tuning();
+
+void set_error(const std::string& what);
+int fail(sdb_status status, const std::string& what);
+int cuda_fail(cudaError_t e, const char* where);
+
+// The device error word of the current device (allocated once per device).
+unsigned* device_error_word();
+
+void count_launch(uint64_t n = 1);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, void* addr,
+                           const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                           CUtensorMapSwizzle swizzle);
+
+int current_sm_count();
+
+#define SDB_CUDA(call)                                        \
+    do {                                                      \
+        cudaError_t e_ = (call);                              \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+    } while (0)
+
+}  // namespace sdb

@@ -1,0 +1,250 @@
+// The weight store and the packing kernel (see store.cuh).
+#include "store.cuh"
+
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
+#include "ptx.cuh"
+#include "runtime.cuh"
+
+namespace sdb {
+
+namespace {
+
+struct PackArgs {
+    const uint8_t* src;
+    int type;             // SDB_TYPE_F16 / SDB_TYPE_F32
+    long long nb[4];      // source strides in bytes
+    int layout;
+    long long n;          // logical rows (gated: 2 * half)
+    long long k;          // logical K (linear) / IC (conv)
+    int kw, kh, icp;
+    long long half, halfpad;
+    long long npad, kpad;
+    long long rows;       // packed rows of one block (npad, or 2 * halfpad for gated)
+    int split;
+    __half* out;
+    unsigned* err;
+};
+
+__global__ void pack_weights_kernel(const PackArgs p) {
+    const long long total = p.rows * p.kpad;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = idx / p.kpad;
+        const long long kp = idx - r * p.kpad;
+        long long off = -1;
+        if (p.layout == 0) {  // linear
+            if (r < p.n && kp < p.k) off = kp * p.nb[0] + r * p.nb[1];
+        } else if (p.layout == 1) {  // conv
+            const long long tap = kp / p.icp, ic = kp - tap * p.icp;
+            if (r < p.n && tap < static_cast<long long>(p.kw) * p.kh && ic < p.k) {
+                const long long kx = tap % p.kw, ky = tap / p.kw;
+                off = kx * p.nb[0] + ky * p.nb[1] + ic * p.nb[2] + r * p.nb[3];
+            }
+        } else {  // gated
+            long long src_row = -1;
+            if (r < p.half) src_row = r;
+            else if (r >= p.halfpad && r - p.halfpad < p.half) src_row = p.half + (r - p.halfpad);
+            if (src_row >= 0 && kp < p.k) off = kp * p.nb[0] + src_row * p.nb[1];
+        }
+        float w = 0.0f;
+        if (off >= 0) {
+            w = p.type == SDB_TYPE_F16 ? __half2float(*reinterpret_cast<const __half*>(p.src + off))
+                                       : *reinterpret_cast<const float*>(p.src + off);
+        }
+        if (p.split) {
+            __half hi, lo;
+            split_half(w, hi, lo);
+            if (!(fabsf(w) <= kHalfLimit)) atomicOr(p.err, kErrRange);
+            p.out[idx] = hi;
+            p.out[p.npad * p.kpad + idx] = lo;
+        } else {
+            p.out[idx] = __float2half_rn(w);  // exact for FP16 sources
+        }
+    }
+}
+
+struct Key {
+    int dev;
+    const void* data;
+    int type;
+    int64_t ne[4];
+    int64_t nb[4];
+    int layout;
+    int icp;
+    int64_t half;
+    bool operator<(const Key& o) const {
+        return std::tie(dev, data, type, ne[0], ne[1], ne[2], ne[3], nb[0], nb[1], nb[2], nb[3], layout, icp, half) <
+               std::tie(o.dev, o.data, o.type, o.ne[0], o.ne[1], o.ne[2], o.ne[3], o.nb[0], o.nb[1], o.nb[2],
+                        o.nb[3], o.layout, o.icp, o.half);
+    }
+};
+
+std::mutex g_store_mutex;
+std::map<Key, std::shared_ptr<Packed>> g_store;
+
+// Bytes spanned by a tensor from its data pointer.
+int64_t extent_bytes(const sdb_tensor* t) {
+    int64_t last = 0;
+    for (int d = 0; d < 4; ++d) last += (t->ne[d] - 1) * t->nb[d];
+    return last + (t->type == SDB_TYPE_F16 ? 2 : 4);
+}
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+int make_maps(Packed& p) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(p.kpad), static_cast<uint64_t>(p.rows_total)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(p.kpad) * 2};
+    for (int bn : {64, 128}) {
+        const uint32_t box[2] = {64, static_cast<uint32_t>(bn)};
+        CUtensorMap* m = bn == 128 ? &p.map128 : &p.map64;
+        const CUresult r = encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.data, dims, strides, box,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (r != CUDA_SUCCESS) return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for packed weights");
+    }
+    return SDB_OK;
+}
+
+}  // namespace
+
+Packed::~Packed() {
+    if (ready) cudaEventDestroy(ready);
+    if (data) cudaFree(data);
+}
+
+int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_t k_logical, int icp, int64_t half,
+                   cudaStream_t stream, std::shared_ptr<Packed>* out) {
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    const bool keep = tuning().store != 0;
+    if (!keep) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
+        if (cap != cudaStreamCaptureStatusNone) return fail(SDB_INVALID, "store=0 packs per call: not under capture");
+    }
+    Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]}, {w->nb[0], w->nb[1], w->nb[2], w->nb[3]},
+            static_cast<int>(layout), icp, half};
+    if (keep) {
+        std::lock_guard<std::mutex> lock(g_store_mutex);
+        auto it = g_store.find(key);
+        if (it != g_store.end()) {
+            // Wait for the packing only while it may still run.  Under stream
+            // capture nothing may be queried: the packing must have finished
+            // (been seen finished) before the capture began.
+            Packed& pk = *it->second;
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
+            if (cap != cudaStreamCaptureStatusNone) {
+                if (!pk.done) return fail(SDB_INVALID, "weights first used under stream capture: call once before");
+            } else if (!pk.done) {
+                const cudaError_t q = cudaEventQuery(pk.ready);
+                if (q == cudaSuccess) pk.done = true;
+                else if (q == cudaErrorNotReady) SDB_CUDA(cudaStreamWaitEvent(stream, pk.ready, 0));
+                else return cuda_fail(q, "cudaEventQuery(packed weights)");
+            }
+            *out = it->second;
+            return SDB_OK;
+        }
+    }
+    auto p = std::make_shared<Packed>();
+    const bool split = w->type == SDB_TYPE_F32;
+    int64_t kdim;
+    if (layout == Layout::conv) kdim = w->ne[0] * w->ne[1] * icp;
+    else kdim = k_logical;
+    p->kpad = round_up(std::max<int64_t>(kdim, 1), 64);
+    p->icp = icp;
+    p->split = split;
+    if (layout == Layout::gated) {
+        const int64_t halfpad = round_up(half, kRowPad);
+        p->npad = 2 * halfpad;
+        p->rows_total = 2 * halfpad;
+        p->b1_row = halfpad;
+    } else {
+        p->npad = round_up(n_logical, kRowPad);
+        p->rows_total = split ? 2 * p->npad : p->npad;
+        p->b1_row = split ? p->npad : 0;
+    }
+    p->bytes = static_cast<size_t>(p->rows_total * p->kpad * 2);
+    SDB_CUDA(cudaMalloc(&p->data, p->bytes));
+    SDB_CUDA(cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming));
+    if (int st = make_maps(*p); st != SDB_OK) return st;
+
+    PackArgs a{};
+    a.src = static_cast<const uint8_t*>(w->data);
+    a.type = w->type;
+    for (int d = 0; d < 4; ++d) a.nb[d] = w->nb[d];
+    a.layout = static_cast<int>(layout);
+    a.n = layout == Layout::gated ? 2 * half : n_logical;
+    a.k = layout == Layout::conv ? w->ne[2] : k_logical;
+    a.kw = static_cast<int>(w->ne[0]);
+    a.kh = static_cast<int>(w->ne[1]);
+    a.icp = icp > 0 ? icp : 1;
+    a.half = half;
+    a.halfpad = p->b1_row;
+    a.npad = p->npad;
+    a.kpad = p->kpad;
+    a.rows = layout == Layout::gated ? p->rows_total : p->npad;
+    a.split = split ? 1 : 0;
+    a.out = static_cast<__half*>(p->data);
+    a.err = device_error_word();
+    const long long total = a.rows * a.kpad;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    pack_weights_kernel<<<blocks, 256, 0, stream>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    SDB_CUDA(cudaEventRecord(p->ready, stream));
+    if (keep) {
+        std::lock_guard<std::mutex> lock(g_store_mutex);
+        g_store[key] = p;
+    }
+    *out = p;
+    return SDB_OK;
+}
+
+}  // namespace sdb
+
+extern "C" void sdb_forget(const void* begin, size_t size) {
+    const auto b = reinterpret_cast<uintptr_t>(begin);
+    const uintptr_t e = b + size;
+    std::vector<std::shared_ptr<sdb::Packed>> dropped;
+    {
+        std::lock_guard<std::mutex> lock(sdb::g_store_mutex);
+        for (auto it = sdb::g_store.begin(); it != sdb::g_store.end();) {
+            const auto s = reinterpret_cast<uintptr_t>(it->first.data);
+            sdb_tensor t{};
+            t.type = it->first.type;
+            for (int d = 0; d < 4; ++d) { t.ne[d] = it->first.ne[d]; t.nb[d] = it->first.nb[d]; }
+            const uintptr_t se = s + static_cast<uintptr_t>(sdb::extent_bytes(&t));
+            if (s < e && b < se) {
+                dropped.push_back(it->second);
+                it = sdb::g_store.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
+    // Entries may still be read by kernels in flight: wait before freeing.
+    if (!dropped.empty()) cudaDeviceSynchronize();
+    dropped.clear();
+}
+
+extern "C" void sdb_store_stats(int64_t* entries, int64_t* bytes) {
+    std::lock_guard<std::mutex> lock(sdb::g_store_mutex);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int64_t n = 0, b = 0;
+    for (const auto& kv : sdb::g_store) {
+        if (kv.first.dev != dev) continue;
+        ++n;
+        b += static_cast<int64_t>(kv.second->bytes);
+    }
+    if (entries) *entries = n;
+    if (bytes) *bytes = b;
+}

@@ -1,0 +1,50 @@
+// The weight store: weights repacked once into the layout the GEMM reads,
+// kept on the device and keyed by where they came from.  It stands in for the
+// reference's store of packed panels (store.h:58-120, store.cc:202-266), with
+// the same key (address, type, shape, strides, layout) and the same
+// invalidation: sdb_forget() on any overlap with memory about to change.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+
+#include "../../include/sdb.h"
+
+namespace sdb {
+
+enum class Layout : int {
+    linear = 0,   // rows n of w [K, N]; k as is
+    conv = 1,     // rows oc of w [KW, KH, IC, OC]; k = (ky * KW + kx) * icp + ic
+    gated = 2,    // GEGLU: rows [0, half) x weights, [halfpad, halfpad + half) gate weights
+};
+
+constexpr int kRowPad = 256;  // packed rows are padded to the widest GEMM tile
+
+struct Packed {
+    void* data = nullptr;     // FP16 [rows_total][kpad]
+    size_t bytes = 0;
+    int64_t rows_total = 0;
+    int64_t kpad = 0;
+    int64_t npad = 0;         // rows of one operand (hi) block
+    int64_t b1_row = 0;       // row of the second operand (lo, or gate), 0 if none
+    int icp = 0;              // conv: channels per tap
+    bool split = false;       // FP32 weights: hi rows then lo rows
+    CUtensorMap map64{};      // box {64, 64}
+    CUtensorMap map128{};     // box {64, 128}
+    cudaEvent_t ready = nullptr;
+    bool done = false;        // the packing was seen complete
+    bool owned_by_store = true;
+    ~Packed();
+};
+
+// The packed form of w for `layout`, from the store or packed now on
+// `stream`.  With the store off (tuning store=0) the result is packed anew
+// and freed when the returned pointer is released (stream-ordered).
+// Returns an sdb_status; *out is set on success.
+int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_t k_logical, int icp,
+                   int64_t half, cudaStream_t stream, std::shared_ptr<Packed>* out);
+
+}  // namespace sdb

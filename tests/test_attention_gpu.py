@@ -1,0 +1,79 @@
+"""Parity of attention (FLASH_ATTN_EXT, no mask) against the exact oracle.
+
+Cases: the reference's (tests/ops_test.cc:925-938) -- SD 1.5's self- and
+cross-attention made smaller, heads of 80 and 160, the VAE's single head of
+512, dims and keys of no multiple of a panel with heads sharing keys, FP16
+keys and values -- and BASELINE config 3 (8 heads x 40, Lq = Lk = 4096 and
+Lk = 77), with and without the residual add fused.  Q, K, V ~ U(-1, 1)
+(ops_test.cc:478-483); bound: the ops_test metric <= 1e-6.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from helpers import canary_like, cuda_tensor, host, rng
+
+pytestmark = pytest.mark.gpu
+
+# (d, lq, lk, h, hk, b, kv dtype) -- ops_test.cc:925-938
+ATTN_CASES = [
+    (40, 300, 4096, 2, 2, 2, np.float32),
+    (40, 200, 77, 2, 2, 2, np.float32),
+    (80, 100, 1024, 2, 2, 1, np.float32),
+    (160, 64, 256, 2, 2, 2, np.float32),
+    (512, 40, 300, 1, 1, 1, np.float32),
+    (13, 37, 29, 4, 2, 3, np.float32),
+    (64, 50, 100, 2, 1, 1, np.float16),
+]
+
+
+def run(cuda, d, lq, lk, h, hk, b, kvtype, seed=oracle.SEED, normal=False, residual=False):
+    import sdb
+
+    g = rng(seed)
+    if normal:
+        q = g.standard_normal((b, lq, h * d)).astype(np.float32)
+        k = g.standard_normal((b, lk, hk * d)).astype(np.float32).astype(kvtype)
+        v = g.standard_normal((b, lk, hk * d)).astype(np.float32).astype(kvtype)
+    else:
+        q = oracle.uniform(g, (b, lq, h * d), 1.0)
+        k = oracle.uniform(g, (b, lk, hk * d), 1.0, kvtype)
+        v = oracle.uniform(g, (b, lk, hk * d), 1.0, kvtype)
+    scale = 1.0 / math.sqrt(d)
+    out = canary_like((b, lq, h * d), cuda)
+    chain = None
+    res = None
+    if residual:
+        res = g.standard_normal((b, lq, h * d)).astype(np.float32)
+        rt = cuda_tensor(res, cuda)
+        # dst is [DV, H, LQ, B]; the residual [H*DV, LQ, B] seen with the same coordinates.
+        chain = sdb.Chain().add(rt, nb=[1, d, h * d, lq * h * d])
+    sdb.attention_heads(cuda_tensor(q, cuda), cuda_tensor(k, cuda), cuda_tensor(v, cuda), h, hk, scale, out=out,
+                        chain=chain)
+    exact, mag = oracle.attention_exact(q, k, v, h, hk, scale)
+    if residual:
+        exact = exact + res.astype(np.float64)
+        mag = mag + np.abs(res.astype(np.float64))
+    return oracle.metric(host(out), exact, mag)
+
+
+@pytest.mark.parametrize("case", ATTN_CASES, ids=lambda c: f"d{c[0]}_q{c[1]}_k{c[2]}_h{c[3]}_{c[4]}_b{c[5]}")
+def test_attention_reference_cases(cuda, case):
+    import sdb
+
+    d = case[0]
+    if d > 160:
+        pytest.xfail("heads wider than 160 are not taken yet (the caller computes them)")
+    err = run(cuda, *case)
+    assert err <= oracle.K_B200, f"error {err:.3g}"
+
+
+@pytest.mark.parametrize("lk,residual", [(4096, False), (77, False), (4096, True), (77, True)])
+def test_attention_config3(cuda, lk, residual):
+    """8 heads x 40, Lq = 4096, Q/K/V ~ N(0, 1), optional fused residual."""
+    err = run(cuda, 40, 4096, lk, 8, 8, 1, np.float32, seed=5, normal=True, residual=residual)
+    assert err <= oracle.K_B200, f"error {err:.3g}"

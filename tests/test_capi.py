@@ -1,0 +1,90 @@
+"""CPU checks of the C ABI: the library loads and exports every symbol include/sdb.h declares.
+
+No compute call is made here (there is no GPU on the CPU runner).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+LIB = ROOT / "stable-diffusion.assembly_b200" / "libsdb.so"
+
+
+def declared_functions(header: Path) -> list[str]:
+    text = header.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sdb_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not LIB.exists():
+        pytest.skip("libsdb.so not built")
+    return ctypes.CDLL(str(LIB))
+
+
+def test_header_declarations_are_exported(lib):
+    names = declared_functions(ROOT / "include" / "sdb.h")
+    assert names, "no declarations found"
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_binding_lists_every_export():
+    import sdb
+
+    names = declared_functions(ROOT / "include" / "sdb.h")
+    assert sorted(sdb.EXPORTS) == names
+
+
+def test_tuning_parser(lib):
+    import sdb
+
+    sdb._lib = None
+    sdb.load()
+    assert sdb.get_tuning("winograd") in (0, 1, 2)
+    sdb.set_tuning("winograd=1,block_n=256")
+    assert sdb.get_tuning("winograd") == 1 and sdb.get_tuning("block_n") == 256
+    sdb.set_tuning("winograd=2,block_n=0")
+    with pytest.raises(sdb.SdbError):
+        sdb.set_tuning("nonsense=1")
+    with pytest.raises(sdb.SdbError):
+        sdb.set_tuning("winograd=7")
+    assert "unknown" in sdb.load().sdb_last_error().decode() or "bad value" in sdb.load().sdb_last_error().decode()
+
+
+def test_token_downsampling(lib):
+    """hooks.cc:166-172: 1 unless todo >= 2 and the grid has todo_tokens tokens."""
+    import sdb
+
+    sdb.load()
+    assert sdb.token_downsampling(64, 64) == 1
+    sdb.set_tuning("todo=2,todo_tokens=4096")
+    try:
+        assert sdb.token_downsampling(64, 64) == 2
+        assert sdb.token_downsampling(32, 32) == 1
+        assert sdb.token_downsampling(0, 64) == 1
+    finally:
+        sdb.set_tuning("todo=1")
+
+
+def test_unsupported_shapes_are_not_taken(lib):
+    """A mul_mat whose inner dimensions disagree is 'not taken' (0), without touching memory."""
+    import sdb
+
+    sdb.load()
+    w, x, y = sdb.Tensor(), sdb.Tensor(), sdb.Tensor()
+    for t, ne in ((w, [64, 32, 1, 1]), (x, [48, 10, 1, 1]), (y, [32, 10, 1, 1])):
+        t.type = sdb.TYPE_F32
+        for k in range(4):
+            t.ne[k] = ne[k]
+        t.nb[0] = 4
+        t.nb[1] = 4 * ne[0]
+        t.nb[2] = t.nb[1] * ne[1]
+        t.nb[3] = t.nb[2]
+        t.data = 16  # never dereferenced
+    assert sdb.load().sdb_mul_mat_supported(w, x, y) == 0
