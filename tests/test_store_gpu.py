@@ -88,7 +88,7 @@ def test_store_off_repacks(cuda):
         n0 = sdb.launch_count()
         a = host(sdb.mul_mat(w, x))
         assert sdb.launch_count() - n0 == 2
-        assert sdb.store_stats()[0] == before
+        assert sdb.store_stats()[0] <= before
     finally:
         sdb.set_tuning("store=1")
     b = host(sdb.mul_mat(w, x))
