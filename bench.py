@@ -56,7 +56,7 @@ def measured_peaks() -> dict:
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 50 ms while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -71,7 +71,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -278,7 +278,7 @@ def run_reference(args) -> None:
         return
     for _ in range(max(0, args.warmup)):
         pass
-    samples = [cpu_baseline() for _ in range(max(1, args.steps // 10 or 1))]
+    samples = [cpu_baseline() for _ in range(max(1, min(3, args.steps)))]
     best = max(samples, key=lambda s: s["value"])
     line = {"metric": METRIC, "value": best["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 / best["value"], "higher_is_better": True,
@@ -292,8 +292,8 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -321,9 +321,6 @@ def main() -> None:
     sdb.load()
     work = HotOps(dev, seed=1234)
     nops = len(work.ops)
-    for i in range(max(3, args.warmup)):
-        work.step(i)
-    torch.cuda.synchronize()
 
     def barrier():
         if dist is not None:
@@ -336,24 +333,60 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # Timed region: K steps, per-op events on the launching stream.
-    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nops)]
-              for _ in range(args.steps)]
+    # Each step's launches are captured once per input set into a CUDA graph
+    # and replayed: the device time of the kernels, without the host's
+    # per-call work (that is in the end-to-end number below).  Warm-up on the
+    # capture stream sizes the library's workspace before capture.
+    cap = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(cap):
+        for i in range(max(3, args.warmup)):
+            work.step(i)
+    torch.cuda.synchronize()
+    graphs, op_graphs = [], [[None] * work.SETS for _ in range(nops)]
+    launches_per_step = 0
+    for sidx in range(work.SETS):
+        g = torch.cuda.CUDAGraph()
+        n0 = sdb.launch_count()
+        with torch.cuda.graph(g, stream=cap):
+            work.step(sidx)
+        launches_per_step = sdb.launch_count() - n0
+        graphs.append(g)
+        for j, (_, _, _, fn) in enumerate(work.ops):
+            gj = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gj, stream=cap):
+                fn(work.sets[sidx])
+            op_graphs[j][sidx] = gj
+    torch.cuda.synchronize()
+    for i in range(args.warmup):
+        graphs[i % work.SETS].replay()
+    torch.cuda.synchronize()
+
+    # Timed region: K steps.
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    launches0 = sdb.launch_count()
     with ClockSampler(local) as clocks:
         start.record()
         for i in range(args.steps):
-            work.step(i, events[i])
+            graphs[i % work.SETS].replay()
         end.record()
         torch.cuda.synchronize()
-    launches = sdb.launch_count() - launches0
+    launches = launches_per_step * args.steps
     barrier()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    per_op_ms = [sum(events[i][j][0].elapsed_time(events[i][j][1]) for i in range(args.steps)) / args.steps
-                 for j in range(nops)]
+
+    # Each op alone (graph replays over the rotating sets), for the roofline.
+    per_op_ms = []
+    reps = max(30, min(300, args.steps))
+    for j in range(nops):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            op_graphs[j][i % work.SETS].replay()
+        e1.record()
+        torch.cuda.synchronize()
+        per_op_ms.append(e0.elapsed_time(e1) / reps)
+    del graphs, op_graphs
 
     # End to end through the public API with host buffers.
     ins, outs, h_in, h_out = work.e2e_buffers()
@@ -398,7 +431,8 @@ def main() -> None:
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "ops": [o[0] for o in work.ops], "parallelism": f"replicas x{world}",
-                   "l2": "3 rotating input sets (~240 MB) > L2", "weights": "random-init FP16, packed once"},
+                   "l2": "3 rotating input sets (~240 MB) > L2", "weights": "random-init FP16, packed once",
+                   "timing": "CUDA-graph replay of each step's launches; per-op times from graphs of each op"},
         "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "peak_source": peaks["source"], "traffic": traffic,
                      "work_per_launch": work_units, "avg_launch_ms": per_op_ms[dom]},

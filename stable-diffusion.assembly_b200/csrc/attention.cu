@@ -1,28 +1,31 @@
 // GGML_OP_FLASH_ATTN_EXT without a mask: softmax(scale q k^T) v per head, the
 // reference's attention_compute (attention.cc:858-1064) on tcgen05.
 //
-// One CTA takes a block of 128 queries of one head and walks the keys in
-// blocks of BK.  Q, K and V arrive in FP32 (or FP16 K/V) and are split by
-// four converter warps into FP16 pairs x = hi + lo 2^-11 (ptx.cuh); each
-// product is taken as three tensor-core products (hi.hi into one FP32
-// accumulator, hi.lo + lo.hi into a second, both in tensor memory):
-//   S   = Q K^T  (M = 128 queries, N = BK keys, K = D)
-//   O  += P V    (M = 128 queries, N = DV, K = BK keys; V read MN-major)
-// Four softmax warps own one query row each: they read S from tensor memory,
-// scale it, and take exponentials (the reference's exponential(), the
-// Cephes-form polynomial of scalar_math.h) against a reference maximum that
-// is raised -- and O rescaled -- only when a block's maximum exceeds it by
-// more than 8 (so every weight stays below e^8 in FP16).  The row sums are
-// kept in double precision and the output is divided once, by
-// float(1 / sum), at the end (attention.cc:1052-1063).  Keys past LK get
-// weight 0; queries past LQ are not written.
+// Q, K and V are split once (split.cuh, split_tiles) into FP16 pairs
+// x = hi + lo 2^-11, stored tile by tile in the UMMA no-swizzle core-matrix
+// layout, so that each tile arrives in shared memory as one contiguous bulk
+// copy.  One CTA takes a block of 128 queries of one
+// head (and up to 80 of its value dims) and walks the keys in blocks of BK;
+// each product is three tensor-core products (hi.hi into one FP32
+// accumulator, hi.lo + lo.hi into a second):
+//   S   = Q K^T  (M = 128 queries, N = BK keys, K = head dims)
+//   O_j = P V    (M = 128 queries, N = value dims, K = BK keys; V MN-major)
+// S is double-buffered in tensor memory, so the next block's Q K^T runs while
+// the softmax warps work on this one.  Eight softmax warps, two per quarter of
+// the tensor-memory lanes, own one query row per lane pair, each half of a
+// block's keys: they read S, scale it by scale * log2(e) and take 2^(s - m)
+// with the ex2 instruction against a reference maximum that is raised -- and
+// the output rescaled -- only when a block's maximum exceeds it by 11.5 (e^8),
+// so every weight stays a normal FP16 pair.  The row sums are kept in double
+// precision, and the output is divided once, by float(1 / sum), at the end
+// (attention.cc:1052-1063).  Keys past LK get weight 0; queries past LQ are
+// not written.
 //
-// The tensor core's FP32 accumulation rounds toward zero, so no sum is left
-// to it for long: each key block's P V lands in a fresh tensor-memory
-// accumulator that the softmax warps add into FP32 registers (where the
-// rescale is a multiply), and the hi product of S is kept per 64 dims and
-// summed in registers.  A CTA computes at most 80 output dims (DVC); wider
-// value heads take several CTAs, each recomputing S.
+// The tensor core's FP32 accumulation rounds toward zero, so no long sum is
+// left to it: each block's P V lands in a fresh accumulator that the softmax
+// warps add into FP32 registers, and the hi product of S is kept per 64 dims
+// and summed in registers.  Value heads wider than 80 dims take several CTAs,
+// each recomputing S.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -34,128 +37,84 @@
 #include "chain.cuh"
 #include "ptx.cuh"
 #include "runtime.cuh"
+#include "split.cuh"
 
 namespace sdb {
 
 namespace {
 
 constexpr int kAttnQ = 128;
-constexpr int kAttnThreads = 288;   // warps 0-3 softmax, 4-7 converters, 8 MMA
-constexpr float kRescaleAbove = 8.0f;
+constexpr int kAttnThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int kStagesKV = 3;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleAbove = 11.5f;  // log2 units: e^8
 
 struct AttnArgs {
-    const void* q;
-    const void* k;
-    const void* v;
+    const uint8_t* qs;   // split tiles of 128 queries x dp: hi plane, then lo plane
+    const uint8_t* ks;   // split tiles of BK keys x dp
+    const uint8_t* vs;   // split tiles of BK keys x dvs (value dims padded to the CTAs' chunks)
+    long long q_plane, k_plane, v_plane;  // bytes of one (hi) plane
+    int ntq, ntk;        // tiles of queries / keys per head
+    int dvs;             // value dims of a stored row
     float* out;
-    long long qnb[4], knb[4], vnb[4], onb[4];  // element strides
-    int k_half, v_half;                         // K / V stored as FP16
+    long long onb[4];  // element strides of dst [DV, H, LQ, B]
     int d, dv, lq, lk, h, hk, b;
-    int dp, dvp;                                // padded to multiples of 16
-    int dv_chunks;                              // CTAs along the value dims
-    float scale;
+    int dp, dvp, dv_chunks;
+    int rq, rk;        // rows of the hi planes of Q and of K / V
+    float scale2;      // scale * log2(e)
     Chain chain;
     unsigned* err;
 };
 
-template <int BK>
 struct AttnLayout {
-    int q_hi, q_lo, stage0, stage_bytes, k_lo_off, v_hi_off, v_lo_off, p_hi, p_lo, bars, total;
-    __host__ __device__ AttnLayout(int dp, int dvp) {
+    static __host__ __device__ int p_bytes(int bk) { return 2 * kAttnQ * bk * 2; }
+    int q_hi, q_lo, stage0, stage_bytes, k_lo, v_hi, v_lo, p_hi, p_lo, xmax, xsum, bars, total;
+    __host__ __device__ AttnLayout(int dp, int dvc, int bk) {
         const int qb = kAttnQ * dp * 2;
         q_hi = 0;
         q_lo = qb;
         stage0 = 2 * qb;
-        const int kb = BK * dp * 2, vb = BK * dvp * 2;
-        k_lo_off = kb;
-        v_hi_off = 2 * kb;
-        v_lo_off = 2 * kb + vb;
+        const int kb = bk * dp * 2, vb = bk * dvc * 2;
+        k_lo = kb;
+        v_hi = 2 * kb;
+        v_lo = 2 * kb + vb;
         stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
-        p_hi = stage0 + 2 * stage_bytes;
-        p_lo = p_hi + kAttnQ * BK * 2;
-        bars = p_lo + kAttnQ * BK * 2;
-        total = bars + 128;
+        p_hi = stage0 + kStagesKV * stage_bytes;   // [2] buffers, p_bytes apart
+        p_lo = p_hi + kAttnQ * bk * 2;
+        xmax = p_hi + 2 * p_bytes(bk);            // [2][128][2] floats
+        xsum = xmax + 2 * kAttnQ * 2 * 4;  // [128][2] doubles
+        bars = xsum + kAttnQ * 2 * 8;
+        total = bars + 512;
     }
 };
 
-__device__ __forceinline__ float load_elem(const void* base, long long off, int half) {
-    return half ? __half2float(__ldg(reinterpret_cast<const __half*>(base) + off))
-                : __ldg(reinterpret_cast<const float*>(base) + off);
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-// 8 consecutive elements (dims) of one row; zero past `limit`.
-__device__ __forceinline__ void load8(const void* base, long long row_off, long long nb0, int c0, int limit, int half,
-                                      float (&v)[8]) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (c0 + i < limit) ? load_elem(base, row_off + (c0 + i) * nb0, half) : 0.0f;
-}
 
-// Converts rows [0, rows) x dims [0, dp) of a K-major operand into the
-// no-swizzle core-matrix layout (rows of 16 B, 8-row groups `sbo` apart,
-// 8-dim groups 128 B apart).  valid(r) gives the row's element offset or -1.
-template <class RowOff>
-__device__ __forceinline__ bool convert_kmajor(const void* src, int half, long long nb0, int d, int dp, int rows,
-                                               uint32_t hi, uint32_t lo, int t, RowOff row_off) {
-    const int chunks = dp / 8;
-    bool over = false;
-    for (int idx = t; idx < rows * chunks; idx += 128) {
-        const int r = idx / chunks, c = idx - (idx / chunks) * chunks;
-        const long long off = row_off(r);
-        float v[8];
-        if (off >= 0) load8(src, off, nb0, c * 8, d, half, v);
-        else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-        }
-        uint4 h4, l4;
-        over |= split8(v, h4, l4);
-        const uint32_t o = static_cast<uint32_t>((r >> 3) * (dp * 16) + c * 128 + (r & 7) * 16);
-        st_shared_v4(hi + o, h4);
-        st_shared_v4(lo + o, l4);
-    }
-    return over;
-}
-
-// V rows (keys) into the MN-major no-swizzle layout of the PV product's B:
-// core matrices of 8 keys x 8 dims, key groups 128 B apart, dim groups
-// BK * 16 B apart.
-template <int BK, class RowOff>
-__device__ __forceinline__ bool convert_v(const void* src, int half, long long nb0, int dv, int dvp, uint32_t hi,
-                                          uint32_t lo, int t, RowOff row_off) {
-    const int chunks = dvp / 8;
-    bool over = false;
-    for (int idx = t; idx < BK * chunks; idx += 128) {
-        const int k = idx / chunks, c = idx - (idx / chunks) * chunks;
-        const long long off = row_off(k);
-        float v[8];
-        if (off >= 0) load8(src, off, nb0, c * 8, dv, half, v);
-        else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-        }
-        uint4 h4, l4;
-        over |= split8(v, h4, l4);
-        const uint32_t o = static_cast<uint32_t>(c * (BK * 16) + (k >> 3) * 128 + (k & 7) * 16);
-        st_shared_v4(hi + o, h4);
-        st_shared_v4(lo + o, l4);
-    }
-    return over;
-}
-
-template <int BK, int DVC>
+template <int BK, int DVC, int NO>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnArgs a) {
+    constexpr int KH = BK / 2;                  // keys of a block per softmax warp
+    constexpr int OCH = DVC / 16;               // 16-column chunks of the output
+    constexpr int OMINE = (OCH + 1) / 2;        // chunks per softmax warp (at most)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const AttnLayout<BK> L(a.dp, DVC);
-    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [2]
-    uint64_t* kv_empty = kv_full + 2;                                // [2]
-    uint64_t* q_full = kv_empty + 2;
-    uint64_t* s_full = q_full + 1;
-    uint64_t* p_full = s_full + 1;
-    uint64_t* pv_done = p_full + 1;
-    uint64_t* drain = pv_done + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    const AttnLayout L(a.dp, DVC, BK);
+    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [3]
+    uint64_t* kv_empty = kv_full + kStagesKV;                        // [3]
+    uint64_t* q_full = kv_empty + kStagesKV;
+    uint64_t* s_full = q_full + 1;    // [2]
+    uint64_t* p_full = s_full + 2;    // [2]
+    uint64_t* pv_done = p_full + 2;   // [2]
+    uint64_t* drain = pv_done + 2;
+    uint64_t* pair = drain + 1;       // [4]: the two softmax warps of a lane quarter meet here
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* xmax = reinterpret_cast<float*>(smem + L.xmax);
+    double* xsum = reinterpret_cast<double*>(smem + L.xsum);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q0 = blockIdx.x * kAttnQ;
@@ -164,102 +123,120 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnAr
     const int batch = blockIdx.z;
     const int khead = head / (a.h / a.hk);
     const int nblk = (a.lk + BK - 1) / BK;
-    const int nsc = (a.dp + 63) / 64;  // hi accumulators of S, one per 64 dims
+    const int nsc = (a.dp + 63) / 64;                 // hi accumulators of S, one per 64 dims
+    const int sbuf = (nsc + 1) * BK;                  // tensor-memory columns of one S buffer
     const uint32_t base = smem_u32(smem);
-    const int need = (nsc + 1) * BK + 2 * DVC;
-    const uint32_t tmem_cols = static_cast<uint32_t>(need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&kv_full[s], 4);
+        for (int s = 0; s < kStagesKV; ++s) {
+            mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(q_full, 4);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 4);
-        mbar_init(pv_done, 1);
+        mbar_init(q_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&p_full[i], 8);
+            mbar_init(&pv_done[i], 1);
+        }
         mbar_init(drain, 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&pair[i], 2);
         *abort = 0;
         fence_barrier_init();
     }
-    if (warp == 8) tmem_alloc(tmem_slot, tmem_cols);
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s_lo = tmem + nsc * BK;
-    const uint32_t t_o_hi = tmem + (nsc + 1) * BK, t_o_lo = t_o_hi + DVC;
+    // Output blocks: NO buffers of (hi, lo), the block in buffer j % NO.
+    auto t_o_hi = [&](int ob) { return tmem + 2 * sbuf + ob * 2 * DVC; };
+    auto t_o_lo = [&](int ob) { return tmem + 2 * sbuf + ob * 2 * DVC + DVC; };
+    const int pbuf = AttnLayout::p_bytes(BK);
 
-    if (warp >= 4 && warp < 8) {
-        // ------------------------------------------------ converters
-        const int t = threadIdx.x - 128;
-        bool over = false;
-        const long long qb = static_cast<long long>(head) * a.qnb[2] + static_cast<long long>(batch) * a.qnb[3];
-        over |= convert_kmajor(a.q, 0, a.qnb[0], a.d, a.dp, kAttnQ, base + L.q_hi, base + L.q_lo, t, [&](int r) {
-            const int i = q0 + r;
-            return i < a.lq ? qb + static_cast<long long>(i) * a.qnb[1] : -1LL;
-        });
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(q_full);
-        const long long kbase = static_cast<long long>(khead) * a.knb[2] + static_cast<long long>(batch) * a.knb[3];
-        const long long vbase = static_cast<long long>(khead) * a.vnb[2] + static_cast<long long>(batch) * a.vnb[3] +
-                                static_cast<long long>(dv0) * a.vnb[0];
-        for (int j = 0; j < nblk; ++j) {
-            const int s = j & 1;
-            if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, a.err)) break;
-            const uint32_t st = base + L.stage0 + s * L.stage_bytes;
-            const int key0 = j * BK;
-            over |= convert_kmajor(a.k, a.k_half, a.knb[0], a.d, a.dp, BK, st, st + L.k_lo_off, t, [&](int r) {
-                const int key = key0 + r;
-                return key < a.lk ? kbase + static_cast<long long>(key) * a.knb[1] : -1LL;
-            });
-            over |= convert_v<BK>(a.v, a.v_half, a.vnb[0], a.dv - dv0, DVC, st + L.v_hi_off, st + L.v_lo_off, t,
-                                  [&](int r) {
-                                      const int key = key0 + r;
-                                      return key < a.lk ? vbase + static_cast<long long>(key) * a.vnb[1] : -1LL;
-                                  });
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&kv_full[s]);
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint32_t qbytes = kAttnQ * a.dp * 2;
+            const uint32_t kbytes = BK * a.dp * 2, vbytes = BK * DVC * 2;
+            const uint8_t* qt = a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + blockIdx.x) * qbytes;
+            mbar_arrive_expect_tx(q_full, 2 * qbytes);
+            bulk_load(smem + L.q_hi, qt, qbytes, q_full);
+            bulk_load(smem + L.q_lo, qt + a.q_plane, qbytes, q_full);
+            const long long ktile0 = static_cast<long long>(batch * a.hk + khead) * a.ntk;
+            int issued = 0;
+            for (int j = 0; j < nblk; ++j) {
+                const int s = j % kStagesKV;
+                if (!mbar_wait(&kv_empty[s], ((j / kStagesKV) & 1) ^ 1, abort, a.err)) break;
+                uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kbytes + 2 * vbytes);
+                const uint8_t* kt = a.ks + (ktile0 + j) * kbytes;
+                const uint8_t* vt = a.vs + (ktile0 + j) * static_cast<long long>(BK) * a.dvs * 2 +
+                                    static_cast<long long>(dv0 / 8) * BK * 16;
+                bulk_load(st, kt, kbytes, &kv_full[s]);
+                bulk_load(st + L.k_lo, kt + a.k_plane, kbytes, &kv_full[s]);
+                bulk_load(st + L.v_hi, vt, vbytes, &kv_full[s]);
+                bulk_load(st + L.v_lo, vt + a.v_plane, vbytes, &kv_full[s]);
+                ++issued;
+            }
+            if (*abort) {
+                mbar_wait_quiet(q_full, 0, 100000000ull);
+                for (int j = (issued > kStagesKV ? issued - kStagesKV : 0); j < issued; ++j)
+                    mbar_wait_quiet(&kv_full[j % kStagesKV], (j / kStagesKV) & 1, 100000000ull);
+            }
         }
-        if (over) atomicOr(a.err, kErrRange);
-    } else if (warp == 8) {
+    } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id_s = idesc_f16_f32(kAttnQ, BK);
             const uint32_t id_pv = idesc_f16_f32_bmajor(kAttnQ, DVC, 1);
-            const uint32_t sbo_q = static_cast<uint32_t>(a.dp * 16);
-            const uint32_t sbo_p = BK * 16;
-            bool ok = mbar_wait(q_full, 0, abort, a.err);
-            for (int j = 0; j < nblk && ok; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort, a.err)) { ok = false; break; }
-                tc_fence_after();
+            const uint32_t q_lbo = kAttnQ * 16, k_lbo = BK * 16, kv_sbo = 128, p_sbo = BK * 16;
+            auto issue_s = [&](int j) {
+                const int s = j % kStagesKV;
                 const uint32_t st = base + L.stage0 + s * L.stage_bytes;
+                const uint32_t sb = tmem + (j & 1) * sbuf;
                 for (int kk = 0; kk < a.dp / 16; ++kk) {
-                    const uint64_t qh = desc_noswizzle(base + L.q_hi + kk * 256, 128, sbo_q);
-                    const uint64_t ql = desc_noswizzle(base + L.q_lo + kk * 256, 128, sbo_q);
-                    const uint64_t kh = desc_noswizzle(st + kk * 256, 128, sbo_q);
-                    const uint64_t kl = desc_noswizzle(st + L.k_lo_off + kk * 256, 128, sbo_q);
-                    mma_f16(tmem + (kk >> 2) * BK, qh, kh, id_s, (kk & 3) ? 1u : 0u);
-                    mma_f16(t_s_lo, qh, kl, id_s, kk > 0 ? 1u : 0u);
-                    mma_f16(t_s_lo, ql, kh, id_s, 1u);
+                    const uint64_t qh = desc_noswizzle(base + L.q_hi + kk * 2 * q_lbo, q_lbo, 128);
+                    const uint64_t ql = desc_noswizzle(base + L.q_lo + kk * 2 * q_lbo, q_lbo, 128);
+                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, kv_sbo);
+                    const uint64_t kl = desc_noswizzle(st + L.k_lo + kk * 2 * k_lbo, k_lbo, kv_sbo);
+                    mma_f16(sb + (kk >> 2) * BK, qh, kh, id_s, (kk & 3) ? 1u : 0u);
+                    mma_f16(sb + nsc * BK, qh, kl, id_s, kk > 0 ? 1u : 0u);
+                    mma_f16(sb + nsc * BK, ql, kh, id_s, 1u);
                 }
-                mma_commit(s_full);
-                if (!mbar_wait(p_full, j & 1, abort, a.err)) { ok = false; break; }
+                mma_commit(&s_full[j & 1]);
+            };
+            bool ok = mbar_wait(q_full, 0, abort, a.err);
+            if (ok && nblk > 0) {
+                ok = mbar_wait(&kv_full[0], 0, abort, a.err);
+                if (ok) {
+                    tc_fence_after();
+                    issue_s(0);
+                }
+            }
+            for (int j = 0; j < nblk && ok; ++j) {
+                if (j + 1 < nblk) {
+                    const int s1 = (j + 1) % kStagesKV;
+                    if (!mbar_wait(&kv_full[s1], ((j + 1) / kStagesKV) & 1, abort, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+                const int pb = j % NO;
+                if (!mbar_wait(&p_full[pb], (j / NO) & 1, abort, a.err)) { ok = false; break; }
                 tc_fence_after();
+                const int s = j % kStagesKV;
+                const uint32_t st = base + L.stage0 + s * L.stage_bytes;
                 for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ph = desc_noswizzle(base + L.p_hi + kk * 256, 128, sbo_p);
-                    const uint64_t pl = desc_noswizzle(base + L.p_lo + kk * 256, 128, sbo_p);
-                    const uint64_t vh = desc_noswizzle(st + L.v_hi_off + kk * 256, 128, sbo_p);
-                    const uint64_t vl = desc_noswizzle(st + L.v_lo_off + kk * 256, 128, sbo_p);
+                    const uint64_t ph = desc_noswizzle(base + L.p_hi + pb * pbuf + kk * 256, 128, p_sbo);
+                    const uint64_t pl = desc_noswizzle(base + L.p_lo + pb * pbuf + kk * 256, 128, p_sbo);
+                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
+                    const uint64_t vl = desc_noswizzle(st + L.v_lo + kk * 256, 128, BK * 16);
                     const uint32_t acc = kk > 0 ? 1u : 0u;
-                    mma_f16(t_o_hi, ph, vh, id_pv, acc);
-                    mma_f16(t_o_lo, ph, vl, id_pv, acc);
-                    mma_f16(t_o_lo, pl, vh, id_pv, 1u);
+                    mma_f16(t_o_hi(pb), ph, vh, id_pv, acc);
+                    mma_f16(t_o_lo(pb), ph, vl, id_pv, acc);
+                    mma_f16(t_o_lo(pb), pl, vh, id_pv, 1u);
                 }
-                mma_commit(pv_done);
+                mma_commit(&pv_done[pb]);
                 mma_commit(&kv_empty[s]);
             }
             if (!ok) {
@@ -269,115 +246,170 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnAr
             }
         }
     } else {
-        // ------------------------------------------------ softmax + epilogue (warps 0-3)
-        const int r = warp * 32 + lane;
+        // ------------------------------------------------ softmax + epilogue (warps 2-9)
+        const int ew = warp - 2;
+        const int q = warp & 3;          // lane quarter
+        const int half = ew >> 2;        // which half of a block's keys, and of the output chunks
+        const int r = q * 32 + lane;     // query row of the tile
         const int qi = q0 + r;
-        const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        // The pair's exchange through shared memory: each warp writes, arrives,
+        // and waits (bounded) for the other's arrival.
+        uint32_t pair_uses = 0;
+        auto pair_sync = [&]() {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pair[q]);
+            const bool met = mbar_wait(&pair[q], pair_uses & 1, abort, a.err);
+            ++pair_uses;
+            return met;
+        };
         float m_ref = -INFINITY;
         double l = 0.0;
-        float o[DVC];
+        float o[OMINE * 16];
 #pragma unroll
-        for (int i = 0; i < DVC; ++i) o[i] = 0.0f;
-        // o += the block product in tensor memory (hi + lo 2^-11).
-        auto drain_o = [&]() {
+        for (int i = 0; i < OMINE * 16; ++i) o[i] = 0.0f;
+        // Rescale factors applied since the weights of the block in each
+        // output buffer were taken (that block's product still in flight).
+        float pend[NO];
 #pragma unroll
-            for (int c = 0; c < DVC; c += 16) {
-                float oh[16], ol[16];
-                tmem_ld16(t_o_hi + lane_off + c, oh);
-                tmem_ld16(t_o_lo + lane_off + c, ol);
-                tmem_ld_wait();
+        for (int i = 0; i < NO; ++i) pend[i] = 1.0f;
+        // o += pend * (the block product in output buffer ob).
+        auto drain_o = [&](int ob) {
+            const float f = pend[ob];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[c + i] += fmaf(ol[i], kLoUnscale, oh[i]);
+            for (int c = 0; c < OMINE; ++c) {
+                const int ch = 2 * c + half;
+                if (ch < OCH) {
+                    float oh[16], ol[16];
+                    tmem_ld16(t_o_hi(ob) + lane_off + ch * 16, oh);
+                    tmem_ld16(t_o_lo(ob) + lane_off + ch * 16, ol);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[c * 16 + i] = fmaf(f, fmaf(ol[i], kLoUnscale, oh[i]), o[c * 16 + i]);
+                }
             }
+        };
+        // Waits for block jb's product and adds it in.
+        auto take = [&](int jb) {
+            const int ob = jb % NO;
+            if (!mbar_wait(&pv_done[ob], (jb / NO) & 1, abort, a.err)) return false;
+            tc_fence_after();
+            drain_o(ob);
+            return true;
         };
         bool ok = true;
         for (int j = 0; j < nblk; ++j) {
-            if (!mbar_wait(s_full, j & 1, abort, a.err)) { ok = false; break; }
+            const int b = j & 1;
+            if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort, a.err)) { ok = false; break; }
             tc_fence_after();
-            float s[BK];
-#pragma unroll
-            for (int c = 0; c < BK; c += 32) {
-                float part[32], lo[32];
-                tmem_ld32(t_s_lo + lane_off + c, lo);
+            const uint32_t sb = tmem + b * sbuf + lane_off + half * KH;
+            float s[KH];
+            {
+                float lo[KH];
+                if constexpr (KH == 32) tmem_ld32(sb + nsc * BK, lo);
+                else tmem_ld16(sb + nsc * BK, lo);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) s[c + i] = lo[i] * kLoUnscale;
+                for (int i = 0; i < KH; ++i) s[i] = lo[i] * kLoUnscale;
                 for (int sc = 0; sc < nsc; ++sc) {
-                    tmem_ld32(tmem + sc * BK + lane_off + c, part);
+                    float part[KH];
+                    if constexpr (KH == 32) tmem_ld32(sb + sc * BK, part);
+                    else tmem_ld16(sb + sc * BK, part);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) s[c + i] += part[i];
+                    for (int i = 0; i < KH; ++i) s[i] += part[i];
                 }
 #pragma unroll
-                for (int i = 0; i < 32; ++i) s[c + i] *= a.scale;
+                for (int i = 0; i < KH; ++i) s[i] *= a.scale2;
             }
-            const int valid = min(BK, a.lk - j * BK);
-            float bmax = -INFINITY;
+            const int valid = min(BK, a.lk - j * BK) - half * KH;  // my keys that exist
+            float mine = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < BK; ++i)
-                if (i < valid) bmax = fmaxf(bmax, s[i]);
-            // The previous block's product: into the registers (P's buffer is then free).
-            if (j > 0) {
-                if (!mbar_wait(pv_done, (j - 1) & 1, abort, a.err)) { ok = false; break; }
-                tc_fence_after();
-                drain_o();
-            }
+            for (int i = 0; i < KH; ++i)
+                if (i < valid) mine = fmaxf(mine, s[i]);
+            xmax[(b * kAttnQ + r) * 2 + half] = mine;
+            if (!pair_sync()) { ok = false; break; }
+            const float bmax = fmaxf(xmax[(b * kAttnQ + r) * 2], xmax[(b * kAttnQ + r) * 2 + 1]);
+            // The product of the block that last used this P / output buffer
+            // into the registers (the buffers are then free).
+            const int pb = j % NO;
+            if (j >= NO && !take(j - NO)) { ok = false; break; }
             if (j == 0) {
                 m_ref = bmax;
             } else if (bmax > m_ref + kRescaleAbove) {
-                const float factor = exponential(m_ref - bmax);
+                const float factor = ex2(m_ref - bmax);
                 m_ref = bmax;
 #pragma unroll
-                for (int i = 0; i < DVC; ++i) o[i] *= factor;
+                for (int i = 0; i < OMINE * 16; ++i) o[i] *= factor;
                 l *= static_cast<double>(factor);
-            }
-            // Weights of this block into P (hi / lo), row r, K-major core matrices.
-            double bsum = 0.0;
 #pragma unroll
-            for (int c = 0; c < BK / 8; ++c) {
+                for (int i = 0; i < NO; ++i)
+                    if (i != pb) pend[i] *= factor;  // blocks still in flight
+            }
+            pend[pb] = 1.0f;
+            // This warp's keys of the block into P (hi / lo), row r, K-major core matrices.
+            // The block's weights summed in FP32 with compensation (Neumaier),
+            // the block sum then added to the row's double total.
+            float bsum = 0.0f, bcomp = 0.0f;
+#pragma unroll
+            for (int c = 0; c < KH / 8; ++c) {
                 float p[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int key = c * 8 + i;
-                    p[i] = key < valid ? exponential(s[key] - m_ref) : 0.0f;
-                    bsum += static_cast<double>(p[i]);
+                    p[i] = key < valid ? ex2(s[key] - m_ref) : 0.0f;
+                    const float t = bsum + p[i];
+                    bcomp += fabsf(bsum) >= p[i] ? (bsum - t) + p[i] : (p[i] - t) + bsum;
+                    bsum = t;
                 }
                 uint4 h4, l4;
                 split8(p, h4, l4);
-                const uint32_t off = static_cast<uint32_t>((r >> 3) * (BK * 16) + c * 128 + (r & 7) * 16);
-                st_shared_v4(base + L.p_hi + off, h4);
-                st_shared_v4(base + L.p_lo + off, l4);
+                const uint32_t off =
+                    static_cast<uint32_t>((r >> 3) * (BK * 16) + (half * (KH / 8) + c) * 128 + (r & 7) * 16);
+                st_shared_v4(base + L.p_hi + pb * pbuf + off, h4);
+                st_shared_v4(base + L.p_lo + pb * pbuf + off, l4);
             }
-            l += bsum;
+            l += static_cast<double>(bsum) + static_cast<double>(bcomp);
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[pb]);
         }
-        if (ok && mbar_wait(pv_done, (nblk - 1) & 1, abort, a.err)) {
-            tc_fence_after();
-            drain_o();
-            if (qi < a.lq) {
-                const float recip = static_cast<float>(1.0 / l);
+        // The blocks still in flight.
+        for (int jb = max(0, nblk - NO); ok && jb < nblk; ++jb) ok = take(jb);
+        if (ok && nblk > 0) {
+            xsum[r * 2 + half] = l;
+            if (!pair_sync()) ok = false;
+            const double total = xsum[r * 2] + xsum[r * 2 + 1];
+            if (ok && qi < a.lq) {
+                const float recip = static_cast<float>(1.0 / total);
                 const long long ob = static_cast<long long>(head) * a.onb[1] + static_cast<long long>(qi) * a.onb[2] +
                                      static_cast<long long>(batch) * a.onb[3];
 #pragma unroll
-                for (int i = 0; i < DVC; ++i) {
-                    const int dcol = dv0 + i;
-                    if (dcol < a.dv) {
-                        const float v = apply_chain(a.chain, o[i] * recip, dcol, head, qi, batch);
-                        a.out[ob + dcol * a.onb[0]] = v;
+                for (int c = 0; c < OMINE; ++c) {
+                    const int ch = 2 * c + half;
+                    if (ch < OCH) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int dcol = dv0 + ch * 16 + i;
+                            if (dcol < a.dv) {
+                                const float v = apply_chain(a.chain, o[c * 16 + i] * recip, dcol, head, qi, batch);
+                                a.out[ob + dcol * a.onb[0]] = v;
+                            }
+                        }
                     }
                 }
             }
         }
     }
 
+    // Single-lane roles rejoin their warps before the CTA-wide barrier.
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, tmem_cols);
+        tmem_dealloc(tmem, 512);
     }
 }
 
@@ -387,33 +419,74 @@ bool floaty(const sdb_tensor* t) {
 
 int esize(const sdb_tensor* t) { return t->type == SDB_TYPE_F16 ? 2 : 4; }
 
-template <int BK, int DVC>
-int launch_attention(const AttnArgs& a, cudaStream_t st) {
-    const AttnLayout<BK> L(a.dp, DVC);
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+// Splits Q, K and V into the workspace as tiles (128 queries, BK keys) and
+// launches the kernel.
+template <int BK, int DVC, int NO>
+int launch_attention(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    const AttnLayout L(a.dp, DVC, BK);
     const int smem = L.total + 1024;
     if (smem > 227 * 1024) return fail(SDB_NOT_SUPPORTED, "sdb_attention: head too wide");
-    SDB_CUDA(cudaFuncSetAttribute(attention_kernel<BK, DVC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    auto dims = [](const sdb_tensor* t, long long (&ne)[4], long long (&nb)[4]) {
+        const int es = t->type == SDB_TYPE_F16 ? 2 : 4;
+        for (int i = 0; i < 4; ++i) {
+            ne[i] = t->ne[i];
+            nb[i] = t->nb[i] / es;
+        }
+    };
+    long long qne[4], qnb[4], kne[4], knb[4], vne[4], vnb[4];
+    dims(q, qne, qnb);
+    dims(k, kne, knb);
+    dims(v, vne, vnb);
+    a.dvs = a.dv_chunks * DVC;
+    a.ntq = static_cast<int>((a.lq + kAttnQ - 1) / kAttnQ);
+    a.ntk = static_cast<int>((a.lk + BK - 1) / BK);
+    a.q_plane = split_tiles_plane(qne, a.dp, kAttnQ);
+    a.k_plane = split_tiles_plane(kne, a.dp, BK);
+    a.v_plane = split_tiles_plane(vne, a.dvs, BK);
+    void* ws = nullptr;
+    const size_t bytes = static_cast<size_t>(2 * (a.q_plane + a.k_plane + a.v_plane) + 256);
+    if (int s = workspace(st, bytes, &ws); s != SDB_OK) return s;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    a.qs = base;
+    a.ks = base + 2 * a.q_plane;
+    a.vs = base + 2 * (a.q_plane + a.k_plane);
+    if (int s = split_tiles(q->data, 0, qne, qnb, a.dp, kAttnQ, const_cast<uint16_t*>(
+                                reinterpret_cast<const uint16_t*>(a.qs)), a.err, st); s != SDB_OK)
+        return s;
+    if (int s = split_tiles(k->data, k->type == SDB_TYPE_F16, kne, knb, a.dp, BK,
+                            const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.ks)), a.err, st);
+        s != SDB_OK)
+        return s;
+    if (int s = split_tiles(v->data, v->type == SDB_TYPE_F16, vne, vnb, a.dvs, BK,
+                            const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.vs)), a.err, st);
+        s != SDB_OK)
+        return s;
+    SDB_CUDA(cudaFuncSetAttribute(attention_kernel<BK, DVC, NO>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const dim3 grid(static_cast<unsigned>((a.lq + kAttnQ - 1) / kAttnQ), static_cast<unsigned>(a.h * a.dv_chunks),
                     static_cast<unsigned>(a.b));
-    attention_kernel<BK, DVC><<<grid, kAttnThreads, smem, st>>>(a);
+    attention_kernel<BK, DVC, NO><<<grid, kAttnThreads, smem, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
 }
 
-template <int BK>
-int launch_dvc(AttnArgs& a, cudaStream_t st) {
-    const int dvp = (a.dv + 15) / 16 * 16;
-    const int chunks = (dvp + 79) / 80;
-    const int dvc = ((dvp / 16 + chunks - 1) / chunks) * 16;
-    a.dv_chunks = chunks;
-    switch (dvc) {
-    case 16: return launch_attention<BK, 16>(a, st);
-    case 32: return launch_attention<BK, 32>(a, st);
-    case 48: return launch_attention<BK, 48>(a, st);
-    case 64: return launch_attention<BK, 64>(a, st);
-    default: return launch_attention<BK, 80>(a, st);
-    }
+// Keys per block (64, else 32) and output buffers (two, so the softmax of a
+// block overlaps the product of the one before; else one): the first choice
+// whose S double buffer and output accumulators fit tensor memory.
+template <int DVC>
+int launch_bk(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    const int nsc = (a.dp + 63) / 64;
+    auto fits = [&](int bk, int no) {
+        return 2 * (nsc + 1) * bk + no * 2 * DVC <= 512 &&
+               AttnLayout(a.dp, DVC, bk).total + 1024 <= 227 * 1024;
+    };
+    if (fits(64, 2)) return launch_attention<64, DVC, 2>(a, q, k, v, st);
+    if (fits(32, 2)) return launch_attention<32, DVC, 2>(a, q, k, v, st);
+    if (fits(64, 1)) return launch_attention<64, DVC, 1>(a, q, k, v, st);
+    if (fits(32, 1)) return launch_attention<32, DVC, 1>(a, q, k, v, st);
+    return fail(SDB_NOT_SUPPORTED, "sdb_attention: head too wide");
 }
 
 }  // namespace
@@ -427,6 +500,7 @@ extern "C" int sdb_attention_supported(const sdb_tensor* q, const sdb_tensor* k,
     if (!q || !k || !v || !dst) return 0;
     if (q->type != SDB_TYPE_F32 || !q->data || !floaty(k) || !floaty(v) || dst->type != SDB_TYPE_F32 || !dst->data)
         return 0;
+    if (k->type != v->type) return 0;
     const int64_t d = q->ne[0], lq = q->ne[1], h = q->ne[2], b = q->ne[3];
     const int64_t lk = k->ne[1], hk = k->ne[2], dv = v->ne[0];
     if (k->ne[0] != d || v->ne[1] != lk || v->ne[2] != hk || k->ne[3] != b || v->ne[3] != b) return 0;
@@ -436,6 +510,8 @@ extern "C" int sdb_attention_supported(const sdb_tensor* q, const sdb_tensor* k,
     for (const sdb_tensor* t : {q, k, v, dst})
         for (int i = 0; i < 4; ++i)
             if (t->nb[i] % esize(t) != 0 || t->nb[i] < 0) return 0;
+    // TMA row coordinates are 32-bit (hi and lo planes).
+    if (2 * b * h * lq >= (1LL << 31) || 2 * b * hk * lk >= (1LL << 31)) return 0;
     return h * ((dv + 79) / 80) <= 65535 && b <= 65535;
 }
 
@@ -444,19 +520,10 @@ extern "C" int sdb_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb
     if (!sdb_attention_supported(q, k, v, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_attention: not supported");
     if (chain && (chain->count < 0 || chain->count > SDB_MAX_STEPS || chain->redirect))
         return fail(SDB_INVALID, "sdb_attention: invalid chain");
+    const auto st = static_cast<cudaStream_t>(stream);
     AttnArgs a{};
-    a.q = q->data;
-    a.k = k->data;
-    a.v = v->data;
     a.out = static_cast<float*>(dst->data);
-    for (int i = 0; i < 4; ++i) {
-        a.qnb[i] = q->nb[i] / 4;
-        a.knb[i] = k->nb[i] / esize(k);
-        a.vnb[i] = v->nb[i] / esize(v);
-        a.onb[i] = dst->nb[i] / 4;
-    }
-    a.k_half = k->type == SDB_TYPE_F16;
-    a.v_half = v->type == SDB_TYPE_F16;
+    for (int i = 0; i < 4; ++i) a.onb[i] = dst->nb[i] / 4;
     a.d = static_cast<int>(q->ne[0]);
     a.lq = static_cast<int>(q->ne[1]);
     a.h = static_cast<int>(q->ne[2]);
@@ -464,16 +531,22 @@ extern "C" int sdb_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb
     a.lk = static_cast<int>(k->ne[1]);
     a.hk = static_cast<int>(k->ne[2]);
     a.dv = static_cast<int>(v->ne[0]);
-    a.dp = (a.d + 15) / 16 * 16;
-    a.dvp = (a.dv + 15) / 16 * 16;
-    a.scale = scale;
+    a.dp = static_cast<int>(round_up(a.d, 16));
+    a.dvp = static_cast<int>(round_up(a.dv, 16));
+    a.rq = a.b * a.h * a.lq;
+    a.rk = a.b * a.hk * a.lk;
+    a.scale2 = scale * kLog2e;
     a.chain = make_chain(chain);
     a.err = device_error_word();
-    const auto st = static_cast<cudaStream_t>(stream);
-    // Keys per block: 64 where the registers hold a block's scores beside a
-    // CTA's output dims (<= 48), 32 otherwise.
-    const int dvp = (a.dv + 15) / 16 * 16;
-    const int dvc = ((dvp / 16 + (dvp + 79) / 80 - 1) / ((dvp + 79) / 80)) * 16;
-    if (a.dp <= 96 && dvc <= 48) return launch_dvc<64>(a, st);
-    return launch_dvc<32>(a, st);
+    const int chunks = (a.dvp + 79) / 80;
+    const int dvc = ((a.dvp / 16 + chunks - 1) / chunks) * 16;
+    a.dv_chunks = chunks;
+
+    switch (dvc) {
+    case 16: return launch_bk<16>(a, q, k, v, st);
+    case 32: return launch_bk<32>(a, q, k, v, st);
+    case 48: return launch_bk<48>(a, q, k, v, st);
+    case 64: return launch_bk<64>(a, q, k, v, st);
+    default: return launch_bk<80>(a, q, k, v, st);
+    }
 }

@@ -1,18 +1,21 @@
 // The tcgen05 GEMM of the linear layers and the direct convolution.
 //
 // C[m][n] = sum_k A[m][k] B[n][k] with
-//   A: the activations (FP32 in HBM), rows m = tokens (linear) or output
-//      positions (convolution, the im2col rows gathered straight from the
-//      image: conv2d.cc:231-316 packs the same columns on the CPU);
+//   A: the activations, split once by the pre-pass (split.cuh) into FP16
+//      pairs x = hi + lo 2^-11: rows of K for a linear layer; for a
+//      convolution the channels-last image, whose im2col rows TMA reads
+//      straight from it -- one box of 64 channels x (OWt x OHt x NT output
+//      positions) per (tap, channel block), at the tap's offset, with the
+//      convolution's stride as TMA's element stride and the padding as its
+//      out-of-bounds zero fill (conv2d.cc:231-316 packs the same columns on
+//      the CPU);
 //   B: the weights, repacked once by the weight store into FP16 [rows][Kpad]
-//      (K-major, zero padded) and loaded by TMA in the 128-byte swizzle.
-// Each A element is split x = hi + lo 2^-11 (ptx.cuh split_half) by the
-// converter warps, which write both halves into shared memory in the UMMA
-// K-major 128B-swizzled layout; one thread issues tcgen05.mma kind::f16 for
-// hi x W and lo x W.  FP32 weights are split the same way (w = whi + wlo 2^-11)
-// and add hi x wlo to the lo product.  The gated variant computes the x and
-// the gate halves of a GEGLU product side by side and writes x * GELU(gate)
-// (fusion.cc:290-310, mul_mat.cc:934-1058).
+//      (K-major, per-tap channels padded to 64 for a convolution).
+// All three tiles arrive by TMA in the 128-byte swizzle; one thread issues
+// tcgen05.mma kind::f16 for hi x W and lo x W.  FP32 weights are split the
+// same way (w = whi + wlo 2^-11) and add hi x wlo to the lo product.  The
+// gated variant computes the x and the gate halves of a GEGLU product side by
+// side and writes x * GELU(gate) (fusion.cc:290-310, mul_mat.cc:934-1058).
 //
 // Precision of the sums.  The tensor core's FP32 accumulation rounds toward
 // zero: one k-step's add loses up to an ulp of the running sum, always in the
@@ -21,15 +24,16 @@
 // sum, is therefore accumulated over one k-block (4 k-steps) at a time, into
 // one of two tensor-memory buffers in turn, and the epilogue warps add each
 // block's partial sum to FP32 registers with round-to-nearest while the next
-// block computes.  The lo product (2^-11 of the sum) accumulates over all of K.
-// The chain (bias, scale, SiLU, residual; fusion.h:51-91) is applied to
-// sum + lo 2^-11 before the store.
+// block computes.  The lo product (2^-11 of the sum) accumulates over all of
+// the CTA's K.  The chain (bias, scale, SiLU, residual; fusion.h:51-91) is
+// applied to sum + lo 2^-11 before the store -- or, when K is split over
+// several CTAs (few output tiles, long K), each CTA writes its sum to the
+// workspace and a reduction adds the splits in order and applies the chain.
 //
-// Warp roles (448 threads): warp 0 TMA producer; warp 1 MMA issuer and the
-// tensor-memory allocation; warps 2-5 converters, which issue the loads of
-// the next k-block while they convert the current one; warps 6-13 epilogue,
-// two per quarter of tensor-memory lanes (warp w reads lanes 32*(w%4)..+31),
-// each taking half the tile's columns.
+// Warp roles (320 threads): warp 0 TMA producer; warp 1 MMA issuer and the
+// tensor-memory allocation; warps 2-9 epilogue, two per quarter of
+// tensor-memory lanes (warp w reads lanes 32*(w%4)..+31), each taking half
+// the tile's columns.
 #pragma once
 
 #include <cuda.h>
@@ -47,34 +51,35 @@ enum : int { kWeightHalf = 0, kWeightSplit = 1, kWeightGated = 2 };
 
 constexpr int kBM = 128;        // rows of A per tile (the MMA's M)
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of FP16
-constexpr int kGemmWarps = 14;  // 4 per SM sub-partition at most: 128 registers a thread
+constexpr int kGemmWarps = 10;
 constexpr int kGemmThreads = kGemmWarps * 32;
-constexpr int kConvWarp0 = 2;   // first converter warp
-constexpr int kEpiWarp0 = 6;    // first epilogue warp
+constexpr int kEpiWarp0 = 2;    // first epilogue warp
 
 struct ConvGeom {
-    int iw, ih, ic, n;      // input [IW, IH, IC, N]
-    int ow, oh;             // output [OW, OH, OC, N]
+    int ow, oh, n;          // output positions [OW, OH, N]
     int kw, kh;
     int s0, s1, p0, p1, d0, d1;
-    int icp;                // channels per tap in the packed K order (a multiple of 16)
-    long long xnb[4];       // input strides in elements
+    int cblocks;            // 64-channel blocks per tap
+    int owt, oht, nt;       // output positions of a tile: OWt x OHt x NT
+    int tw, th, tn;         // tiles along W, H, N
 };
 
 struct GemmArgs {
-    const float* x;         // A source
-    long long xld;          // linear: elements between rows of x
-    int m;                  // rows of C
-    int kpad;               // K padded to a multiple of kBK (packed weights' row length)
-    int klog;               // logical K of a linear layer (columns of x read)
+    int m;                  // rows of C (linear: tokens; conv: unused, see cg)
+    int a_lo_row;           // row (linear) / image (conv) offset of the lo plane in A's map
+    int kblocks;            // K / kBK of the whole product
+    int ksplit;             // CTAs along K (grid.z)
     int n;                  // columns of C (linear: output features; gated: the half)
     int b1_row;             // row offset in the packed weights of the second B operand
+    uint32_t a_tx;          // bytes of one A tile (hi or lo) as TMA writes it
     float* y;               // output (the redirect when the chain has one)
+    float* part;            // split-K: partial sums [ksplit][rows][part_ld]
+    long long part_ld;      // columns of a partial row
+    long long part_split;   // elements between splits
     long long ynb[4];       // output strides in elements
     long long rne1, rne2;   // linear: row m -> (i1, i2, i3) = (m % rne1, m / rne1 % rne2, m / (rne1 rne2))
     ConvGeom cg;
     Chain chain;
-    int vec;                // linear: x rows 16-byte aligned
     unsigned* err;
 };
 
@@ -97,94 +102,26 @@ struct GemmShape {
     static_assert(kStages * kStageBytes >= 2 * 8 * 32 * 33 * 4 + 8 * 32 * 32, "epilogue staging does not fit");
 };
 
-// ---------------------------------------------------------------- producers
-//
-// A k-block of A is 128 rows x 64 columns: 1024 chunks of 8 values, one
-// 16-byte chunk of hi and one of lo in shared memory.  Each of the 128
-// converter threads takes 8 chunks, in two halves of 4; the loads of a half
-// go into 32 registers, which are converted and stored while the loads of the
-// next half are in flight.
+// ---------------------------------------------------------------- tiles
 
-// Linear: chunk (r, c) of k-block kb is x[m0 + r][kb*64 + 8c .. +7]; the
-// thread takes chunks it*128 + t, it = 4h .. 4h + 3 (8 threads share a row:
-// a row's 256 bytes are read by neighbouring threads).
-__device__ __forceinline__ void load_linear(const GemmArgs& a, int m0, int kb, int h, int t, float (&v)[32]) {
-#pragma unroll
-    for (int i4 = 0; i4 < 4; ++i4) {
-        const int chunk = (4 * h + i4) * 128 + t;
-        const int r = chunk >> 3, c = chunk & 7;
-        const int m = m0 + r;
-        const int k = kb * kBK + c * 8;
-        if (m < a.m && a.vec && k + 8 <= a.klog) {
-            const float4* p = reinterpret_cast<const float4*>(a.x + static_cast<long long>(m) * a.xld + k);
-            const float4 u = __ldg(p), w = __ldg(p + 1);
-            v[i4 * 8 + 0] = u.x; v[i4 * 8 + 1] = u.y; v[i4 * 8 + 2] = u.z; v[i4 * 8 + 3] = u.w;
-            v[i4 * 8 + 4] = w.x; v[i4 * 8 + 5] = w.y; v[i4 * 8 + 6] = w.z; v[i4 * 8 + 7] = w.w;
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                v[i4 * 8 + i] =
-                    (m < a.m && k + i < a.klog) ? __ldg(a.x + static_cast<long long>(m) * a.xld + k + i) : 0.0f;
-        }
-    }
-}
+// The output position of lane row r of conv tile `tile`: valid when inside
+// the output.
+struct ConvPos {
+    int ox, oy, img;
+    bool ok;
+};
 
-__device__ __forceinline__ uint32_t chunk_offset_linear(int h, int i4, int t) {
-    const int chunk = (4 * h + i4) * 128 + t;
-    return sw128_offset(chunk >> 3, chunk & 7);
-}
-
-// Convolution: row r = output position m0 + r; packed k = tap * icp + ic.
-// Thread t takes row t, chunks 4h .. 4h + 3 (32 channels of a tap): a
-// warp's loads of one channel are 32 neighbouring positions.
-__device__ __forceinline__ void load_conv(const GemmArgs& a, int m0, int kb, int h, int t, float (&v)[32]) {
-    const ConvGeom& g = a.cg;
-    const int m = m0 + t;
-    const bool row_ok = m < a.m;
-    const int ox = m % g.ow;
-    const int oy = (m / g.ow) % g.oh;
-    const int img = m / (g.ow * g.oh);
-    const float* base = a.x + static_cast<long long>(img) * g.xnb[3];
-#pragma unroll
-    for (int i4 = 0; i4 < 4; ++i4) {
-        const int k = kb * kBK + (4 * h + i4) * 8;  // 8 channels of one tap (icp % 16 == 0)
-        const int tap = k / g.icp;
-        const int ic0 = k - tap * g.icp;
-        const int ky = tap / g.kw, kx = tap - ky * g.kw;
-        const int iy = oy * g.s1 + ky * g.d1 - g.p1;
-        const int ix = ox * g.s0 + kx * g.d0 - g.p0;
-        const bool in = row_ok && tap < g.kw * g.kh && iy >= 0 && iy < g.ih && ix >= 0 && ix < g.iw;
-        const float* p = base + static_cast<long long>(iy) * g.xnb[1] + static_cast<long long>(ix) * g.xnb[0];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int ic = ic0 + i;
-            v[i4 * 8 + i] = (in && ic < g.ic) ? __ldg(p + static_cast<long long>(ic) * g.xnb[2]) : 0.0f;
-        }
-    }
-}
-
-template <int MODE>
-__device__ __forceinline__ void load_half(const GemmArgs& a, int m0, int kb, int h, int t, float (&v)[32]) {
-    if (MODE == kModeLinear) load_linear(a, m0, kb, h, t, v);
-    else load_conv(a, m0, kb, h, t, v);
-}
-
-// Splits and stores a half; returns true when a value was beyond FP16's range.
-template <int MODE>
-__device__ __forceinline__ bool store_half(const float (&v)[32], int h, int t, uint32_t a_hi, uint32_t a_lo) {
-    bool over = false;
-#pragma unroll
-    for (int i4 = 0; i4 < 4; ++i4) {
-        float x[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = v[i4 * 8 + i];
-        uint4 hi, lo;
-        over |= split8(x, hi, lo);
-        const uint32_t off = MODE == kModeLinear ? chunk_offset_linear(h, i4, t) : sw128_offset(t, 4 * h + i4);
-        st_shared_v4(a_hi + off, hi);
-        st_shared_v4(a_lo + off, lo);
-    }
-    return over;
+__device__ __forceinline__ ConvPos conv_pos(const ConvGeom& g, int tile, int r) {
+    const int tx = tile % g.tw;
+    const int ty = (tile / g.tw) % g.th;
+    const int tz = tile / (g.tw * g.th);
+    const int per = g.owt * g.oht;
+    ConvPos p;
+    p.ox = tx * g.owt + r % g.owt;
+    p.oy = ty * g.oht + (r / g.owt) % g.oht;
+    p.img = tz * g.nt + r / per;
+    p.ok = r < per * g.nt && p.ox < g.ow && p.oy < g.oh && p.img < g.n;
+    return p;
 }
 
 // ---------------------------------------------------------------- epilogue
@@ -247,13 +184,9 @@ __device__ __forceinline__ void store_linear(const GemmArgs& a, uint8_t* smem, i
 // position and neighbouring lanes are neighbouring positions, so each column
 // (channel) is written by the warp as one run.
 template <int NV>
-__device__ __forceinline__ void store_conv(const GemmArgs& a, int m, int col0, const float (&v)[NV]) {
-    if (m >= a.m) return;
-    const ConvGeom& g = a.cg;
-    const long long ox = m % g.ow;
-    const long long oy = (m / g.ow) % g.oh;
-    const long long img = m / (g.ow * g.oh);
-    const long long base = ox * a.ynb[0] + oy * a.ynb[1] + img * a.ynb[3];
+__device__ __forceinline__ void store_conv(const GemmArgs& a, const ConvPos& p, int col0, const float (&v)[NV]) {
+    if (!p.ok) return;
+    const long long base = p.ox * a.ynb[0] + static_cast<long long>(p.oy) * a.ynb[1] + p.img * a.ynb[3];
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
         const int col = col0 + j;
@@ -261,16 +194,27 @@ __device__ __forceinline__ void store_conv(const GemmArgs& a, int m, int col0, c
             float* out = a.y + base + col * a.ynb[2];
             float val = v[j];
             if (a.chain.from_redirect) val = *out + val;
-            *out = apply_chain(a.chain, val, ox, oy, col, img);
+            *out = apply_chain(a.chain, val, p.ox, p.oy, col, p.img);
         }
     }
+}
+
+// Split-K: the CTA's raw sums into its slice of the workspace, [row][col]
+// with row = tile * 128 + lane row.
+template <int NV>
+__device__ __forceinline__ void store_partial(const GemmArgs& a, int split, int row, int col0, const float (&v)[NV]) {
+    float* dst = a.part + split * a.part_split + static_cast<long long>(row) * a.part_ld + col0;
+#pragma unroll
+    for (int j = 0; j < NV; j += 4)
+        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
 }
 
 // ---------------------------------------------------------------- kernel
 
 template <int MODE, int WMODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args) {
+gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+                  const GemmArgs args) {
     using S = GemmShape<WMODE>;
     constexpr int BN = S::BN;
     constexpr bool kGated = WMODE == kWeightGated;
@@ -287,14 +231,18 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kBM;
+    const int tile = blockIdx.x;
     const int n0 = blockIdx.y * BN;
-    const int kblocks = args.kpad / kBK;
+    const int split = blockIdx.z;
+    const int per_split = (args.kblocks + args.ksplit - 1) / args.ksplit;
+    const int kb0 = split * per_split;
+    const int kb1 = min(args.kblocks, kb0 + per_split);
+    const int kblocks = max(0, kb1 - kb0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::kStages; ++s) {
-            mbar_init(&full[s], 1 + 4);  // TMA arrive.expect_tx + the four converter warps
-            mbar_init(&empty[s], 1);     // the MMA commit
+            mbar_init(&full[s], 1);   // TMA arrive.expect_tx
+            mbar_init(&empty[s], 1);  // the MMA commit
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&hi_full[b], 1);
@@ -304,6 +252,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
         mbar_init(drain, 1);
         *abort = 0;
         fence_barrier_init();
+        tma_prefetch_desc(&amap);
         tma_prefetch_desc(&wmap);
     }
     if (warp == 1) tmem_alloc(tmem_slot, S::kTmemCols);
@@ -320,20 +269,42 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
+            // This tile's A coordinates.
+            int ax = 0, ay = 0, az = 0;
+            const ConvGeom& g = args.cg;
+            if (MODE == kModeConv) {
+                const int tx = tile % g.tw, ty = (tile / g.tw) % g.th, tz = tile / (g.tw * g.th);
+                ax = tx * g.owt * g.s0 - g.p0;
+                ay = ty * g.oht * g.s1 - g.p1;
+                az = tz * g.nt;
+            }
             int issued = 0;
-            for (int kb = 0; kb < kblocks; ++kb) {
-                const int s = kb % S::kStages;
-                const uint32_t parity = ((kb / S::kStages) & 1) ^ 1;
+            const uint32_t tx_bytes = 2 * args.a_tx + S::kBBytes * (S::kHasB1 ? 2 : 1);
+            for (int i = 0; i < kblocks; ++i) {
+                const int kb = kb0 + i;
+                const int s = i % S::kStages;
+                const uint32_t parity = ((i / S::kStages) & 1) ^ 1;
                 if (!mbar_wait(&empty[s], parity, abort, args.err)) break;
-                mbar_arrive_expect_tx(&full[s], S::kBBytes * (S::kHasB1 ? 2 : 1));
+                mbar_arrive_expect_tx(&full[s], tx_bytes);
+                if (MODE == kModeLinear) {
+                    tma_load_2d(stage_a_hi(s), &amap, &full[s], kb * kBK, tile * kBM);
+                    tma_load_2d(stage_a_lo(s), &amap, &full[s], kb * kBK, args.a_lo_row + tile * kBM);
+                } else {
+                    const int tap = kb / g.cblocks;
+                    const int cx0 = (kb - tap * g.cblocks) * kBK;
+                    const int ky = tap / g.kw, kx = tap - ky * g.kw;
+                    const int x = ax + kx * g.d0, y = ay + ky * g.d1;
+                    tma_load_4d(stage_a_hi(s), &amap, &full[s], cx0, x, y, az);
+                    tma_load_4d(stage_a_lo(s), &amap, &full[s], cx0, x, y, args.a_lo_row + az);
+                }
                 tma_load_2d(stage_b0(s), &wmap, &full[s], kb * kBK, n0);
                 if (S::kHasB1) tma_load_2d(stage_b1(s), &wmap, &full[s], kb * kBK, args.b1_row + n0);
                 ++issued;
             }
             if (*abort) {
                 // Let the loads this thread started land before the CTA exits.
-                for (int kb = (issued > S::kStages ? issued - S::kStages : 0); kb < issued; ++kb)
-                    mbar_wait_quiet(&full[kb % S::kStages], (kb / S::kStages) & 1, 100000000ull);
+                for (int i = (issued > S::kStages ? issued - S::kStages : 0); i < issued; ++i)
+                    mbar_wait_quiet(&full[i % S::kStages], (i / S::kStages) & 1, 100000000ull);
             }
         }
     } else if (warp == 1) {
@@ -341,11 +312,11 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
             bool ok = true;
-            for (int kb = 0; kb < kblocks && ok; ++kb) {
-                const int s = kb % S::kStages;
-                const int b = kb & 1;
-                if (!mbar_wait(&full[s], (kb / S::kStages) & 1, abort, args.err)) { ok = false; break; }
-                if (!mbar_wait(&hi_empty[b], ((kb >> 1) & 1) ^ 1, abort, args.err)) { ok = false; break; }
+            for (int i = 0; i < kblocks && ok; ++i) {
+                const int s = i % S::kStages;
+                const int b = i & 1;
+                if (!mbar_wait(&full[s], (i / S::kStages) & 1, abort, args.err)) { ok = false; break; }
+                if (!mbar_wait(&hi_empty[b], ((i >> 1) & 1) ^ 1, abort, args.err)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t ahi = smem_u32(stage_a_hi(s)), alo = smem_u32(stage_a_lo(s));
                 const uint32_t b0 = smem_u32(stage_b0(s)), b1 = smem_u32(stage_b1(s));
@@ -353,7 +324,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk) {
                     const uint32_t fresh = kk > 0 ? 1u : 0u;
-                    const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                     const uint64_t dah = desc_kmajor_sw128(ahi + kk * 32), dal = desc_kmajor_sw128(alo + kk * 32);
                     const uint64_t db0 = desc_kmajor_sw128(b0 + kk * 32);
                     mma_f16(d_hi, dah, db0, idesc, fresh);
@@ -377,30 +348,6 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
                 mbar_wait_quiet(drain, 0, 100000000ull);
             }
         }
-    } else if (warp < kEpiWarp0) {
-        // ------------------------------------------------ converters
-        const int t = threadIdx.x - kConvWarp0 * 32;
-        bool over = false;
-        float v0[32], v1[32];
-        if (kblocks > 0) {
-            load_half<MODE>(args, m0, 0, 0, t, v0);
-            load_half<MODE>(args, m0, 0, 1, t, v1);
-        }
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int s = kb % S::kStages;
-            const uint32_t parity = ((kb / S::kStages) & 1) ^ 1;
-            if (!mbar_wait(&empty[s], parity, abort, args.err)) break;
-            const uint32_t ahi = smem_u32(stage_a_hi(s)), alo = smem_u32(stage_a_lo(s));
-            const bool more = kb + 1 < kblocks;
-            over |= store_half<MODE>(v0, 0, t, ahi, alo);
-            if (more) load_half<MODE>(args, m0, kb + 1, 0, t, v0);
-            over |= store_half<MODE>(v1, 1, t, ahi, alo);
-            if (more) load_half<MODE>(args, m0, kb + 1, 1, t, v1);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full[s]);
-        }
-        if (over) atomicOr(args.err, kErrRange);
     } else {
         // ------------------------------------------------ epilogue (drains hi per k-block)
         const int ew = warp - kEpiWarp0;      // 0..7
@@ -415,9 +362,9 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
             gsum[j] = 0.0f;
         }
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int b = kb & 1;
-            if (!mbar_wait(&hi_full[b], (kb >> 1) & 1, abort, args.err)) { ok = false; break; }
+        for (int i = 0; i < kblocks; ++i) {
+            const int b = i & 1;
+            if (!mbar_wait(&hi_full[b], (i >> 1) & 1, abort, args.err)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < NV; c += 32) {
@@ -439,7 +386,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
             __syncwarp();
             if (lane == 0) mbar_arrive(&hi_empty[b]);
         }
-        if (ok && mbar_wait(lo_full, 0, abort, args.err)) {
+        if (ok && kblocks > 0 && mbar_wait(lo_full, 0, abort, args.err)) {
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < NV; c += 32) {
@@ -458,18 +405,61 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap wmap, const GemmArgs args)
                 for (int j = 0; j < 32; ++j) sum[c + j] = fmaf(lo[j], kLoUnscale, sum[c + j]);
             }
             const int col0 = n0 + half * NV;
-            if (MODE == kModeLinear)
-                store_linear<WMODE, NV>(args, smem, ew, q, lane, m0, col0, sum, gsum);
-            else
-                store_conv<NV>(args, m0 + q * 32 + lane, col0, sum);
+            const int row = q * 32 + lane;
+            if (args.ksplit > 1) {
+                store_partial<NV>(args, split, tile * kBM + row, col0, sum);
+            } else if (MODE == kModeLinear) {
+                store_linear<WMODE, NV>(args, smem, ew, q, lane, tile * kBM, col0, sum, gsum);
+            } else {
+                store_conv<NV>(args, conv_pos(args.cg, tile, row), col0, sum);
+            }
+        } else if (ok && kblocks == 0 && args.ksplit > 1) {
+            float zero[NV];
+#pragma unroll
+            for (int j = 0; j < NV; ++j) zero[j] = 0.0f;
+            store_partial<NV>(args, split, tile * kBM + q * 32 + lane, n0 + half * NV, zero);
         }
     }
 
+    // Single-lane roles rejoin their warps before the CTA-wide barrier.
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, S::kTmemCols);
+    }
+}
+
+// Split-K reduction: output (row, col) = sum over the splits in order, then
+// the chain; rows enumerate tiles as the GEMM's (conv positions via conv_pos).
+template <int MODE>
+__global__ void splitk_reduce_kernel(const GemmArgs a, int tiles) {
+    // Rows a warp at a time, columns along the lanes (the host keeps
+    // tiles * 128 * n below 2^31).
+    const int rows = tiles * kBM;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int wr = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wr < rows * ((a.n + 31) / 32); wr += warps) {
+        const int row = wr % rows;
+        const int col = (wr / rows) * 32 + (threadIdx.x & 31);
+        if (col >= a.n) continue;
+        float v = 0.0f;
+        for (int s = 0; s < a.ksplit; ++s) v += a.part[s * a.part_split + row * a.part_ld + col];
+        if (MODE == kModeLinear) {
+            const long long m = row;
+            if (m >= a.m) continue;
+            const long long i1 = m % a.rne1, t = m / a.rne1, i2 = t % a.rne2, i3 = t / a.rne2;
+            float* out = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3] + col * a.ynb[0];
+            if (a.chain.from_redirect) v = *out + v;
+            *out = apply_chain(a.chain, v, col, i1, i2, i3);
+        } else {
+            const ConvPos p = conv_pos(a.cg, static_cast<int>(row / kBM), static_cast<int>(row % kBM));
+            if (!p.ok) continue;
+            float* out = a.y + p.ox * a.ynb[0] + static_cast<long long>(p.oy) * a.ynb[1] + p.img * a.ynb[3] +
+                         col * a.ynb[2];
+            if (a.chain.from_redirect) v = *out + v;
+            *out = apply_chain(a.chain, v, p.ox, p.oy, col, p.img);
+        }
     }
 }
 

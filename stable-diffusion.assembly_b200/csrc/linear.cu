@@ -1,5 +1,8 @@
 // Entry points of the GEMM-backed operations: MUL_MAT (with and without the
-// gated GELU) and the direct convolution.
+// gated GELU) and the direct convolution.  Each splits its activation once
+// into the workspace (split.cuh), takes the packed weights from the store
+// (store.cuh) and runs the TMA-fed tcgen05 GEMM (gemm.cuh), with K split over
+// several CTAs when the output has too few tiles to fill the GPU.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -8,30 +11,65 @@
 #include "../../include/sdb.h"
 #include "gemm.cuh"
 #include "runtime.cuh"
+#include "split.cuh"
 #include "store.cuh"
 
 namespace sdb {
 
 namespace {
 
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
 template <int MODE, int WMODE>
-int launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const GemmArgs& a, int tiles, cudaStream_t st) {
     using S = GemmShape<WMODE>;
     auto kern = gemm_split_kernel<MODE, WMODE>;
     SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
-    const dim3 grid(static_cast<unsigned>((a.m + kBM - 1) / kBM), static_cast<unsigned>((a.n + S::BN - 1) / S::BN));
-    if (grid.y > 65535u) return fail(SDB_NOT_SUPPORTED, "gemm: too many column tiles");
-    kern<<<grid, kGemmThreads, S::kSmemBytes, st>>>(map, a);
+    const int ntiles = (a.n + S::BN - 1) / S::BN;
+    if (ntiles > 65535 || a.ksplit > 65535) return fail(SDB_NOT_SUPPORTED, "gemm: too many tiles");
+    const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(ntiles), static_cast<unsigned>(a.ksplit));
+    kern<<<grid, kGemmThreads, S::kSmemBytes, st>>>(amap, wmap, a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
+    if (a.ksplit > 1) {
+        const long long total = static_cast<long long>(tiles) * kBM * a.n;
+        const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, tiles);
+        count_launch();
+        SDB_CUDA(cudaGetLastError());
+    }
     return SDB_OK;
 }
 
 template <int MODE>
-int dispatch(const Packed& p, int wmode, const GemmArgs& a, cudaStream_t st) {
-    if (wmode == kWeightGated) return launch_gemm<MODE, kWeightGated>(p.map64, a, st);
-    return wmode == kWeightSplit ? launch_gemm<MODE, kWeightSplit>(p.map128, a, st)
-                                 : launch_gemm<MODE, kWeightHalf>(p.map128, a, st);
+int dispatch(const CUtensorMap& amap, const Packed& p, int wmode, const GemmArgs& a, int tiles, cudaStream_t st) {
+    if (wmode == kWeightGated) return launch_gemm<MODE, kWeightGated>(amap, p.map64, a, tiles, st);
+    return wmode == kWeightSplit ? launch_gemm<MODE, kWeightSplit>(amap, p.map128, a, tiles, st)
+                                 : launch_gemm<MODE, kWeightHalf>(amap, p.map128, a, tiles, st);
+}
+
+// K is split over CTAs when the output tiles leave most SMs idle: enough
+// splits to fill the GPU once, at least 8 k-blocks each.
+int choose_ksplit(int tiles, int kblocks, int wmode) {
+    if (wmode == kWeightGated) return 1;
+    const int sms = current_sm_count();
+    if (tiles >= sms / 2 || kblocks < 16) return 1;
+    const int want = (sms + tiles - 1) / tiles;
+    return std::max(1, std::min(want, kblocks / 8));
+}
+
+// Bytes of split-K partial sums: [ksplit][tiles * 128][npad].
+size_t partial_bytes(int ksplit, int tiles, int64_t n, int bn) {
+    if (ksplit <= 1) return 0;
+    return static_cast<size_t>(ksplit) * tiles * kBM * round_up(n, bn) * 4;
+}
+
+void set_partials(GemmArgs& a, void* ws, size_t offset, int tiles, int bn) {
+    if (a.ksplit <= 1) return;
+    const long long ld = round_up(a.n, bn);
+    a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + offset);
+    a.part_ld = ld;
+    a.part_split = static_cast<long long>(tiles) * kBM * ld;
 }
 
 bool is_type(const sdb_tensor* t, int type) { return t != nullptr && t->type == type && t->data != nullptr; }
@@ -80,6 +118,68 @@ bool mul_mat_shapes(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* 
     return true;
 }
 
+int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
+               cudaStream_t st, bool gated) {
+    const int64_t k = w->ne[0];
+    const int64_t n = gated ? w->ne[1] / 2 : w->ne[1];
+    const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
+    if (m > (1LL << 30) || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "mul_mat: too large");
+    std::shared_ptr<Packed> p;
+    const int rc = gated ? packed_weights(w, Layout::gated, 2 * n, k, 0, n, st, &p)
+                         : packed_weights(w, Layout::linear, n, k, 0, 0, st, &p);
+    if (rc != SDB_OK) return rc;
+    const int wmode = gated ? kWeightGated : p->split ? kWeightSplit : kWeightHalf;
+    const int bn = wmode == kWeightGated ? 64 : 128;
+    const int tiles = static_cast<int>((m + kBM - 1) / kBM);
+
+    GemmArgs a{};
+    a.m = static_cast<int>(m);
+    a.a_lo_row = static_cast<int>(m);
+    a.kblocks = static_cast<int>(p->kpad / kBK);
+    a.n = static_cast<int>(n);
+    a.b1_row = static_cast<int>(p->b1_row);
+    a.a_tx = kBM * kBK * 2;
+    a.rne1 = dst->ne[1];
+    a.rne2 = dst->ne[2];
+    set_out(a, dst, chain);
+    a.ksplit = choose_ksplit(tiles * static_cast<int>((n + bn - 1) / bn), a.kblocks, wmode);
+
+    // Workspace: the split rows [0, M) hi, [M, 2M) lo of kp8 FP16, then any partial sums.
+    const int64_t kp8 = round_up(k, 8);
+    const size_t a_bytes = static_cast<size_t>(round_up(2 * m * kp8 * 2, 256));
+    void* ws = nullptr;
+    if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, n, bn), &ws); s != SDB_OK) return s;
+    set_partials(a, ws, a_bytes, tiles, bn);
+    const long long ne[4] = {x->ne[0], x->ne[1], x->ne[2], x->ne[3]};
+    const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
+    if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err, st);
+        s != SDB_OK)
+        return s;
+    CUtensorMap amap;
+    const uint64_t dims[2] = {static_cast<uint64_t>(kp8), static_cast<uint64_t>(2 * m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(kp8) * 2};
+    const uint32_t box[2] = {64, 128};
+    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the activations");
+    return dispatch<kModeLinear>(amap, *p, wmode, a, tiles, st);
+}
+
+// The output positions of a conv tile: OWt x OHt x NT <= 128 with the box's
+// extents within TMA's 256 elements a dimension (with the stride as the
+// element stride, a box spans OWt * s0 elements).
+bool conv_tiles(ConvGeom& g) {
+    g.owt = std::min(g.ow, 128);
+    if (g.owt * g.s0 > 256) g.owt = 256 / g.s0;
+    g.oht = std::max(1, std::min(g.oh, 128 / g.owt));
+    if (g.oht * g.s1 > 256) g.oht = 256 / g.s1;
+    g.nt = std::max(1, std::min(g.n, 128 / (g.owt * g.oht)));
+    g.tw = (g.ow + g.owt - 1) / g.owt;
+    g.th = (g.oh + g.oht - 1) / g.oht;
+    g.tn = (g.n + g.nt - 1) / g.nt;
+    return g.owt >= 1 && g.oht >= 1 && static_cast<long long>(g.tw) * g.th * g.tn < (1LL << 31);
+}
+
 }  // namespace
 
 }  // namespace sdb
@@ -97,26 +197,7 @@ int sdb_mul_mat(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst,
                 void* stream) {
     if (!sdb_mul_mat_supported(w, x, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat: shapes not supported");
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_mul_mat: invalid chain");
-    const auto st = static_cast<cudaStream_t>(stream);
-    const int64_t k = w->ne[0], n = w->ne[1];
-    const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
-    if (m > (1LL << 31) - kBM || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat: too large");
-    std::shared_ptr<Packed> p;
-    if (int s = packed_weights(w, Layout::linear, n, k, 0, 0, st, &p); s != SDB_OK) return s;
-    GemmArgs a{};
-    a.x = static_cast<const float*>(x->data);
-    a.xld = k;
-    a.m = static_cast<int>(m);
-    a.kpad = static_cast<int>(p->kpad);
-    a.klog = static_cast<int>(k);
-    a.n = static_cast<int>(n);
-    a.b1_row = static_cast<int>(p->b1_row);
-    a.rne1 = dst->ne[1];
-    a.rne2 = dst->ne[2];
-    a.vec = (reinterpret_cast<uintptr_t>(x->data) % 16 == 0) && (k % 4 == 0);
-    set_out(a, dst, chain);
-    const int wmode = p->split ? kWeightSplit : kWeightHalf;
-    return dispatch<kModeLinear>(*p, wmode, a, st);
+    return run_linear(w, x, dst, chain, static_cast<cudaStream_t>(stream), false);
 }
 
 int sdb_mul_mat_gated_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* out) {
@@ -131,27 +212,8 @@ int sdb_mul_mat_gated(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor
         return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat_gated: shapes not supported");
     if (!valid_chain(chain) || (chain && (chain->redirect || chain->from_redirect)))
         return fail(SDB_INVALID, "sdb_mul_mat_gated: invalid chain");
-    const auto st = static_cast<cudaStream_t>(stream);
-    const int64_t k = w->ne[0], half = w->ne[1] / 2;
-    const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
-    std::shared_ptr<Packed> p;
-    if (int s = packed_weights(w, Layout::gated, 2 * half, k, 0, half, st, &p); s != SDB_OK) return s;
-    GemmArgs a{};
-    a.x = static_cast<const float*>(x->data);
-    a.xld = k;
-    a.m = static_cast<int>(m);
-    a.kpad = static_cast<int>(p->kpad);
-    a.klog = static_cast<int>(k);
-    a.n = static_cast<int>(half);
-    a.b1_row = static_cast<int>(p->b1_row);
-    a.rne1 = out->ne[1];
-    a.rne2 = out->ne[2];
-    a.vec = (reinterpret_cast<uintptr_t>(x->data) % 16 == 0) && (k % 4 == 0);
-    set_out(a, out, chain);
-    return dispatch<kModeLinear>(*p, kWeightGated, a, st);
+    return run_linear(w, x, out, chain, static_cast<cudaStream_t>(stream), true);
 }
-
-// ---------------------------------------------------------------- conv2d
 
 int sdb_conv2d_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6]) {
     if (w == nullptr || x == nullptr || dst == nullptr || params == nullptr) return 0;
@@ -159,7 +221,7 @@ int sdb_conv2d_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
         !is_type(dst, SDB_TYPE_F32))
         return 0;
     const int s0 = params[0], s1 = params[1], p0 = params[2], p1 = params[3], d0 = params[4], d1 = params[5];
-    if (s0 < 1 || s1 < 1 || d0 < 1 || d1 < 1 || p0 < 0 || p1 < 0) return 0;
+    if (s0 < 1 || s1 < 1 || d0 < 1 || d1 < 1 || p0 < 0 || p1 < 0 || s0 > 8 || s1 > 8) return 0;
     if (w->ne[2] != x->ne[2] || dst->ne[2] != w->ne[3] || dst->ne[3] != x->ne[3]) return 0;
     const int64_t ow = (x->ne[0] + 2 * p0 - d0 * (w->ne[0] - 1) - 1) / s0 + 1;
     const int64_t oh = (x->ne[1] + 2 * p1 - d1 * (w->ne[1] - 1) - 1) / s1 + 1;
@@ -170,8 +232,9 @@ int sdb_conv2d_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
     const int64_t es = w->type == SDB_TYPE_F16 ? 2 : 4;
     for (int d = 0; d < 4; ++d)
         if (w->nb[d] % es != 0 || w->nb[d] < 0) return 0;
-    const int64_t m = ow * oh * x->ne[3];
-    return m < (1LL << 31) - kBM && w->ne[0] * w->ne[1] <= 64 * 64;
+    // TMA coordinates are 32-bit and its images are at most 2^16 deep here.
+    if (x->ne[0] > (1 << 24) || x->ne[1] > (1 << 24) || x->ne[2] > (1 << 20) || 2 * x->ne[3] > 65535) return 0;
+    return w->ne[0] * w->ne[1] <= 64 * 64;
 }
 
 int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
@@ -180,31 +243,56 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_conv2d: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
     const int64_t ic = x->ne[2], oc = w->ne[3];
-    const int icp = static_cast<int>((ic + 15) / 16 * 16);
+    const int icp = static_cast<int>(round_up(ic, 64));
     std::shared_ptr<Packed> p;
     if (int s = packed_weights(w, Layout::conv, oc, 0, icp, 0, st, &p); s != SDB_OK) return s;
+
     GemmArgs a{};
-    a.x = static_cast<const float*>(x->data);
     ConvGeom& g = a.cg;
-    g.iw = static_cast<int>(x->ne[0]);
-    g.ih = static_cast<int>(x->ne[1]);
-    g.ic = static_cast<int>(ic);
-    g.n = static_cast<int>(x->ne[3]);
     g.ow = static_cast<int>(dst->ne[0]);
     g.oh = static_cast<int>(dst->ne[1]);
+    g.n = static_cast<int>(x->ne[3]);
     g.kw = static_cast<int>(w->ne[0]);
     g.kh = static_cast<int>(w->ne[1]);
     g.s0 = params[0]; g.s1 = params[1]; g.p0 = params[2]; g.p1 = params[3]; g.d0 = params[4]; g.d1 = params[5];
-    g.icp = icp;
-    for (int d = 0; d < 4; ++d) g.xnb[d] = x->nb[d] / 4;
-    a.m = g.ow * g.oh * g.n;
-    a.kpad = static_cast<int>(p->kpad);
-    a.klog = 0;
+    g.cblocks = icp / 64;
+    if (!conv_tiles(g)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: tiling");
+    const int tiles = g.tw * g.th * g.tn;
+    const int wmode = p->split ? kWeightSplit : kWeightHalf;
+    a.m = 0;
+    a.kblocks = static_cast<int>(p->kpad / kBK);
     a.n = static_cast<int>(oc);
     a.b1_row = static_cast<int>(p->b1_row);
+    a.a_tx = static_cast<uint32_t>(64 * 2 * g.owt * g.oht * g.nt);
     set_out(a, dst, chain);
-    const int wmode = p->split ? kWeightSplit : kWeightHalf;
-    return dispatch<kModeConv>(*p, wmode, a, st);
+    a.ksplit = choose_ksplit(tiles * static_cast<int>((oc + 127) / 128), a.kblocks, wmode);
+
+    // Workspace: the image split and channels-last, [2N][H][W][cp8] (hi images,
+    // then lo), then any partial sums.
+    const int64_t cp8 = round_up(ic, 8);
+    const int64_t W = x->ne[0], H = x->ne[1], N = x->ne[3];
+    a.a_lo_row = static_cast<int>(N);
+    const size_t a_bytes = static_cast<size_t>(round_up(2 * N * H * W * cp8 * 2, 256));
+    void* ws = nullptr;
+    if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, oc, 128), &ws); s != SDB_OK) return s;
+    set_partials(a, ws, a_bytes, tiles, 128);
+    const long long ne[4] = {W, H, ic, N};
+    const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
+    if (int s = split_nhwc(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
+        s != SDB_OK)
+        return s;
+    CUtensorMap amap;
+    const uint64_t dims[4] = {static_cast<uint64_t>(cp8), static_cast<uint64_t>(W), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(2 * N)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(cp8 * 2), static_cast<uint64_t>(W * cp8 * 2),
+                                 static_cast<uint64_t>(H * W * cp8 * 2)};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(g.owt * g.s0), static_cast<uint32_t>(g.oht * g.s1),
+                             static_cast<uint32_t>(g.nt)};
+    const uint32_t estr[4] = {1, static_cast<uint32_t>(g.s0), static_cast<uint32_t>(g.s1), 1};
+    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, ws, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B, estr) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the image");
+    return dispatch<kModeConv>(amap, *p, wmode, a, tiles, st);
 }
 
 }  // extern "C"

@@ -136,6 +136,72 @@ __global__ void __launch_bounds__(kNormThreads) group_apply_kernel(const GroupAr
     }
 }
 
+// The whole (image, group) in shared memory: read once from HBM, the two
+// passes of the statistics and the normalisation from shared memory, written
+// once.  One CTA per (image, group); for groups of up to kResident floats.
+constexpr int kResidentThreads = 1024;
+constexpr long long kResident = 50 * 1024;  // floats: 200 KB
+
+__global__ void __launch_bounds__(kResidentThreads) group_resident_kernel(const GroupArgs a) {
+    extern __shared__ float xs[];
+    __shared__ double scratch[32];
+    __shared__ float stats[2];
+    const int item = blockIdx.x;
+    const int i3 = item / a.groups, g = item % a.groups;
+    const long long c0 = static_cast<long long>(g) * a.per_group;
+    const long long c1 = min(a.ne2, c0 + a.per_group);
+    if (c0 >= c1) return;
+    const long long count = a.ne0 * a.ne1 * (c1 - c0);
+    const float* xb = a.x + i3 * a.xnb[3] + c0 * a.xnb[2];
+    double s = 0.0;
+    if ((reinterpret_cast<uintptr_t>(xb) & 15) == 0 && (count & 3) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(xb);
+        float4* s4 = reinterpret_cast<float4*>(xs);
+        // Unrolled: the loads of eight iterations are in flight together.
+#pragma unroll 8
+        for (long long e = threadIdx.x; e < count / 4; e += blockDim.x) {
+            const float4 v = __ldg(x4 + e);
+            s4[e] = v;
+            s += static_cast<double>(v.x) + static_cast<double>(v.y) + static_cast<double>(v.z) +
+                 static_cast<double>(v.w);
+        }
+    } else {
+#pragma unroll 8
+        for (long long e = threadIdx.x; e < count; e += blockDim.x) {
+            const float v = __ldg(xb + e);
+            xs[e] = v;
+            s += static_cast<double>(v);
+        }
+    }
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) stats[0] = static_cast<float>(s / static_cast<double>(count));
+    __syncthreads();
+    const float mean = stats[0];
+    double q = 0.0;
+    for (long long e = threadIdx.x; e < count; e += blockDim.x) {
+        const float v = xs[e] - mean;
+        q += static_cast<double>(v * v);
+    }
+    q = block_sum(q, scratch);
+    if (threadIdx.x == 0) stats[1] = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(count)) + a.eps);
+    __syncthreads();
+    const float scale = stats[1];
+    // Rows of ne0 (positions of an image row) a warp at a time: no division per element.
+    const int rows = static_cast<int>(a.ne1 * (c1 - c0));
+    const int ne0 = static_cast<int>(a.ne0), ne1 = static_cast<int>(a.ne1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int row = warp; row < rows; row += nwarps) {
+        const int c = static_cast<int>(c0) + row / ne1;
+        const int r = row - (row / ne1) * ne1;
+        const float* src = xs + static_cast<long long>(row) * ne0;
+        float* dst = a.y + static_cast<long long>(r) * a.ynb[1] + c * a.ynb[2] + i3 * a.ynb[3];
+        for (int i0 = lane; i0 < ne0; i0 += 32) {
+            const float v = apply_chain(a.chain, (src[i0] - mean) * scale, i0, r, c, i3);
+            dst[i0 * a.ynb[0]] = v;
+        }
+    }
+}
+
 struct RowArgs {
     const float* x;
     float* y;
@@ -237,6 +303,15 @@ extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_
     a.chain = make_chain(chain);
     const long long items = static_cast<long long>(groups) * a.ne3;
     const long long group_elems = a.ne0 * a.ne1 * a.per_group;
+    if (group_elems <= kResident && items <= 0x7fffffffLL) {
+        const int smem = static_cast<int>(group_elems * 4);
+        SDB_CUDA(cudaFuncSetAttribute(group_resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kResident * 4)));
+        group_resident_kernel<<<static_cast<unsigned>(items), kResidentThreads, smem, st>>>(a);
+        count_launch();
+        SDB_CUDA(cudaGetLastError());
+        return SDB_OK;
+    }
     // Enough CTAs for every SM several times over, each slice at least 8K elements.
     const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
     a.split = static_cast<int>(std::min<long long>(want, std::max<long long>(1, group_elems / 8192)));

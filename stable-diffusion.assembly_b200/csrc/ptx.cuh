@@ -134,6 +134,25 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* desc, ui
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
+// A contiguous run of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from global into shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 // Allocates `ncols` columns of tensor memory (a power of two >= 32) for the
@@ -278,24 +297,35 @@ __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
     lo = __float2half_rn((x - __half2float(hi)) * kLoScale);
 }
 
-// Splits 8 floats into one 16-byte chunk of hi and one of lo; returns true
-// when any input is beyond the FP16 range.
+// The FP32 value of the FP16 bits in the low half of `w`: the exponent and
+// significand moved into FP32's fields and scaled by 2^112 (exact for normal
+// and subnormal values alike) -- integer ops and one multiply, where a
+// conversion instruction would take the slower conversion pipe.
+__device__ __forceinline__ float half_bits_to_float(uint32_t w) {
+    const uint32_t h = w & 0xffffu;
+    const float mag = __uint_as_float((h & 0x7fffu) << 13) * 0x1p112f;
+    return __uint_as_float(__float_as_uint(mag) | ((h & 0x8000u) << 16));
+}
+
+// Splits 8 floats into one 16-byte chunk of hi and one of lo (the same pair
+// as split_half: hi = x rounded to FP16, lo = (x - hi) 2^11 rounded to FP16);
+// returns true when any input is beyond the FP16 range.  Four packed
+// conversions (two values each) for hi and four for lo.
 __device__ __forceinline__ bool split8(const float (&x)[8], uint4& hi, uint4& lo) {
-    __half h[8], l[8];
+    uint32_t h[4], l[4];
     bool over = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        split_half(x[i], h[i], l[i]);
-        over |= !(fabsf(x[i]) <= kHalfLimit);
+    for (int i = 0; i < 4; ++i) {
+        const __half2 hh = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        const float r0 = (x[2 * i] - half_bits_to_float(h[i])) * kLoScale;
+        const float r1 = (x[2 * i + 1] - half_bits_to_float(h[i] >> 16)) * kLoScale;
+        const __half2 ll = __floats2half2_rn(r0, r1);
+        l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+        over |= !(fabsf(x[2 * i]) <= kHalfLimit) | !(fabsf(x[2 * i + 1]) <= kHalfLimit);
     }
-    hi.x = static_cast<uint32_t>(__half_as_ushort(h[0])) | (static_cast<uint32_t>(__half_as_ushort(h[1])) << 16);
-    hi.y = static_cast<uint32_t>(__half_as_ushort(h[2])) | (static_cast<uint32_t>(__half_as_ushort(h[3])) << 16);
-    hi.z = static_cast<uint32_t>(__half_as_ushort(h[4])) | (static_cast<uint32_t>(__half_as_ushort(h[5])) << 16);
-    hi.w = static_cast<uint32_t>(__half_as_ushort(h[6])) | (static_cast<uint32_t>(__half_as_ushort(h[7])) << 16);
-    lo.x = static_cast<uint32_t>(__half_as_ushort(l[0])) | (static_cast<uint32_t>(__half_as_ushort(l[1])) << 16);
-    lo.y = static_cast<uint32_t>(__half_as_ushort(l[2])) | (static_cast<uint32_t>(__half_as_ushort(l[3])) << 16);
-    lo.z = static_cast<uint32_t>(__half_as_ushort(l[4])) | (static_cast<uint32_t>(__half_as_ushort(l[5])) << 16);
-    lo.w = static_cast<uint32_t>(__half_as_ushort(l[6])) | (static_cast<uint32_t>(__half_as_ushort(l[7])) << 16);
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
     return over;
 }
 

@@ -108,7 +108,7 @@ void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxe
 
 CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, void* addr,
                            const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                           CUtensorMapSwizzle swizzle) {
+                           CUtensorMapSwizzle swizzle, const uint32_t* element_strides) {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -119,6 +119,7 @@ CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t 
     }();
     if (!fn) return CUDA_ERROR_NOT_FOUND;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    for (uint32_t i = 0; element_strides && i < rank && i < 5; ++i) estr[i] = element_strides[i];
     return fn(map, type, rank, addr, reinterpret_cast<const cuuint64_t*>(dims),
               reinterpret_cast<const cuuint64_t*>(strides_bytes), reinterpret_cast<const cuuint32_t*>(box), estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -40,9 +40,10 @@ void count_launch(uint64_t n = 1);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda).
+// element_strides: TMA's traversal stride per dimension (nullptr: all 1).
 CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, void* addr,
                            const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                           CUtensorMapSwizzle swizzle);
+                           CUtensorMapSwizzle swizzle, const uint32_t* element_strides = nullptr);
 
 int current_sm_count();
 
