@@ -17,6 +17,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
+#include <string>
+#include <unordered_map>
 
 #include "../../include/sdb.h"
 #include "chain.cuh"
@@ -344,6 +347,93 @@ extern "C" int sdb_norm(const sdb_tensor* x, const sdb_tensor* dst, float eps, c
     const long long threads = a.rows * 32;
     norm_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(a);
     count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+// ---- GroupNorm for callers that cannot allocate device memory ---------------
+//
+// Some callers may not call cudaMalloc at all: a host whose device memory is
+// owned by another allocator (a memory pool or arena that must account for
+// every byte), code running while a CUDA graph is being captured, or a
+// real-time loop that may not take the driver's allocation lock.
+// sdb_group_norm_no_alloc is sdb_group_norm for them: it takes the split path
+// (sum pass, centred-sum pass, apply) and keeps the per-slice double partial
+// sums in the fixed array below, which the module reserves when it loads on a
+// device and holds until the process exits (512 KiB on every GPU that loads
+// this library).  That bounds the work it takes: at most kStaticSlices slices,
+// i.e. (images x groups) <= 32768.  Larger inputs are rejected.
+//
+// Every slot a call reads is written earlier in the same call (pass one writes
+// the sums, pass two the centred sums, the apply pass reads both), so nothing
+// has to be cleared between calls.  All calls share the array: two calls whose
+// kernels overlap on the GPU (different streams, no ordering between them)
+// race on it and give wrong results.
+
+namespace sdb {
+namespace {
+
+constexpr long long kStaticSlices = 32768;                   // slices of (image, group)
+static __device__ __align__(256) double g_static_partials[kStaticSlices * 2];
+
+// The device address of g_static_partials on the current device, looked up
+// once per device (the first call on a device does this; make that call
+// before any stream capture begins).
+double* static_partials(int* status) {
+    static std::mutex lock;
+    static std::unordered_map<int, double*> addresses;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { *status = cuda_fail(e, "cudaGetDevice"); return nullptr; }
+    std::lock_guard<std::mutex> guard(lock);
+    auto it = addresses.find(dev);
+    if (it != addresses.end()) return it->second;
+    double* p = nullptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_static_partials);
+    if (e != cudaSuccess) { *status = cuda_fail(e, "cudaGetSymbolAddress(g_static_partials)"); return nullptr; }
+    addresses.emplace(dev, p);
+    return p;
+}
+
+}  // namespace
+}  // namespace sdb
+
+extern "C" int sdb_group_norm_no_alloc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps,
+                                       const sdb_chain* chain, void* stream) {
+    if (!f32(x) || !f32(dst) || !contiguous(x) || !same_shape(x, dst) || groups <= 0)
+        return fail(SDB_NOT_SUPPORTED, "sdb_group_norm_no_alloc: not supported");
+    if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))
+        return fail(SDB_INVALID, "sdb_group_norm_no_alloc: invalid chain");
+    for (int d = 0; d < 4; ++d)
+        if (dst->nb[d] % 4) return fail(SDB_NOT_SUPPORTED, "sdb_group_norm_no_alloc: misaligned output");
+    const long long items = static_cast<long long>(groups) * x->ne[3];
+    if (items > kStaticSlices)
+        return fail(SDB_INVALID, "sdb_group_norm_no_alloc: images x groups = " + std::to_string(items) +
+                                     " exceeds the static scratch limit of " + std::to_string(kStaticSlices));
+    int status = SDB_OK;
+    double* partials = static_partials(&status);
+    if (!partials) return status;
+    GroupArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.y = static_cast<float*>(dst->data);
+    a.ne0 = x->ne[0]; a.ne1 = x->ne[1]; a.ne2 = x->ne[2]; a.ne3 = x->ne[3];
+    for (int d = 0; d < 4; ++d) { a.xnb[d] = x->nb[d] / 4; a.ynb[d] = dst->nb[d] / 4; }
+    a.groups = groups;
+    a.per_group = static_cast<int>((a.ne2 + groups - 1) / groups);
+    a.eps = eps;
+    a.chain = make_chain(chain);
+    const long long group_elems = a.ne0 * a.ne1 * a.per_group;
+    // As sdb_group_norm's split path, but no more slices than the array holds.
+    const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
+    const long long split = std::min({want, std::max<long long>(1, group_elems / 8192), kStaticSlices / items});
+    a.split = static_cast<int>(split);
+    a.partial = partials;
+    const auto st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = static_cast<unsigned>(items * a.split);
+    group_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 0);
+    group_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 1);
+    group_apply_kernel<<<grid, kNormThreads, 0, st>>>(a);
+    count_launch(3);
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
 }

@@ -36,7 +36,7 @@ STATUS_NAMES = ["OK", "NOT_SUPPORTED", "INVALID", "CUDA_ERROR", "OUT_OF_MEMORY",
 EXPORTS = [
     "sdb_mul_mat_supported", "sdb_mul_mat", "sdb_mul_mat_gated_supported", "sdb_mul_mat_gated",
     "sdb_conv2d_supported", "sdb_conv2d", "sdb_attention_supported", "sdb_attention",
-    "sdb_group_norm", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
+    "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
 ]
 
@@ -88,6 +88,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_attention_supported": (i, [T, T, T, T]),
         "sdb_attention": (i, [T, T, T, T, ctypes.c_float, C, vp]),
         "sdb_group_norm": (i, [T, T, ctypes.c_int32, ctypes.c_float, C, vp]),
+        "sdb_group_norm_no_alloc": (i, [T, T, ctypes.c_int32, ctypes.c_float, C, vp]),
         "sdb_norm": (i, [T, T, ctypes.c_float, C, vp]),
         "sdb_forget": (None, [vp, ctypes.c_size_t]),
         "sdb_store_stats": (None, [ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
@@ -332,6 +333,14 @@ def group_norm(x, groups: int, eps: float, out=None, chain: Chain | None = None,
         out = torch.empty_like(x)
     _check(lib.sdb_group_norm(describe(x), describe(out), groups, ctypes.c_float(eps), _chain_ptr(chain),
                               ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def group_norm_no_alloc(x, groups: int, eps: float, out, chain: Chain | None = None, stream=None):
+    """group_norm without any device allocation (sdb_group_norm_no_alloc): out must be given."""
+    lib = load()
+    _check(lib.sdb_group_norm_no_alloc(describe(x), describe(out), groups, ctypes.c_float(eps), _chain_ptr(chain),
+                                       ctypes.c_void_p(_stream_ptr(stream))))
     return out
 
 
