@@ -80,4 +80,58 @@ __device__ __forceinline__ float apply_chain(const Chain& c, float v, long long 
     return v;
 }
 
+// The chain for a tile epilogue: each thread owns one output row (an output
+// position) and walks its columns, so the part of every operand's offset that
+// depends on the row is computed once (row_offsets) and each element adds only
+// column * stride (apply_chain_col).  col_dim names the ggml coordinate the
+// columns run along (0 for a linear layer's features, 2 for a convolution's
+// channels).  The step loop is unrolled so that the launch-parameter arrays
+// are indexed statically.
+struct ChainRow {
+    long long off[SDB_MAX_STEPS];
+};
+
+__device__ __forceinline__ void row_offsets(const Chain& c, ChainRow& r, int col_dim, long long j0, long long j1,
+                                            long long j2) {
+    // j0..j2: the three row coordinates in ggml order without col_dim.
+#pragma unroll
+    for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+        if (col_dim == 0)
+            r.off[s] = j0 * c.nb[s][1] + j1 * c.nb[s][2] + j2 * c.nb[s][3];
+        else
+            r.off[s] = j0 * c.nb[s][0] + j1 * c.nb[s][1] + j2 * c.nb[s][3];
+    }
+}
+
+// The chain over NVAL consecutive columns col0.. of one row, in place: one
+// step at a time over all the columns, so that a step's operand loads are
+// issued together (columns past col_max read column col_max; their results
+// are not stored).
+template <int COL_DIM, int NVAL>
+__device__ __forceinline__ void apply_chain_cols(const Chain& c, const ChainRow& r, float* v, long long col0,
+                                                 long long col_max) {
+#pragma unroll
+    for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+        if (s >= c.count) break;
+        if (c.kind[s] == SDB_STEP_SILU) {
+#pragma unroll
+            for (int j = 0; j < NVAL; ++j) v[j] = silu(v[j]);
+        } else {
+            const float* base = c.operand[s] + r.off[s];
+            const long long stride = c.nb[s][COL_DIM];
+            float o[NVAL];
+#pragma unroll
+            for (int j = 0; j < NVAL; ++j) o[j] = __ldg(base + min(col0 + j, col_max) * stride);
+            if (c.kind[s] == SDB_STEP_ADD) {
+#pragma unroll
+                for (int j = 0; j < NVAL; ++j) v[j] += o[j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < NVAL; ++j) v[j] *= o[j];
+            }
+        }
+    }
+}
+
 }  // namespace sdb
+

@@ -66,14 +66,18 @@ struct ConvGeom {
 
 struct GemmArgs {
     int m;                  // rows of C (linear: tokens; conv: unused, see cg)
-    int a_lo_row;           // row (linear) / image (conv) offset of the lo plane in A's map
     int kblocks;            // K / kBK of the whole product
-    int ksplit;             // CTAs along K (grid.z)
+    int ksplit;             // parts K is split into (each at least one k-block)
+    int per_split;          // k-blocks of a part
     int n;                  // columns of C (linear: output features; gated: the half)
     int b1_row;             // row offset in the packed weights of the second B operand
     uint32_t a_tx;          // bytes of one A tile (hi or lo) as TMA writes it
+    int a_planes;           // 2: one TMA box brings hi and lo (a full 128-row tile); 1: one box each
+    int tiles_m, tiles_n;   // output tiles along rows / columns
+    int items;              // tiles_m * tiles_n * ksplit work items, taken round-robin by the CTAs
+    int store;              // kStoreTma / kStoreDirect (linear); conv always stores directly
     float* y;               // output (the redirect when the chain has one)
-    float* part;            // split-K: partial sums [ksplit][rows][part_ld]
+    float* part;            // split-K: partial sums [ksplit][tiles_m * 128][part_ld]
     long long part_ld;      // columns of a partial row
     long long part_split;   // elements between splits
     long long ynb[4];       // output strides in elements
@@ -83,6 +87,8 @@ struct GemmArgs {
     unsigned* err;
 };
 
+enum : int { kStoreDirect = 0, kStoreTma = 1 };
+
 template <int WMODE>
 struct GemmShape {
     static constexpr int BN = WMODE == kWeightGated ? 64 : 128;
@@ -90,16 +96,19 @@ struct GemmShape {
     static constexpr int kABytes = kBM * kBK * 2;  // one of hi / lo
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = 2 * kABytes + kBBytes * (kHasB1 ? 2 : 1);
-    static constexpr int kStages = (200 * 1024) / kStageBytes >= 6 ? 6 : (200 * 1024) / kStageBytes;
+    // Output staging for the TMA stores: a 32 x 32 FP32 box (4 KB) per epilogue warp.
+    static constexpr int kStagingBytes = 8 * 32 * 128;
+    static constexpr int kBudget = 227 * 1024 - kStagingBytes - 1024 /*align*/ - 256 /*barriers*/;
+    static constexpr int kStages = kBudget / kStageBytes >= 6 ? 6 : kBudget / kStageBytes;
     // Tensor-memory columns: hi buffers (two; gated: x0 x1 g0 g1) then lo (gated: x, g).
     static constexpr int kHiCols = WMODE == kWeightGated ? 4 * BN : 2 * BN;
     static constexpr int kLoCol = kHiCols;
     static constexpr int kAccCols = kHiCols + (WMODE == kWeightGated ? 2 * BN : BN);
     static constexpr int kTmemCols = 512;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 256;
     static_assert(kAccCols <= 512, "accumulators exceed tensor memory");
     static_assert(kStages >= 2, "too few stages");
-    static_assert(kStages * kStageBytes >= 2 * 8 * 32 * 33 * 4 + 8 * 32 * 32, "epilogue staging does not fit");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // ---------------------------------------------------------------- tiles
@@ -126,118 +135,51 @@ __device__ __forceinline__ ConvPos conv_pos(const ConvGeom& g, int tile, int r) 
 
 // ---------------------------------------------------------------- epilogue
 
-struct RowInfo {
-    long long base, i1, i2, i3;
-};
-
-// A linear layer's rows are contiguous: the 32 x 32 values of a warp go
-// through shared memory (the pipeline stages, idle once the lo accumulator is
-// full) and the warp writes 32 rows as 128-byte runs.
-template <int WMODE, int NV>
-__device__ __forceinline__ void store_linear(const GemmArgs& a, uint8_t* smem, int ew, int q, int lane, int m0,
-                                             int col0, const float (&v)[NV], const float (&gv)[NV]) {
-    constexpr bool kGated = WMODE == kWeightGated;
-    float* tile = reinterpret_cast<float*>(smem) + ew * (32 * 33);
-    RowInfo* info = reinterpret_cast<RowInfo*>(smem + 8 * 32 * 33 * 4) + ew * 32;
-    float* gtile = reinterpret_cast<float*>(smem + 8 * 32 * 33 * 4 + 8 * 32 * 32) + ew * (32 * 33);
-    {
-        const long long m = m0 + q * 32 + lane;
-        RowInfo r;
-        r.i1 = m % a.rne1;
-        const long long t = m / a.rne1;
-        r.i2 = t % a.rne2;
-        r.i3 = t / a.rne2;
-        r.base = r.i1 * a.ynb[1] + r.i2 * a.ynb[2] + r.i3 * a.ynb[3];
-        info[lane] = r;
+// A linear layer's output rows are contiguous: each epilogue warp writes its
+// 32 rows x 32 columns as one TMA store from a 4 KB staging box in the
+// 128-byte swizzle (row r's 16-byte chunk k at r * 128 + ((k ^ r % 8) * 16),
+// so the 32 lanes' vector stores hit every bank once per 8 lanes).
+__device__ __forceinline__ void stage_row32(uint8_t* box, int lane, const float* v) {
+    const uint32_t base = smem_u32(box) + lane * 128;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint4 q = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                   __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+        st_shared_v4(base + ((k ^ (lane & 7)) << 4), q);
     }
-    const int rows = min(32, a.m - (m0 + q * 32));
-#pragma unroll
-    for (int c = 0; c < NV / 32; ++c) {
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            tile[lane * 33 + j] = v[c * 32 + j];
-            if (kGated) gtile[lane * 33 + j] = gv[c * 32 + j];
-        }
-        __syncwarp();
-        const int col = col0 + c * 32 + lane;
-        if (col < a.n) {
-#pragma unroll 4
-            for (int r = 0; r < rows; ++r) {
-                const RowInfo ri = info[r];
-                float* out = a.y + ri.base + col * a.ynb[0];
-                float val = tile[r * 33 + lane];
-                if (kGated) {
-                    const float xv = apply_chain(a.chain, val, col, ri.i1, ri.i2, ri.i3);
-                    const float g = apply_chain(a.chain, gtile[r * 33 + lane], a.n + col, ri.i1, ri.i2, ri.i3);
-                    *out = xv * gelu(g);
-                } else {
-                    if (a.chain.from_redirect) val = *out + val;
-                    *out = apply_chain(a.chain, val, col, ri.i1, ri.i2, ri.i3);
-                }
-            }
-        }
-    }
-}
-
-// A convolution's output is [OW, OH, OC, N]: a lane's row is an output
-// position and neighbouring lanes are neighbouring positions, so each column
-// (channel) is written by the warp as one run.
-template <int NV>
-__device__ __forceinline__ void store_conv(const GemmArgs& a, const ConvPos& p, int col0, const float (&v)[NV]) {
-    if (!p.ok) return;
-    const long long base = p.ox * a.ynb[0] + static_cast<long long>(p.oy) * a.ynb[1] + p.img * a.ynb[3];
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int col = col0 + j;
-        if (col < a.n) {
-            float* out = a.y + base + col * a.ynb[2];
-            float val = v[j];
-            if (a.chain.from_redirect) val = *out + val;
-            *out = apply_chain(a.chain, val, p.ox, p.oy, col, p.img);
-        }
-    }
-}
-
-// Split-K: the CTA's raw sums into its slice of the workspace, [row][col]
-// with row = tile * 128 + lane row.
-template <int NV>
-__device__ __forceinline__ void store_partial(const GemmArgs& a, int split, int row, int col0, const float (&v)[NV]) {
-    float* dst = a.part + split * a.part_split + static_cast<long long>(row) * a.part_ld + col0;
-#pragma unroll
-    for (int j = 0; j < NV; j += 4)
-        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
 }
 
 // ---------------------------------------------------------------- kernel
+//
+// Persistent: each CTA takes work items blockIdx.x, blockIdx.x + gridDim.x, ...
+// (item = (row tile fastest, column tile, K part)).  The TMA warp streams the
+// items' k-blocks through one ring of stages; the MMA warp fills the two hi
+// buffers and the lo accumulator item after item; the epilogue warps read the
+// lo accumulator at an item's end and release it at once, so the next item's
+// products run while they apply the chain and store.
 
 template <int MODE, int WMODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
-                  const GemmArgs args) {
+                  const __grid_constant__ CUtensorMap ymap, const GemmArgs args) {
     using S = GemmShape<WMODE>;
     constexpr int BN = S::BN;
     constexpr bool kGated = WMODE == kWeightGated;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+    uint8_t* staging = smem + S::kStages * S::kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + S::kStagingBytes);
     uint64_t* empty = full + S::kStages;
     uint64_t* hi_full = empty + S::kStages;   // [2]
     uint64_t* hi_empty = hi_full + 2;         // [2]
     uint64_t* lo_full = hi_empty + 2;
-    uint64_t* drain = lo_full + 1;
+    uint64_t* lo_empty = lo_full + 1;
+    uint64_t* drain = lo_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int tile = blockIdx.x;
-    const int n0 = blockIdx.y * BN;
-    const int split = blockIdx.z;
-    const int per_split = (args.kblocks + args.ksplit - 1) / args.ksplit;
-    const int kb0 = split * per_split;
-    const int kb1 = min(args.kblocks, kb0 + per_split);
-    const int kblocks = max(0, kb1 - kb0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::kStages; ++s) {
@@ -249,11 +191,13 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
             mbar_init(&hi_empty[b], 8);  // the eight epilogue warps
         }
         mbar_init(lo_full, 1);
+        mbar_init(lo_empty, 8);
         mbar_init(drain, 1);
         *abort = 0;
         fence_barrier_init();
         tma_prefetch_desc(&amap);
         tma_prefetch_desc(&wmap);
+        if (MODE == kModeLinear && args.store == kStoreTma) tma_prefetch_desc(&ymap);
     }
     if (warp == 1) tmem_alloc(tmem_slot, S::kTmemCols);
     tc_fence_before();
@@ -261,49 +205,62 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    auto stage_a_hi = [&](int s) { return smem + s * S::kStageBytes; };
-    auto stage_a_lo = [&](int s) { return smem + s * S::kStageBytes + S::kABytes; };
+    auto stage_a = [&](int s) { return smem + s * S::kStageBytes; };            // hi, then lo at + kABytes
     auto stage_b0 = [&](int s) { return smem + s * S::kStageBytes + 2 * S::kABytes; };
     auto stage_b1 = [&](int s) { return smem + s * S::kStageBytes + 2 * S::kABytes + S::kBBytes; };
+    // The k-block range of an item.
+    auto item_range = [&](int item, int& tm, int& tn, int& split, int& kb0, int& kb1) {
+        tm = item % args.tiles_m;
+        const int rest = item / args.tiles_m;
+        tn = rest % args.tiles_n;
+        split = rest / args.tiles_n;
+        kb0 = split * args.per_split;
+        kb1 = min(args.kblocks, kb0 + args.per_split);
+    };
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            // This tile's A coordinates.
-            int ax = 0, ay = 0, az = 0;
             const ConvGeom& g = args.cg;
-            if (MODE == kModeConv) {
-                const int tx = tile % g.tw, ty = (tile / g.tw) % g.th, tz = tile / (g.tw * g.th);
-                ax = tx * g.owt * g.s0 - g.p0;
-                ay = ty * g.oht * g.s1 - g.p1;
-                az = tz * g.nt;
-            }
-            int issued = 0;
             const uint32_t tx_bytes = 2 * args.a_tx + S::kBBytes * (S::kHasB1 ? 2 : 1);
-            for (int i = 0; i < kblocks; ++i) {
-                const int kb = kb0 + i;
-                const int s = i % S::kStages;
-                const uint32_t parity = ((i / S::kStages) & 1) ^ 1;
-                if (!mbar_wait(&empty[s], parity, abort, args.err)) break;
-                mbar_arrive_expect_tx(&full[s], tx_bytes);
-                if (MODE == kModeLinear) {
-                    tma_load_2d(stage_a_hi(s), &amap, &full[s], kb * kBK, tile * kBM);
-                    tma_load_2d(stage_a_lo(s), &amap, &full[s], kb * kBK, args.a_lo_row + tile * kBM);
-                } else {
-                    const int tap = kb / g.cblocks;
-                    const int cx0 = (kb - tap * g.cblocks) * kBK;
-                    const int ky = tap / g.kw, kx = tap - ky * g.kw;
-                    const int x = ax + kx * g.d0, y = ay + ky * g.d1;
-                    tma_load_4d(stage_a_hi(s), &amap, &full[s], cx0, x, y, az);
-                    tma_load_4d(stage_a_lo(s), &amap, &full[s], cx0, x, y, args.a_lo_row + az);
+            int it = 0;  // k-blocks issued
+            bool ok = true;
+            for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x) {
+                int tm, tn, split, kb0, kb1;
+                item_range(item, tm, tn, split, kb0, kb1);
+                int ax = 0, ay = 0, az = 0;
+                if (MODE == kModeConv) {
+                    const int tx = tm % g.tw, ty = (tm / g.tw) % g.th, tz = tm / (g.tw * g.th);
+                    ax = tx * g.owt * g.s0 - g.p0;
+                    ay = ty * g.oht * g.s1 - g.p1;
+                    az = tz * g.nt;
                 }
-                tma_load_2d(stage_b0(s), &wmap, &full[s], kb * kBK, n0);
-                if (S::kHasB1) tma_load_2d(stage_b1(s), &wmap, &full[s], kb * kBK, args.b1_row + n0);
-                ++issued;
+                const int n0 = tn * BN;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S::kStages;
+                    if (!mbar_wait(&empty[s], ((it / S::kStages) & 1) ^ 1, abort, args.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], tx_bytes);
+                    if (MODE == kModeLinear) {
+                        tma_load_3d(stage_a(s), &amap, &full[s], kb * kBK, tm * kBM, 0);
+                    } else {
+                        const int tap = kb / g.cblocks;
+                        const int cx0 = (kb - tap * g.cblocks) * kBK;
+                        const int ky = tap / g.kw, kx = tap - ky * g.kw;
+                        const int x = ax + kx * g.d0, y = ay + ky * g.d1;
+                        if (args.a_planes == 2) {
+                            tma_load_5d(stage_a(s), &amap, &full[s], cx0, x, y, az, 0);
+                        } else {
+                            tma_load_5d(stage_a(s), &amap, &full[s], cx0, x, y, az, 0);
+                            tma_load_5d(stage_a(s) + S::kABytes, &amap, &full[s], cx0, x, y, az, 1);
+                        }
+                    }
+                    tma_load_2d(stage_b0(s), &wmap, &full[s], kb * kBK, n0);
+                    if (S::kHasB1) tma_load_2d(stage_b1(s), &wmap, &full[s], kb * kBK, args.b1_row + n0);
+                }
             }
             if (*abort) {
                 // Let the loads this thread started land before the CTA exits.
-                for (int i = (issued > S::kStages ? issued - S::kStages : 0); i < issued; ++i)
+                for (int i = (it > S::kStages ? it - S::kStages : 0); i < it; ++i)
                     mbar_wait_quiet(&full[i % S::kStages], (i / S::kStages) & 1, 100000000ull);
             }
         }
@@ -312,81 +269,93 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
             bool ok = true;
-            for (int i = 0; i < kblocks && ok; ++i) {
-                const int s = i % S::kStages;
-                const int b = i & 1;
-                if (!mbar_wait(&full[s], (i / S::kStages) & 1, abort, args.err)) { ok = false; break; }
-                if (!mbar_wait(&hi_empty[b], ((i >> 1) & 1) ^ 1, abort, args.err)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t ahi = smem_u32(stage_a_hi(s)), alo = smem_u32(stage_a_lo(s));
-                const uint32_t b0 = smem_u32(stage_b0(s)), b1 = smem_u32(stage_b1(s));
-                const uint32_t d_hi = tmem + b * BN;
+            int it = 0, t = 0;  // k-blocks consumed, items done
+            for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x, ++t) {
+                int tm, tn, split, kb0, kb1;
+                item_range(item, tm, tn, split, kb0, kb1);
+                // The previous item's lo accumulator has been read.
+                if (!mbar_wait(lo_empty, (t & 1) ^ 1, abort, args.err)) { ok = false; break; }
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S::kStages;
+                    const int b = it & 1;
+                    if (!mbar_wait(&full[s], (it / S::kStages) & 1, abort, args.err)) { ok = false; break; }
+                    if (!mbar_wait(&hi_empty[b], ((it >> 1) & 1) ^ 1, abort, args.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t ahi = smem_u32(stage_a(s)), alo = ahi + S::kABytes;
+                    const uint32_t b0 = smem_u32(stage_b0(s)), b1 = smem_u32(stage_b1(s));
+                    const uint32_t d_hi = tmem + b * BN;
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint32_t fresh = kk > 0 ? 1u : 0u;
-                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    const uint64_t dah = desc_kmajor_sw128(ahi + kk * 32), dal = desc_kmajor_sw128(alo + kk * 32);
-                    const uint64_t db0 = desc_kmajor_sw128(b0 + kk * 32);
-                    mma_f16(d_hi, dah, db0, idesc, fresh);
-                    mma_f16(tmem + S::kLoCol, dal, db0, idesc, acc);
-                    if (WMODE == kWeightSplit) {
-                        mma_f16(tmem + S::kLoCol, dah, desc_kmajor_sw128(b1 + kk * 32), idesc, 1u);
-                    } else if (kGated) {
-                        const uint64_t db1 = desc_kmajor_sw128(b1 + kk * 32);
-                        mma_f16(tmem + 2 * BN + b * BN, dah, db1, idesc, fresh);
-                        mma_f16(tmem + S::kLoCol + BN, dal, db1, idesc, acc);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t fresh = kk > 0 ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
+                        const uint64_t dah = desc_kmajor_sw128(ahi + kk * 32), dal = desc_kmajor_sw128(alo + kk * 32);
+                        const uint64_t db0 = desc_kmajor_sw128(b0 + kk * 32);
+                        mma_f16(d_hi, dah, db0, idesc, fresh);
+                        mma_f16(tmem + S::kLoCol, dal, db0, idesc, acc);
+                        if (WMODE == kWeightSplit) {
+                            mma_f16(tmem + S::kLoCol, dah, desc_kmajor_sw128(b1 + kk * 32), idesc, 1u);
+                        } else if (kGated) {
+                            const uint64_t db1 = desc_kmajor_sw128(b1 + kk * 32);
+                            mma_f16(tmem + 2 * BN + b * BN, dah, db1, idesc, fresh);
+                            mma_f16(tmem + S::kLoCol + BN, dal, db1, idesc, acc);
+                        }
                     }
+                    mma_commit(&empty[s]);
+                    mma_commit(&hi_full[b]);
                 }
-                mma_commit(&empty[s]);
-                mma_commit(&hi_full[b]);
+                if (ok) mma_commit(lo_full);
             }
-            if (ok) {
-                mma_commit(lo_full);
-            } else {
+            if (!ok) {
                 // Wind down: every MMA issued completes before tensor memory is freed.
                 mma_commit(drain);
                 mbar_wait_quiet(drain, 0, 100000000ull);
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (drains hi per k-block)
+        // ------------------------------------------------ epilogue
         const int ew = warp - kEpiWarp0;      // 0..7
         const int q = warp & 3;               // TMEM lane quarter this warp may read
         const int half = ew >> 2;             // which half of the tile's columns
         constexpr int NV = BN / 2;            // columns per warp
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-        float sum[NV], gsum[NV];
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-            sum[j] = 0.0f;
-            gsum[j] = 0.0f;
-        }
+        uint8_t* box = staging + ew * (32 * 128);
         bool ok = true;
-        for (int i = 0; i < kblocks; ++i) {
-            const int b = i & 1;
-            if (!mbar_wait(&hi_full[b], (i >> 1) & 1, abort, args.err)) { ok = false; break; }
-            tc_fence_after();
+        int it = 0, t = 0;
+        for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x, ++t) {
+            int tm, tn, split, kb0, kb1;
+            item_range(item, tm, tn, split, kb0, kb1);
+            float sum[NV], gsum[NV];
 #pragma unroll
-            for (int c = 0; c < NV; c += 32) {
-                float part[32];
-                tmem_ld32(lane_addr + b * BN + half * NV + c, part);
-                if (kGated) {
-                    float gpart[32];
-                    tmem_ld32(lane_addr + 2 * BN + b * BN + half * NV + c, gpart);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) gsum[c + j] += gpart[j];
-                } else {
-                    tmem_ld_wait();
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) sum[c + j] += part[j];
+            for (int j = 0; j < NV; ++j) {
+                sum[j] = 0.0f;
+                gsum[j] = 0.0f;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&hi_empty[b]);
-        }
-        if (ok && kblocks > 0 && mbar_wait(lo_full, 0, abort, args.err)) {
+            // Drain the hi product k-block by k-block.
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                const int b = it & 1;
+                if (!mbar_wait(&hi_full[b], (it >> 1) & 1, abort, args.err)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < NV; c += 32) {
+                    float part[32];
+                    tmem_ld32(lane_addr + b * BN + half * NV + c, part);
+                    if (kGated) {
+                        float gpart[32];
+                        tmem_ld32(lane_addr + 2 * BN + b * BN + half * NV + c, gpart);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) gsum[c + j] += gpart[j];
+                    } else {
+                        tmem_ld_wait();
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[c + j] += part[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&hi_empty[b]);
+            }
+            if (!ok || !mbar_wait(lo_full, t & 1, abort, args.err)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < NV; c += 32) {
@@ -404,21 +373,102 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sum[c + j] = fmaf(lo[j], kLoUnscale, sum[c + j]);
             }
-            const int col0 = n0 + half * NV;
-            const int row = q * 32 + lane;
+            // Tensor memory is free for the next item.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(lo_empty);
+
+            const int row = q * 32 + lane;                  // row of the tile this thread owns
+            const int col0 = tn * BN + half * NV;
             if (args.ksplit > 1) {
-                store_partial<NV>(args, split, tile * kBM + row, col0, sum);
-            } else if (MODE == kModeLinear) {
-                store_linear<WMODE, NV>(args, smem, ew, q, lane, tile * kBM, col0, sum, gsum);
-            } else {
-                store_conv<NV>(args, conv_pos(args.cg, tile, row), col0, sum);
-            }
-        } else if (ok && kblocks == 0 && args.ksplit > 1) {
-            float zero[NV];
+                // Raw sums into the workspace: rows (split, tile row), TMA-stored.
 #pragma unroll
-            for (int j = 0; j < NV; ++j) zero[j] = 0.0f;
-            store_partial<NV>(args, split, tile * kBM + q * 32 + lane, n0 + half * NV, zero);
+                for (int c = 0; c < NV; c += 32) {
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                    stage_row32(box, lane, sum + c);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&ymap, box, col0 + c, (split * args.tiles_m + tm) * kBM + q * 32);
+                        bulk_commit_group();
+                    }
+                }
+            } else if (MODE == kModeLinear) {
+                const long long m = static_cast<long long>(tm) * kBM + row;
+                const bool live = m < args.m;
+                // Rows past the end take the last row's operand offsets (their results are not stored).
+                const long long mc = live ? m : args.m - 1;
+                const long long i1 = mc % args.rne1, rest = mc / args.rne1;
+                const long long i2 = rest % args.rne2, i3 = rest / args.rne2;
+                ChainRow cr;
+                row_offsets(args.chain, cr, 0, i1, i2, i3);
+                float* yrow = args.y + i1 * args.ynb[1] + i2 * args.ynb[2] + i3 * args.ynb[3];
+#pragma unroll
+                for (int c = 0; c < NV; c += 32) {
+                    float* v = sum + c;   // the chain's results replace the sums
+                    const long long cb = col0 + c;
+                    if (kGated) {
+                        apply_chain_cols<0, 32>(args.chain, cr, v, cb, args.n - 1);
+                        apply_chain_cols<0, 32>(args.chain, cr, gsum + c, args.n + cb, 2LL * args.n - 1);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] *= gelu(gsum[c + j]);
+                    } else {
+                        if (args.chain.from_redirect) {
+                            float old[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) old[j] = yrow[min(cb + j, args.n - 1LL) * args.ynb[0]];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = old[j] + v[j];
+                        }
+                        apply_chain_cols<0, 32>(args.chain, cr, v, cb, args.n - 1);
+                    }
+                    if (args.store == kStoreTma) {
+                        if (lane == 0) bulk_wait_read_all();
+                        __syncwarp();
+                        stage_row32(box, lane, v);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&ymap, box, static_cast<int>(cb), tm * kBM + q * 32);
+                            bulk_commit_group();
+                        }
+                    } else if (live) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (cb + j < args.n) yrow[(cb + j) * args.ynb[0]] = v[j];
+                    }
+                }
+            } else {
+                // Convolution: a lane's row is an output position; the warp's 32
+                // positions are neighbours, so each channel is written as one run.
+                const ConvPos p = conv_pos(args.cg, tm, row);
+                const int ox = p.ok ? p.ox : 0, oy = p.ok ? p.oy : 0, img = p.ok ? p.img : 0;
+                ChainRow cr;
+                row_offsets(args.chain, cr, 2, ox, oy, img);
+                float* ybase = args.y + ox * args.ynb[0] + static_cast<long long>(oy) * args.ynb[1] + img * args.ynb[3];
+#pragma unroll
+                for (int c = 0; c < NV; c += 32) {
+                    float* v = sum + c;
+                    const long long cb = col0 + c;
+                    if (args.chain.from_redirect) {
+                        float old[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) old[j] = ybase[min(cb + j, args.n - 1LL) * args.ynb[2]];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = old[j] + v[j];
+                    }
+                    apply_chain_cols<2, 32>(args.chain, cr, v, cb, args.n - 1);
+                    if (p.ok) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (cb + j < args.n) ybase[(cb + j) * args.ynb[2]] = v[j];
+                    }
+                }
+            }
         }
+        // Bulk stores read their staging before the CTA's shared memory goes away.
+        if (lane == 0) bulk_wait_all();
     }
 
     // Single-lane roles rejoin their warps before the CTA-wide barrier.

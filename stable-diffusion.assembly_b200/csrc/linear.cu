@@ -20,21 +20,39 @@ namespace {
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
+// The partial sums' map: [ksplit * tiles_m * 128 rows][part_ld] FP32, stored in 32 x 32 boxes.
+int partial_map(const GemmArgs& a, CUtensorMap* map) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(a.part_ld),
+                              static_cast<uint64_t>(a.ksplit) * static_cast<uint64_t>(a.tiles_m) * kBM};
+    const uint64_t strides[1] = {static_cast<uint64_t>(a.part_ld) * 4};
+    const uint32_t box[2] = {32, 32};
+    if (encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.part, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the partial sums");
+    return SDB_OK;
+}
+
 template <int MODE, int WMODE>
-int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const GemmArgs& a, int tiles, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const CUtensorMap& ymap, GemmArgs a,
+                cudaStream_t st) {
     using S = GemmShape<WMODE>;
     auto kern = gemm_split_kernel<MODE, WMODE>;
     SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
-    const int ntiles = (a.n + S::BN - 1) / S::BN;
-    if (ntiles > 65535 || a.ksplit > 65535) return fail(SDB_NOT_SUPPORTED, "gemm: too many tiles");
-    const dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(ntiles), static_cast<unsigned>(a.ksplit));
-    kern<<<grid, kGemmThreads, S::kSmemBytes, st>>>(amap, wmap, a);
+    a.tiles_n = (a.n + S::BN - 1) / S::BN;
+    const long long items = static_cast<long long>(a.tiles_m) * a.tiles_n * a.ksplit;
+    if (items >= (1LL << 31)) return fail(SDB_NOT_SUPPORTED, "gemm: too many tiles");
+    a.items = static_cast<int>(items);
+    const int grid = static_cast<int>(std::min<long long>(items, current_sm_count()));
+    CUtensorMap pmap;
+    if (a.ksplit > 1)
+        if (int s = partial_map(a, &pmap); s != SDB_OK) return s;
+    kern<<<grid, kGemmThreads, S::kSmemBytes, st>>>(amap, wmap, a.ksplit > 1 ? pmap : ymap, a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     if (a.ksplit > 1) {
-        const long long total = static_cast<long long>(tiles) * kBM * a.n;
+        const long long total = static_cast<long long>(a.tiles_m) * kBM * a.n;
         const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, tiles);
+        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
         count_launch();
         SDB_CUDA(cudaGetLastError());
     }
@@ -42,20 +60,24 @@ int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const GemmArgs
 }
 
 template <int MODE>
-int dispatch(const CUtensorMap& amap, const Packed& p, int wmode, const GemmArgs& a, int tiles, cudaStream_t st) {
-    if (wmode == kWeightGated) return launch_gemm<MODE, kWeightGated>(amap, p.map64, a, tiles, st);
-    return wmode == kWeightSplit ? launch_gemm<MODE, kWeightSplit>(amap, p.map128, a, tiles, st)
-                                 : launch_gemm<MODE, kWeightHalf>(amap, p.map128, a, tiles, st);
+int dispatch(const CUtensorMap& amap, const Packed& p, int wmode, const CUtensorMap& ymap, const GemmArgs& a,
+             cudaStream_t st) {
+    if (wmode == kWeightGated) return launch_gemm<MODE, kWeightGated>(amap, p.map64, ymap, a, st);
+    return wmode == kWeightSplit ? launch_gemm<MODE, kWeightSplit>(amap, p.map128, ymap, a, st)
+                                 : launch_gemm<MODE, kWeightHalf>(amap, p.map128, ymap, a, st);
 }
 
-// K is split over CTAs when the output tiles leave most SMs idle: enough
-// splits to fill the GPU once, at least 8 k-blocks each.
-int choose_ksplit(int tiles, int kblocks, int wmode) {
-    if (wmode == kWeightGated) return 1;
+// K is split when the output tiles leave most SMs idle: enough parts to fill
+// the GPU once, at least 8 k-blocks each, none empty.
+void choose_ksplit(GemmArgs& a, int tiles, int wmode) {
+    a.ksplit = 1;
+    a.per_split = a.kblocks;
+    if (wmode == kWeightGated) return;
     const int sms = current_sm_count();
-    if (tiles >= sms / 2 || kblocks < 16) return 1;
-    const int want = (sms + tiles - 1) / tiles;
-    return std::max(1, std::min(want, kblocks / 8));
+    if (tiles >= sms / 2 || a.kblocks < 16) return;
+    const int want = std::max(1, std::min((sms + tiles - 1) / tiles, a.kblocks / 8));
+    a.per_split = (a.kblocks + want - 1) / want;
+    a.ksplit = (a.kblocks + a.per_split - 1) / a.per_split;
 }
 
 // Bytes of split-K partial sums: [ksplit][tiles * 128][npad].
@@ -134,15 +156,16 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
 
     GemmArgs a{};
     a.m = static_cast<int>(m);
-    a.a_lo_row = static_cast<int>(m);
     a.kblocks = static_cast<int>(p->kpad / kBK);
     a.n = static_cast<int>(n);
     a.b1_row = static_cast<int>(p->b1_row);
     a.a_tx = kBM * kBK * 2;
+    a.a_planes = 2;
+    a.tiles_m = tiles;
     a.rne1 = dst->ne[1];
     a.rne2 = dst->ne[2];
     set_out(a, dst, chain);
-    a.ksplit = choose_ksplit(tiles * static_cast<int>((n + bn - 1) / bn), a.kblocks, wmode);
+    choose_ksplit(a, tiles * static_cast<int>((n + bn - 1) / bn), wmode);
 
     // Workspace: the split rows [0, M) hi, [M, 2M) lo of kp8 FP16, then any partial sums.
     const int64_t kp8 = round_up(k, 8);
@@ -155,14 +178,26 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err, st);
         s != SDB_OK)
         return s;
+    // A as [plane][row][k]: one box {64, 128, 2} brings a tile's hi and lo rows.
     CUtensorMap amap;
-    const uint64_t dims[2] = {static_cast<uint64_t>(kp8), static_cast<uint64_t>(2 * m)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(kp8) * 2};
-    const uint32_t box[2] = {64, 128};
-    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws, dims, strides, box,
+    const uint64_t dims[3] = {static_cast<uint64_t>(kp8), static_cast<uint64_t>(m), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(kp8) * 2, static_cast<uint64_t>(m * kp8) * 2};
+    const uint32_t box[3] = {64, 128, 2};
+    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ws, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
         return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the activations");
-    return dispatch<kModeLinear>(amap, *p, wmode, a, tiles, st);
+    // The output by TMA stores when its rows are 16-byte aligned runs.
+    CUtensorMap ymap{};
+    a.store = kStoreDirect;
+    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ynb[0] == 1 && a.ynb[1] == n) {
+        const uint64_t ydims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(m)};
+        const uint64_t ystrides[1] = {static_cast<uint64_t>(n) * 4};
+        const uint32_t ybox[2] = {32, 32};
+        if (encode_tensor_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydims, ystrides, ybox,
+                              CU_TENSOR_MAP_SWIZZLE_128B) == CUDA_SUCCESS)
+            a.store = kStoreTma;
+    }
+    return dispatch<kModeLinear>(amap, *p, wmode, ymap, a, st);
 }
 
 // The output positions of a conv tile: OWt x OHt x NT <= 128 with the box's
@@ -264,14 +299,16 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     a.n = static_cast<int>(oc);
     a.b1_row = static_cast<int>(p->b1_row);
     a.a_tx = static_cast<uint32_t>(64 * 2 * g.owt * g.oht * g.nt);
+    a.a_planes = g.owt * g.oht * g.nt == kBM ? 2 : 1;
+    a.tiles_m = tiles;
+    a.store = kStoreDirect;
     set_out(a, dst, chain);
-    a.ksplit = choose_ksplit(tiles * static_cast<int>((oc + 127) / 128), a.kblocks, wmode);
+    choose_ksplit(a, tiles * static_cast<int>((oc + 127) / 128), wmode);
 
     // Workspace: the image split and channels-last, [2N][H][W][cp8] (hi images,
     // then lo), then any partial sums.
     const int64_t cp8 = round_up(ic, 8);
     const int64_t W = x->ne[0], H = x->ne[1], N = x->ne[3];
-    a.a_lo_row = static_cast<int>(N);
     const size_t a_bytes = static_cast<size_t>(round_up(2 * N * H * W * cp8 * 2, 256));
     void* ws = nullptr;
     if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, oc, 128), &ws); s != SDB_OK) return s;
@@ -281,18 +318,20 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (int s = split_nhwc(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
         s != SDB_OK)
         return s;
+    // The split image as [plane][N][H][W][cp8]: a box {64 channels, OWt s0, OHt s1, NT, planes}.
     CUtensorMap amap;
-    const uint64_t dims[4] = {static_cast<uint64_t>(cp8), static_cast<uint64_t>(W), static_cast<uint64_t>(H),
-                              static_cast<uint64_t>(2 * N)};
-    const uint64_t strides[3] = {static_cast<uint64_t>(cp8 * 2), static_cast<uint64_t>(W * cp8 * 2),
-                                 static_cast<uint64_t>(H * W * cp8 * 2)};
-    const uint32_t box[4] = {64, static_cast<uint32_t>(g.owt * g.s0), static_cast<uint32_t>(g.oht * g.s1),
-                             static_cast<uint32_t>(g.nt)};
-    const uint32_t estr[4] = {1, static_cast<uint32_t>(g.s0), static_cast<uint32_t>(g.s1), 1};
-    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, ws, dims, strides, box,
+    const uint64_t dims[5] = {static_cast<uint64_t>(cp8), static_cast<uint64_t>(W), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(N), 2};
+    const uint64_t strides[4] = {static_cast<uint64_t>(cp8 * 2), static_cast<uint64_t>(W * cp8 * 2),
+                                 static_cast<uint64_t>(H * W * cp8 * 2), static_cast<uint64_t>(N * H * W * cp8 * 2)};
+    const uint32_t box[5] = {64, static_cast<uint32_t>(g.owt * g.s0), static_cast<uint32_t>(g.oht * g.s1),
+                             static_cast<uint32_t>(g.nt), static_cast<uint32_t>(a.a_planes)};
+    const uint32_t estr[5] = {1, static_cast<uint32_t>(g.s0), static_cast<uint32_t>(g.s1), 1, 1};
+    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, ws, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B, estr) != CUDA_SUCCESS)
         return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the image");
-    return dispatch<kModeConv>(amap, *p, wmode, a, tiles, st);
+    const CUtensorMap none{};
+    return dispatch<kModeConv>(amap, *p, wmode, none, a, st);
 }
 
 }  // extern "C"

@@ -59,8 +59,108 @@ struct GroupArgs {
     float eps;
     int split;                  // CTAs per (image, group)
     double* partial;            // [items][split][2]
+    int uniform;                // every chain operand is constant over (i0, i1): one value per channel
     Chain chain;
 };
+
+// The chain's operand values for channel c of image i3 (uniform chains).
+__device__ __forceinline__ void channel_operands(const Chain& ch, long long c, long long i3, float (&op)[SDB_MAX_STEPS]) {
+#pragma unroll
+    for (int s = 0; s < SDB_MAX_STEPS; ++s)
+        op[s] = (s < ch.count && ch.kind[s] != SDB_STEP_SILU) ? __ldg(ch.operand[s] + c * ch.nb[s][2] + i3 * ch.nb[s][3])
+                                                              : 0.0f;
+}
+
+__device__ __forceinline__ float apply_uniform(const Chain& ch, const float (&op)[SDB_MAX_STEPS], float v) {
+#pragma unroll
+    for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+        if (s >= ch.count) break;
+        v = ch.kind[s] == SDB_STEP_SILU ? silu(v) : ch.kind[s] == SDB_STEP_ADD ? v + op[s] : v * op[s];
+    }
+    return v;
+}
+
+// Normalises elements [e0, e1) of a group (channels c0.. contiguous, element
+// e of the group in channel c0 + e / plane) from src into the output, with
+// the chain.  A thread takes four elements (or four float4s) at a time and
+// issues their operand loads before any of their stores, so the loads'
+// latency is paid once per batch rather than once per element.
+template <bool kSmem>
+__device__ __forceinline__ void apply_range(const GroupArgs& a, const float* src, long long c0, long long i3,
+                                            float mean, float scale, long long e0, long long e1) {
+    const int ne0 = static_cast<int>(a.ne0);
+    const int plane = static_cast<int>(a.ne0 * a.ne1);
+    float* ybase = a.y + i3 * a.ynb[3];
+    const bool flat = a.ynb[0] == 1 && a.ynb[1] == a.ne0 && a.ynb[2] == a.ne0 * a.ne1;
+    if (a.uniform && flat && (plane & 3) == 0 && ((e0 | e1) & 3) == 0 &&
+        ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(ybase + c0 * a.ynb[2])) & 15) == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(ybase + c0 * a.ynb[2]);
+        const int plane4 = plane / 4;
+        const int b4 = static_cast<int>(e0 / 4), n4 = static_cast<int>(e1 / 4);
+        for (int base = b4 + threadIdx.x; base < n4; base += 4 * blockDim.x) {
+            float4 v[4];
+            float op[4][SDB_MAX_STEPS];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int e = min(base + k * static_cast<int>(blockDim.x), n4 - 1);
+                v[k] = kSmem ? s4[e] : __ldg(s4 + e);
+                channel_operands(a.chain, c0 + e / plane4, i3, op[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[k].x = apply_uniform(a.chain, op[k], (v[k].x - mean) * scale);
+                v[k].y = apply_uniform(a.chain, op[k], (v[k].y - mean) * scale);
+                v[k].z = apply_uniform(a.chain, op[k], (v[k].z - mean) * scale);
+                v[k].w = apply_uniform(a.chain, op[k], (v[k].w - mean) * scale);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int e = base + k * static_cast<int>(blockDim.x);
+                if (e < n4) d4[e] = v[k];
+            }
+        }
+        return;
+    }
+    // General layouts and chains: batches of four elements.
+    for (long long b = e0 + threadIdx.x; b < e1; b += 4 * blockDim.x) {
+        float v[4];
+        int i0[4], i1[4];
+        long long c[4];
+        bool live[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const long long e = b + k * static_cast<long long>(blockDim.x);
+            live[k] = e < e1;
+            const long long ec = live[k] ? e : e0;
+            const int cc = static_cast<int>(ec / plane);
+            const int pe = static_cast<int>(ec - static_cast<long long>(cc) * plane);
+            c[k] = c0 + cc;
+            i1[k] = pe / ne0;
+            i0[k] = pe - i1[k] * ne0;
+            v[k] = ((kSmem ? src[ec] : __ldg(src + ec)) - mean) * scale;
+        }
+#pragma unroll
+        for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+            if (s >= a.chain.count) break;
+            if (a.chain.kind[s] == SDB_STEP_SILU) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = silu(v[k]);
+            } else {
+                float o[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    o[k] = __ldg(a.chain.operand[s] + i0[k] * a.chain.nb[s][0] + i1[k] * a.chain.nb[s][1] +
+                                 c[k] * a.chain.nb[s][2] + i3 * a.chain.nb[s][3]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = a.chain.kind[s] == SDB_STEP_ADD ? v[k] + o[k] : v[k] * o[k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (live[k]) ybase[i0[k] * a.ynb[0] + i1[k] * a.ynb[1] + c[k] * a.ynb[2]] = v[k];
+    }
+}
 
 // Element e of the group's contiguous run (channels c0.. are contiguous: the
 // tensor is contiguous, as group_norm_supported requires).
@@ -81,7 +181,7 @@ __global__ void __launch_bounds__(kNormThreads) group_sum_kernel(const GroupArgs
     if (c0 >= c1) return;
     const long long count = a.ne0 * a.ne1 * (c1 - c0);
     const float* base = a.x + i3 * a.xnb[3] + c0 * a.xnb[2];
-    const long long per = (count + a.split - 1) / a.split;
+    const long long per = (count + 4 * a.split - 1) / (4 * a.split) * 4;
     const long long e0 = part * per, e1 = min(count, e0 + per);
     double s = 0.0;
     if (phase == 0) {
@@ -126,17 +226,9 @@ __global__ void __launch_bounds__(kNormThreads) group_apply_kernel(const GroupAr
     __syncthreads();
     const float mean = stats[0], scale = stats[1];
     const float* xb = a.x + i3 * a.xnb[3] + c0 * a.xnb[2];
-    const long long per = (count + a.split - 1) / a.split;
+    const long long per = (count + 4 * a.split - 1) / (4 * a.split) * 4;
     const long long e0 = part * per, e1 = min(count, e0 + per);
-    const long long plane = a.ne0 * a.ne1;
-    for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
-        const long long c = c0 + e / plane;
-        const long long r = (e % plane) / a.ne0;
-        const long long i0 = e % a.ne0;
-        float v = (__ldg(xb + e) - mean) * scale;
-        v = apply_chain(a.chain, v, i0, r, c, i3);
-        a.y[i0 * a.ynb[0] + r * a.ynb[1] + c * a.ynb[2] + i3 * a.ynb[3]] = v;
-    }
+    apply_range<false>(a, xb, c0, i3, mean, scale, e0, e1);
 }
 
 // The whole (image, group) in shared memory: read once from HBM, the two
@@ -189,20 +281,7 @@ __global__ void __launch_bounds__(kResidentThreads) group_resident_kernel(const 
     if (threadIdx.x == 0) stats[1] = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(count)) + a.eps);
     __syncthreads();
     const float scale = stats[1];
-    // Rows of ne0 (positions of an image row) a warp at a time: no division per element.
-    const int rows = static_cast<int>(a.ne1 * (c1 - c0));
-    const int ne0 = static_cast<int>(a.ne0), ne1 = static_cast<int>(a.ne1);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    for (int row = warp; row < rows; row += nwarps) {
-        const int c = static_cast<int>(c0) + row / ne1;
-        const int r = row - (row / ne1) * ne1;
-        const float* src = xs + static_cast<long long>(row) * ne0;
-        float* dst = a.y + static_cast<long long>(r) * a.ynb[1] + c * a.ynb[2] + i3 * a.ynb[3];
-        for (int i0 = lane; i0 < ne0; i0 += 32) {
-            const float v = apply_chain(a.chain, (src[i0] - mean) * scale, i0, r, c, i3);
-            dst[i0 * a.ynb[0]] = v;
-        }
-    }
+    apply_range<true>(a, xs, c0, i3, mean, scale, 0, count);
 }
 
 struct RowArgs {
@@ -238,9 +317,34 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(const RowArgs a) {
     q = warp_sum(q);
     const float var = static_cast<float>(q / static_cast<double>(a.ne0));
     const float scale = 1.0f / sqrtf(var + a.eps);
-    for (long long i = lane; i < a.ne0; i += 32) {
-        const float v = (__ldg(xr + i * a.xnb[0]) - mean) * scale;
-        yr[i * a.ynb[0]] = apply_chain(a.chain, v, i, i1, i2, i3);
+    // Four elements per lane at a time, each chain step's loads together.
+    ChainRow cr;
+    row_offsets(a.chain, cr, 0, i1, i2, i3);
+    for (long long i0 = lane; i0 < a.ne0; i0 += 128) {
+        float v[4];
+        long long col[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            col[k] = min(i0 + 32 * k, a.ne0 - 1);
+            v[k] = (__ldg(xr + col[k] * a.xnb[0]) - mean) * scale;
+        }
+#pragma unroll
+        for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+            if (s >= a.chain.count) break;
+            if (a.chain.kind[s] == SDB_STEP_SILU) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = silu(v[k]);
+            } else {
+                float o[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) o[k] = __ldg(a.chain.operand[s] + cr.off[s] + col[k] * a.chain.nb[s][0]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = a.chain.kind[s] == SDB_STEP_ADD ? v[k] + o[k] : v[k] * o[k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (i0 + 32 * k < a.ne0) yr[(i0 + 32 * k) * a.ynb[0]] = v[k];
     }
 }
 
@@ -304,6 +408,9 @@ extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_
     a.per_group = static_cast<int>((a.ne2 + groups - 1) / groups);
     a.eps = eps;
     a.chain = make_chain(chain);
+    a.uniform = 1;
+    for (int s = 0; s < a.chain.count; ++s)
+        if (a.chain.kind[s] != SDB_STEP_SILU && (a.chain.nb[s][0] != 0 || a.chain.nb[s][1] != 0)) a.uniform = 0;
     const long long items = static_cast<long long>(groups) * a.ne3;
     const long long group_elems = a.ne0 * a.ne1 * a.per_group;
     if (group_elems <= kResident && items <= 0x7fffffffLL) {
@@ -422,6 +529,9 @@ extern "C" int sdb_group_norm_no_alloc(const sdb_tensor* x, const sdb_tensor* ds
     a.per_group = static_cast<int>((a.ne2 + groups - 1) / groups);
     a.eps = eps;
     a.chain = make_chain(chain);
+    a.uniform = 1;
+    for (int s = 0; s < a.chain.count; ++s)
+        if (a.chain.kind[s] != SDB_STEP_SILU && (a.chain.nb[s][0] != 0 || a.chain.nb[s][1] != 0)) a.uniform = 0;
     const long long group_elems = a.ne0 * a.ne1 * a.per_group;
     // As sdb_group_norm's split path, but no more slices than the array holds.
     const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
