@@ -1,26 +1,29 @@
 #!/usr/bin/env python
 """Benchmark of the B200 kernels behind stable-diffusion.assembly's hook surface.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload unet|hot_ops]
 
 One process per GPU (torchrun for N > 1); every rank runs the same workload on
 its own GPU (replicas: weak scaling, no data-path collective), the step time
 is the max over ranks, and rank 0 prints one JSON line.
 
-The step (workload "sd15_hot_ops"): the hot-path operations of an SD 1.5
-UNet at 512 x 512 at the BASELINE configs 1-3, each at full size:
-  config 1   linear 4096 x 320 -> 1280 + bias (FP16 weights)
-  config 2   conv 3x3 + bias, then GroupNorm(32) + gamma + beta + SiLU, at
-             [1,320,64,64], [1,640,32,32], [1,1280,8,8]
-  config 3   attention 8 heads x 40, Lq 4096, Lk 4096 and 77, each + residual
-Inputs are synthetic (seeded normal), weights random-init; three rotating
-input sets (about 240 MB) keep every step's activations out of L2.
+Workload "sd15_unet_step" (default): one sampler step of SD
+1.5 at 512 x 512 -- the UNet forward on the classifier-free-guidance batch of 2
+(latent 64 x 64, context 2 x 77 x 768; ~860M random-init FP16 weights) and the
+fused guidance (scale 7) + Euler update -- captured once as a CUDA graph and
+replayed K times; ms_per_step is the UNet ms/step, value the whole job's UNet
+steps/s.  A second, eager pass with CUDA events around every library call
+gives the step's per-class times and the roofline of the dominant class.
+Weights (1.7 GB) and activations exceed L2 every step.
 
-The JSON line follows the driver contract: value = steps/s over all GPUs,
-roofline of the dominant kernel (CUDA events on its own stream), clocks
-sampled during the timed region, an end-to-end number through the public API
-with host buffers, the CPU baseline (the reference's single-precision forms
-restated in C, oracle/ref_forms.c, on the host cores).
+Workload "sd15_hot_ops" (--workload hot_ops): the BASELINE configs 1-3 op set.
+
+The JSON line follows the driver contract: roofline of the dominant kernel
+class, clocks sampled during the timed region, an end-to-end number through
+the public API with host buffers (the latent and context in, the latent out,
+every step), and the CPU baseline: the reference's single-precision forms
+restated in C (oracle/ref_forms.c) on the host cores, on a sample of the
+step's operations.
 """
 from __future__ import annotations
 
@@ -38,9 +41,14 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "stable-diffusion.assembly_b200"))
 
-WORKLOAD = "sd15_hot_ops"
-METRIC = "SD1.5 UNet hot-path op set (BASELINE configs 1-3) steps/s"
-UNIT = "steps/s"
+HOT_WORKLOAD = "sd15_hot_ops"
+HOT_METRIC = "SD1.5 UNet hot-path op set (BASELINE configs 1-3) steps/s"
+HOT_UNIT = "steps/s"
+UNET_WORKLOAD = "sd15_unet_step"
+UNET_METRIC = ("UNet ms/step (SD1.5 512x512, CFG batch 2, Euler): whole-job UNet steps/s; "
+               "ms_per_step is the UNet ms/step")
+UNET_UNIT = "UNet steps/s"
+SAMPLER_STEPS = 20
 
 
 # ---------------------------------------------------------------- peaks
@@ -49,8 +57,9 @@ def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 # ---------------------------------------------------------------- clocks
@@ -250,12 +259,189 @@ def cpu_baseline(budget_s: float = 20.0) -> dict:
         t = timed(lambda: ref_forms.attention(q, k, v, 8, 8, 40 ** -0.5, q_range=(0, qn))) * (4096 / qn)
         parts[f"attention_k{lk}"] = t
     total = sum(parts.values())
-    return {"value": 1.0 / total, "unit": UNIT, "cores": lib_threads, "kind": "port",
+    return {"value": 1.0 / total, "unit": HOT_UNIT, "cores": lib_threads, "kind": "port",
             "sample": "linear 512/4096 rows, convs 1/16 (1/8 at 1280) of output channels, attention 128 (Lk 4096) "
                       "and 1024 (Lk 77) of 4096 queries; GroupNorm whole; each timed once after a warm run, "
                       "scaled by the inverse fraction",
             "seconds_per_step": total, "parts_s": {k: round(v, 4) for k, v in parts.items()},
             "cpu": _cpu_model()}
+
+
+def unet_ops(batch: int = 2, h: int = 64, w: int = 64, ctx: int = 77) -> list[tuple]:
+    """The hot operations of one SD 1.5 UNet forward, in order, with their shapes -- the calls
+    stable-diffusion.assembly_b200/unet.py makes (LayerNorm and the glue nodes left out):
+      ("conv", N, IC, OC, H, W, K, stride)   ("linear", M, K, N)   ("geglu", M, K, 2 x out)
+      ("attn", B, heads, Lq, Lk, d)          ("gn", N, C, H, W)"""
+    import unet as U
+
+    c = U.SD15
+    mc, td = c.model_channels, c.model_channels * c.time_dim_mult
+    ops: list[tuple] = []
+    blocks: list[tuple] = []   # ("res", cin, cout, hh, ww) / ("tr", ch, hh, ww) / ("down"|"up"|"cat", ...)
+    chans, ch, hh, ww = [mc], mc, h, w
+    for lvl, mult in enumerate(c.channel_mult):
+        for _ in range(c.num_res_blocks):
+            blocks.append(("res", ch, mult * mc, hh, ww))
+            ch = mult * mc
+            if lvl in c.attention_levels:
+                blocks.append(("tr", ch, hh, ww))
+            chans.append(ch)
+        if lvl != len(c.channel_mult) - 1:
+            blocks.append(("down", ch, hh, ww))
+            hh, ww = (hh + 1) // 2, (ww + 1) // 2
+            chans.append(ch)
+    blocks += [("res", ch, ch, hh, ww), ("tr", ch, hh, ww), ("res", ch, ch, hh, ww)]
+    for lvl, mult in reversed(list(enumerate(c.channel_mult))):
+        for _ in range(c.num_res_blocks + 1):
+            skip = chans.pop()
+            blocks.append(("res", ch + skip, mult * mc, hh, ww))
+            ch = mult * mc
+            if lvl in c.attention_levels:
+                blocks.append(("tr", ch, hh, ww))
+        if lvl != 0:
+            blocks.append(("up", ch, hh, ww))
+            hh, ww = hh * 2, ww * 2
+    emb_total = sum(b[2] for b in blocks if b[0] == "res")
+    kv_total = sum(2 * b[1] for b in blocks if b[0] == "tr")
+    ops += [("linear", batch, mc, td), ("linear", batch, td, td), ("linear", batch, td, emb_total),
+            ("linear", batch * ctx, c.context_dim, kv_total), ("conv", batch, c.in_channels, mc, h, w, 3, 1)]
+    for b in blocks:
+        if b[0] == "res":
+            _, cin, cout, bh, bw = b
+            ops += [("gn", batch, cin, bh, bw), ("conv", batch, cin, cout, bh, bw, 3, 1), ("gn", batch, cout, bh, bw)]
+            if cin != cout:
+                ops.append(("conv", batch, cin, cout, bh, bw, 1, 1))
+            ops.append(("conv", batch, cout, cout, bh, bw, 3, 1))
+        elif b[0] == "tr":
+            _, cc, bh, bw = b
+            m = batch * bh * bw
+            ops += [("gn", batch, cc, bh, bw), ("linear", m, cc, cc), ("linear", m, cc, 3 * cc),
+                    ("attn", batch, c.heads, bh * bw, bh * bw, cc // c.heads), ("linear", m, cc, cc),
+                    ("linear", m, cc, cc), ("attn", batch, c.heads, bh * bw, ctx, cc // c.heads),
+                    ("linear", m, cc, cc), ("geglu", m, cc, 8 * cc), ("linear", m, 4 * cc, cc), ("linear", m, cc, cc)]
+        elif b[0] == "down":
+            _, cc, bh, bw = b
+            ops.append(("conv", batch, cc, cc, bh, bw, 3, 2))
+        elif b[0] == "up":
+            _, cc, bh, bw = b
+            ops.append(("conv", batch, cc, cc, 2 * bh, 2 * bw, 3, 1))
+    ops += [("gn", batch, mc, h, w), ("conv", batch, mc, c.out_channels, h, w, 3, 1)]
+    return ops
+
+
+def _reference_kernels():
+    """oracle/_ref/libsdasm_ref.so -- the reference's own x86-64 micro-kernels assembled from its sources
+    (oracle/ref_asm.py) with this project's threaded driver -- when it was built, else None."""
+    import ctypes
+
+    lib_path = ROOT / "oracle" / "_ref" / "libsdasm_ref.so"
+    if not lib_path.exists():
+        return None
+    try:
+        lib = ctypes.CDLL(str(lib_path))
+    except OSError:
+        return None
+    P, i = ctypes.c_void_p, ctypes.c_int
+    lib.refk_mul_mat_mt.argtypes = [P, i, i, P, i, P]
+    lib.refk_conv2d_mt.argtypes = [P, i, i, i, i, P, i, i, i, i, i, i, i, P]
+    lib.refk_attention_mt.argtypes = [P, P, P, P, i, i, i, i, i, i, ctypes.c_float, i]
+    return lib
+
+
+def cpu_unet_step(budget_fraction: int = 4) -> dict:
+    """The reference's CPU path on a sample of one UNet step, on all host threads.
+
+    Linear layers, convolutions and attention's two products run the
+    reference's own AVX2 micro-kernel (sdasm_gemm_6x16_avx2, assembled from
+    its sources) as its mul_mat / conv2d / attention drive it; the softmax and
+    GroupNorm its single-precision forms restated in C (oracle/ref_driver.c,
+    oracle/ref_forms.c).  Every distinct operation shape of the
+    step runs once on a fraction of its work (1/budget_fraction of its rows or
+    queries, at least one) after a warm run; its time, scaled by the inverse
+    fraction, counts once per occurrence in the step.
+    """
+    import ctypes
+
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import ref_forms
+
+    refk = _reference_kernels()
+    P = ctypes.c_void_p
+    ptr = lambda a: a.ctypes.data_as(P)
+    rng = np.random.default_rng(0)
+    ops = unet_ops()
+    counts: dict[tuple, int] = {}
+    for o in ops:
+        counts[o] = counts.get(o, 0) + 1
+
+    def timed(fn):
+        fn()
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    parts: dict[str, float] = {}
+    for op, n in counts.items():
+        kind = op[0]
+        if kind == "conv":
+            _, b, ic, oc, hh, ww, k, st = op
+            wt = (rng.standard_normal((oc, ic, k, k)) / math.sqrt(ic * k * k)).astype(np.float16)
+            oh, ow = (hh + 2 * (k // 2) - k) // st + 1, (ww + 2 * (k // 2) - k) // st + 1
+            if refk is not None:
+                # A band of output rows of one image: a fraction of the positions.
+                rows_out = max(1, oh // budget_fraction)
+                band = min(hh, rows_out * st + k)
+                x = rng.standard_normal((1, ic, band, ww)).astype(np.float32)
+                y = np.empty((rows_out * ow, oc), np.float32)
+                t = timed(lambda: refk.refk_conv2d_mt(ptr(wt), oc, ic, k, k, ptr(x), 1, band, ww, st, k // 2,
+                                                      rows_out, ow, ptr(y)))
+                t *= b * oh / rows_out
+            else:
+                x = rng.standard_normal((b, ic, hh, ww)).astype(np.float32)
+                part = max(1, oc // budget_fraction)
+                t = timed(lambda: ref_forms.conv2d(wt, x, (st, st), (k // 2, k // 2), (1, 1), oc_range=(0, part)))
+                t *= oc / part
+        elif kind in ("linear", "geglu"):
+            _, m, k, nn = op
+            rows = max(1, m // budget_fraction)
+            x = rng.standard_normal((rows, k)).astype(np.float32)
+            wt = (rng.standard_normal((nn, k)) / math.sqrt(k)).astype(np.float16)
+            if refk is not None:
+                y = np.empty((rows, nn), np.float32)
+                t = timed(lambda: refk.refk_mul_mat_mt(ptr(wt), nn, k, ptr(x), rows, ptr(y))) * (m / rows)
+            else:
+                t = timed(lambda: ref_forms.mul_mat(wt, x)) * (m / rows)
+        elif kind == "attn":
+            _, b, heads, lq, lk, d = op
+            q = rng.standard_normal((b, lq, heads * d)).astype(np.float32)
+            kk = rng.standard_normal((b, lk, heads * d)).astype(np.float32)
+            v = rng.standard_normal((b, lk, heads * d)).astype(np.float32)
+            qn = max(1, lq // budget_fraction)
+            if refk is not None:
+                o = np.empty((b, lq, heads * d), np.float32)
+                t = timed(lambda: refk.refk_attention_mt(ptr(q), ptr(kk), ptr(v), ptr(o), b, heads, lq, lk, d, d,
+                                                         d ** -0.5, qn)) * (lq / qn)
+            else:
+                t = timed(lambda: ref_forms.attention(q, kk, v, heads, heads, d ** -0.5, q_range=(0, qn))) * (lq / qn)
+        else:
+            _, b, cc, hh, ww = op
+            x = rng.standard_normal((b, cc, hh, ww)).astype(np.float32)
+            g = np.ones(cc, np.float32)
+            t = timed(lambda: ref_forms.group_norm(x, 32, 1e-5, g, g, True))
+        parts[kind] = parts.get(kind, 0.0) + t * n
+    total = sum(parts.values())
+    how = ("linear layers, convolutions and attention's two products on the reference's AVX2 micro-kernel "
+           "(assembled from its sources), the softmax and GroupNorm in its single-precision forms restated in C"
+           if refk is not None else
+           "the reference's single-precision forms restated in C")
+    return {"value": 1.0 / total, "unit": UNET_UNIT, "cores": ref_forms.threads(),
+            "kind": "reference" if refk is not None else "port",
+            "sample": f"every distinct operation shape of the SD 1.5 UNet step (CFG batch 2) once on 1/{budget_fraction} "
+                      "of its output rows / positions / queries, scaled by the inverse fraction and its count in the "
+                      f"step; {how}; LayerNorm and the glue nodes not counted",
+            "seconds_per_step": total, "parts_s": {k: round(v, 3) for k, v in parts.items()}, "cpu": _cpu_model()}
 
 
 def _cpu_model() -> str:
@@ -272,66 +458,29 @@ def _cpu_model() -> str:
 # ---------------------------------------------------------------- main
 
 def run_reference(args) -> None:
-    """The reference arm: the reference's CPU forms (restated in C) on the host cores."""
+    """The reference arm: the reference's CPU forms (restated in C) on the host cores, on this arm's workload."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    for _ in range(max(0, args.warmup)):
-        pass
-    samples = [cpu_baseline() for _ in range(max(1, min(3, args.steps)))]
+    unet = args.workload == "unet"
+    measure = cpu_unet_step if unet else cpu_baseline
+    samples = [measure() for _ in range(max(1, min(2 if unet else 3, args.steps)))]
     best = max(samples, key=lambda s: s["value"])
-    line = {"metric": METRIC, "value": best["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+    metric, unit, workload = (UNET_METRIC, UNET_UNIT, UNET_WORKLOAD) if unet else (HOT_METRIC, HOT_UNIT, HOT_WORKLOAD)
+    line = {"metric": metric, "value": best["value"], "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 / best["value"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "sample": best["sample"]},
+            "config": {"workload": workload, "sample": best["sample"]},
             "cpu_baseline": {k: best[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": best["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": best["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args()
-    if args.impl == "reference":
-        run_reference(args)
-        return
-
-    import torch
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
+def run_hot_ops(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
     import sdb
 
-    sdb.load()
     work = HotOps(dev, seed=1234)
     nops = len(work.ops)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     # Each step's launches are captured once per input set into a CUDA graph
     # and replayed: the device time of the kernels, without the host's
@@ -427,17 +576,17 @@ def main() -> None:
     if tfile.exists():
         traffic = json.loads(tfile.read_text()).get(name)
     line = {
-        "metric": METRIC, "value": world * 1e3 / ms, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": HOT_METRIC, "value": world * 1e3 / ms, "unit": HOT_UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "ops": [o[0] for o in work.ops], "parallelism": f"replicas x{world}",
+        "config": {"workload": HOT_WORKLOAD, "ops": [o[0] for o in work.ops], "parallelism": f"replicas x{world}",
                    "l2": "3 rotating input sets (~240 MB) > L2", "weights": "random-init FP16, packed once",
                    "timing": "CUDA-graph replay of each step's launches; per-op times from graphs of each op"},
         "roofline": {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "peak_source": peaks["source"], "traffic": traffic,
                      "work_per_launch": work_units, "avg_launch_ms": per_op_ms[dom]},
         "per_op_ms": {work.ops[j][0]: round(per_op_ms[j], 5) for j in range(nops)},
-        "e2e": {"value": world * 1e3 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": world * 1e3 / e2e_ms, "unit": HOT_UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "device_status": status,
@@ -447,6 +596,272 @@ def main() -> None:
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         line["cpu_baseline"]["cpu"] = cb["cpu"]
     print(json.dumps(line), flush=True)
+
+
+
+# ---------------------------------------------------------------- the UNet step
+
+CLASSES = {"conv3x3": "tensor", "conv3x3_s2": "tensor", "conv1x1": "tensor", "linear": "tensor", "geglu": "tensor",
+           "self_attention": "tensor", "cross_attention": "tensor", "groupnorm": "hbm", "layernorm": "hbm",
+           "glue": "hbm"}
+
+
+class OpClock:
+    """Records the library calls one UNet forward makes, then times each alone: the call captured
+    into a CUDA graph of its own and replayed, with CUDA events on the capture stream around the
+    replays (device time only).  Each call has its class and algorithmic work (FLOPs in the
+    reference's convention for products, bytes read + written for the rest)."""
+
+    NAMES = ("conv2d_nhwc", "mul_mat", "mul_mat_gated", "attention_heads", "group_norm_nhwc", "norm",
+             "concat_channels_nhwc", "upscale_nearest_nhwc", "timestep_embedding")
+
+    def __init__(self, sdb, torch):
+        self.sdb, self.torch = sdb, torch
+        self.records: list[tuple] = []
+        self.saved = {}
+
+    @staticmethod
+    def work(name, args, out):
+        if name == "conv2d_nhwc":
+            w = args[0]
+            oc, ic, kh, kw = w.shape
+            n, oh, ow, _ = out.shape
+            stride = args[2] if len(args) > 2 else (1, 1)
+            cls = "conv1x1" if kh == 1 else ("conv3x3_s2" if stride[0] == 2 else "conv3x3")
+            return cls, 2 * kh * kw * ic * oc * oh * ow * n
+        if name in ("mul_mat", "mul_mat_gated"):
+            w, x = args[0], args[1]
+            k = w.shape[1]
+            m = x.numel() // k
+            return ("geglu" if name == "mul_mat_gated" else "linear"), 2 * m * w.shape[0] * k
+        if name == "attention_heads":
+            q, k, heads = args[0], args[1], args[3]
+            b, lq, hd = q.shape
+            lk = k.shape[1]
+            return ("self_attention" if lk == lq else "cross_attention"), 4 * (hd // heads) * heads * lq * lk * b
+        if name in ("group_norm_nhwc", "norm"):
+            return ("groupnorm" if name == "group_norm_nhwc" else "layernorm"), 8 * args[0].numel()
+        return "glue", 8 * out.numel()
+
+    def __enter__(self):
+        for name in self.NAMES:
+            fn = getattr(self.sdb, name)
+            self.saved[name] = fn
+
+            def wrapped(*a, _fn=fn, _name=name, **kw):
+                out = _fn(*a, **kw)
+                self.records.append((_name, _fn, a, kw, out))
+                return out
+
+            setattr(self.sdb, name, wrapped)
+        return self
+
+    def __exit__(self, *exc):
+        for name, fn in self.saved.items():
+            setattr(self.sdb, name, fn)
+
+    def measure(self, stream, reps: int = 3) -> dict:
+        torch = self.torch
+        classes: dict[str, list] = {}
+        for name, fn, a, kw, out in self.records:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                fn(*a, **kw)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0.record()
+                for _ in range(reps):
+                    g.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            cls, work = self.work(name, a, out)
+            c = classes.setdefault(cls, [0, 0.0, 0])
+            c[0] += work
+            c[1] += e0.elapsed_time(e1) / reps
+            c[2] += 1
+            del g
+        return {k: {"work": v[0], "ms": v[1], "calls": v[2]} for k, v in classes.items()}
+
+
+def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
+    import sdb
+    import unet as U
+
+    net = U.UNet(U.SD15, device=dev, seed=20261011)
+    sampler = U.Sampler(net, 64, 64, steps=SAMPLER_STEPS)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    latent = torch.randn(1, 64, 64, 4, device=dev, generator=g)
+    context = torch.randn(2, 77, 768, device=dev, generator=g)
+    sampler.x.copy_(latent * sampler.sigmas[0])
+    sampler.context.copy_(context)
+    sampler.set_step(0)
+    n0 = sdb.launch_count()
+    sampler.capture(warmup=max(3, args.warmup))
+    launches_forward = sdb.launch_count() - n0
+    # Per step on the device: the timestep, the captured forward, the guidance + Euler update (which
+    # also writes the next step's model input).
+    ts = torch.tensor([U.sigma_to_t(sg) for sg in sampler.sigmas[:-1]], device=dev, dtype=torch.float32)
+    c_in = [1.0 / math.sqrt(sg * sg + 1.0) for sg in sampler.sigmas]
+
+    def step(i: int) -> None:
+        j = i % SAMPLER_STEPS
+        sampler.t.copy_(ts[j:j + 1].expand(2))
+        eps = sampler.step_forward()
+        sdb.euler_cfg_step(eps, sampler.x, sampler.x_in, sampler.cfg_scale, sampler.sigmas[j],
+                           sampler.sigmas[j + 1], c_in[(j + 1) % SAMPLER_STEPS])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    n0 = sdb.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+    # Graph replays do not pass through the library's launch counter: the forward's launches times K,
+    # plus the update kernel each step.
+    launches = launches_forward // (max(3, args.warmup) + 1) * args.steps + (sdb.launch_count() - n0)
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+
+    # The step's classes: the calls of one forward, each timed alone (graph replays).
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(torch.cuda.current_stream())
+    with OpClock(sdb, torch) as oc:
+        with torch.cuda.stream(cap):
+            net.forward(sampler.x_in, sampler.t, sampler.context)
+    torch.cuda.synchronize()
+    classes = oc.measure(cap)
+    del oc
+
+    # End to end through the public API: latent and context from pinned host memory, the sampler step,
+    # the updated latent back to the host.
+    h_lat = latent.cpu().pin_memory()
+    h_ctx = context.cpu().pin_memory()
+    h_out = torch.empty(1, 64, 64, 4).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step(i: int) -> None:
+        sampler.x.copy_(h_lat, non_blocking=True)
+        sampler.context.copy_(h_ctx, non_blocking=True)
+        step(i)
+        h_out.copy_(sampler.x, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_step(0)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_steps)
+    h2d = h_lat.numel() * 4 + h_ctx.numel() * 4
+    d2h = h_out.numel() * 4
+    status = sdb.device_status(clear=True)
+    del sampler
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = measured_peaks()
+    step_flops = net.flops(2, 64, 64)
+    dom = max((k for k in classes if CLASSES[k] == "tensor"), key=lambda k: classes[k]["ms"])
+    d = classes[dom]
+    achieved = d["work"] / (d["ms"] * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(dom)
+    line = {
+        "metric": UNET_METRIC, "value": world * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": UNET_WORKLOAD, "resolution": "512x512 (latent 64x64)", "batch": "2 (CFG)",
+                   "context": "2x77x768", "sampler": f"Euler, {SAMPLER_STEPS} steps, CFG 7",
+                   "weights": f"random-init FP16, {net.params / 1e6:.1f}M parameters, packed once",
+                   "parallelism": f"replicas x{world} (one image a GPU)",
+                   "l2": "weights (1.7 GB) and activations exceed L2 every step",
+                   "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step"},
+        "unet_ms_per_step": ms,
+        "imgs_per_s_unet_only": world * 1e3 / ms / SAMPLER_STEPS,
+        "step_tflop": step_flops / 1e12,
+        "step_frac_of_sustained_peak": step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
+        "roofline": {"kernel": f"{dom} (all calls of the class in one forward)", "bound": "tensor",
+                     "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "peak_source": peaks["source"] + " (burst)",
+                     "traffic": traffic, "work_per_launch": d["work"] / d["calls"],
+                     "avg_launch_ms": d["ms"] / d["calls"]},
+        "classes_ms": {k: round(v["ms"], 4) for k, v in sorted(classes.items(), key=lambda kv: -kv[1]["ms"])},
+        "classes_tflops": {k: round(v["work"] / (v["ms"] * 1e-3) / 1e12, 1) for k, v in classes.items()
+                           if CLASSES[k] == "tensor"},
+        "e2e": {"value": world * 1e3 / e2e_ms, "unit": UNET_UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_unet_step()
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"]["cpu"] = cb["cpu"]
+        line["cpu_baseline"]["parts_s"] = cb["parts_s"]
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 100 if args.workload == "unet" else 1000
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    import sdb
+
+    sdb.load()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    run = run_unet if args.workload == "unet" else run_hot_ops
+    run(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks)
 
 
 if __name__ == "__main__":

@@ -112,6 +112,8 @@ int sdb_attention(const sdb_tensor *q, const sdb_tensor *k, const sdb_tensor *v,
  * (norm.cc:100-175).  Replaces sdasm::group_norm_* / norm_* (ops.h:140-146). */
 int sdb_group_norm(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps, const sdb_chain *chain,
                    void *stream);
+/* (x and dst may also be channels-last images -- [W, H, C, N] with nb[2] = 4 --
+ * when C % groups == 0 and every chain step is one value per channel.) */
 int sdb_norm(const sdb_tensor *x, const sdb_tensor *dst, float eps, const sdb_chain *chain, void *stream);
 /* GroupNorm that allocates nothing, for callers that may not call cudaMalloc
  * (memory owned by another allocator, code running under stream capture, loops
@@ -124,6 +126,28 @@ int sdb_norm(const sdb_tensor *x, const sdb_tensor *dst, float eps, const sdb_ch
  * overlap on the GPU race. */
 int sdb_group_norm_no_alloc(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps,
                             const sdb_chain *chain, void *stream);
+
+/* ---- the graph's data-movement nodes (device-resident runner) -----------
+ * The reference takes only CONV_2D, MUL_MAT, FLASH_ATTN_EXT, GROUP_NORM and
+ * NORM and leaves every other node of stable-diffusion.cpp's UNet graph to
+ * ggml's CPU kernels ("the rest go by", hooks.cc:29-55).  With activations
+ * resident on the GPU these nodes run here too:
+ * sdb_concat: GGML_OP_CONCAT of a and b along ggml dim `dim` into dst; the three
+ * tensors dense in one memory order (e.g. channels-last images along C). */
+int sdb_concat(const sdb_tensor *a, const sdb_tensor *b, const sdb_tensor *dst, int32_t dim, void *stream);
+/* GGML_OP_UPSCALE, nearest, by integer factors of W and H; channels-last images
+ * [W, H, C, N] with C % 4 == 0. */
+int sdb_upscale_nearest(const sdb_tensor *src, const sdb_tensor *dst, void *stream);
+/* GGML_OP_TIMESTEP_EMBEDDING: timesteps [N] FP32 -> dst [>= dim, N]:
+ * cos(t f_j) for j < dim/2, then sin(t f_j), f_j = max_period^(-j / (dim/2)). */
+int sdb_timestep_embedding(const sdb_tensor *timesteps, const sdb_tensor *dst, int32_t dim, int32_t max_period,
+                           void *stream);
+/* One Euler step of the sampler with classifier-free guidance, in place:
+ * e = eps[i] + cfg (eps[n + i] - eps[i]) (unconditional half first),
+ * x[i] += (sigma_next - sigma) e, and, when x_in is given, both halves of the
+ * next model input x_in[i] = x_in[n + i] = x[i] * c_in_next. */
+int sdb_euler_cfg_step(const float *eps, float *x, float *x_in, int64_t n, float cfg, float sigma, float sigma_next,
+                       float c_in_next, void *stream);
 
 /* ---- the weight store (store.h:58-120, store.cc:202-266) ----------------
  * Weights are repacked once into the layout the kernels read and kept on the

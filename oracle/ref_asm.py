@@ -14,8 +14,10 @@ that packs operands as the reference's gemm.cc does and calls the kernels:
     sdasm_gemm_6x16_avx2      (gemm_avx2.S)        the 6 x 16 FP32 tile
     sdasm_gated_gelu_avx2     (activation_avx2.S)  out = x GELU(gate)
     sdasm_exponentials_avx2   (softmax_avx2.S)     exp(s - max) and its sums
-The library pins the oracle (tests/test_golden.py) and generates the golden
-fixtures (tests/golden/make_golden.py); nothing in the product links it.
+The library pins the oracle (tests/test_golden.py), generates the golden
+fixtures (tests/golden/make_golden.py) and, driven on all host threads
+(refk_mul_mat_mt, refk_conv2d_mt), is the CPU baseline of bench.py for the
+linear layers and convolutions; nothing in the product links it.
 """
 from __future__ import annotations
 
@@ -65,7 +67,7 @@ def build(reference: Path = Path("/root/reference")) -> Path:
         subprocess.run(["as", "--64", "-o", str(o), str(s)], check=True, capture_output=True)
         objs.append(str(o))
     lib = OUT / "libsdasm_ref.so"
-    subprocess.run(["gcc", "-O2", "-shared", "-fPIC", "-mavx2", "-mfma", "-mf16c", "-o", str(lib),
+    subprocess.run(["gcc", "-O2", "-fopenmp", "-shared", "-fPIC", "-mavx2", "-mfma", "-mf16c", "-o", str(lib),
                     str(HERE / "ref_driver.c"), *objs, "-lm", "-Wl,-z,noexecstack"], check=True, capture_output=True)
     return lib
 

@@ -149,3 +149,337 @@ void refk_exponentials(float *s, int64_t n, const float *max, double *total) {
 void refk_c_exponential(const float *x, float *y, int64_t n) {
     for (int64_t i = 0; i < n; ++i) y[i] = c_exponential(x[i]);
 }
+
+/* ---- the CPU baseline: the reference's micro-kernel on all host threads --------
+ * The reference splits a product's row tiles over its thread pool with a
+ * work queue (gemm.cc:142-186); here OpenMP hands out blocks of 48 rows the
+ * same way (dynamic schedule), each thread packing its own rows.  The
+ * weights are widened into panels once, by all threads. */
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int refk_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+static int refk_threads_internal(void) { return refk_threads(); }
+
+/* Widened weight panels are kept between calls, keyed by the weights' address
+ * and shape, as the reference's store keeps packed weights (store.cc:202-266):
+ * its products never repack a weight they have seen. */
+typedef struct {
+    const void *w;
+    int n, k, layout;
+    float *panels;
+} packed_entry;
+static packed_entry packed_cache[256];
+static int packed_next;
+
+static float *cached_panels(const void *w, int n, int k, int layout) {
+    for (int i = 0; i < 256; ++i)
+        if (packed_cache[i].w == w && packed_cache[i].n == n && packed_cache[i].k == k &&
+            packed_cache[i].layout == layout)
+            return packed_cache[i].panels;
+    return NULL;
+}
+
+static void keep_panels(const void *w, int n, int k, int layout, float *panels) {
+    packed_entry *e = &packed_cache[packed_next];
+    packed_next = (packed_next + 1) % 256;
+    free(e->panels);
+    e->w = w;
+    e->n = n;
+    e->k = k;
+    e->layout = layout;
+    e->panels = panels;
+}
+
+/* Forgets every kept panel set (the weights' memory is about to be reused). */
+void refk_forget(void) {
+    for (int i = 0; i < 256; ++i) {
+        free(packed_cache[i].panels);
+        packed_cache[i].panels = NULL;
+        packed_cache[i].w = NULL;
+    }
+}
+
+static float *widen_panels(const uint16_t *w16, int N, int K) {
+    const int npanels = (N + NR - 1) / NR;
+    float *wp = aligned(sizeof(float) * (size_t)npanels * NR * K);
+    if (!wp) return NULL;
+#pragma omp parallel for schedule(static)
+    for (int p = 0; p < npanels; ++p)
+        for (int k = 0; k < K; ++k)
+            for (int j = 0; j < NR; ++j) {
+                const int n = p * NR + j;
+                wp[((size_t)p * K + k) * NR + j] = n < N ? half_to_float(w16[(size_t)n * K + k]) : 0.0f;
+            }
+    return wp;
+}
+
+/* One block of up to 48 rows whose A panels for stretch k0 are in ap, column
+ * panels [p0, p1) (all when p1 <= 0). */
+static void block_product_cols(const float *ap, const float *wp, int N, int K, int k0, int kc, int rows_total,
+                               float *y, float *tile, int p0, int p1) {
+    for (int p = p0; p < p1; ++p) {
+        const float *b = wp + ((size_t)p * K + k0) * NR;
+        const int cols = N - p * NR < NR ? N - p * NR : NR;
+        for (int i0 = 0; i0 < rows_total; i0 += MR) {
+            const float *a = ap + (size_t)(i0 / MR) * kc * MR;
+            const int rows = rows_total - i0 < MR ? rows_total - i0 : MR;
+            float *c = y + (size_t)i0 * N + p * NR;
+            if (rows == MR && cols == NR) {
+                sdasm_gemm_6x16_avx2(kc, a, b, c, (int64_t)N * 4, k0 > 0);
+            } else {
+                sdasm_gemm_6x16_avx2(kc, a, b, tile, NR * 4, 0);
+                for (int i = 0; i < rows; ++i)
+                    for (int j = 0; j < cols; ++j)
+                        c[(size_t)i * N + j] = k0 > 0 ? c[(size_t)i * N + j] + tile[i * NR + j] : tile[i * NR + j];
+            }
+        }
+    }
+}
+
+static void block_product(const float *ap, const float *wp, int N, int K, int k0, int kc, int rows_total, float *y,
+                          float *tile) {
+    block_product_cols(ap, wp, N, K, k0, kc, rows_total, y, tile, 0, (N + NR - 1) / NR);
+}
+
+/* Work items: blocks of 48 rows, each split over column-panel chunks when the
+ * rows alone would leave threads idle (the reference's queue hands out tiles). */
+static int column_chunks(int mblocks, int npanels) {
+    const int want = (4 * refk_threads_internal() + mblocks - 1) / mblocks;
+    return want < 1 ? 1 : (want > npanels ? npanels : want);
+}
+
+/* y (M, N) = x (M, K) w16 (N, K)^T on all threads. */
+int refk_mul_mat_mt(const uint16_t *w16, int N, int K, const float *x, int M, float *y) {
+    float *wp = cached_panels(w16, N, K, 0);
+    if (!wp) {
+        wp = widen_panels(w16, N, K);
+        if (!wp) return 1;
+        keep_panels(w16, N, K, 0, wp);
+    }
+    const int mblocks = (M + 47) / 48, npanels = (N + NR - 1) / NR;
+    const int chunks = column_chunks(mblocks, npanels), per = (npanels + chunks - 1) / chunks;
+    int bad = 0;
+#pragma omp parallel
+    {
+        float *ap = aligned(sizeof(float) * 48 * KC);
+        float tile[MR * NR] __attribute__((aligned(64)));
+        if (!ap) bad = 1;
+#pragma omp for schedule(dynamic)
+        for (int w = 0; w < mblocks * chunks; ++w) {
+            if (!ap) continue;
+            const int mb = w / chunks, p0 = (w % chunks) * per, p1 = p0 + per < npanels ? p0 + per : npanels;
+            const int m0 = mb * 48, rows = M - m0 < 48 ? M - m0 : 48;
+            for (int k0 = 0; k0 < K; k0 += KC) {
+                const int kc = K - k0 < KC ? K - k0 : KC;
+                for (int i0 = 0; i0 < rows; i0 += MR)
+                    for (int k = 0; k < kc; ++k)
+                        for (int i = 0; i < MR; ++i) {
+                            const int m = i0 + i;
+                            ap[((size_t)(i0 / MR) * kc + k) * MR + i] =
+                                m < rows ? x[(size_t)(m0 + m) * K + k0 + k] : 0.0f;
+                        }
+                block_product_cols(ap, wp, N, K, k0, kc, rows, y + (size_t)m0 * N, tile, p0, p1);
+            }
+        }
+        free(ap);
+    }
+    return bad;
+}
+
+/* The direct convolution as the same product (conv2d.cc:231-316): rows are
+ * output positions, columns the output channels, k runs over the taps and, in
+ * each tap, the input channels -- the image is first laid channels-last so
+ * that a row's k-stretch packs from contiguous channels, and the weights
+ * [OC][IC][KH][KW] are widened in that k order.  x [N][IC][H][W], y
+ * [position][OC]. */
+int refk_conv2d_mt(const uint16_t *w16, int OC, int IC, int KH, int KW, const float *x, int NI, int H, int W,
+                   int stride, int pad, int OH, int OW, float *y) {
+    const int K = IC * KH * KW;
+    const int M = NI * OH * OW;
+    const int npanels = (OC + NR - 1) / NR;
+    float *wp = cached_panels(w16, OC, K, 1 + KH * 16 + KW);
+    const int fresh = wp == NULL;
+    if (fresh) wp = aligned(sizeof(float) * (size_t)npanels * NR * K);
+    float *xl = aligned(sizeof(float) * (size_t)NI * H * W * IC);
+    if (!wp || !xl) return 1;
+    if (fresh) keep_panels(w16, OC, K, 1 + KH * 16 + KW, wp);
+#pragma omp parallel for schedule(static) if (fresh)
+    for (int p = 0; p < (fresh ? npanels : 0); ++p)
+        for (int k = 0; k < K; ++k) {
+            const int tap = k / IC, ic = k % IC, ky = tap / KW, kx = tap % KW;
+            for (int j = 0; j < NR; ++j) {
+                const int n = p * NR + j;
+                wp[((size_t)p * K + k) * NR + j] =
+                    n < OC ? half_to_float(w16[(((size_t)n * IC + ic) * KH + ky) * KW + kx]) : 0.0f;
+            }
+        }
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < NI * H; ++r) {
+        const int n = r / H, iy = r % H;
+        for (int ix = 0; ix < W; ++ix)
+            for (int ic = 0; ic < IC; ++ic)
+                xl[(((size_t)n * H + iy) * W + ix) * IC + ic] = x[(((size_t)n * IC + ic) * H + iy) * W + ix];
+    }
+    const int mblocks = (M + 47) / 48;
+    const int chunks = column_chunks(mblocks, npanels), per = (npanels + chunks - 1) / chunks;
+    int bad = 0;
+#pragma omp parallel
+    {
+        float *ap = aligned(sizeof(float) * 48 * KC);
+        float tile[MR * NR] __attribute__((aligned(64)));
+        if (!ap) bad = 1;
+#pragma omp for schedule(dynamic)
+        for (int w = 0; w < mblocks * chunks; ++w) {
+            if (!ap) continue;
+            const int mb = w / chunks, p0 = (w % chunks) * per, p1 = p0 + per < npanels ? p0 + per : npanels;
+            const int m0 = mb * 48, rows = M - m0 < 48 ? M - m0 : 48;
+            for (int k0 = 0; k0 < K; k0 += KC) {
+                const int kc = K - k0 < KC ? K - k0 : KC;
+                for (int i0 = 0; i0 < rows; i0 += MR) {
+                    float *dst = ap + (size_t)(i0 / MR) * kc * MR;
+                    for (int i = 0; i < MR; ++i) {
+                        const int live = i0 + i < rows, m = live ? m0 + i0 + i : m0;
+                        const int n = m / (OH * OW), pos = m % (OH * OW);
+                        const int iy0 = (pos / OW) * stride - pad, ix0 = (pos % OW) * stride - pad;
+                        int k = 0;
+                        while (k < kc) {
+                            const int kk = k0 + k, tap = kk / IC, ic0 = kk % IC, ky = tap / KW, kx = tap % KW;
+                            const int run = IC - ic0 < kc - k ? IC - ic0 : kc - k;
+                            const int iy = iy0 + ky, ix = ix0 + kx;
+                            if (live && iy >= 0 && iy < H && ix >= 0 && ix < W) {
+                                const float *src = xl + (((size_t)n * H + iy) * W + ix) * IC + ic0;
+                                for (int t = 0; t < run; ++t) dst[(size_t)(k + t) * MR + i] = src[t];
+                            } else {
+                                for (int t = 0; t < run; ++t) dst[(size_t)(k + t) * MR + i] = 0.0f;
+                            }
+                            k += run;
+                        }
+                    }
+                }
+                block_product_cols(ap, wp, OC, K, k0, kc, rows, y + (size_t)m0 * OC, tile, p0, p1);
+            }
+        }
+        free(ap);
+    }
+    free(xl);
+    return bad;
+}
+
+/* Attention as the reference computes it (attention.cc:858-1064), products on
+ * its micro-kernel: per head and block of 48 queries, the scores S = scale Q K^T
+ * (the keys as a panel matrix of 16 keys x D), per query the maximum, the
+ * exponentials (the C++ form's exponential, scalar_math.h:34-51) summed in
+ * double, then O = P V (V^T as panels of 16 value dims x LK) and one
+ * reciprocal per query.  q [B][LQ][H*D], k [B][LK][H*D], v [B][LK][H*DV],
+ * out [B][LQ][H*DV]; queries [0, nq) of each head. */
+static float *panels_rows(const float *src, long stride, int N, int K) {
+    /* rows n of src (stride floats apart), K floats each, into [panel][k][16]. */
+    const int np = (N + NR - 1) / NR;
+    float *wp = aligned(sizeof(float) * (size_t)np * NR * K);
+    if (!wp) return NULL;
+    for (int p = 0; p < np; ++p)
+        for (int k = 0; k < K; ++k)
+            for (int j = 0; j < NR; ++j) {
+                const int n = p * NR + j;
+                wp[((size_t)p * K + k) * NR + j] = n < N ? src[(size_t)n * stride + k] : 0.0f;
+            }
+    return wp;
+}
+
+int refk_attention_mt(const float *q, const float *k, const float *v, float *out, int B, int H, int LQ, int LK, int D,
+                      int DV, float scale, int nq) {
+    const int heads = B * H;
+    float **kp = calloc((size_t)heads, sizeof(float *)), **vp = calloc((size_t)heads, sizeof(float *));
+    int bad = 0;
+    if (!kp || !vp) return 1;
+#pragma omp parallel for schedule(dynamic)
+    for (int bh = 0; bh < heads; ++bh) {
+        const int b = bh / H, h = bh % H;
+        kp[bh] = panels_rows(k + ((size_t)b * LK * H + h) * D, (long)H * D, LK, D);
+        /* V^T: value dim j's row is v[.][key][h*DV + j] over the keys. */
+        float *vt = aligned(sizeof(float) * (size_t)DV * LK);
+        if (vt) {
+            for (int key = 0; key < LK; ++key)
+                for (int j = 0; j < DV; ++j) vt[(size_t)j * LK + key] = v[((size_t)b * LK + key) * H * DV + h * DV + j];
+            vp[bh] = panels_rows(vt, LK, DV, LK);
+            free(vt);
+        }
+        if (!kp[bh] || !vp[bh]) bad = 1;
+    }
+    const int qblocks = (nq + 47) / 48;
+    if (!bad) {
+#pragma omp parallel
+        {
+            float *s = aligned(sizeof(float) * 48 * (size_t)((LK + NR - 1) / NR * NR));
+            float *ap = aligned(sizeof(float) * 48 * (size_t)(D > KC ? D : KC));
+            float *o = aligned(sizeof(float) * 48 * (size_t)((DV + NR - 1) / NR * NR));
+            double *sum = malloc(sizeof(double) * 48);
+            float tile[MR * NR] __attribute__((aligned(64)));
+#pragma omp for schedule(dynamic)
+            for (int w = 0; w < heads * qblocks; ++w) {
+                if (!s || !ap || !o || !sum) continue;
+                const int bh = w / qblocks, qb = w % qblocks, b = bh / H, h = bh % H;
+                const int q0 = qb * 48, rows = nq - q0 < 48 ? nq - q0 : 48;
+                /* S = Q K^T over K = D (one stretch when D <= 256). */
+                for (int k0 = 0; k0 < D; k0 += KC) {
+                    const int kc = D - k0 < KC ? D - k0 : KC;
+                    for (int i0 = 0; i0 < rows; i0 += MR)
+                        for (int kk = 0; kk < kc; ++kk)
+                            for (int i = 0; i < MR; ++i)
+                                ap[((size_t)(i0 / MR) * kc + kk) * MR + i] =
+                                    i0 + i < rows ? q[((size_t)b * LQ + q0 + i0 + i) * H * D + h * D + k0 + kk] : 0.0f;
+                    block_product(ap, kp[bh], LK, D, k0, kc, rows, s, tile);
+                }
+                for (int i = 0; i < rows; ++i) {
+                    float *row = s + (size_t)i * LK;
+                    float mx = -INFINITY;
+                    for (int key = 0; key < LK; ++key) {
+                        row[key] *= scale;
+                        mx = row[key] > mx ? row[key] : mx;
+                    }
+                    double t = 0.0;
+                    for (int key = 0; key < LK; ++key) {
+                        row[key] = c_exponential(row[key] - mx);
+                        t += row[key];
+                    }
+                    sum[i] = t;
+                }
+                /* O = P V over K = LK, stretch by stretch. */
+                for (int k0 = 0; k0 < LK; k0 += KC) {
+                    const int kc = LK - k0 < KC ? LK - k0 : KC;
+                    for (int i0 = 0; i0 < rows; i0 += MR)
+                        for (int kk = 0; kk < kc; ++kk)
+                            for (int i = 0; i < MR; ++i)
+                                ap[((size_t)(i0 / MR) * kc + kk) * MR + i] =
+                                    i0 + i < rows ? s[(size_t)(i0 + i) * LK + k0 + kk] : 0.0f;
+                    block_product(ap, vp[bh], DV, LK, k0, kc, rows, o, tile);
+                }
+                for (int i = 0; i < rows; ++i) {
+                    const float r = (float)(1.0 / sum[i]);
+                    for (int j = 0; j < DV; ++j)
+                        out[((size_t)b * LQ + q0 + i) * H * DV + h * DV + j] = o[(size_t)i * DV + j] * r;
+                }
+            }
+            free(s);
+            free(ap);
+            free(o);
+            free(sum);
+        }
+    }
+    for (int bh = 0; bh < heads; ++bh) {
+        free(kp[bh]);
+        free(vp[bh]);
+    }
+    free(kp);
+    free(vp);
+    return bad;
+}

@@ -75,7 +75,7 @@ struct GemmArgs {
     int a_planes;           // 2: one TMA box brings hi and lo (a full 128-row tile); 1: one box each
     int tiles_m, tiles_n;   // output tiles along rows / columns
     int items;              // tiles_m * tiles_n * ksplit work items, taken round-robin by the CTAs
-    int store;              // kStoreTma / kStoreDirect (linear); conv always stores directly
+    int store;              // kStoreTma: the output through ymap in 32 x 32 boxes; kStoreDirect
     float* y;               // output (the redirect when the chain has one)
     float* part;            // split-K: partial sums [ksplit][tiles_m * 128][part_ld]
     long long part_ld;      // columns of a partial row
@@ -197,7 +197,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
         fence_barrier_init();
         tma_prefetch_desc(&amap);
         tma_prefetch_desc(&wmap);
-        if (MODE == kModeLinear && args.store == kStoreTma) tma_prefetch_desc(&ymap);
+        if (args.store == kStoreTma || args.ksplit > 1) tma_prefetch_desc(&ymap);
     }
     if (warp == 1) tmem_alloc(tmem_slot, S::kTmemCols);
     tc_fence_before();
@@ -459,7 +459,21 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                         for (int j = 0; j < 32; ++j) v[j] = old[j] + v[j];
                     }
                     apply_chain_cols<2, 32>(args.chain, cr, v, cb, args.n - 1);
-                    if (p.ok) {
+                    if (args.store == kStoreTma) {
+                        // Channels-last output whose tiles are runs of 128 consecutive positions.
+                        const ConvGeom& g = args.cg;
+                        const int ty = (tm / g.tw) % g.th, tz = tm / (g.tw * g.th);
+                        const int row0 = (tz * g.nt * g.oh + ty * g.oht) * g.ow;
+                        if (lane == 0) bulk_wait_read_all();
+                        __syncwarp();
+                        stage_row32(box, lane, v);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&ymap, box, static_cast<int>(cb), row0 + q * 32);
+                            bulk_commit_group();
+                        }
+                    } else if (p.ok) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
                             if (cb + j < args.n) ybase[(cb + j) * args.ynb[2]] = v[j];

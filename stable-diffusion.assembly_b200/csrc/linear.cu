@@ -107,6 +107,13 @@ bool contiguous_f32(const sdb_tensor* t) {
     return true;
 }
 
+// A channels-last (NHWC) image described in ggml order [W, H, C, N]: channels
+// contiguous, then positions, rows, images.
+bool channels_last(const sdb_tensor* t) {
+    const int64_t c = t->ne[2], w = t->ne[0], h = t->ne[1];
+    return t->nb[2] == 4 && t->nb[0] == 4 * c && t->nb[1] == 4 * c * w && t->nb[3] == 4 * c * w * h;
+}
+
 bool valid_chain(const sdb_chain* c) {
     if (c == nullptr) return true;
     if (c->count < 0 || c->count > SDB_MAX_STEPS) return false;
@@ -313,11 +320,20 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     void* ws = nullptr;
     if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, oc, 128), &ws); s != SDB_OK) return s;
     set_partials(a, ws, a_bytes, tiles, 128);
-    const long long ne[4] = {W, H, ic, N};
-    const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
-    if (int s = split_nhwc(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
-        s != SDB_OK)
-        return s;
+    if (channels_last(x)) {
+        // Already channels-last: the split is a split of rows (positions).
+        const long long ne[4] = {ic, W, H, N};
+        const long long nb[4] = {1, ic, W * ic, H * W * ic};
+        if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
+            s != SDB_OK)
+            return s;
+    } else {
+        const long long ne[4] = {W, H, ic, N};
+        const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
+        if (int s = split_nhwc(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
+            s != SDB_OK)
+            return s;
+    }
     // The split image as [plane][N][H][W][cp8]: a box {64 channels, OWt s0, OHt s1, NT, planes}.
     CUtensorMap amap;
     const uint64_t dims[5] = {static_cast<uint64_t>(cp8), static_cast<uint64_t>(W), static_cast<uint64_t>(H),
@@ -330,8 +346,18 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, ws, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B, estr) != CUDA_SUCCESS)
         return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the image");
-    const CUtensorMap none{};
-    return dispatch<kModeConv>(amap, *p, wmode, none, a, st);
+    // A channels-last output whose tiles are whole runs of 128 positions leaves by TMA stores.
+    CUtensorMap ymap{};
+    const bool whole_tiles = g.owt == g.ow && g.owt * g.oht * g.nt == kBM && g.oh % g.oht == 0 && g.n % g.nt == 0;
+    if (channels_last(dst) && whole_tiles && oc % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0) {
+        const uint64_t ydims[2] = {static_cast<uint64_t>(oc), static_cast<uint64_t>(g.n) * g.oh * g.ow};
+        const uint64_t ystrides[1] = {static_cast<uint64_t>(oc) * 4};
+        const uint32_t ybox[2] = {32, 32};
+        if (encode_tensor_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydims, ystrides, ybox,
+                              CU_TENSOR_MAP_SWIZZLE_128B) == CUDA_SUCCESS)
+            a.store = kStoreTma;
+    }
+    return dispatch<kModeConv>(amap, *p, wmode, ymap, a, st);
 }
 
 }  // extern "C"

@@ -284,6 +284,112 @@ __global__ void __launch_bounds__(kResidentThreads) group_resident_kernel(const 
     apply_range<true>(a, xs, c0, i3, mean, scale, 0, count);
 }
 
+// ---- channels-last (NHWC) images -----------------------------------------
+//
+// x and y are [N][P positions][C] with C % groups == 0: a group is cpg
+// contiguous channels of every position.  Each (image, group) is cut into
+// slices of positions, one CTA a slice, so even one image's 32 groups fill
+// the GPU; a thread keeps one channel of the group (cpg threads a position),
+// so its chain operands are loaded once.  Three passes over x as the
+// reference's algorithm reads it: sums -> mean, centred sums -> variance,
+// then the normalisation and the chain; the double partial sums of the
+// slices meet in global memory between the launches.
+struct NhwcArgs {
+    const float* x;
+    float* y;
+    long long positions;        // H * W
+    int c, groups, cpg;
+    int slices;                 // CTAs per (image, group)
+    int per;                    // positions per slice
+    float eps;
+    double* partial;            // [images * groups][slices][2]
+    Chain chain;
+};
+
+__device__ __forceinline__ void nhwc_slice(const NhwcArgs& a, int& item, int& slice, long long& p0, long long& p1,
+                                           int& ch, int& prow, int& rows_per_pass) {
+    item = blockIdx.x / a.slices;
+    slice = blockIdx.x - item * a.slices;
+    p0 = static_cast<long long>(slice) * a.per;
+    p1 = min(a.positions, p0 + a.per);
+    rows_per_pass = blockDim.x / a.cpg;
+    ch = threadIdx.x % a.cpg;
+    prow = threadIdx.x / a.cpg;
+}
+
+__global__ void __launch_bounds__(kNormThreads) nhwc_sum_kernel(const NhwcArgs a, int phase) {
+    __shared__ double scratch[32];
+    __shared__ float mean_s;
+    int item, slice, ch, prow, rpp;
+    long long p0, p1;
+    nhwc_slice(a, item, slice, p0, p1, ch, prow, rpp);
+    const int i3 = item / a.groups, g = item - i3 * a.groups;
+    const long long count = a.positions * a.cpg;
+    if (phase == 1) {
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int sl = 0; sl < a.slices; ++sl) t += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2];
+            mean_s = static_cast<float>(t / static_cast<double>(count));
+        }
+        __syncthreads();
+    }
+    const float mean = phase == 1 ? mean_s : 0.0f;
+    const float* xb = a.x + static_cast<long long>(i3) * a.positions * a.c + g * a.cpg + ch;
+    double s = 0.0;
+    if (prow < rpp) {
+#pragma unroll 4
+        for (long long p = p0 + prow; p < p1; p += rpp) {
+            const float v = __ldg(xb + p * a.c);
+            if (phase == 0) {
+                s += static_cast<double>(v);
+            } else {
+                const float d = v - mean;
+                s += static_cast<double>(d * d);
+            }
+        }
+    }
+    s = block_sum(s, scratch);
+    if (threadIdx.x == 0) a.partial[(static_cast<long long>(item) * a.slices + slice) * 2 + phase] = s;
+}
+
+__global__ void __launch_bounds__(kNormThreads) nhwc_apply_kernel(const NhwcArgs a) {
+    __shared__ float stats[2];
+    int item, slice, ch, prow, rpp;
+    long long p0, p1;
+    nhwc_slice(a, item, slice, p0, p1, ch, prow, rpp);
+    const int i3 = item / a.groups, g = item - i3 * a.groups;
+    const long long count = a.positions * a.cpg;
+    if (threadIdx.x == 0) {
+        double s = 0.0, q = 0.0;
+        for (int sl = 0; sl < a.slices; ++sl) {
+            s += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2];
+            q += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2 + 1];
+        }
+        stats[0] = static_cast<float>(s / static_cast<double>(count));
+        stats[1] = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(count)) + a.eps);
+    }
+    __syncthreads();
+    if (prow >= rpp) return;
+    const float mean = stats[0], scale = stats[1];
+    const long long c = static_cast<long long>(g) * a.cpg + ch;
+    const long long off = static_cast<long long>(i3) * a.positions * a.c + c;
+    // The chain's operands are one value per channel (the host sends no other chain here).
+    float op[SDB_MAX_STEPS];
+    channel_operands(a.chain, c, i3, op);
+    // Four positions at a time: their loads before their stores.
+    for (long long p = p0 + prow; p < p1; p += 4LL * rpp) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const long long pk = min(p + k * rpp, p1 - 1);
+            v[k] = __ldg(a.x + off + pk * a.c);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (p + k * rpp < p1) a.y[off + (p + k * rpp) * a.c] = apply_uniform(a.chain, op, (v[k] - mean) * scale);
+    }
+}
+
 struct RowArgs {
     const float* x;
     float* y;
@@ -390,8 +496,62 @@ double* partial_buffer(size_t count) {
 
 using namespace sdb;
 
+namespace sdb {
+namespace {
+
+bool channels_last(const sdb_tensor* t) {
+    const int64_t c = t->ne[2], w = t->ne[0], h = t->ne[1];
+    return t->nb[2] == 4 && t->nb[0] == 4 * c && t->nb[1] == 4 * c * w && t->nb[3] == 4 * c * w * h;
+}
+
+bool uniform_chain(const sdb_chain* c) {
+    if (!c) return true;
+    for (int s = 0; s < c->count; ++s)
+        if (c->steps[s].kind != SDB_STEP_SILU && (c->steps[s].nb[0] != 0 || c->steps[s].nb[1] != 0)) return false;
+    return true;
+}
+
+int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps, const sdb_chain* chain,
+                    cudaStream_t st) {
+    NhwcArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.y = static_cast<float*>(dst->data);
+    a.positions = x->ne[0] * x->ne[1];
+    a.c = static_cast<int>(x->ne[2]);
+    a.groups = groups;
+    a.cpg = a.c / groups;
+    a.eps = eps;
+    a.chain = make_chain(chain);
+    const long long items = static_cast<long long>(groups) * x->ne[3];
+    // Slices: the GPU several times over, at least 16 positions a thread row.
+    const int rpp = kNormThreads / a.cpg;
+    const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
+    const long long most = std::max<long long>(1, a.positions / (16LL * rpp));
+    a.slices = static_cast<int>(std::min(want, most));
+    a.per = static_cast<int>((a.positions + a.slices - 1) / a.slices);
+    a.partial = partial_buffer(static_cast<size_t>(items * a.slices * 2));
+    if (!a.partial) return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: partial sums");
+    const unsigned grid = static_cast<unsigned>(items * a.slices);
+    nhwc_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 0);
+    nhwc_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 1);
+    nhwc_apply_kernel<<<grid, kNormThreads, 0, st>>>(a);
+    count_launch(3);
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+}  // namespace
+}  // namespace sdb
+
 extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps,
                               const sdb_chain* chain, void* stream) {
+    if (f32(x) && f32(dst) && same_shape(x, dst) && groups > 0 && channels_last(x) && channels_last(dst)) {
+        if (x->ne[2] % groups != 0 || x->ne[2] / groups > kNormThreads || !uniform_chain(chain))
+            return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: channels-last needs C % groups == 0 and a per-channel chain");
+        if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))
+            return fail(SDB_INVALID, "sdb_group_norm: invalid chain");
+        return group_norm_nhwc(x, dst, groups, eps, chain, static_cast<cudaStream_t>(stream));
+    }
     if (!f32(x) || !f32(dst) || !contiguous(x) || !same_shape(x, dst) || groups <= 0)
         return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: not supported");
     if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))

@@ -38,6 +38,7 @@ EXPORTS = [
     "sdb_conv2d_supported", "sdb_conv2d", "sdb_attention_supported", "sdb_attention",
     "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
+    "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step",
 ]
 
 
@@ -98,6 +99,11 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_device_status": (ctypes.c_uint, [i]),
         "sdb_last_error": (ctypes.c_char_p, []),
         "sdb_launch_count": (ctypes.c_uint64, []),
+        "sdb_concat": (i, [T, T, T, ctypes.c_int32, vp]),
+        "sdb_upscale_nearest": (i, [T, T, vp]),
+        "sdb_timestep_embedding": (i, [T, T, ctypes.c_int32, ctypes.c_int32, vp]),
+        "sdb_euler_cfg_step": (i, [vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                   ctypes.c_float, vp]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(lib, name)
@@ -395,3 +401,94 @@ def launch_count() -> int:
 
 def token_downsampling(width: int, height: int) -> int:
     return int(load().sdb_token_downsampling(width, height))
+
+
+# ---------------------------------------------------------------- channels-last images
+
+def describe_nhwc(t) -> Tensor:
+    """A contiguous (N, H, W, C) FP32 tensor as the ggml image [W, H, C, N] it holds (channels-last strides)."""
+    n, h, w, c = t.shape
+    es = t.element_size()
+    return describe(t, [w, h, c, n], [c * es, w * c * es, es, h * w * c * es])
+
+
+def conv2d_nhwc(w, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1), out=None, chain: Chain | None = None,
+                stream=None):
+    """ggml_conv_2d_direct on channels-last images: w (OC, IC, KH, KW), x (N, H, W, IC) -> (N, OH, OW, OC)."""
+    import torch
+
+    lib = load()
+    oc, _, kh, kw = w.shape
+    n, h, wd, _ = x.shape
+    oh = conv_out_size(h, kh, stride[1], padding[1], dilation[1])
+    ow = conv_out_size(wd, kw, stride[0], padding[0], dilation[0])
+    if out is None:
+        out = torch.empty(n, oh, ow, oc, dtype=torch.float32, device=x.device)
+    params = (ctypes.c_int32 * 6)(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1])
+    _guard_weight(w)
+    _check(lib.sdb_conv2d(describe(w), describe_nhwc(x), describe_nhwc(out), params, _chain_ptr(chain),
+                          ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def channel_operand(t):
+    """ggml strides of a per-channel operand (C,) for a channels-last image output: broadcast over W, H, N."""
+    return [0, 0, 1, 0]
+
+
+def group_norm_nhwc(x, groups: int, eps: float, out=None, chain: Chain | None = None, stream=None):
+    """GGML_OP_GROUP_NORM on a channels-last image (N, H, W, C), C % groups == 0."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib.sdb_group_norm(describe_nhwc(x), describe_nhwc(out), groups, ctypes.c_float(eps), _chain_ptr(chain),
+                              ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def concat_channels_nhwc(a, b, out=None, stream=None):
+    """GGML_OP_CONCAT along C of channels-last images (N, H, W, Ca) and (N, H, W, Cb)."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty(*a.shape[:3], a.shape[3] + b.shape[3], dtype=torch.float32, device=a.device)
+    _check(lib.sdb_concat(describe_nhwc(a), describe_nhwc(b), describe_nhwc(out), 2,
+                          ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def upscale_nearest_nhwc(x, factor: int = 2, out=None, stream=None):
+    """GGML_OP_UPSCALE (nearest) of a channels-last image by an integer factor."""
+    import torch
+
+    lib = load()
+    n, h, w, c = x.shape
+    if out is None:
+        out = torch.empty(n, h * factor, w * factor, c, dtype=torch.float32, device=x.device)
+    _check(lib.sdb_upscale_nearest(describe_nhwc(x), describe_nhwc(out), ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def timestep_embedding(t, dim: int, max_period: int = 10000, out=None, stream=None):
+    """GGML_OP_TIMESTEP_EMBEDDING: t (N,) FP32 -> (N, dim) = [cos(t f) | sin(t f)]."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty(t.shape[0], dim, dtype=torch.float32, device=t.device)
+    _check(lib.sdb_timestep_embedding(describe(t), describe(out), dim, max_period,
+                                      ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def euler_cfg_step(eps, x, x_in, cfg: float, sigma: float, sigma_next: float, c_in_next: float, stream=None):
+    """x += (sigma_next - sigma) (eps_u + cfg (eps_c - eps_u)); x_in[0] = x_in[1] = x c_in_next (eps = [eps_u, eps_c])."""
+    lib = load()
+    _check(lib.sdb_euler_cfg_step(ctypes.c_void_p(eps.data_ptr()), ctypes.c_void_p(x.data_ptr()),
+                                  ctypes.c_void_p(x_in.data_ptr() if x_in is not None else 0),
+                                  ctypes.c_int64(x.numel()), ctypes.c_float(cfg), ctypes.c_float(sigma),
+                                  ctypes.c_float(sigma_next), ctypes.c_float(c_in_next),
+                                  ctypes.c_void_p(_stream_ptr(stream))))
