@@ -10,6 +10,7 @@
 
 #include "../../include/sdb.h"
 #include "gemm.cuh"
+#include "gemm_wide.cuh"
 #include "runtime.cuh"
 #include "split.cuh"
 #include "store.cuh"
@@ -78,6 +79,83 @@ void choose_ksplit(GemmArgs& a, int tiles, int wmode) {
     const int want = std::max(1, std::min((sms + tiles - 1) / tiles, a.kblocks / 8));
     a.per_split = (a.kblocks + want - 1) / want;
     a.ksplit = (a.kblocks + a.per_split - 1) / a.per_split;
+}
+
+// A 2-D FP32 map for the epilogue's TMA stores: `cols` x `rows` with rows
+// `ld` floats apart, boxes of 32 rows x box_cols (32: 128-byte swizzle for the
+// 128-wide kernel; 16: 64-byte swizzle for the wide kernel).
+bool store_map(CUtensorMap* map, void* base, long long cols, long long rows, long long ld, int box_cols) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
+    const uint32_t box[2] = {static_cast<uint32_t>(box_cols), 32};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                             box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) == CUDA_SUCCESS;
+}
+
+// Tile width of the wide kernel for N output columns (gated: N of the output,
+// 2N of the product) over tiles_m row tiles: the k-block's shared-memory bytes
+// per tile (MMA operand reads of the hi and lo products plus the TMA writes)
+// times the tiles each SM must take.  0 when the 128-wide kernel is to run.
+int choose_wide_bn(int64_t n, int tiles_m, bool gated) {
+    const int64_t forced = tuning().block_n;
+    if (forced == 128 && !gated) return 0;
+    const int64_t cols = gated ? 2 * n : n;
+    const int sms = current_sm_count();
+    int best = 0;
+    double best_cost = 0.0;
+    for (int bn : {256, 192, 128}) {
+        if (gated && bn == 192) continue;
+        if (forced == 256 && bn != 256) continue;
+        const int64_t tiles_n = (cols + bn - 1) / bn;
+        const int64_t waves = (tiles_m * tiles_n + sms - 1) / sms;
+        const double kb_bytes = 2.0 * (16384 + bn * 128) + 32768 + bn * 128;
+        const double cost = static_cast<double>(waves) * kb_bytes * (tiles_m * tiles_n > sms ? 1.0 : 1.0);
+        if (best == 0 || cost < best_cost) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+template <int MODE, bool GATED, int BN>
+int launch_wide_bn(const CUtensorMap& amap, const CUtensorMap& wmap, const CUtensorMap& ymap, GemmArgs a,
+                   cudaStream_t st) {
+    using S = WideShape<BN>;
+    auto kern = gemm_wide_kernel<MODE, GATED, BN>;
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
+    const long long items = static_cast<long long>(a.tiles_m) * a.tiles_n * a.ksplit;
+    if (items >= (1LL << 31)) return fail(SDB_NOT_SUPPORTED, "gemm: too many tiles");
+    a.items = static_cast<int>(items);
+    const int grid = static_cast<int>(std::min<long long>(items, current_sm_count()));
+    CUtensorMap pmap;
+    if (a.ksplit > 1) {
+        const long long rows = static_cast<long long>(a.ksplit) * a.tiles_m * kBM;
+        if (!store_map(&pmap, a.part, a.part_ld, rows, a.part_ld, 16))
+            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the partial sums");
+    }
+    kern<<<grid, kWideThreads, S::kSmemBytes, st>>>(amap, wmap, a.ksplit > 1 ? pmap : ymap, a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    if (a.ksplit > 1) {
+        const long long total = static_cast<long long>(a.tiles_m) * kBM * a.n;
+        const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
+        count_launch();
+        SDB_CUDA(cudaGetLastError());
+    }
+    return SDB_OK;
+}
+
+template <int MODE>
+int launch_wide(const CUtensorMap& amap, const Packed& p, bool gated, int bn, const CUtensorMap& ymap,
+                const GemmArgs& a, cudaStream_t st) {
+    if (gated)
+        return bn == 256 ? launch_wide_bn<MODE, true, 256>(amap, p.map128, ymap, a, st)
+                         : launch_wide_bn<MODE, true, 128>(amap, p.map64, ymap, a, st);
+    if (bn == 256) return launch_wide_bn<MODE, false, 256>(amap, p.map256, ymap, a, st);
+    if (bn == 192) return launch_wide_bn<MODE, false, 192>(amap, p.map192, ymap, a, st);
+    return launch_wide_bn<MODE, false, 128>(amap, p.map128, ymap, a, st);
 }
 
 // Bytes of split-K partial sums: [ksplit][tiles * 128][npad].
@@ -158,8 +236,10 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
                          : packed_weights(w, Layout::linear, n, k, 0, 0, st, &p);
     if (rc != SDB_OK) return rc;
     const int wmode = gated ? kWeightGated : p->split ? kWeightSplit : kWeightHalf;
-    const int bn = wmode == kWeightGated ? 64 : 128;
     const int tiles = static_cast<int>((m + kBM - 1) / kBM);
+    // FP16 weights take the wide kernel (tile width by choose_wide_bn); FP32 weights the 128-wide one.
+    const int wide_bn = wmode == kWeightSplit ? 0 : choose_wide_bn(n, tiles, gated);
+    const int bn = wide_bn ? (gated ? wide_bn / 2 : wide_bn) : (wmode == kWeightGated ? 64 : 128);
 
     GemmArgs a{};
     a.m = static_cast<int>(m);
@@ -196,13 +276,12 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     // The output by TMA stores when its rows are 16-byte aligned runs.
     CUtensorMap ymap{};
     a.store = kStoreDirect;
-    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ynb[0] == 1 && a.ynb[1] == n) {
-        const uint64_t ydims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(m)};
-        const uint64_t ystrides[1] = {static_cast<uint64_t>(n) * 4};
-        const uint32_t ybox[2] = {32, 32};
-        if (encode_tensor_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydims, ystrides, ybox,
-                              CU_TENSOR_MAP_SWIZZLE_128B) == CUDA_SUCCESS)
-            a.store = kStoreTma;
+    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ynb[0] == 1 && a.ynb[1] == n &&
+        store_map(&ymap, a.y, n, m, n, wide_bn ? 16 : 32))
+        a.store = kStoreTma;
+    if (wide_bn) {
+        a.tiles_n = static_cast<int>((n + bn - 1) / bn);
+        return launch_wide<kModeLinear>(amap, *p, gated, wide_bn, ymap, a, st);
     }
     return dispatch<kModeLinear>(amap, *p, wmode, ymap, a, st);
 }
@@ -301,6 +380,8 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (!conv_tiles(g)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: tiling");
     const int tiles = g.tw * g.th * g.tn;
     const int wmode = p->split ? kWeightSplit : kWeightHalf;
+    const int wide_bn = wmode == kWeightSplit ? 0 : choose_wide_bn(oc, tiles, false);
+    const int bn = wide_bn ? wide_bn : 128;
     a.m = 0;
     a.kblocks = static_cast<int>(p->kpad / kBK);
     a.n = static_cast<int>(oc);
@@ -310,7 +391,7 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     a.tiles_m = tiles;
     a.store = kStoreDirect;
     set_out(a, dst, chain);
-    choose_ksplit(a, tiles * static_cast<int>((oc + 127) / 128), wmode);
+    choose_ksplit(a, tiles * static_cast<int>((oc + bn - 1) / bn), wmode);
 
     // Workspace: the image split and channels-last, [2N][H][W][cp8] (hi images,
     // then lo), then any partial sums.
@@ -318,8 +399,8 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     const int64_t W = x->ne[0], H = x->ne[1], N = x->ne[3];
     const size_t a_bytes = static_cast<size_t>(round_up(2 * N * H * W * cp8 * 2, 256));
     void* ws = nullptr;
-    if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, oc, 128), &ws); s != SDB_OK) return s;
-    set_partials(a, ws, a_bytes, tiles, 128);
+    if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, oc, bn), &ws); s != SDB_OK) return s;
+    set_partials(a, ws, a_bytes, tiles, bn);
     if (channels_last(x)) {
         // Already channels-last: the split is a split of rows (positions).
         const long long ne[4] = {ic, W, H, N};
@@ -349,13 +430,12 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     // A channels-last output whose tiles are whole runs of 128 positions leaves by TMA stores.
     CUtensorMap ymap{};
     const bool whole_tiles = g.owt == g.ow && g.owt * g.oht * g.nt == kBM && g.oh % g.oht == 0 && g.n % g.nt == 0;
-    if (channels_last(dst) && whole_tiles && oc % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0) {
-        const uint64_t ydims[2] = {static_cast<uint64_t>(oc), static_cast<uint64_t>(g.n) * g.oh * g.ow};
-        const uint64_t ystrides[1] = {static_cast<uint64_t>(oc) * 4};
-        const uint32_t ybox[2] = {32, 32};
-        if (encode_tensor_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydims, ystrides, ybox,
-                              CU_TENSOR_MAP_SWIZZLE_128B) == CUDA_SUCCESS)
-            a.store = kStoreTma;
+    if (channels_last(dst) && whole_tiles && oc % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+        store_map(&ymap, a.y, oc, static_cast<long long>(g.n) * g.oh * g.ow, oc, wide_bn ? 16 : 32))
+        a.store = kStoreTma;
+    if (wide_bn) {
+        a.tiles_n = static_cast<int>((oc + bn - 1) / bn);
+        return launch_wide<kModeConv>(amap, *p, false, wide_bn, ymap, a, st);
     }
     return dispatch<kModeConv>(amap, *p, wmode, ymap, a, st);
 }

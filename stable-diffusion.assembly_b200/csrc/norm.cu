@@ -23,6 +23,7 @@
 
 #include "../../include/sdb.h"
 #include "chain.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 
 namespace sdb {
@@ -286,107 +287,273 @@ __global__ void __launch_bounds__(kResidentThreads) group_resident_kernel(const 
 
 // ---- channels-last (NHWC) images -----------------------------------------
 //
-// x and y are [N][P positions][C] with C % groups == 0: a group is cpg
-// contiguous channels of every position.  Each (image, group) is cut into
-// slices of positions, one CTA a slice, so even one image's 32 groups fill
-// the GPU; a thread keeps one channel of the group (cpg threads a position),
-// so its chain operands are loaded once.  Three passes over x as the
-// reference's algorithm reads it: sums -> mean, centred sums -> variance,
-// then the normalisation and the chain; the double partial sums of the
-// slices meet in global memory between the launches.
+// x and y are [N][P positions][C], C % groups == 0 and C % 4 == 0: a group is
+// cpg contiguous channels of every position.  One cooperative launch does the
+// reference's three passes (norm.cc:100-140): every CTA takes a chunk of one
+// image's positions -- whole rows, read with float4 loads and, when they fit,
+// kept in shared memory -- and the CTAs of an image exchange their groups'
+// double partial sums through global memory at two grid barriers: sums ->
+// mean, centred sums -> variance, then the normalisation with the chain.  x is
+// read from HBM once (the chunks that do not fit re-read it from L2).
+constexpr int kClThreads = 512;
+constexpr int kClMaxCols = 2;     // float4 columns a thread may own: C <= 2 * 4 * 512
+constexpr int kClMaxGroups = 128;
+constexpr int kClMaxChannels = 3072;
+constexpr int kClMaxCsum = kClMaxChannels;   // channel sums of the CTA's row phases (rpp * C <= 4 * threads)
+constexpr int kClSmemBudget = 160 * 1024;
+
 struct NhwcArgs {
     const float* x;
     float* y;
-    long long positions;        // H * W
-    int c, groups, cpg;
-    int slices;                 // CTAs per (image, group)
-    int per;                    // positions per slice
+    int positions;              // H * W
+    int c, c4;                  // channels, channels / 4
+    int groups, cpg;
+    int cpi;                    // CTAs per image
+    int per;                    // positions per CTA
+    int rpp;                    // rows (positions) a pass of the CTA covers
+    int resident;               // 1: the CTA's rows stay in shared memory between the passes
     float eps;
-    double* partial;            // [images * groups][slices][2]
+    double* partial;            // [2][images][cpi][groups]
+    unsigned* bar;              // the grid barrier's counter, zero at launch
+    unsigned* err;
     Chain chain;
 };
 
-__device__ __forceinline__ void nhwc_slice(const NhwcArgs& a, int& item, int& slice, long long& p0, long long& p1,
-                                           int& ch, int& prow, int& rows_per_pass) {
-    item = blockIdx.x / a.slices;
-    slice = blockIdx.x - item * a.slices;
-    p0 = static_cast<long long>(slice) * a.per;
-    p1 = min(a.positions, p0 + a.per);
-    rows_per_pass = blockDim.x / a.cpg;
-    ch = threadIdx.x % a.cpg;
-    prow = threadIdx.x / a.cpg;
+// This thread's float4 columns and first row of a pass.
+__device__ __forceinline__ int cl_columns(const NhwcArgs& a, int (&col)[kClMaxCols], int& r0) {
+    int n = 0;
+    if (a.c4 <= kClThreads) {
+        r0 = threadIdx.x / a.c4;
+        col[0] = threadIdx.x - r0 * a.c4;
+        n = r0 < a.rpp ? 1 : 0;
+    } else {
+        r0 = 0;
+        for (int j = threadIdx.x; j < a.c4 && n < kClMaxCols; j += kClThreads) col[n++] = j;
+    }
+    return n;
 }
 
-__global__ void __launch_bounds__(kNormThreads) nhwc_sum_kernel(const NhwcArgs a, int phase) {
-    __shared__ double scratch[32];
-    __shared__ float mean_s;
-    int item, slice, ch, prow, rpp;
-    long long p0, p1;
-    nhwc_slice(a, item, slice, p0, p1, ch, prow, rpp);
-    const int i3 = item / a.groups, g = item - i3 * a.groups;
-    const long long count = a.positions * a.cpg;
-    if (phase == 1) {
+// All CTAs of the grid meet here (they are co-resident: a cooperative launch).
+// Bounded: after kWaitLimitCycles the CTA gives up, sets the timeout bit and
+// reports false.
+__device__ bool grid_barrier(unsigned* bar, unsigned target, unsigned* err) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1u);
+        int ok = 1;
+        const long long t0 = clock64();
+        for (int it = 0;; ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+            if (v >= target) break;
+            if ((it & 63) == 63 && clock64() - t0 > kWaitLimitCycles) {
+                if (err) atomicOr(err, kErrTimeout);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+// The image's per-group totals of one pass, eight threads a group, eight
+// loads in flight each.
+__device__ __forceinline__ void cl_fold(const NhwcArgs& a, const double* part, int i3, double* out) {
+    const int lanes = 8;
+    for (int base = 0; base < a.groups * lanes; base += blockDim.x) {
+        const int t = base + threadIdx.x;
+        const int g = t / lanes, k = t % lanes;
+        double s = 0.0;
+        if (g < a.groups) {
+            const double* pp = part + static_cast<long long>(i3) * a.cpi * a.groups + g;
+            int ch = k;
+            for (; ch + 7 * lanes < a.cpi; ch += 8 * lanes) {
+                double v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(pp + static_cast<long long>(ch + u * lanes) * a.groups);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s += v[u];
+            }
+            for (; ch < a.cpi; ch += lanes) s += __ldcg(pp + static_cast<long long>(ch) * a.groups);
+        }
+#pragma unroll
+        for (int o = lanes / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (g < a.groups && k == 0) out[g] = s;
+    }
+}
+
+// Chain patterns the apply pass compiles on their own: the GroupNorm's scale
+// and shift (per channel), with or without the SiLU after them.
+enum : int { kChainGeneral = 0, kChainAffine = 1, kChainAffineSilu = 2, kChainNone = 3 };
+
+template <int PATTERN>
+__device__ __forceinline__ float chain_pattern(const Chain& ch, const float (&op)[SDB_MAX_STEPS], float v) {
+    if (PATTERN == kChainNone) return v;
+    if (PATTERN == kChainAffine) return fmaf(v, op[0], op[1]);
+    if (PATTERN == kChainAffineSilu) return silu(fmaf(v, op[0], op[1]));
+    return apply_uniform(ch, op, v);
+}
+
+template <int PATTERN>
+__global__ void __launch_bounds__(kClThreads) nhwc_group_norm_kernel(const NhwcArgs a) {
+    extern __shared__ float4 tile[];                 // [per][c4] when resident
+    __shared__ double csum[kClMaxCsum];             // [row phase][channel]: the threads' sums
+    __shared__ double gsum[kClMaxGroups];
+    __shared__ double total[kClMaxGroups];
+    __shared__ float mean[kClMaxGroups], scale[kClMaxGroups];
+    const int i3 = blockIdx.x / a.cpi, chunk = blockIdx.x - i3 * a.cpi;
+    const long long p0 = static_cast<long long>(chunk) * a.per;
+    const long long p1 = min(static_cast<long long>(a.positions), p0 + a.per);
+    const long long base = static_cast<long long>(i3) * a.positions * a.c4;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x) + base;
+    float4* y4 = reinterpret_cast<float4*>(a.y) + base;
+    const long long images = gridDim.x / a.cpi;
+    double* part0 = a.partial;
+    double* part1 = a.partial + images * a.cpi * a.groups;
+    int col[kClMaxCols], r0;
+    const int ncols = cl_columns(a, col, r0);
+    const double n = static_cast<double>(a.positions) * a.cpg;
+    auto row_at = [&](long long p, int j) -> float4 {
+        return a.resident ? tile[(p - p0) * a.c4 + j] : __ldcg(x4 + p * a.c4 + j);
+    };
+    // Resident: the chunk -- one contiguous run of x -- arrives by bulk copies.
+    __shared__ uint64_t landed;
+    const uint32_t bytes = static_cast<uint32_t>((p1 - p0) * a.c4 * 16);
+    if (a.resident) {
         if (threadIdx.x == 0) {
-            double t = 0.0;
-            for (int sl = 0; sl < a.slices; ++sl) t += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2];
-            mean_s = static_cast<float>(t / static_cast<double>(count));
+            mbar_init(&landed, 1);
+            fence_barrier_init();
+            mbar_arrive_expect_tx(&landed, bytes);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(x4 + p0 * a.c4);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+                bulk_load(reinterpret_cast<uint8_t*>(tile) + off, src + off, min(32768u, bytes - off), &landed);
+        }
+        __shared__ int landed_ok, gave_up;
+        if (threadIdx.x == 0) gave_up = 0;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            landed_ok = mbar_wait(&landed, 0, &gave_up, a.err) ? 1 : 0;
+            // Gave up: the copies still land before the CTA's shared memory goes away.
+            if (!landed_ok) mbar_wait_quiet(&landed, 0, 100000000ull);
+        }
+        __syncthreads();
+        if (!landed_ok) return;
+    }
+
+    for (int phase = 0; phase < 2; ++phase) {
+        for (int k = 0; k < ncols; ++k) {
+            const int j = col[k];
+            const int g0 = 4 * j / a.cpg, g1 = (4 * j + 1) / a.cpg, g2 = (4 * j + 2) / a.cpg, g3 = (4 * j + 3) / a.cpg;
+            const float m0 = phase ? mean[g0] : 0.0f, m1 = phase ? mean[g1] : 0.0f;
+            const float m2 = phase ? mean[g2] : 0.0f, m3 = phase ? mean[g3] : 0.0f;
+            double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll 4
+            for (long long p = p0 + r0; p < p1; p += a.rpp) {
+                float4 v;
+                if (phase == 0) {
+                    v = row_at(p, j);
+                    s0 += v.x;
+                    s1 += v.y;
+                    s2 += v.z;
+                    s3 += v.w;
+                } else {
+                    v = row_at(p, j);
+                    const float d0 = v.x - m0, d1 = v.y - m1, d2 = v.z - m2, d3 = v.w - m3;
+                    s0 += static_cast<double>(d0 * d0);
+                    s1 += static_cast<double>(d1 * d1);
+                    s2 += static_cast<double>(d2 * d2);
+                    s3 += static_cast<double>(d3 * d3);
+                }
+            }
+            double* cs = csum + r0 * a.c + 4 * j;
+            cs[0] = s0;
+            cs[1] = s1;
+            cs[2] = s2;
+            cs[3] = s3;
+        }
+        __syncthreads();
+        // Each group's channels over the row phases, eight threads a group.
+        {
+            const int phases = a.c4 <= kClThreads ? a.rpp : 1;
+            const int span = phases * a.cpg;
+            for (int base = 0; base < a.groups * 8; base += blockDim.x) {
+                const int t = base + threadIdx.x;
+                const int g = t / 8, k = t % 8;
+                double v = 0.0;
+                if (g < a.groups)
+                    for (int e = k; e < span; e += 8) {
+                        const int ph = e / a.cpg, ch = g * a.cpg + (e - ph * a.cpg);
+                        v += csum[ph * a.c + ch];
+                    }
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (g < a.groups && k == 0) gsum[g] = v;
+            }
+        }
+        __syncthreads();
+        double* part = phase ? part1 : part0;
+        for (int g = threadIdx.x; g < a.groups; g += blockDim.x)
+            part[(static_cast<long long>(i3) * a.cpi + chunk) * a.groups + g] = gsum[g];
+        if (!grid_barrier(a.bar, (phase + 1) * gridDim.x, a.err)) return;
+        cl_fold(a, part, i3, total);
+        __syncthreads();
+        for (int g = threadIdx.x; g < a.groups; g += blockDim.x) {
+            if (phase == 0)
+                mean[g] = static_cast<float>(total[g] / n);
+            else
+                scale[g] = 1.0f / sqrtf(static_cast<float>(total[g] / n) + a.eps);
         }
         __syncthreads();
     }
-    const float mean = phase == 1 ? mean_s : 0.0f;
-    const float* xb = a.x + static_cast<long long>(i3) * a.positions * a.c + g * a.cpg + ch;
-    double s = 0.0;
-    if (prow < rpp) {
-#pragma unroll 4
-        for (long long p = p0 + prow; p < p1; p += rpp) {
-            const float v = __ldg(xb + p * a.c);
-            if (phase == 0) {
-                s += static_cast<double>(v);
-            } else {
-                const float d = v - mean;
-                s += static_cast<double>(d * d);
+
+    for (int k = 0; k < ncols; ++k) {
+        const int j = col[k];
+        float mu[4], sc[4], op[4][SDB_MAX_STEPS];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int g = (4 * j + e) / a.cpg;
+            mu[e] = mean[g];
+            sc[e] = scale[g];
+            channel_operands(a.chain, 4 * j + e, i3, op[e]);
+        }
+        for (long long p = p0 + r0; p < p1; p += 2LL * a.rpp) {
+            float4 v[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) v[u] = row_at(min(p + u * a.rpp, p1 - 1), j);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                v[u].x = chain_pattern<PATTERN>(a.chain, op[0], (v[u].x - mu[0]) * sc[0]);
+                v[u].y = chain_pattern<PATTERN>(a.chain, op[1], (v[u].y - mu[1]) * sc[1]);
+                v[u].z = chain_pattern<PATTERN>(a.chain, op[2], (v[u].z - mu[2]) * sc[2]);
+                v[u].w = chain_pattern<PATTERN>(a.chain, op[3], (v[u].w - mu[3]) * sc[3]);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (p + u * a.rpp >= p1) continue;
+                if (a.resident)
+                    tile[(p + u * a.rpp - p0) * a.c4 + j] = v[u];
+                else
+                    y4[(p + u * a.rpp) * a.c4 + j] = v[u];
             }
         }
     }
-    s = block_sum(s, scratch);
-    if (threadIdx.x == 0) a.partial[(static_cast<long long>(item) * a.slices + slice) * 2 + phase] = s;
-}
-
-__global__ void __launch_bounds__(kNormThreads) nhwc_apply_kernel(const NhwcArgs a) {
-    __shared__ float stats[2];
-    int item, slice, ch, prow, rpp;
-    long long p0, p1;
-    nhwc_slice(a, item, slice, p0, p1, ch, prow, rpp);
-    const int i3 = item / a.groups, g = item - i3 * a.groups;
-    const long long count = a.positions * a.cpg;
-    if (threadIdx.x == 0) {
-        double s = 0.0, q = 0.0;
-        for (int sl = 0; sl < a.slices; ++sl) {
-            s += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2];
-            q += a.partial[(static_cast<long long>(item) * a.slices + sl) * 2 + 1];
+    if (a.resident) {
+        // The normalised chunk back out by bulk copies.
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint8_t* dst = reinterpret_cast<uint8_t*>(y4 + p0 * a.c4);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+                bulk_store(dst + off, reinterpret_cast<const uint8_t*>(tile) + off, min(32768u, bytes - off));
+            bulk_commit_group();
+            bulk_wait_all();
         }
-        stats[0] = static_cast<float>(s / static_cast<double>(count));
-        stats[1] = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(count)) + a.eps);
-    }
-    __syncthreads();
-    if (prow >= rpp) return;
-    const float mean = stats[0], scale = stats[1];
-    const long long c = static_cast<long long>(g) * a.cpg + ch;
-    const long long off = static_cast<long long>(i3) * a.positions * a.c + c;
-    // The chain's operands are one value per channel (the host sends no other chain here).
-    float op[SDB_MAX_STEPS];
-    channel_operands(a.chain, c, i3, op);
-    // Four positions at a time: their loads before their stores.
-    for (long long p = p0 + prow; p < p1; p += 4LL * rpp) {
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const long long pk = min(p + k * rpp, p1 - 1);
-            v[k] = __ldg(a.x + off + pk * a.c);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (p + k * rpp < p1) a.y[off + (p + k * rpp) * a.c] = apply_uniform(a.chain, op, (v[k] - mean) * scale);
     }
 }
 
@@ -454,6 +621,64 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(const RowArgs a) {
     }
 }
 
+// One warp per row with the row in registers (rows of up to 32 * kLnPer
+// elements, contiguous): x is read from memory once, both statistics and the
+// normalisation come from the registers.
+constexpr int kLnPer = 40;   // the widest row kept in registers: 32 x 40 elements
+
+template <int kLnPer>
+__global__ void __launch_bounds__(256) norm_rows_reg_kernel(const RowArgs a) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= a.rows) return;
+    const long long i1 = row % a.ne1;
+    const long long i2 = (row / a.ne1) % a.ne2;
+    const long long i3 = row / (a.ne1 * a.ne2);
+    const float* xr = a.x + i1 * a.xnb[1] + i2 * a.xnb[2] + i3 * a.xnb[3];
+    float* yr = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3];
+    const int n = static_cast<int>(a.ne0);
+    float v[kLnPer];
+#pragma unroll
+    for (int k = 0; k < kLnPer; ++k) v[k] = lane + 32 * k < n ? __ldg(xr + lane + 32 * k) : 0.0f;
+    double s = 0.0;
+#pragma unroll
+    for (int k = 0; k < kLnPer; ++k) s += static_cast<double>(v[k]);
+    s = warp_sum(s);
+    const float mean = static_cast<float>(s / static_cast<double>(n));
+    double q = 0.0;
+#pragma unroll
+    for (int k = 0; k < kLnPer; ++k) {
+        if (lane + 32 * k < n) {
+            const float d = v[k] - mean;
+            q += static_cast<double>(d * d);
+        }
+    }
+    q = warp_sum(q);
+    const float scale = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(n)) + a.eps);
+#pragma unroll
+    for (int k = 0; k < kLnPer; ++k) v[k] = (v[k] - mean) * scale;
+    ChainRow cr;
+    row_offsets(a.chain, cr, 0, i1, i2, i3);
+#pragma unroll
+    for (int st = 0; st < SDB_MAX_STEPS; ++st) {
+        if (st >= a.chain.count) break;
+        if (a.chain.kind[st] == SDB_STEP_SILU) {
+#pragma unroll
+            for (int k = 0; k < kLnPer; ++k) v[k] = silu(v[k]);
+        } else {
+            float o[kLnPer];
+#pragma unroll
+            for (int k = 0; k < kLnPer; ++k)
+                o[k] = __ldg(a.chain.operand[st] + cr.off[st] + min(lane + 32 * k, n - 1) * a.chain.nb[st][0]);
+#pragma unroll
+            for (int k = 0; k < kLnPer; ++k) v[k] = a.chain.kind[st] == SDB_STEP_ADD ? v[k] + o[k] : v[k] * o[k];
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kLnPer; ++k)
+        if (lane + 32 * k < n) yr[(lane + 32 * k) * a.ynb[0]] = v[k];
+}
+
 bool f32(const sdb_tensor* t) { return t && t->type == SDB_TYPE_F32 && t->data; }
 
 bool contiguous(const sdb_tensor* t) {
@@ -511,31 +736,86 @@ bool uniform_chain(const sdb_chain* c) {
     return true;
 }
 
+// Scratch of the channels-last path (the grid barrier's counter, then the
+// partial sums), grown on demand, per thread and device, outside stream
+// capture only.
+double* cl_buffer(size_t count, cudaStream_t st) {
+    static thread_local double* buf = nullptr;
+    static thread_local size_t cap = 0;
+    static thread_local int dev = -1;
+    int d = 0;
+    cudaGetDevice(&d);
+    if (count > cap || d != dev) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+        if (buf && d == dev) {
+            cudaStreamSynchronize(st);
+            cudaFree(buf);
+        }
+        buf = nullptr;
+        cap = 0;
+        if (cudaMalloc(&buf, count * sizeof(double)) != cudaSuccess) return nullptr;
+        cap = count;
+        dev = d;
+    }
+    return buf;
+}
+
+template <int PATTERN>
+int launch_nhwc(const NhwcArgs& a, int grid, size_t smem, cudaStream_t st) {
+    auto kern = nhwc_group_norm_kernel<PATTERN>;
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kClSmemBudget));
+    int per_sm = 0;
+    SDB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kClThreads, smem));
+    if (per_sm * current_sm_count() < grid) return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: grid not co-resident");
+    void* args[] = {const_cast<NhwcArgs*>(&a)};
+    SDB_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(grid), dim3(kClThreads), args, smem, st));
+    return SDB_OK;
+}
+
 int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps, const sdb_chain* chain,
                     cudaStream_t st) {
     NhwcArgs a{};
     a.x = static_cast<const float*>(x->data);
     a.y = static_cast<float*>(dst->data);
-    a.positions = x->ne[0] * x->ne[1];
+    a.positions = static_cast<int>(x->ne[0] * x->ne[1]);
     a.c = static_cast<int>(x->ne[2]);
+    a.c4 = a.c / 4;
     a.groups = groups;
     a.cpg = a.c / groups;
     a.eps = eps;
     a.chain = make_chain(chain);
-    const long long items = static_cast<long long>(groups) * x->ne[3];
-    // Slices: the GPU several times over, at least 16 positions a thread row.
-    const int rpp = kNormThreads / a.cpg;
-    const long long want = std::max<long long>(1, (4LL * current_sm_count() + items - 1) / items);
-    const long long most = std::max<long long>(1, a.positions / (16LL * rpp));
-    a.slices = static_cast<int>(std::min(want, most));
-    a.per = static_cast<int>((a.positions + a.slices - 1) / a.slices);
-    a.partial = partial_buffer(static_cast<size_t>(items * a.slices * 2));
-    if (!a.partial) return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: partial sums");
-    const unsigned grid = static_cast<unsigned>(items * a.slices);
-    nhwc_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 0);
-    nhwc_sum_kernel<<<grid, kNormThreads, 0, st>>>(a, 1);
-    nhwc_apply_kernel<<<grid, kNormThreads, 0, st>>>(a);
-    count_launch(3);
+    a.err = device_error_word();
+    a.rpp = a.c4 <= kClThreads ? kClThreads / a.c4 : 1;
+    const int images = static_cast<int>(x->ne[3]);
+    const int sms = current_sm_count();
+    // CTAs: about one per SM over all images, at least two passes of rows each;
+    // the rows stay in shared memory when a CTA's share fits.
+    const int most = std::max(1, a.positions / (2 * a.rpp));
+    a.cpi = std::max(1, std::min(most, (sms + images - 1) / images));
+    a.per = (a.positions + a.cpi - 1) / a.cpi;
+    a.cpi = (a.positions + a.per - 1) / a.per;
+    const size_t tile = static_cast<size_t>(a.per) * a.c * 4;
+    a.resident = tile <= static_cast<size_t>(kClSmemBudget) ? 1 : 0;
+    const size_t smem = a.resident ? tile : 0;
+    const int grid = images * a.cpi;
+    double* buf = cl_buffer(2 + 2 * static_cast<size_t>(grid) * groups, st);
+    if (!buf) return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: scratch");
+    a.bar = reinterpret_cast<unsigned*>(buf);
+    a.partial = buf + 2;
+    SDB_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), st));
+    // The chain's pattern: mul then add (then SiLU) -- the GroupNorm's affine -- compiles alone.
+    const Chain& c = a.chain;
+    int rc;
+    if (c.count == 0)
+        rc = launch_nhwc<kChainNone>(a, grid, smem, st);
+    else if (c.count >= 2 && c.kind[0] == SDB_STEP_MUL && c.kind[1] == SDB_STEP_ADD &&
+             (c.count == 2 || (c.count == 3 && c.kind[2] == SDB_STEP_SILU)))
+        rc = c.count == 2 ? launch_nhwc<kChainAffine>(a, grid, smem, st) : launch_nhwc<kChainAffineSilu>(a, grid, smem, st);
+    else
+        rc = launch_nhwc<kChainGeneral>(a, grid, smem, st);
+    if (rc != SDB_OK) return rc;
+    count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
 }
@@ -546,8 +826,12 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
 extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps,
                               const sdb_chain* chain, void* stream) {
     if (f32(x) && f32(dst) && same_shape(x, dst) && groups > 0 && channels_last(x) && channels_last(dst)) {
-        if (x->ne[2] % groups != 0 || x->ne[2] / groups > kNormThreads || !uniform_chain(chain))
-            return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: channels-last needs C % groups == 0 and a per-channel chain");
+        if (x->ne[2] % groups != 0 || x->ne[2] % 4 != 0 || x->ne[2] > kClMaxChannels ||
+            x->ne[0] * x->ne[1] > (1LL << 30) || x->ne[3] > 148 || groups > kClMaxGroups || !uniform_chain(chain) ||
+            (reinterpret_cast<uintptr_t>(x->data) & 15) || (reinterpret_cast<uintptr_t>(dst->data) & 15))
+            return fail(SDB_NOT_SUPPORTED,
+                        "sdb_group_norm: channels-last needs C % groups == 0, C % 4 == 0, C <= 3072, aligned "
+                        "images and a per-channel chain");
         if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect))
             return fail(SDB_INVALID, "sdb_group_norm: invalid chain");
         return group_norm_nhwc(x, dst, groups, eps, chain, static_cast<cudaStream_t>(stream));
@@ -612,7 +896,18 @@ extern "C" int sdb_norm(const sdb_tensor* x, const sdb_tensor* dst, float eps, c
     a.eps = eps;
     a.chain = make_chain(chain);
     const long long threads = a.rows * 32;
-    norm_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(a);
+    const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+    const int per = static_cast<int>((a.ne0 + 31) / 32);
+    if (a.xnb[0] == 1 && per <= 8)
+        norm_rows_reg_kernel<8><<<blocks, 256, 0, st>>>(a);
+    else if (a.xnb[0] == 1 && per <= 12)
+        norm_rows_reg_kernel<12><<<blocks, 256, 0, st>>>(a);
+    else if (a.xnb[0] == 1 && per <= 20)
+        norm_rows_reg_kernel<20><<<blocks, 256, 0, st>>>(a);
+    else if (a.xnb[0] == 1 && per <= kLnPer)
+        norm_rows_reg_kernel<kLnPer><<<blocks, 256, 0, st>>>(a);
+    else
+        norm_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;

@@ -179,6 +179,14 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
         : "memory");
 }
 
+// A contiguous run of shared memory to global memory (bytes and both
+// addresses multiples of 16), in this thread's bulk group.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+                 "r"(smem_u32(smem_src)), "r"(bytes)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 // Allocates `ncols` columns of tensor memory (a power of two >= 32) for the

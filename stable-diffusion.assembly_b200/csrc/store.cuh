@@ -34,6 +34,8 @@ struct Packed {
     bool split = false;       // FP32 weights: hi rows then lo rows
     CUtensorMap map64{};      // box {64, 64}
     CUtensorMap map128{};     // box {64, 128}
+    CUtensorMap map192{};     // box {64, 192}
+    CUtensorMap map256{};     // box {64, 256}
     cudaEvent_t ready = nullptr;
     bool done = false;        // the packing was seen complete
     bool owned_by_store = true;

@@ -78,3 +78,28 @@ def test_group_norm_matches_double(cuda):
     out = sdb.group_norm(cuda_tensor(x, cuda), 32, 1e-5)
     exact = oracle.group_norm_exact(x, 32, 1e-5)
     assert np.abs(host(out) - exact).max() <= 2e-6 * np.abs(exact).max()
+
+
+@pytest.mark.parametrize("shape,groups", [
+    ((2, 64, 64, 320), 32),    # the UNet's first level, CFG batch 2
+    ((2, 32, 32, 640), 32),
+    ((1, 8, 8, 1280), 32),
+    ((2, 16, 16, 2560), 32),   # decoder concatenations
+    ((1, 5, 7, 96), 8),        # ragged positions
+])
+def test_group_norm_channels_last(cuda, shape, groups):
+    """Channels-last images (N, H, W, C): the same algorithm, the same bound."""
+    import sdb
+
+    g = rng(11)
+    n, h, w, c = shape
+    x = oracle.uniform(g, shape, 3.0) + np.float32(0.5)
+    gamma = oracle.uniform(g, (c,), 1.0)
+    beta = oracle.uniform(g, (c,), 1.0)
+    chain = sdb.Chain().mul(cuda_tensor(gamma, cuda), [0, 0, 1, 0]).add(cuda_tensor(beta, cuda), [0, 0, 1, 0]).silu()
+    out = canary_like(shape, cuda)
+    sdb.group_norm_nhwc(cuda_tensor(x, cuda), groups, 1e-5, out=out, chain=chain)
+    nchw = np.ascontiguousarray(x.transpose(0, 3, 1, 2))
+    want = oracle.apply_chain(oracle.group_norm_ref(nchw, groups, 1e-5),
+                              [("mul", gamma.reshape(1, c, 1, 1)), ("add", beta.reshape(1, c, 1, 1)), ("silu", None)])
+    close(host(out).transpose(0, 3, 1, 2), want)
