@@ -413,6 +413,348 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnAr
     }
 }
 
+// ---- two softmax warpgroups, one query row a thread ----------------------
+//
+// For heads up to 128 dims whose accumulators fit tensor memory twice over.
+// Warps 2-5 (warpgroup 0) take the key blocks j = 0, 2, 4, ...; warps 6-9
+// (warpgroup 1) j = 1, 3, 5, ...: each thread owns one query row of its
+// warpgroup's blocks -- all BK keys of it, so a block's maximum needs no
+// exchange -- and each warpgroup keeps its own online softmax (reference
+// maximum, double row sum, output in registers) and its own output
+// accumulator in tensor memory.  A block's product P V is taken into the
+// registers at the warpgroup's next block, so it runs under that block's
+// softmax.  The two streams merge once at the end: m = max(m0, m1),
+// O = O0 2^(m0 - m) + O1 2^(m1 - m), l likewise, then O / l with the chain.
+// A block's weights are summed in FP32 as a pairwise tree (at most log2(BK)
+// roundings), blocks in double.
+struct AttnWgLayout {
+    int q_hi, q_lo, stage0, stage_bytes, k_lo, v_hi, v_lo, p0, p_bytes, merge_o, merge_m, merge_l, bars, total;
+    __host__ __device__ AttnWgLayout(int dp, int dvc, int bk) {
+        const int qb = kAttnQ * dp * 2;
+        q_hi = 0;
+        q_lo = qb;
+        stage0 = 2 * qb;
+        const int kb = bk * dp * 2, vb = bk * dvc * 2;
+        k_lo = kb;
+        v_hi = 2 * kb;
+        v_lo = 2 * kb + vb;
+        stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
+        p_bytes = 2 * kAttnQ * bk * 2;                     // hi then lo plane of one warpgroup's P
+        p0 = stage0 + kStagesKV * stage_bytes;           // [2] buffers
+        merge_o = p0 + 2 * p_bytes;                      // [128][dvc] floats of warpgroup 1
+        merge_m = merge_o + kAttnQ * dvc * 4;            // [128] floats
+        merge_l = merge_m + kAttnQ * 4;                  // [128] doubles
+        bars = merge_l + kAttnQ * 8;
+        total = bars + 512;
+    }
+};
+
+template <int BK, int NSC, int DVC>
+__global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const AttnArgs a) {
+    constexpr int OCH = DVC / 16;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const AttnWgLayout L(a.dp, DVC, BK);
+    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [3]
+    uint64_t* kv_empty = kv_full + kStagesKV;                        // [3]
+    uint64_t* q_full = kv_empty + kStagesKV;
+    uint64_t* s_full = q_full + 1;    // [2] per S buffer (block parity)
+    uint64_t* p_full = s_full + 2;    // [2] per warpgroup
+    uint64_t* o_full = p_full + 2;    // [2] per warpgroup
+    uint64_t* merged = o_full + 2;
+    uint64_t* drain = merged + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* merge_o = reinterpret_cast<float*>(smem + L.merge_o);
+    float* merge_m = reinterpret_cast<float*>(smem + L.merge_m);
+    double* merge_l = reinterpret_cast<double*>(smem + L.merge_l);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kAttnQ;
+    const int head = blockIdx.y / a.dv_chunks;
+    const int dv0 = (blockIdx.y - head * a.dv_chunks) * DVC;
+    const int batch = blockIdx.z;
+    const int khead = head / (a.h / a.hk);
+    const int nblk = (a.lk + BK - 1) / BK;
+    constexpr int sbuf = (NSC + 1) * BK;              // tensor-memory columns of one S buffer
+    const uint32_t base = smem_u32(smem);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesKV; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_full[i], 1);
+        }
+        mbar_init(merged, 4);
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto t_o_hi = [&](int wg) { return tmem + 2 * sbuf + wg * 2 * DVC; };
+    auto t_o_lo = [&](int wg) { return tmem + 2 * sbuf + wg * 2 * DVC + DVC; };
+
+    if (warp == 0) {
+        // ------------------------------------------------ bulk-copy producer
+        if (lane == 0) {
+            const uint32_t qbytes = kAttnQ * a.dp * 2;
+            const uint32_t kbytes = BK * a.dp * 2, vbytes = BK * DVC * 2;
+            const uint8_t* qt = a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + blockIdx.x) * qbytes;
+            mbar_arrive_expect_tx(q_full, 2 * qbytes);
+            bulk_load(smem + L.q_hi, qt, qbytes, q_full);
+            bulk_load(smem + L.q_lo, qt + a.q_plane, qbytes, q_full);
+            const long long ktile0 = static_cast<long long>(batch * a.hk + khead) * a.ntk;
+            int issued = 0;
+            for (int j = 0; j < nblk; ++j) {
+                const int s = j % kStagesKV;
+                if (!mbar_wait(&kv_empty[s], ((j / kStagesKV) & 1) ^ 1, abort, a.err)) break;
+                uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kbytes + 2 * vbytes);
+                const uint8_t* kt = a.ks + (ktile0 + j) * kbytes;
+                const uint8_t* vt = a.vs + (ktile0 + j) * static_cast<long long>(BK) * a.dvs * 2 +
+                                    static_cast<long long>(dv0 / 8) * BK * 16;
+                bulk_load(st, kt, kbytes, &kv_full[s]);
+                bulk_load(st + L.k_lo, kt + a.k_plane, kbytes, &kv_full[s]);
+                bulk_load(st + L.v_hi, vt, vbytes, &kv_full[s]);
+                bulk_load(st + L.v_lo, vt + a.v_plane, vbytes, &kv_full[s]);
+                ++issued;
+            }
+            if (*abort) {
+                mbar_wait_quiet(q_full, 0, 100000000ull);
+                for (int j = (issued > kStagesKV ? issued - kStagesKV : 0); j < issued; ++j)
+                    mbar_wait_quiet(&kv_full[j % kStagesKV], (j / kStagesKV) & 1, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16_f32(kAttnQ, BK);
+            const uint32_t id_pv = idesc_f16_f32_bmajor(kAttnQ, DVC, 1);
+            const uint32_t q_lbo = kAttnQ * 16, k_lbo = BK * 16, kv_sbo = 128, p_sbo = BK * 16;
+            auto issue_s = [&](int j) {
+                const int s = j % kStagesKV;
+                const uint32_t st = base + L.stage0 + s * L.stage_bytes;
+                const uint32_t sb = tmem + (j & 1) * sbuf;
+                for (int kk = 0; kk < a.dp / 16; ++kk) {
+                    const uint64_t qh = desc_noswizzle(base + L.q_hi + kk * 2 * q_lbo, q_lbo, 128);
+                    const uint64_t ql = desc_noswizzle(base + L.q_lo + kk * 2 * q_lbo, q_lbo, 128);
+                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, kv_sbo);
+                    const uint64_t kl = desc_noswizzle(st + L.k_lo + kk * 2 * k_lbo, k_lbo, kv_sbo);
+                    mma_f16(sb + (kk >> 2) * BK, qh, kh, id_s, (kk & 3) ? 1u : 0u);
+                    mma_f16(sb + NSC * BK, qh, kl, id_s, kk > 0 ? 1u : 0u);
+                    mma_f16(sb + NSC * BK, ql, kh, id_s, 1u);
+                }
+                mma_commit(&s_full[j & 1]);
+            };
+            bool ok = mbar_wait(q_full, 0, abort, a.err);
+            if (ok) ok = mbar_wait(&kv_full[0], 0, abort, a.err);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; j < nblk && ok; ++j) {
+                // S of the next block into the other buffer (the warpgroup that read it last published P).
+                if (j + 1 < nblk) {
+                    const int s1 = (j + 1) % kStagesKV;
+                    if (!mbar_wait(&kv_full[s1], ((j + 1) / kStagesKV) & 1, abort, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+                // P V of this block once its warpgroup published P (it drained its output first).
+                const int wg = j & 1;
+                if (!mbar_wait(&p_full[wg], (j >> 1) & 1, abort, a.err)) { ok = false; break; }
+                tc_fence_after();
+                const int s = j % kStagesKV;
+                const uint32_t st = base + L.stage0 + s * L.stage_bytes;
+                const uint32_t pb = base + L.p0 + wg * L.p_bytes;
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t ph = desc_noswizzle(pb + kk * 256, 128, p_sbo);
+                    const uint64_t pl = desc_noswizzle(pb + kAttnQ * BK * 2 + kk * 256, 128, p_sbo);
+                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
+                    const uint64_t vl = desc_noswizzle(st + L.v_lo + kk * 256, 128, BK * 16);
+                    const uint32_t acc = kk > 0 ? 1u : 0u;
+                    mma_f16(t_o_hi(wg), ph, vh, id_pv, acc);
+                    mma_f16(t_o_lo(wg), ph, vl, id_pv, acc);
+                    mma_f16(t_o_lo(wg), pl, vh, id_pv, 1u);
+                }
+                mma_commit(&o_full[wg]);
+                mma_commit(&kv_empty[s]);
+            }
+            if (!ok) {
+                mma_commit(drain);
+                mbar_wait_quiet(drain, 0, 100000000ull);
+            }
+        }
+    } else {
+        // ------------------------------------------------ softmax warpgroups
+        const int wg = (warp - 2) >> 2;  // 0: blocks 0, 2, ...; 1: blocks 1, 3, ...
+        const int q = warp & 3;          // lane quarter: the rows this warp owns
+        const int r = q * 32 + lane;     // query row of the tile
+        const int qi = q0 + r;
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        const uint32_t pbuf = base + L.p0 + wg * L.p_bytes;
+        float m_ref = -INFINITY;
+        double l = 0.0;
+        float o[DVC];
+#pragma unroll
+        for (int i = 0; i < DVC; ++i) o[i] = 0.0f;
+        // All lanes wait together; the warp's verdict is unanimous.
+        auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, a.err) ? 1 : 0) != 0;
+        };
+        // o += (the warpgroup's last block product, normalised to m_ref).
+        auto take = [&](int jb) {
+            if (!warp_wait(&o_full[wg], (jb >> 1) & 1)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < OCH; ++ch) {
+                float oh[16], ol[16];
+                tmem_ld16(t_o_hi(wg) + lane_off + ch * 16, oh);
+                tmem_ld16(t_o_lo(wg) + lane_off + ch * 16, ol);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[ch * 16 + i] += fmaf(ol[i], kLoUnscale, oh[i]);
+            }
+            return true;
+        };
+        bool ok = true;
+        bool first = true;
+        for (int j = wg; j < nblk; j += 2) {
+            if (!warp_wait(&s_full[wg], (j >> 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sb = tmem + wg * sbuf + lane_off;
+            float s[BK];
+#pragma unroll
+            for (int c = 0; c < BK; c += 16) {
+                // The lo accumulator and the hi ones of these 16 keys, one wait.
+                float lo[16], h0[16], h1[16];
+                tmem_ld16(sb + NSC * BK + c, lo);
+                tmem_ld16(sb + c, h0);
+                if (NSC > 1) tmem_ld16(sb + BK + c, h1);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) s[c + i] = fmaf(lo[i], kLoUnscale, NSC > 1 ? h0[i] + h1[i] : h0[i]);
+            }
+            const int valid = min(BK, a.lk - j * BK);
+            const bool full = valid == BK;
+            float bmax = -INFINITY;
+            if (full) {
+#pragma unroll
+                for (int i = 0; i < BK; ++i) bmax = fmaxf(bmax, s[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < BK; ++i)
+                    if (i < valid) bmax = fmaxf(bmax, s[i]);
+            }
+            bmax *= a.scale2;
+            // The block product of two blocks ago into the registers: its P buffer
+            // and output accumulator are then free.
+            if (j >= 2 && !take(j - 2)) { ok = false; break; }
+            if (first) {
+                m_ref = bmax;
+                first = false;
+            } else if (bmax > m_ref + kRescaleAbove) {
+                const float factor = ex2(m_ref - bmax);
+                m_ref = bmax;
+#pragma unroll
+                for (int i = 0; i < DVC; ++i) o[i] *= factor;
+                l *= static_cast<double>(factor);
+            }
+            // The weights (0 past the last key), their pairwise sum, and P in
+            // the UMMA no-swizzle K-major layout: row r, 8 keys per 16-byte chunk.
+            if (full) {
+#pragma unroll
+                for (int i = 0; i < BK; ++i) s[i] = ex2(fmaf(s[i], a.scale2, -m_ref));
+            } else {
+#pragma unroll
+                for (int i = 0; i < BK; ++i) s[i] = i < valid ? ex2(fmaf(s[i], a.scale2, -m_ref)) : 0.0f;
+            }
+#pragma unroll
+            for (int c = 0; c < BK / 8; ++c) {
+                float p8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p8[i] = s[c * 8 + i];
+                uint4 h4, l4;
+                split8_inrange(p8, h4, l4);
+                const uint32_t off = static_cast<uint32_t>((r >> 3) * (BK * 16) + c * 128 + (r & 7) * 16);
+                st_shared_v4(pbuf + off, h4);
+                st_shared_v4(pbuf + kAttnQ * BK * 2 + off, l4);
+            }
+#pragma unroll
+            for (int w = BK / 2; w > 0; w >>= 1) {
+#pragma unroll
+                for (int i = 0; i < w; ++i) s[i] += s[i + w];
+            }
+            l += static_cast<double>(s[0]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[wg]);
+        }
+        // The warpgroup's last block product.
+        if (ok) {
+            const int last = nblk - 1 - ((nblk - 1 - wg) & 1);   // the last j with j % 2 == wg
+            if (last >= wg && !take(last)) ok = false;
+        }
+        // Merge: warpgroup 1 hands its stream to warpgroup 0 through shared memory.
+        if (wg == 1) {
+            merge_m[r] = m_ref;
+            merge_l[r] = l;
+#pragma unroll
+            for (int i = 0; i < DVC; ++i) merge_o[r * DVC + ((i + r) % DVC)] = o[i];
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(merged);
+        } else if (ok && mbar_wait(merged, 0, abort, a.err)) {
+            const float m1 = merge_m[r];
+            const float m = fmaxf(m_ref, m1);
+            const float f0 = m_ref == -INFINITY ? 0.0f : ex2(m_ref - m);
+            const float f1 = m1 == -INFINITY ? 0.0f : ex2(m1 - m);
+            const double total = l * static_cast<double>(f0) + merge_l[r] * static_cast<double>(f1);
+#pragma unroll
+            for (int i = 0; i < DVC; ++i) o[i] = o[i] * f0 + merge_o[r * DVC + ((i + r) % DVC)] * f1;
+            if (qi < a.lq) {
+                const float recip = static_cast<float>(1.0 / total);
+#pragma unroll
+                for (int i = 0; i < DVC; ++i) o[i] *= recip;
+                ChainRow cr;
+                row_offsets(a.chain, cr, 0, head, qi, batch);
+                const int ncols = min(DVC, a.dv - dv0);
+#pragma unroll
+                for (int c = 0; c < DVC; c += 16) apply_chain_cols<0, 16>(a.chain, cr, o + c, dv0 + c, a.dv - 1);
+                float* orow = a.out + static_cast<long long>(head) * a.onb[1] + static_cast<long long>(qi) * a.onb[2] +
+                              static_cast<long long>(batch) * a.onb[3];
+                if (a.onb[0] == 1 && ncols == DVC && ((reinterpret_cast<uintptr_t>(orow + dv0)) & 15) == 0) {
+#pragma unroll
+                    for (int i = 0; i < DVC; i += 4)
+                        *reinterpret_cast<float4*>(orow + dv0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < DVC; ++i)
+                        if (i < ncols) orow[static_cast<long long>(dv0 + i) * a.onb[0]] = o[i];
+                }
+            }
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 bool floaty(const sdb_tensor* t) {
     return t && t->data && (t->type == SDB_TYPE_F32 || t->type == SDB_TYPE_F16);
 }
@@ -423,11 +765,9 @@ int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
 // Splits Q, K and V into the workspace as tiles (128 queries, BK keys) and
 // launches the kernel.
-template <int BK, int DVC, int NO>
-int launch_attention(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
-    const AttnLayout L(a.dp, DVC, BK);
-    const int smem = L.total + 1024;
-    if (smem > 227 * 1024) return fail(SDB_NOT_SUPPORTED, "sdb_attention: head too wide");
+// Splits Q, K and V into the workspace as tiles of 128 queries / BK keys.
+template <int BK, int DVC>
+int prepare_tiles(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
     auto dims = [](const sdb_tensor* t, long long (&ne)[4], long long (&nb)[4]) {
         const int es = t->type == SDB_TYPE_F16 ? 2 : 4;
         for (int i = 0; i < 4; ++i) {
@@ -463,6 +803,15 @@ int launch_attention(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, cons
                             const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.vs)), a.err, st);
         s != SDB_OK)
         return s;
+    return SDB_OK;
+}
+
+template <int BK, int DVC, int NO>
+int launch_attention(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    const AttnLayout L(a.dp, DVC, BK);
+    const int smem = L.total + 1024;
+    if (smem > 227 * 1024) return fail(SDB_NOT_SUPPORTED, "sdb_attention: head too wide");
+    if (int s = prepare_tiles<BK, DVC>(a, q, k, v, st); s != SDB_OK) return s;
     SDB_CUDA(cudaFuncSetAttribute(attention_kernel<BK, DVC, NO>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const dim3 grid(static_cast<unsigned>((a.lq + kAttnQ - 1) / kAttnQ), static_cast<unsigned>(a.h * a.dv_chunks),
                     static_cast<unsigned>(a.b));
@@ -472,11 +821,52 @@ int launch_attention(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, cons
     return SDB_OK;
 }
 
+template <int BK, int NSC, int DVC>
+int launch_attention_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    const AttnWgLayout L(a.dp, DVC, BK);
+    const int smem = L.total + 1024;
+    if (int s = prepare_tiles<BK, DVC>(a, q, k, v, st); s != SDB_OK) return s;
+    auto kern = attention_wg_kernel<BK, NSC, DVC>;
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const dim3 grid(static_cast<unsigned>((a.lq + kAttnQ - 1) / kAttnQ), static_cast<unsigned>(a.h * a.dv_chunks),
+                    static_cast<unsigned>(a.b));
+    kern<<<grid, kAttnThreads, smem, st>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+// The two-warpgroup kernel when its S buffers and two output accumulators fit
+// tensor memory (heads up to 64 dims with 64-key blocks, up to 128 with 32).
+template <int DVC>
+int launch_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st,
+              bool* taken) {
+    *taken = false;
+    const int nsc = (a.dp + 63) / 64;
+    auto fits = [&](int bk) {
+        return 2 * (nsc + 1) * bk + 4 * DVC <= 512 && AttnWgLayout(a.dp, DVC, bk).total + 1024 <= 227 * 1024;
+    };
+    if (nsc == 1 && fits(64)) {
+        *taken = true;
+        return launch_attention_wg<64, 1, DVC>(a, q, k, v, st);
+    }
+    if (nsc == 2 && fits(32)) {
+        *taken = true;
+        return launch_attention_wg<32, 2, DVC>(a, q, k, v, st);
+    }
+    return SDB_OK;
+}
+
 // Keys per block (64, else 32) and output buffers (two, so the softmax of a
 // block overlaps the product of the one before; else one): the first choice
 // whose S double buffer and output accumulators fit tensor memory.
 template <int DVC>
 int launch_bk(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    if (tuning().attention_wg) {
+        bool taken = false;
+        const int rc = launch_wg<DVC>(a, q, k, v, st, &taken);
+        if (taken || rc != SDB_OK) return rc;
+    }
     const int nsc = (a.dp + 63) / 64;
     auto fits = [&](int bk, int no) {
         return 2 * (nsc + 1) * bk + no * 2 * DVC <= 512 &&

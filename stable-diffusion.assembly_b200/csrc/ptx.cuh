@@ -345,6 +345,22 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t w) {
 // as split_half: hi = x rounded to FP16, lo = (x - hi) 2^11 rounded to FP16);
 // returns true when any input is beyond the FP16 range.  Four packed
 // conversions (two values each) for hi and four for lo.
+// split8 for values known to be inside the FP16 range (softmax weights): no
+// range check, and the hi part read back by the hardware's FP16 unpack.
+__device__ __forceinline__ void split8_inrange(const float (&x)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 hh = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn((x[2 * i] - hf.x) * kLoScale, (x[2 * i + 1] - hf.y) * kLoScale);
+        h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 __device__ __forceinline__ bool split8(const float (&x)[8], uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
     bool over = false;

@@ -41,6 +41,7 @@ int64_t* knob(Tuning& t, const std::string& name) {
     if (name == "bits") return &t.bits;
     if (name == "group") return &t.group;
     if (name == "block_n") return &t.block_n;
+    if (name == "attention_wg") return &t.attention_wg;
     return nullptr;
 }
 
@@ -50,6 +51,7 @@ bool valid(const std::string& name, int64_t v) {
     if (name == "group") return v == 0 || v == 32 || v == 64 || v == 128 || v == 256;
     if (name == "block_n") return v == 0 || v == 128 || v == 256;
     if (name == "todo") return v >= 1 && v <= 4;
+    if (name == "attention_wg") return v == 0 || v == 1;
     return v >= 0;
 }
 

@@ -25,6 +25,7 @@ struct Tuning {
     int64_t bits = 0;            // 8: the int8 path
     int64_t group = 64;          // quantisation group along K
     int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
+    int64_t attention_wg = 1;    // 1: two-warpgroup attention where it fits; 0: the pair kernel
 };
 
 Tuning& tuning();
