@@ -660,9 +660,23 @@ class OpClock:
         for name, fn in self.saved.items():
             setattr(self.sdb, name, fn)
 
+    @staticmethod
+    def shape_key(name, args, out) -> str:
+        if name == "conv2d_nhwc":
+            w, x = args[0], args[1]
+            return f"conv {w.shape[1]}->{w.shape[0]} k{w.shape[2]} @{x.shape[1]}x{x.shape[2]}x{x.shape[0]}"
+        if name in ("mul_mat", "mul_mat_gated"):
+            w, x = args[0], args[1]
+            return f"{'geglu' if name == 'mul_mat_gated' else 'linear'} M{x.numel() // w.shape[1]} K{w.shape[1]} N{w.shape[0]}"
+        if name == "attention_heads":
+            q, k, heads = args[0], args[1], args[3]
+            return f"attention L{q.shape[1]}x{k.shape[1]} d{q.shape[2] // heads} b{q.shape[0]}"
+        return f"{name} {tuple(args[0].shape)}"
+
     def measure(self, stream, reps: int = 3) -> dict:
         torch = self.torch
         classes: dict[str, list] = {}
+        self.shapes: dict[str, list] = {}
         for name, fn, a, kw, out in self.records:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
@@ -677,9 +691,14 @@ class OpClock:
             torch.cuda.synchronize()
             cls, work = self.work(name, a, out)
             c = classes.setdefault(cls, [0, 0.0, 0])
+            ms = e0.elapsed_time(e1) / reps
             c[0] += work
-            c[1] += e0.elapsed_time(e1) / reps
+            c[1] += ms
             c[2] += 1
+            sh = self.shapes.setdefault(self.shape_key(name, a, out), [0, 0.0, 0])
+            sh[0] += work
+            sh[1] += ms
+            sh[2] += 1
             del g
         return {k: {"work": v[0], "ms": v[1], "calls": v[2]} for k, v in classes.items()}
 
@@ -738,6 +757,9 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
             net.forward(sampler.x_in, sampler.t, sampler.context)
     torch.cuda.synchronize()
     classes = oc.measure(cap)
+    top_shapes = sorted(oc.shapes.items(), key=lambda kv: -kv[1][1])[:16]
+    shapes = {k: {"ms": round(v[1], 4), "calls": v[2], "tflops": round(v[0] / (v[1] * 1e-3) / 1e12, 1)}
+              for k, v in top_shapes}
     del oc
 
     # End to end through the public API: latent and context from pinned host memory, the sampler step,
@@ -802,6 +824,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
         "classes_ms": {k: round(v["ms"], 4) for k, v in sorted(classes.items(), key=lambda kv: -kv[1]["ms"])},
         "classes_tflops": {k: round(v["work"] / (v["ms"] * 1e-3) / 1e12, 1) for k, v in classes.items()
                            if CLASSES[k] == "tensor"},
+        "top_shapes": shapes,
         "e2e": {"value": world * 1e3 / e2e_ms, "unit": UNET_UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks.summary(),

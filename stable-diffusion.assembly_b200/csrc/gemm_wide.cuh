@@ -92,6 +92,38 @@ __device__ __forceinline__ void store_box16(const CUtensorMap* map, uint8_t* box
     }
 }
 
+// v[0..15] += the existing output of this thread's row in the warp's 32 x 16
+// box (rows row0.., columns col0.. of a row-major FP32 matrix, ld floats a
+// row): the warp reads the box coalesced -- a float4 a lane, eight rows an
+// instruction -- into the staging box in the store layout, then each thread
+// takes its row.  Rows and columns past the valid ones read as 0.
+__device__ __forceinline__ void add_old_box16(const float* y, long long ld, long long row0, long long rows,
+                                              long long col0, long long cols, uint8_t* box, int lane, float* v) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    const uint32_t b = smem_u32(box);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = (lane >> 2) + 8 * i, c4 = lane & 3;
+        float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (row0 + r < rows && col0 + 4 * c4 < cols)
+            val = __ldg(reinterpret_cast<const float4*>(y + (row0 + r) * ld + col0 + 4 * c4));
+        st_shared_v4(b + r * 64 + ((c4 ^ ((r >> 1) & 3)) << 4),
+                     make_uint4(__float_as_uint(val.x), __float_as_uint(val.y), __float_as_uint(val.z),
+                                __float_as_uint(val.w)));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint4 o = ld_shared_v4(b + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
+        v[4 * k] += __uint_as_float(o.x);
+        v[4 * k + 1] += __uint_as_float(o.y);
+        v[4 * k + 2] += __uint_as_float(o.z);
+        v[4 * k + 3] += __uint_as_float(o.w);
+    }
+    __syncwarp();
+}
+
 template <int MODE, bool GATED, int BN>
 __global__ void __launch_bounds__(kWideThreads, 1)
 gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
@@ -317,11 +349,16 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
                     for (int j = 0; j < 16; ++j) v[j] *= gelu(sum[CPW / 2 + c + j]);
                 } else {
                     if (args.chain.from_redirect) {
-                        float old[16];
+                        if (args.store == kStoreTma) {
+                            add_old_box16(args.y, args.n, static_cast<long long>(tm) * kBM + q * 32, args.m, cb,
+                                          args.n, box, lane, v);
+                        } else {
+                            float old[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) old[j] = yrow[min(cb + j, args.n - 1LL) * args.ynb[0]];
+                            for (int j = 0; j < 16; ++j) old[j] = yrow[min(cb + j, args.n - 1LL) * args.ynb[0]];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
+                            for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
+                        }
                     }
                     apply_chain_cols<0, 16>(args.chain, cr, v, cb, args.n - 1);
                 }
@@ -346,11 +383,16 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
                 float* v = sum + c;
                 const long long cb = static_cast<long long>(tn) * BN + colA + c;
                 if (args.chain.from_redirect) {
-                    float old[16];
+                    if (args.store == kStoreTma) {
+                        add_old_box16(args.y, args.n, row0 + q * 32, static_cast<long long>(g.n) * g.oh * g.ow, cb,
+                                      args.n, box, lane, v);
+                    } else {
+                        float old[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) old[j] = ybase[min(cb + j, args.n - 1LL) * args.ynb[2]];
+                        for (int j = 0; j < 16; ++j) old[j] = ybase[min(cb + j, args.n - 1LL) * args.ynb[2]];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
+                        for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
+                    }
                 }
                 apply_chain_cols<2, 16>(args.chain, cr, v, cb, args.n - 1);
                 if (args.store == kStoreTma) {

@@ -92,30 +92,50 @@ bool store_map(CUtensorMap* map, void* base, long long cols, long long rows, lon
                              box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) == CUDA_SUCCESS;
 }
 
-// Tile width of the wide kernel for N output columns (gated: N of the output,
-// 2N of the product) over tiles_m row tiles: the k-block's shared-memory bytes
-// per tile (MMA operand reads of the hi and lo products plus the TMA writes)
-// times the tiles each SM must take.  0 when the 128-wide kernel is to run.
-int choose_wide_bn(int64_t n, int tiles_m, bool gated) {
+// The wide kernel's plan for an M x N x K product (gated: N of the output, 2N
+// of the product): the tile width and the K split that minimise
+//   waves x (k-blocks of an item) x (a k-block's shared-memory bytes)
+// + the split's partial sums (written and read back by the reduction),
+// where waves = ceil(items / SMs) -- a wave with fewer items than SMs costs
+// as much as a full one.  A k-block moves 2 (A + B) for the MMA operand
+// reads of the hi and lo products plus A (both planes) + B for the TMA
+// writes; B = BN x 128 bytes.  Returns the width (0: run the 128-wide
+// kernel) and sets ksplit / per_split.
+int plan_wide(GemmArgs& a, int64_t n, int tiles_m, int64_t m, bool gated) {
     const int64_t forced = tuning().block_n;
+    a.ksplit = 1;
+    a.per_split = a.kblocks;
     if (forced == 128 && !gated) return 0;
     const int64_t cols = gated ? 2 * n : n;
     const int sms = current_sm_count();
-    int best = 0;
+    int best_bn = 0, best_split = 1;
     double best_cost = 0.0;
     for (int bn : {256, 192, 128}) {
         if (gated && bn == 192) continue;
         if (forced == 256 && bn != 256) continue;
-        const int64_t tiles_n = (cols + bn - 1) / bn;
-        const int64_t waves = (tiles_m * tiles_n + sms - 1) / sms;
+        const int64_t tiles = tiles_m * ((cols + bn - 1) / bn);
         const double kb_bytes = 2.0 * (16384 + bn * 128) + 32768 + bn * 128;
-        const double cost = static_cast<double>(waves) * kb_bytes * (tiles_m * tiles_n > sms ? 1.0 : 1.0);
-        if (best == 0 || cost < best_cost) {
-            best = bn;
-            best_cost = cost;
+        const int max_split = gated ? 1 : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, a.kblocks / 4)));
+        for (int split = 1; split <= max_split; ++split) {
+            const int per = (a.kblocks + split - 1) / split;
+            const int parts = (a.kblocks + per - 1) / per;
+            if (parts != split) continue;
+            const int64_t items = tiles * parts;
+            const int64_t waves = (items + sms - 1) / sms;
+            double cost = static_cast<double>(waves) * per * kb_bytes;
+            // The reduction: partial sums written, read back, the output written -- over all SMs,
+            // about 48 bytes a clock each, in the units of one SM's shared-memory bytes above.
+            if (parts > 1) cost += (2.0 * parts + 1.0) * static_cast<double>(m) * n * 4 / sms / 48.0 * 128.0;
+            if (best_bn == 0 || cost < best_cost * 0.98) {
+                best_bn = bn;
+                best_split = parts;
+                best_cost = cost;
+            }
         }
     }
-    return best;
+    a.per_split = (a.kblocks + best_split - 1) / best_split;
+    a.ksplit = best_split;
+    return best_bn;
 }
 
 template <int MODE, bool GATED, int BN>
@@ -237,9 +257,7 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (rc != SDB_OK) return rc;
     const int wmode = gated ? kWeightGated : p->split ? kWeightSplit : kWeightHalf;
     const int tiles = static_cast<int>((m + kBM - 1) / kBM);
-    // FP16 weights take the wide kernel (tile width by choose_wide_bn); FP32 weights the 128-wide one.
-    const int wide_bn = wmode == kWeightSplit ? 0 : choose_wide_bn(n, tiles, gated);
-    const int bn = wide_bn ? (gated ? wide_bn / 2 : wide_bn) : (wmode == kWeightGated ? 64 : 128);
+    const int kblocks = static_cast<int>(p->kpad / kBK);
 
     GemmArgs a{};
     a.m = static_cast<int>(m);
@@ -252,7 +270,11 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     a.rne1 = dst->ne[1];
     a.rne2 = dst->ne[2];
     set_out(a, dst, chain);
-    choose_ksplit(a, tiles * static_cast<int>((n + bn - 1) / bn), wmode);
+    // FP16 weights take the wide kernel (tile width and K split by plan_wide); FP32 weights the 128-wide one.
+    a.kblocks = kblocks;
+    const int wide_bn = wmode == kWeightSplit ? 0 : plan_wide(a, n, tiles, m, gated);
+    const int bn = wide_bn ? (gated ? wide_bn / 2 : wide_bn) : (wmode == kWeightGated ? 64 : 128);
+    if (!wide_bn) choose_ksplit(a, tiles * static_cast<int>((n + bn - 1) / bn), wmode);
 
     // Workspace: the split rows [0, M) hi, [M, 2M) lo of kp8 FP16, then any partial sums.
     const int64_t kp8 = round_up(k, 8);
@@ -380,8 +402,7 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (!conv_tiles(g)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: tiling");
     const int tiles = g.tw * g.th * g.tn;
     const int wmode = p->split ? kWeightSplit : kWeightHalf;
-    const int wide_bn = wmode == kWeightSplit ? 0 : choose_wide_bn(oc, tiles, false);
-    const int bn = wide_bn ? wide_bn : 128;
+
     a.m = 0;
     a.kblocks = static_cast<int>(p->kpad / kBK);
     a.n = static_cast<int>(oc);
@@ -391,7 +412,10 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     a.tiles_m = tiles;
     a.store = kStoreDirect;
     set_out(a, dst, chain);
-    choose_ksplit(a, tiles * static_cast<int>((oc + bn - 1) / bn), wmode);
+    const int wide_bn =
+        wmode == kWeightSplit ? 0 : plan_wide(a, oc, tiles, static_cast<int64_t>(tiles) * kBM, false);
+    const int bn = wide_bn ? wide_bn : 128;
+    if (!wide_bn) choose_ksplit(a, tiles * static_cast<int>((oc + bn - 1) / bn), wmode);
 
     // Workspace: the image split and channels-last, [2N][H][W][cp8] (hi images,
     // then lo), then any partial sums.
