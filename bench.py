@@ -838,6 +838,69 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- single operations for profiler captures
+
+OPS = {
+    # name: builder(torch, sdb, dev) -> callable running the operation once
+    "conv3x3_320x64x64x2": lambda torch, sdb, dev: _op_conv(torch, sdb, dev, 320, 320, 64, 2),
+    "conv3x3_1280x16x16x2": lambda torch, sdb, dev: _op_conv(torch, sdb, dev, 1280, 1280, 16, 2),
+    "attention_4096x4096_d40_b1": lambda torch, sdb, dev: _op_attention(torch, sdb, dev, 4096, 4096, 40, 1),
+    "linear_8192x320x320": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 320),
+    "groupnorm_2x64x64x320": lambda torch, sdb, dev: _op_groupnorm(torch, sdb, dev, 2, 64, 320),
+}
+
+
+def _op_conv(torch, sdb, dev, ic, oc, hw, n):
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(n, hw, hw, ic, device=dev, generator=g)
+    w = (torch.randn(oc, ic, 3, 3, device=dev, generator=g) / math.sqrt(9 * ic)).half()
+    b = torch.randn(oc, device=dev, generator=g)
+    y = torch.empty(n, hw, hw, oc, device=dev)
+    return lambda: sdb.conv2d_nhwc(w, x, (1, 1), (1, 1), out=y, chain=sdb.Chain().add(b, [0, 0, 1, 0]))
+
+
+def _op_attention(torch, sdb, dev, lq, lk, d, b):
+    g = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(b, lq, 8 * d, device=dev, generator=g)
+    k = torch.randn(b, lk, 8 * d, device=dev, generator=g)
+    v = torch.randn(b, lk, 8 * d, device=dev, generator=g)
+    o = torch.empty(b, lq, 8 * d, device=dev)
+    return lambda: sdb.attention_heads(q, k, v, 8, 8, d ** -0.5, out=o)
+
+
+def _op_linear(torch, sdb, dev, m, k, n):
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(m, k, device=dev, generator=g)
+    w = (torch.randn(n, k, device=dev, generator=g) / math.sqrt(k)).half()
+    b = torch.randn(n, device=dev, generator=g)
+    y = torch.empty(m, n, device=dev)
+    return lambda: sdb.mul_mat(w, x, y, chain=sdb.Chain().add(b))
+
+
+def _op_groupnorm(torch, sdb, dev, n, hw, c):
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(n, hw, hw, c, device=dev, generator=g)
+    gamma = torch.randn(c, device=dev, generator=g)
+    beta = torch.randn(c, device=dev, generator=g)
+    y = torch.empty_like(x)
+    chain = sdb.Chain().mul(gamma, [0, 0, 1, 0]).add(beta, [0, 0, 1, 0]).silu()
+    return lambda: sdb.group_norm_nhwc(x, 32, 1e-5, out=y, chain=chain)
+
+
+def run_op(name: str, reps: int = 3) -> None:
+    """Runs one named operation `reps` times (for ncu captures of a single kernel on a small case)."""
+    import torch
+    import sdb
+
+    dev = torch.device("cuda", 0)
+    sdb.load()
+    fn = OPS[name](torch, sdb, dev)
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"op": name, "reps": reps, "device_status": sdb.device_status(clear=True)}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -846,7 +909,11 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=sorted(OPS), help="run one operation three times (profiler captures) and exit")
     args = ap.parse_args()
+    if args.op:
+        run_op(args.op)
+        return
     if args.steps is None:
         args.steps = 100 if args.workload == "unet" else 1000
     if args.impl == "reference":
