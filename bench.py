@@ -838,6 +838,20 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- ranks
+
+def max_over_ranks(value: float, dist=None, device=None) -> float:
+    """The largest of the ranks' values (the step time every rank reports): an all-reduce of one
+    double, on `device` (the rank's GPU under NCCL, the CPU under gloo)."""
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ---------------------------------------------------------------- single operations for profiler captures
 
 OPS = {
@@ -943,15 +957,8 @@ def main() -> None:
         if dist is not None:
             dist.barrier()
 
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     run = run_unet if args.workload == "unet" else run_hot_ops
-    run(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks)
+    run(args, torch, dev, dist, world, rank, local, barrier, lambda v: max_over_ranks(v, dist, dev))
 
 
 if __name__ == "__main__":
