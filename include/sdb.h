@@ -165,8 +165,10 @@ int sdb_token_downsampling(int64_t width, int64_t height);
 /* ---- tuning and diagnostics ----------------------------------------------
  * sdb_set_tuning parses "name=value,..." as SDASM_TUNE does (cpu.cc:166-220):
  * fuse, fuse_residual, winograd (0 direct, 1 F(2x2), 2 F(4x4)), store (0 repack
- * every call), todo, todo_tokens, bits (0 or 8), group, block_n.  Returns
- * SDB_INVALID on an unknown name or value. */
+ * every call), todo, todo_tokens, bits (0, or 2..8: the linear layers of 256
+ * rows or more as integer products, quant.cc), input_bits (2..8), group (32,
+ * 64, 128 or 256), weight_group (1 per group, 0 per row), quantize (bit 1:
+ * linear layers), block_n.  Returns SDB_INVALID on an unknown name or value. */
 int sdb_set_tuning(const char *spec);
 int sdb_get_tuning(const char *name, int64_t *value);
 /* The device error word of the current device (kernel-reported: bit 0 a

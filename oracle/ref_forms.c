@@ -307,3 +307,109 @@ void rf_group_norm(const float *x, float *y, int N, int C, long HW, int groups, 
             }
         }
 }
+
+/* ---- the quantized linear layer (bits = 8), quant.h / quant.cc ---------------
+ * The inputs: per row, per group of `group` numbers of k (the last group
+ * short, its missing numbers standing for zeros): the least and the greatest
+ * with 0 between them, s = (hi - lo) / levels, inverse = s > 0 ? 1 / s : 0,
+ * zero = rint(-lo * inverse), q = clamp(rint(x * inverse) + zero, 0, levels),
+ * the group's scale s and offset s * zero (quant.cc quantize_input_row).
+ * The weights: per row of k (an output feature), per group or the whole row,
+ * m = max |w|, s = m / wmax, inverse = s > 0 ? 1 / s : 0,
+ * q = clamp(rint(w * inverse), -wmax, wmax), scale s, offset s * sum(q)
+ * (quant.cc quantize_weights).  The product: per tile element, from 0 (or the
+ * output's value, with accumulate), group by group in order,
+ * t = fma(sa * sb, sum(qa qb), t); t = fma(-oa, ob, t) (quant.cc qgemm).
+ * rint rounds to the nearest and to even on a tie, as nearbyint does in the
+ * default mode. */
+static void quantize_input_group(const float *x, int n, int group, int levels, uint8_t *q, float *scale,
+                                 float *offset) {
+    float lo = 0.0f, hi = 0.0f;
+    for (int e = 0; e < n; ++e) {
+        lo = x[e] < lo ? x[e] : lo;
+        hi = x[e] > hi ? x[e] : hi;
+    }
+    const float s = (hi - lo) / (float)levels;
+    const float inverse = s > 0.0f ? 1.0f / s : 0.0f;
+    const float zero = rintf(-lo * inverse);
+    for (int e = 0; e < group; ++e) {
+        float v;
+        if (e < n) {
+            const float r = rintf(x[e] * inverse);
+            v = r + zero;
+        } else {
+            v = zero;
+        }
+        v = v < 0.0f ? 0.0f : (v > (float)levels ? (float)levels : v);
+        q[e] = (uint8_t)v;
+    }
+    *scale = s;
+    *offset = s * zero;
+}
+
+void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, int group, int levels, int wmax,
+                 int weight_groups, int accumulate) {
+    const int groups = (K + group - 1) / group;
+    int8_t *qw = (int8_t *)malloc((size_t)N * groups * group);
+    float *sw = (float *)malloc(sizeof(float) * (size_t)N * groups), *ow = (float *)malloc(sizeof(float) * (size_t)N * groups);
+    uint8_t *qx = (uint8_t *)malloc((size_t)M * groups * group);
+    float *sx = (float *)malloc(sizeof(float) * (size_t)M * groups), *ox = (float *)malloc(sizeof(float) * (size_t)M * groups);
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        float row_max = 0.0f;
+        if (!weight_groups)
+            for (int k = 0; k < K; ++k) {
+                const float a = fabsf(w[(size_t)n * K + k]);
+                row_max = a > row_max ? a : row_max;
+            }
+        for (int g = 0; g < groups; ++g) {
+            const int cnt = K - g * group < group ? K - g * group : group;
+            float m = row_max;
+            if (weight_groups)
+                for (int e = 0; e < cnt; ++e) {
+                    const float a = fabsf(w[(size_t)n * K + g * group + e]);
+                    m = a > m ? a : m;
+                }
+            const float s = m / (float)wmax;
+            const float inverse = s > 0.0f ? 1.0f / s : 0.0f;
+            int sum = 0;
+            for (int e = 0; e < group; ++e) {
+                const float we = e < cnt ? w[(size_t)n * K + g * group + e] : 0.0f;
+                float r = rintf(we * inverse);
+                r = r < (float)-wmax ? (float)-wmax : (r > (float)wmax ? (float)wmax : r);
+                qw[((size_t)n * groups + g) * group + e] = (int8_t)r;
+                sum += (int)r;
+            }
+            sw[(size_t)n * groups + g] = s;
+            ow[(size_t)n * groups + g] = s * (float)sum;
+        }
+    }
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; ++m)
+        for (int g = 0; g < groups; ++g) {
+            const int cnt = K - g * group < group ? K - g * group : group;
+            quantize_input_group(x + (size_t)m * K + g * group, cnt, group, levels, qx + ((size_t)m * groups + g) * group,
+                                 &sx[(size_t)m * groups + g], &ox[(size_t)m * groups + g]);
+        }
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; ++m)
+        for (int n = 0; n < N; ++n) {
+            float t = accumulate ? y[(size_t)m * N + n] : 0.0f;
+            for (int g = 0; g < groups; ++g) {
+                const uint8_t *a = qx + ((size_t)m * groups + g) * group;
+                const int8_t *b = qw + ((size_t)n * groups + g) * group;
+                int32_t acc = 0;
+                for (int e = 0; e < group; ++e) acc += (int32_t)a[e] * (int32_t)b[e];
+                const float sab = sx[(size_t)m * groups + g] * sw[(size_t)n * groups + g];
+                t = fmaf(sab, (float)acc, t);
+                t = fmaf(-ox[(size_t)m * groups + g], ow[(size_t)n * groups + g], t);
+            }
+            y[(size_t)m * N + n] = t;
+        }
+    free(qw);
+    free(sw);
+    free(ow);
+    free(qx);
+    free(sx);
+    free(ox);
+}

@@ -54,6 +54,7 @@ def load() -> ctypes.CDLL:
         lib.rf_conv2d.argtypes = [P, i, i, i, i, P, i, i, i, i, i, i, i, i, i, P, i, i]
         lib.rf_attention.argtypes = [P, P, P, P, i, i, i, i, i, i, i, f, i, i]
         lib.rf_group_norm.argtypes = [P, P, i, i, ctypes.c_long, i, f, P, P, i]
+        lib.rf_qmul_mat.argtypes = [P, i, i, P, i, P, i, i, i, i, i]
         lib.rf_threads.restype = i
         lib.rf_set_threads.argtypes = [i]
         _lib = lib
@@ -76,7 +77,7 @@ def mul_mat(w16: np.ndarray, x: np.ndarray) -> np.ndarray:
     """w16 (N, K) float16, x (M, K) float32 -> (M, N) float32 (mul_mat.cc's form)."""
     w16 = np.ascontiguousarray(w16, dtype=np.float16)
     x = np.ascontiguousarray(x, dtype=np.float32)
-    n, k = w16.shape
+    n, k = w32.shape
     m = x.shape[0]
     y = np.empty((m, n), dtype=np.float32)
     load().rf_mul_mat(_p(w16), n, k, _p(x), m, _p(y))
@@ -123,4 +124,19 @@ def group_norm(x, groups: int, eps: float, gamma=None, beta=None, silu=False) ->
     b = np.ascontiguousarray(beta, dtype=np.float32) if beta is not None else None
     load().rf_group_norm(_p(x), _p(y), n, c, hw, groups, eps, _p(g) if g is not None else None,
                          _p(b) if b is not None else None, 1 if silu else 0)
+    return y
+
+
+def qmul_mat(w: np.ndarray, x: np.ndarray, group: int = 64, levels: int = 255, wmax: int = 127,
+             weight_groups: bool = True, y0: np.ndarray | None = None) -> np.ndarray:
+    """The reference's quantized linear layer (bits = 8, quant.cc's C++ form): w (N, K) float16 or
+    float32 (read as float32, which FP16 values are exactly), x (M, K) float32 -> (M, N) float32;
+    with y0, the sums start from it (accumulate)."""
+    w32 = np.ascontiguousarray(w, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, k = w32.shape
+    m = x.shape[0]
+    y = np.ascontiguousarray(y0, dtype=np.float32).copy() if y0 is not None else np.empty((m, n), np.float32)
+    load().rf_qmul_mat(_p(w32), n, k, _p(x), m, _p(y), group, levels, wmax,
+                       1 if weight_groups else 0, 1 if y0 is not None else 0)
     return y

@@ -11,6 +11,7 @@
 #include "../../include/sdb.h"
 #include "gemm.cuh"
 #include "gemm_wide.cuh"
+#include "quant.cuh"
 #include "runtime.cuh"
 #include "split.cuh"
 #include "store.cuh"
@@ -251,6 +252,7 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     const int64_t n = gated ? w->ne[1] / 2 : w->ne[1];
     const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
     if (m > (1LL << 30) || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "mul_mat: too large");
+    if (quantized_linear(m)) return run_quantized_linear(w, x, dst, chain, st, gated);
     std::shared_ptr<Packed> p;
     const int rc = gated ? packed_weights(w, Layout::gated, 2 * n, k, 0, n, st, &p)
                          : packed_weights(w, Layout::linear, n, k, 0, 0, st, &p);
@@ -346,6 +348,8 @@ int sdb_mul_mat(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst,
 int sdb_mul_mat_gated_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* out) {
     if (!mul_mat_shapes(w, x, out) || w->type != SDB_TYPE_F16 || w->ne[1] % 2 != 0) return 0;
     const int64_t half = w->ne[1] / 2;
+    // Quantized, each half's columns begin a panel of 16 (mul_mat.cc:1130-1133).
+    if (quantized_linear(x->ne[1] * x->ne[2] * x->ne[3]) && half % 16 != 0) return 0;
     return out->ne[0] == half && out->ne[1] == x->ne[1] && out->ne[2] == x->ne[2] && out->ne[3] == x->ne[3];
 }
 

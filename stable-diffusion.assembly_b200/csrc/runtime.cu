@@ -40,6 +40,9 @@ int64_t* knob(Tuning& t, const std::string& name) {
     if (name == "todo_tokens") return &t.todo_tokens;
     if (name == "bits") return &t.bits;
     if (name == "group") return &t.group;
+    if (name == "input_bits") return &t.input_bits;
+    if (name == "weight_group") return &t.weight_group;
+    if (name == "quantize") return &t.quantize;
     if (name == "block_n") return &t.block_n;
     if (name == "attention_wg") return &t.attention_wg;
     return nullptr;
@@ -47,8 +50,11 @@ int64_t* knob(Tuning& t, const std::string& name) {
 
 bool valid(const std::string& name, int64_t v) {
     if (name == "winograd") return v >= 0 && v <= 2;
-    if (name == "bits") return v == 0 || v == 8;
-    if (name == "group") return v == 0 || v == 32 || v == 64 || v == 128 || v == 256;
+    if (name == "bits") return v == 0 || (v >= 2 && v <= 8);
+    if (name == "input_bits") return v >= 2 && v <= 8;
+    if (name == "group") return v == 32 || v == 64 || v == 128 || v == 256;
+    if (name == "weight_group") return v == 0 || v == 1;
+    if (name == "quantize") return v >= 0 && v <= 7;
     if (name == "block_n") return v == 0 || v == 128 || v == 256;
     if (name == "todo") return v >= 1 && v <= 4;
     if (name == "attention_wg") return v == 0 || v == 1;

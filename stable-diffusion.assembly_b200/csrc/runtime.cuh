@@ -22,8 +22,11 @@ struct Tuning {
     int64_t store = 1;           // keep packed weights between calls
     int64_t todo = 1;            // ToDo K/V downsampling factor (1 = none)
     int64_t todo_tokens = 4096;  // least tokens of a grid downsampled
-    int64_t bits = 0;            // 8: the int8 path
-    int64_t group = 64;          // quantisation group along K
+    int64_t bits = 0;            // 2..8: integer products, weights of that many bits (0: FP32)
+    int64_t input_bits = 8;      // the inputs' bits, 2..8, unsigned with a zero point
+    int64_t group = 64;          // numbers of k sharing a scale: 32, 64, 128 or 256
+    int64_t weight_group = 1;    // the weights' scale per group: 1; per whole row: 0
+    int64_t quantize = 7;        // with bits, what is quantized: 1 linear layers (2, 4: not taken here)
     int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
     int64_t attention_wg = 1;    // 1: two-warpgroup attention where it fits; 0: the pair kernel
 };

@@ -71,6 +71,93 @@ __global__ void pack_weights_kernel(const PackArgs p) {
     }
 }
 
+// The reference's weight quantization (quant.cc:204-244): per packed row (an
+// output feature), per group of `group` numbers of k (the last group's
+// missing numbers zeros), m = max |w| over the group (or the whole row),
+// s = m / wmax, inverse = s > 0 ? 1 / s : 0, q = clamp(rint(w * inverse),
+// -wmax, wmax); the group's scale s and offset s * sum(q).  One warp a row;
+// every operation rounds as the reference's scalar one does.
+struct QPackArgs {
+    const uint8_t* src;
+    int type;
+    long long nb0, nb1;   // source strides in bytes (k, row)
+    long long n;          // logical rows (gated: of one half)
+    long long k;
+    int gated;
+    long long halfpad;
+    long long rows;       // packed rows
+    int group, groups, wmax, weight_groups;
+    long long kpad;
+    int8_t* q;
+    float* scales;        // [2 * groups][rows]
+};
+
+template <int EPL>
+__global__ void quantize_weights_kernel(const QPackArgs a) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < a.rows;
+         r += warps) {
+        long long src_row = -1;
+        if (!a.gated) {
+            if (r < a.n) src_row = r;
+        } else if (r < a.n) {
+            src_row = r;
+        } else if (r >= a.halfpad && r - a.halfpad < a.n) {
+            src_row = a.n + (r - a.halfpad);
+        }
+        const uint8_t* row = src_row >= 0 ? a.src + src_row * a.nb1 : nullptr;
+        auto load = [&](long long kk) -> float {
+            if (row == nullptr || kk >= a.k) return 0.0f;
+            const uint8_t* p = row + kk * a.nb0;
+            return a.type == SDB_TYPE_F16 ? __half2float(*reinterpret_cast<const __half*>(p))
+                                          : *reinterpret_cast<const float*>(p);
+        };
+        float row_max = 0.0f;
+        if (!a.weight_groups) {
+            for (long long kk = lane; kk < a.k; kk += 32) row_max = fmaxf(row_max, fabsf(load(kk)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, o));
+        }
+        for (int g = 0; g < a.groups; ++g) {
+            float w[EPL];
+            float m = row_max;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                w[e] = load(static_cast<long long>(g) * a.group + lane * EPL + e);
+                if (a.weight_groups) m = fmaxf(m, fabsf(w[e]));
+            }
+            if (a.weight_groups) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            }
+            const float s = __fdiv_rn(m, static_cast<float>(a.wmax));
+            const float inverse = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+            int sum = 0;
+            uint64_t bytes = 0;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                const float v = fminf(fmaxf(rintf(__fmul_rn(w[e], inverse)), static_cast<float>(-a.wmax)),
+                                      static_cast<float>(a.wmax));
+                const int qi = static_cast<int>(v);
+                sum += qi;
+                bytes |= static_cast<uint64_t>(static_cast<uint8_t>(static_cast<int8_t>(qi))) << (8 * e);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            int8_t* dst = a.q + r * a.kpad + static_cast<long long>(g) * a.group + lane * EPL;
+            if (EPL == 8) *reinterpret_cast<uint64_t*>(dst) = bytes;
+            else if (EPL == 4) *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(bytes);
+            else if (EPL == 2) *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
+            else *reinterpret_cast<uint8_t*>(dst) = static_cast<uint8_t>(bytes);
+            if (lane == 0) {
+                a.scales[(2LL * g) * a.rows + r] = s;
+                a.scales[(2LL * g + 1) * a.rows + r] = __fmul_rn(s, static_cast<float>(sum));
+            }
+        }
+    }
+}
+
 struct Key {
     int dev;
     const void* data;
@@ -80,10 +167,12 @@ struct Key {
     int layout;
     int icp;
     int64_t half;
+    int64_t variant;
     bool operator<(const Key& o) const {
-        return std::tie(dev, data, type, ne[0], ne[1], ne[2], ne[3], nb[0], nb[1], nb[2], nb[3], layout, icp, half) <
+        return std::tie(dev, data, type, ne[0], ne[1], ne[2], ne[3], nb[0], nb[1], nb[2], nb[3], layout, icp, half,
+                        variant) <
                std::tie(o.dev, o.data, o.type, o.ne[0], o.ne[1], o.ne[2], o.ne[3], o.nb[0], o.nb[1], o.nb[2],
-                        o.nb[3], o.layout, o.icp, o.half);
+                        o.nb[3], o.layout, o.icp, o.half, o.variant);
     }
 };
 
@@ -98,6 +187,44 @@ int64_t extent_bytes(const sdb_tensor* t) {
 }
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+// The store's entry for `key`, if any (*found), made safe to read on `stream`.
+int lookup(const Key& key, cudaStream_t stream, std::shared_ptr<Packed>* out, bool* found) {
+    *found = false;
+    const bool keep = tuning().store != 0;
+    if (!keep) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
+        if (cap != cudaStreamCaptureStatusNone) return fail(SDB_INVALID, "store=0 packs per call: not under capture");
+        return SDB_OK;
+    }
+    std::lock_guard<std::mutex> lock(g_store_mutex);
+    auto it = g_store.find(key);
+    if (it == g_store.end()) return SDB_OK;
+    // Wait for the packing only while it may still run.  Under stream
+    // capture nothing may be queried: the packing must have finished
+    // (been seen finished) before the capture began.
+    Packed& pk = *it->second;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
+    if (cap != cudaStreamCaptureStatusNone) {
+        if (!pk.done) return fail(SDB_INVALID, "weights first used under stream capture: call once before");
+    } else if (!pk.done) {
+        const cudaError_t q = cudaEventQuery(pk.ready);
+        if (q == cudaSuccess) pk.done = true;
+        else if (q == cudaErrorNotReady) SDB_CUDA(cudaStreamWaitEvent(stream, pk.ready, 0));
+        else return cuda_fail(q, "cudaEventQuery(packed weights)");
+    }
+    *out = it->second;
+    *found = true;
+    return SDB_OK;
+}
+
+void remember(const Key& key, const std::shared_ptr<Packed>& p) {
+    if (tuning().store == 0) return;
+    std::lock_guard<std::mutex> lock(g_store_mutex);
+    g_store[key] = p;
+}
 
 int make_maps(Packed& p) {
     const uint64_t dims[2] = {static_cast<uint64_t>(p.kpad), static_cast<uint64_t>(p.rows_total)};
@@ -117,42 +244,17 @@ int make_maps(Packed& p) {
 Packed::~Packed() {
     if (ready) cudaEventDestroy(ready);
     if (data) cudaFree(data);
+    if (qscales) cudaFree(qscales);
 }
 
 int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_t k_logical, int icp, int64_t half,
                    cudaStream_t stream, std::shared_ptr<Packed>* out) {
     int dev = 0;
     SDB_CUDA(cudaGetDevice(&dev));
-    const bool keep = tuning().store != 0;
-    if (!keep) {
-        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-        SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
-        if (cap != cudaStreamCaptureStatusNone) return fail(SDB_INVALID, "store=0 packs per call: not under capture");
-    }
-    Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]}, {w->nb[0], w->nb[1], w->nb[2], w->nb[3]},
-            static_cast<int>(layout), icp, half};
-    if (keep) {
-        std::lock_guard<std::mutex> lock(g_store_mutex);
-        auto it = g_store.find(key);
-        if (it != g_store.end()) {
-            // Wait for the packing only while it may still run.  Under stream
-            // capture nothing may be queried: the packing must have finished
-            // (been seen finished) before the capture began.
-            Packed& pk = *it->second;
-            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-            SDB_CUDA(cudaStreamIsCapturing(stream, &cap));
-            if (cap != cudaStreamCaptureStatusNone) {
-                if (!pk.done) return fail(SDB_INVALID, "weights first used under stream capture: call once before");
-            } else if (!pk.done) {
-                const cudaError_t q = cudaEventQuery(pk.ready);
-                if (q == cudaSuccess) pk.done = true;
-                else if (q == cudaErrorNotReady) SDB_CUDA(cudaStreamWaitEvent(stream, pk.ready, 0));
-                else return cuda_fail(q, "cudaEventQuery(packed weights)");
-            }
-            *out = it->second;
-            return SDB_OK;
-        }
-    }
+    const Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]},
+                  {w->nb[0], w->nb[1], w->nb[2], w->nb[3]}, static_cast<int>(layout), icp, half, 0};
+    bool found = false;
+    if (int s = lookup(key, stream, out, &found); s != SDB_OK || found) return s;
     auto p = std::make_shared<Packed>();
     const bool split = w->type == SDB_TYPE_F32;
     int64_t kdim;
@@ -200,10 +302,85 @@ int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_
     count_launch();
     SDB_CUDA(cudaGetLastError());
     SDB_CUDA(cudaEventRecord(p->ready, stream));
-    if (keep) {
-        std::lock_guard<std::mutex> lock(g_store_mutex);
-        g_store[key] = p;
+    remember(key, p);
+    *out = p;
+    return SDB_OK;
+}
+
+int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_t k_logical, int64_t half,
+                      const QuantSpec& q, cudaStream_t stream, std::shared_ptr<Packed>* out) {
+    if (q.group % 32 != 0 || q.group < 32 || q.group > 256)
+        return fail(SDB_NOT_SUPPORTED, "quantized products: group must be 32, 64, 128 or 256");
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    const Layout layout = gated ? Layout::quantized_gated : Layout::quantized;
+    const Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]},
+                  {w->nb[0], w->nb[1], w->nb[2], w->nb[3]}, static_cast<int>(layout), 0, gated ? half : 0,
+                  q.variant()};
+    bool found = false;
+    if (int s = lookup(key, stream, out, &found); s != SDB_OK || found) return s;
+
+    auto p = std::make_shared<Packed>();
+    p->group = q.group;
+    p->groups = static_cast<int>((k_logical + q.group - 1) / q.group);
+    p->kpad = static_cast<int64_t>(p->groups) * q.group;
+    if (gated) {
+        const int64_t halfpad = round_up(half, kRowPad);
+        p->npad = 2 * halfpad;
+        p->rows_total = 2 * halfpad;
+        p->b1_row = halfpad;
+    } else {
+        p->npad = round_up(n_logical, kRowPad);
+        p->rows_total = p->npad;
     }
+    p->bytes = static_cast<size_t>(p->rows_total * p->kpad) + static_cast<size_t>(2 * p->groups * p->rows_total * 4);
+    SDB_CUDA(cudaMalloc(&p->data, static_cast<size_t>(p->rows_total * p->kpad)));
+    SDB_CUDA(cudaMalloc(&p->qscales, static_cast<size_t>(2 * p->groups * p->rows_total * 4)));
+    SDB_CUDA(cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming));
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(p->kpad), static_cast<uint64_t>(p->rows_total)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(p->kpad)};
+        const uint32_t box[2] = {64, 64};
+        if (encode_tensor_map(&p->qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->data, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_64B) != CUDA_SUCCESS)
+            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for quantized weights");
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(p->rows_total), static_cast<uint64_t>(2 * p->groups)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(p->rows_total) * 4};
+        const uint32_t box[2] = {64, 2};
+        if (encode_tensor_map(&p->qsmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p->qscales, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for quantized weight scales");
+    }
+    QPackArgs a{};
+    a.src = static_cast<const uint8_t*>(w->data);
+    a.type = w->type;
+    a.nb0 = w->nb[0];
+    a.nb1 = w->nb[1];
+    a.n = gated ? half : n_logical;
+    a.k = k_logical;
+    a.gated = gated ? 1 : 0;
+    a.halfpad = p->b1_row;
+    a.rows = p->rows_total;
+    a.group = q.group;
+    a.groups = p->groups;
+    a.wmax = q.wmax;
+    a.weight_groups = q.weight_groups ? 1 : 0;
+    a.kpad = p->kpad;
+    a.q = static_cast<int8_t*>(p->data);
+    a.scales = static_cast<float*>(p->qscales);
+    const int blocks = static_cast<int>(std::min<long long>((a.rows + 7) / 8, 148LL * 8));
+    switch (q.group / 32) {
+        case 1: quantize_weights_kernel<1><<<blocks, 256, 0, stream>>>(a); break;
+        case 2: quantize_weights_kernel<2><<<blocks, 256, 0, stream>>>(a); break;
+        case 4: quantize_weights_kernel<4><<<blocks, 256, 0, stream>>>(a); break;
+        default: quantize_weights_kernel<8><<<blocks, 256, 0, stream>>>(a); break;
+    }
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    SDB_CUDA(cudaEventRecord(p->ready, stream));
+    remember(key, p);
     *out = p;
     return SDB_OK;
 }

@@ -19,6 +19,21 @@ enum class Layout : int {
     linear = 0,   // rows n of w [K, N]; k as is
     conv = 1,     // rows oc of w [KW, KH, IC, OC]; k = (ky * KW + kx) * icp + ic
     gated = 2,    // GEGLU: rows [0, half) x weights, [halfpad, halfpad + half) gate weights
+    quantized = 3,        // linear, quantized (quant.cuh): int8 rows n, k padded to whole groups
+    quantized_gated = 4,  // GEGLU, quantized: rows as `gated`
+};
+
+// What a quantized packing depends on (the reference's quantized_variant,
+// mul_mat.cc:378-381): the group, the weights' greatest magnitude and whether
+// each group has its own scale.
+struct QuantSpec {
+    int group = 64;
+    int wmax = 127;
+    bool weight_groups = true;
+    int64_t variant() const {
+        return static_cast<int64_t>(group) | static_cast<int64_t>(wmax) << 16 |
+               static_cast<int64_t>(weight_groups ? 1 : 0) << 32;
+    }
 };
 
 constexpr int kRowPad = 256;  // packed rows are padded to the widest GEMM tile
@@ -36,6 +51,13 @@ struct Packed {
     CUtensorMap map128{};     // box {64, 128}
     CUtensorMap map192{};     // box {64, 192}
     CUtensorMap map256{};     // box {64, 256}
+    // Quantized layouts: data is int8 [rows_total][kpad], kpad = groups * group;
+    // qscales FP32 [2 * groups][rows_total]: row 2g the scales of group g, 2g + 1
+    // the offsets (scale * sum of the group's integers).
+    void* qscales = nullptr;
+    int group = 0, groups = 0;
+    CUtensorMap qmap{};       // int8, box {64, 64}, 64-byte swizzle
+    CUtensorMap qsmap{};      // FP32, box {64, 2}
     cudaEvent_t ready = nullptr;
     bool done = false;        // the packing was seen complete
     bool owned_by_store = true;
@@ -48,5 +70,11 @@ struct Packed {
 // Returns an sdb_status; *out is set on success.
 int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_t k_logical, int icp,
                    int64_t half, cudaStream_t stream, std::shared_ptr<Packed>* out);
+
+// The quantized form of w (Layout::quantized, or quantized_gated with `half`),
+// from the store or quantized now on `stream`, as the reference's
+// quantize_weights_f16/_f32 quantize (quant.cc:204-244, 366-377).
+int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_t k_logical, int64_t half,
+                      const QuantSpec& q, cudaStream_t stream, std::shared_ptr<Packed>* out);
 
 }  // namespace sdb

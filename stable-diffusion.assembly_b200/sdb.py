@@ -256,6 +256,16 @@ def mul_mat(w, x, out=None, chain: Chain | None = None, stream=None):
     return out
 
 
+def mul_mat_supported(w, x, out) -> bool:
+    """Whether sdb_mul_mat takes these operands (under the tuning in effect)."""
+    return bool(load().sdb_mul_mat_supported(describe(w), describe(x), describe(out)))
+
+
+def mul_mat_gated_supported(w, x, out) -> bool:
+    """Whether sdb_mul_mat_gated takes these operands (under the tuning in effect)."""
+    return bool(load().sdb_mul_mat_gated_supported(describe(w), describe(x), describe(out)))
+
+
 def mul_mat_gated(w, x, out=None, chain: Chain | None = None, stream=None):
     """GEGLU: y = x w^T (+chain), out = y[..., :N/2] * GELU(y[..., N/2:])."""
     import torch
