@@ -14,6 +14,8 @@ that packs operands as the reference's gemm.cc does and calls the kernels:
     sdasm_gemm_6x16_avx2      (gemm_avx2.S)        the 6 x 16 FP32 tile
     sdasm_gated_gelu_avx2     (activation_avx2.S)  out = x GELU(gate)
     sdasm_exponentials_avx2   (softmax_avx2.S)     exp(s - max) and its sums
+    sdasm_qgemm_6x16_au_avx512 (quant_avx512.S)    the quantized 6 x 16 tile (AVX512-VNNI)
+    sdasm_quantize16_avx2     (quantize_avx2.S)    a panel of 16 columns quantized
 The library pins the oracle (tests/test_golden.py), generates the golden
 fixtures (tests/golden/make_golden.py) and, driven on all host threads
 (refk_mul_mat_mt, refk_conv2d_mt), is the CPU baseline of bench.py for the
@@ -30,7 +32,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-KERNELS = ["gemm_avx2", "activation_avx2", "softmax_avx2"]
+KERNELS = ["gemm_avx2", "activation_avx2", "softmax_avx2", "quant_avx512", "quantize_avx2"]
 HEXFLOAT = re.compile(r"(?<![\w.])(-?0x[0-9a-fA-F]+(?:\.[0-9a-fA-F]*)?p[+-]?\d+)")
 
 

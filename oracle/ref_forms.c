@@ -347,13 +347,10 @@ static void quantize_input_group(const float *x, int n, int group, int levels, u
     *offset = s * zero;
 }
 
-void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, int group, int levels, int wmax,
-                 int weight_groups, int accumulate) {
+/* Weights (N, K) -> q [N][groups * group] int8, scale and offset [N][groups]. */
+void rf_quantize_weights(const float *w, int N, int K, int group, int wmax, int weight_groups, int8_t *qw, float *sw,
+                         float *ow) {
     const int groups = (K + group - 1) / group;
-    int8_t *qw = (int8_t *)malloc((size_t)N * groups * group);
-    float *sw = (float *)malloc(sizeof(float) * (size_t)N * groups), *ow = (float *)malloc(sizeof(float) * (size_t)N * groups);
-    uint8_t *qx = (uint8_t *)malloc((size_t)M * groups * group);
-    float *sx = (float *)malloc(sizeof(float) * (size_t)M * groups), *ox = (float *)malloc(sizeof(float) * (size_t)M * groups);
 #pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
         float row_max = 0.0f;
@@ -384,6 +381,11 @@ void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, 
             ow[(size_t)n * groups + g] = s * (float)sum;
         }
     }
+}
+
+/* Inputs (M, K) -> q [M][groups * group] uint8, scale and offset [M][groups]. */
+void rf_quantize_inputs(const float *x, int M, int K, int group, int levels, uint8_t *qx, float *sx, float *ox) {
+    const int groups = (K + group - 1) / group;
 #pragma omp parallel for schedule(static)
     for (int m = 0; m < M; ++m)
         for (int g = 0; g < groups; ++g) {
@@ -391,6 +393,11 @@ void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, 
             quantize_input_group(x + (size_t)m * K + g * group, cnt, group, levels, qx + ((size_t)m * groups + g) * group,
                                  &sx[(size_t)m * groups + g], &ox[(size_t)m * groups + g]);
         }
+}
+
+/* The fold of quantized operands: y (M, N), from 0 or (accumulate) y's values. */
+void rf_qfold(const uint8_t *qx, const float *sx, const float *ox, int M, const int8_t *qw, const float *sw,
+              const float *ow, int N, int groups, int group, float *y, int accumulate) {
 #pragma omp parallel for schedule(static)
     for (int m = 0; m < M; ++m)
         for (int n = 0; n < N; ++n) {
@@ -406,6 +413,18 @@ void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, 
             }
             y[(size_t)m * N + n] = t;
         }
+}
+
+void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, int group, int levels, int wmax,
+                 int weight_groups, int accumulate) {
+    const int groups = (K + group - 1) / group;
+    int8_t *qw = (int8_t *)malloc((size_t)N * groups * group);
+    float *sw = (float *)malloc(sizeof(float) * (size_t)N * groups), *ow = (float *)malloc(sizeof(float) * (size_t)N * groups);
+    uint8_t *qx = (uint8_t *)malloc((size_t)M * groups * group);
+    float *sx = (float *)malloc(sizeof(float) * (size_t)M * groups), *ox = (float *)malloc(sizeof(float) * (size_t)M * groups);
+    rf_quantize_weights(w, N, K, group, wmax, weight_groups, qw, sw, ow);
+    rf_quantize_inputs(x, M, K, group, levels, qx, sx, ox);
+    rf_qfold(qx, sx, ox, M, qw, sw, ow, N, groups, group, y, accumulate);
     free(qw);
     free(sw);
     free(ow);

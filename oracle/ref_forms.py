@@ -55,6 +55,9 @@ def load() -> ctypes.CDLL:
         lib.rf_attention.argtypes = [P, P, P, P, i, i, i, i, i, i, i, f, i, i]
         lib.rf_group_norm.argtypes = [P, P, i, i, ctypes.c_long, i, f, P, P, i]
         lib.rf_qmul_mat.argtypes = [P, i, i, P, i, P, i, i, i, i, i]
+        lib.rf_quantize_weights.argtypes = [P, i, i, i, i, i, P, P, P]
+        lib.rf_quantize_inputs.argtypes = [P, i, i, i, i, P, P, P]
+        lib.rf_qfold.argtypes = [P, P, P, i, P, P, P, i, i, i, P, i]
         lib.rf_threads.restype = i
         lib.rf_set_threads.argtypes = [i]
         _lib = lib
@@ -139,4 +142,39 @@ def qmul_mat(w: np.ndarray, x: np.ndarray, group: int = 64, levels: int = 255, w
     y = np.ascontiguousarray(y0, dtype=np.float32).copy() if y0 is not None else np.empty((m, n), np.float32)
     load().rf_qmul_mat(_p(w32), n, k, _p(x), m, _p(y), group, levels, wmax,
                        1 if weight_groups else 0, 1 if y0 is not None else 0)
+    return y
+
+
+def quantize_inputs(x: np.ndarray, group: int = 64, levels: int = 255):
+    """Inputs (M, K) float32 -> (bytes (M, groups * group) uint8, scales (M, groups), offsets (M, groups))."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    groups = -(-k // group)
+    q = np.empty((m, groups * group), np.uint8)
+    s = np.empty((m, groups), np.float32)
+    o = np.empty((m, groups), np.float32)
+    load().rf_quantize_inputs(_p(x), m, k, group, levels, _p(q), _p(s), _p(o))
+    return q, s, o
+
+
+def quantize_weights(w: np.ndarray, group: int = 64, wmax: int = 127, weight_groups: bool = True):
+    """Weights (N, K) -> (bytes (N, groups * group) int8, scales (N, groups), offsets (N, groups))."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    groups = -(-k // group)
+    q = np.empty((n, groups * group), np.int8)
+    s = np.empty((n, groups), np.float32)
+    o = np.empty((n, groups), np.float32)
+    load().rf_quantize_weights(_p(w), n, k, group, wmax, 1 if weight_groups else 0, _p(q), _p(s), _p(o))
+    return q, s, o
+
+
+def qfold(xq, wq, group: int = 64, y0: np.ndarray | None = None) -> np.ndarray:
+    """The fold of quantized operands (quantize_inputs' and quantize_weights' triples) -> (M, N) float32."""
+    qx, sx, ox = (np.ascontiguousarray(a) for a in xq)
+    qw, sw, ow = (np.ascontiguousarray(a) for a in wq)
+    m, n, groups = qx.shape[0], qw.shape[0], sx.shape[1]
+    y = np.ascontiguousarray(y0, dtype=np.float32).copy() if y0 is not None else np.empty((m, n), np.float32)
+    load().rf_qfold(_p(qx), _p(sx), _p(ox), m, _p(qw), _p(sw), _p(ow), n, groups, group, _p(y),
+                    1 if y0 is not None else 0)
     return y
