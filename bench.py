@@ -805,8 +805,9 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     line = {
         "metric": UNET_METRIC, "value": world * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": "f32" if not args.tune else f"f32 ({args.tune})", "data": "synthetic",
         "config": {"workload": UNET_WORKLOAD, "resolution": "512x512 (latent 64x64)", "batch": "2 (CFG)",
+                   "tuning": args.tune or "default (FP32-accurate products)",
                    "context": "2x77x768", "sampler": f"Euler, {SAMPLER_STEPS} steps, CFG 7",
                    "weights": f"random-init FP16, {net.params / 1e6:.1f}M parameters, packed once",
                    "parallelism": f"replicas x{world} (one image a GPU)",
@@ -860,6 +861,8 @@ OPS = {
     "conv3x3_1280x16x16x2": lambda torch, sdb, dev: _op_conv(torch, sdb, dev, 1280, 1280, 16, 2),
     "attention_4096x4096_d40_b1": lambda torch, sdb, dev: _op_attention(torch, sdb, dev, 4096, 4096, 40, 1),
     "linear_8192x320x320": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 320),
+    "linear_8192x320x1280": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 1280),
+    "linear_2048x640x640": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 2048, 640, 640),
     "groupnorm_2x64x64x320": lambda torch, sdb, dev: _op_groupnorm(torch, sdb, dev, 2, 64, 320),
 }
 
@@ -901,13 +904,15 @@ def _op_groupnorm(torch, sdb, dev, n, hw, c):
     return lambda: sdb.group_norm_nhwc(x, 32, 1e-5, out=y, chain=chain)
 
 
-def run_op(name: str, reps: int = 3) -> None:
+def run_op(name: str, tune: str = "", reps: int = 3) -> None:
     """Runs one named operation `reps` times (for ncu captures of a single kernel on a small case)."""
     import torch
     import sdb
 
     dev = torch.device("cuda", 0)
     sdb.load()
+    if tune:
+        sdb.set_tuning(tune)
     fn = OPS[name](torch, sdb, dev)
     for _ in range(reps):
         fn()
@@ -924,9 +929,10 @@ def main() -> None:
     ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=sorted(OPS), help="run one operation three times (profiler captures) and exit")
+    ap.add_argument("--tune", default="", help="sdb_set_tuning spec for the run, e.g. bits=8 (the quantized linear layers)")
     args = ap.parse_args()
     if args.op:
-        run_op(args.op)
+        run_op(args.op, args.tune)
         return
     if args.steps is None:
         args.steps = 100 if args.workload == "unet" else 1000
@@ -952,6 +958,8 @@ def main() -> None:
     import sdb
 
     sdb.load()
+    if args.tune:
+        sdb.set_tuning(args.tune)
 
     def barrier():
         if dist is not None:

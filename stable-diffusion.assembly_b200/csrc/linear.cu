@@ -82,17 +82,6 @@ void choose_ksplit(GemmArgs& a, int tiles, int wmode) {
     a.ksplit = (a.kblocks + a.per_split - 1) / a.per_split;
 }
 
-// A 2-D FP32 map for the epilogue's TMA stores: `cols` x `rows` with rows
-// `ld` floats apart, boxes of 32 rows x box_cols (32: 128-byte swizzle for the
-// 128-wide kernel; 16: 64-byte swizzle for the wide kernel).
-bool store_map(CUtensorMap* map, void* base, long long cols, long long rows, long long ld, int box_cols) {
-    const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
-    const uint32_t box[2] = {static_cast<uint32_t>(box_cols), 32};
-    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
-                             box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) == CUDA_SUCCESS;
-}
-
 // The wide kernel's plan for an M x N x K product (gated: N of the output, 2N
 // of the product): the tile width and the K split that minimise
 //   waves x (k-blocks of an item) x (a k-block's shared-memory bytes)

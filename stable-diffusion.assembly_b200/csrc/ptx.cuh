@@ -63,6 +63,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Both phases complete, tested in one round trip.
+__device__ __forceinline__ bool mbar_try_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 q, [%3], %4;\n\t"
+        "and.pred p, p, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b1)), "r"(p1), "r"(smem_u32(b2)), "r"(p2)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `parity` to complete.  Returns false when the kernel
 // is winding down: either another thread set *abort, or this wait ran past
 // kWaitLimitCycles SM clocks (about 2 s at the B200's clocks), in which case
@@ -169,6 +184,8 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 // Waits until the shared-memory sources of this thread's bulk stores may be
 // reused (.read) / until the stores are complete.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Until at most the most recent bulk group may still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_but_one() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

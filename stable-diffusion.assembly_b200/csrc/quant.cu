@@ -16,19 +16,19 @@ namespace sdb {
 
 namespace {
 
-int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
-
 // The reference's quantization of a row's group of inputs (quant.cc:282-313):
 // lo, hi the least and greatest of the group's numbers and 0,
 // s = (hi - lo) / levels, inverse = s > 0 ? 1 / s : 0, zero = rint(-lo * inverse),
 // q = clamp(rint(x * inverse) + zero, 0, levels); the numbers past k the zero
 // point; the group's scale s and offset s * zero.  One warp a (row, group),
-// EPL numbers a lane.  Output: q [m][kpad] bytes, scales [2 * groups][ld]
-// (row 2g scales, 2g + 1 offsets).
+// EPL numbers a lane.  Output in the GEMM's tiles: the bytes of row
+// 128 tm + r, k-byte 64 ls + b at q[(tm * nstages + ls) * 8192 +
+// quant_tile_offset(r, b)]; its group g's scale and offset at
+// scales[((tm * groups + g) * 2 + {0, 1}) * 128 + r].
 template <int EPL>
 __global__ void quantize_inputs_kernel(const float* __restrict__ x, long long m, long long k, int group, int groups,
-                                       long long kpad, int levels, uint8_t* __restrict__ q,
-                                       float* __restrict__ scales, long long ld) {
+                                       int nstages, int levels, uint8_t* __restrict__ q,
+                                       float* __restrict__ scales) {
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
     const long long total = m * groups;
@@ -62,24 +62,27 @@ __global__ void quantize_inputs_kernel(const float* __restrict__ x, long long m,
                                         : zero;
             bytes |= static_cast<uint64_t>(static_cast<uint8_t>(qv)) << (8 * e);
         }
-        uint8_t* dst = q + row * kpad + k0;
+        const long long tm = row >> 7;
+        const int r = static_cast<int>(row & 127);
+        uint8_t* dst = q + (tm * nstages + (k0 >> 6)) * 8192 + quant_tile_offset(r, static_cast<int>(k0 & 63));
         if (EPL == 8) *reinterpret_cast<uint64_t*>(dst) = bytes;
         else if (EPL == 4) *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(bytes);
         else if (EPL == 2) *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
         else *dst = static_cast<uint8_t>(bytes);
         if (lane == 0) {
-            scales[(2LL * g) * ld + row] = s;
-            scales[(2LL * g + 1) * ld + row] = __fmul_rn(s, zero);
+            float* sc = scales + (tm * groups + g) * 256;
+            sc[r] = s;
+            sc[128 + r] = __fmul_rn(s, zero);
         }
     }
 }
 
 template <bool GATED>
-int launch_qgemm(const CUtensorMap& amap, const CUtensorMap& asmap, const Packed& p, QGemmArgs a, cudaStream_t st) {
+int launch_qgemm(const CUtensorMap& ymap, QGemmArgs a, cudaStream_t st) {
     auto kern = qgemm_kernel<GATED>;
     SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmemBytes));
     const int grid = std::min(a.items, current_sm_count());
-    kern<<<grid, kQThreads, kQSmemBytes, st>>>(amap, asmap, p.qmap, p.qsmap, a);
+    kern<<<grid, kQThreads, kQSmemBytes, st>>>(ymap, a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
@@ -117,10 +120,11 @@ int run_quantized_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
     if (int s = quantized_weights(w, gated, gated ? 2 * n : n, k, gated ? n : 0, spec, st, &p); s != SDB_OK)
         return s;
     const int groups = p->groups;
-    const int64_t kpad = p->kpad;
-    const int64_t ld = round_up(m, 4);
-    const size_t q_bytes = static_cast<size_t>(round_up(m * kpad, 256));
-    const size_t s_bytes = static_cast<size_t>(2 * groups * ld * 4);
+    const int cpg = spec.group / 32;
+    const int nstages = (groups * cpg + 1) / 2;
+    const int64_t tiles_m = (m + kQRows - 1) / kQRows;
+    const size_t q_bytes = static_cast<size_t>(tiles_m * nstages * kQABytes);
+    const size_t s_bytes = static_cast<size_t>(tiles_m * groups * 1024);
     void* ws = nullptr;
     if (int s = workspace(st, q_bytes + s_bytes, &ws); s != SDB_OK) return s;
     uint8_t* qa = static_cast<uint8_t*>(ws);
@@ -129,44 +133,30 @@ int run_quantized_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
     const long long warps = m * groups;
     const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 16));
     const float* xs = static_cast<const float*>(x->data);
-    switch (spec.group / 32) {
-        case 1: quantize_inputs_kernel<1><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, kpad, levels, qa, sa, ld); break;
-        case 2: quantize_inputs_kernel<2><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, kpad, levels, qa, sa, ld); break;
-        case 4: quantize_inputs_kernel<4><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, kpad, levels, qa, sa, ld); break;
-        default: quantize_inputs_kernel<8><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, kpad, levels, qa, sa, ld); break;
+    switch (cpg) {
+        case 1: quantize_inputs_kernel<1><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, nstages, levels, qa, sa); break;
+        case 2: quantize_inputs_kernel<2><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, nstages, levels, qa, sa); break;
+        case 4: quantize_inputs_kernel<4><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, nstages, levels, qa, sa); break;
+        default: quantize_inputs_kernel<8><<<blocks, 256, 0, st>>>(xs, m, k, spec.group, groups, nstages, levels, qa, sa); break;
     }
     count_launch();
     SDB_CUDA(cudaGetLastError());
 
-    CUtensorMap amap, asmap;
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(kpad), static_cast<uint64_t>(m)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(kpad)};
-        const uint32_t box[2] = {64, 128};
-        if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qa, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_64B) != CUDA_SUCCESS)
-            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the quantized inputs");
-    }
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(ld), static_cast<uint64_t>(2 * groups)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
-        const uint32_t box[2] = {128, 2};
-        if (encode_tensor_map(&asmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, sa, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
-            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the input scales");
-    }
     QGemmArgs a{};
+    a.a = qa;
+    a.as = sa;
+    a.w = static_cast<const uint8_t*>(p->data);
+    a.ws = static_cast<const float*>(p->qscales);
     a.m = static_cast<int>(m);
     a.n = static_cast<int>(n);
     a.groups = groups;
-    a.cpg = spec.group / 32;
+    a.cpg = cpg;
     a.kchunks = groups * a.cpg;
-    a.tiles_m = static_cast<int>((m + kQRows - 1) / kQRows);
+    a.tiles_m = static_cast<int>(tiles_m);
     a.tiles_n = static_cast<int>(gated ? (n + 63) / 64 : (n + 127) / 128);
     const long long items = static_cast<long long>(a.tiles_m) * a.tiles_n;
     if (items >= (1LL << 31)) return fail(SDB_NOT_SUPPORTED, "quantized product: too many tiles");
     a.items = static_cast<int>(items);
-    a.b_second = static_cast<int>(p->b1_row);
     a.magic = static_cast<long long>(spec.group) * levels * spec.wmax < (1LL << 22) ? 1 : 0;
     a.y = static_cast<float*>(chain && chain->redirect ? chain->redirect : dst->data);
     for (int d = 0; d < 4; ++d) a.ynb[d] = dst->nb[d] / 4;
@@ -174,7 +164,14 @@ int run_quantized_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
     a.rne2 = dst->ne[2];
     a.chain = make_chain(chain);
     a.err = device_error_word();
-    return gated ? launch_qgemm<true>(amap, asmap, *p, a, st) : launch_qgemm<false>(amap, asmap, *p, a, st);
+    // The output by TMA stores when its rows are 16-byte aligned runs.
+    CUtensorMap ymap{};
+    a.store = kStoreDirect;
+    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ynb[0] == 1 && a.ynb[1] == n &&
+        store_map(&ymap, a.y, n, m, n, 16))
+        a.store = kStoreTma;
+    if (p->tiles != a.tiles_n) return fail(SDB_INVALID, "quantized weights: tile count mismatch");
+    return gated ? launch_qgemm<true>(ymap, a, st) : launch_qgemm<false>(ymap, a, st);
 }
 
 }  // namespace sdb

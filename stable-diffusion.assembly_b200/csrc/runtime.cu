@@ -195,3 +195,15 @@ int sdb_token_downsampling(int64_t width, int64_t height) {
 }
 
 }  // extern "C"
+
+namespace sdb {
+
+bool store_map(CUtensorMap* map, void* base, long long cols, long long rows, long long ld, int box_cols) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
+    const uint32_t box[2] = {static_cast<uint32_t>(box_cols), 32};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                             box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) == CUDA_SUCCESS;
+}
+
+}  // namespace sdb

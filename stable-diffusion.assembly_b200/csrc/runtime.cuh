@@ -51,6 +51,10 @@ CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t 
 
 int current_sm_count();
 
+// The map of a row-major FP32 matrix (`cols` x `rows`, `ld` floats a row) for
+// TMA stores of 32-row boxes of `box_cols` (32: 128-byte swizzle; 16: 64-byte).
+bool store_map(CUtensorMap* map, void* base, long long cols, long long rows, long long ld, int box_cols);
+
 #define SDB_CUDA(call)                                        \
     do {                                                      \
         cudaError_t e_ = (call);                              \

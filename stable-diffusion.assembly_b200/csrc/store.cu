@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "ptx.cuh"
+#include "quant.cuh"
 #include "runtime.cuh"
 
 namespace sdb {
@@ -76,7 +77,8 @@ __global__ void pack_weights_kernel(const PackArgs p) {
 // missing numbers zeros), m = max |w| over the group (or the whole row),
 // s = m / wmax, inverse = s > 0 ? 1 / s : 0, q = clamp(rint(w * inverse),
 // -wmax, wmax); the group's scale s and offset s * sum(q).  One warp a row;
-// every operation rounds as the reference's scalar one does.
+// every operation rounds as the reference's scalar one does.  Written in the
+// quantized GEMM's tiles (store.cuh, Packed).
 struct QPackArgs {
     const uint8_t* src;
     int type;
@@ -84,12 +86,10 @@ struct QPackArgs {
     long long n;          // logical rows (gated: of one half)
     long long k;
     int gated;
-    long long halfpad;
-    long long rows;       // packed rows
-    int group, groups, wmax, weight_groups;
-    long long kpad;
+    long long rows;       // packed rows: tiles * 128
+    int group, groups, nstages, wmax, weight_groups;
     int8_t* q;
-    float* scales;        // [2 * groups][rows]
+    float* scales;
 };
 
 template <int EPL>
@@ -98,20 +98,21 @@ __global__ void quantize_weights_kernel(const QPackArgs a) {
     const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
     for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < a.rows;
          r += warps) {
+        const long long tile = r >> 7;
+        const int p = static_cast<int>(r & 127);
         long long src_row = -1;
         if (!a.gated) {
             if (r < a.n) src_row = r;
-        } else if (r < a.n) {
-            src_row = r;
-        } else if (r >= a.halfpad && r - a.halfpad < a.n) {
-            src_row = a.n + (r - a.halfpad);
+        } else {
+            const long long c = tile * 64 + (p & 63);
+            if (c < a.n) src_row = p < 64 ? c : a.n + c;
         }
         const uint8_t* row = src_row >= 0 ? a.src + src_row * a.nb1 : nullptr;
         auto load = [&](long long kk) -> float {
             if (row == nullptr || kk >= a.k) return 0.0f;
-            const uint8_t* p = row + kk * a.nb0;
-            return a.type == SDB_TYPE_F16 ? __half2float(*reinterpret_cast<const __half*>(p))
-                                          : *reinterpret_cast<const float*>(p);
+            const uint8_t* ptr = row + kk * a.nb0;
+            return a.type == SDB_TYPE_F16 ? __half2float(*reinterpret_cast<const __half*>(ptr))
+                                          : *reinterpret_cast<const float*>(ptr);
         };
         float row_max = 0.0f;
         if (!a.weight_groups) {
@@ -122,9 +123,10 @@ __global__ void quantize_weights_kernel(const QPackArgs a) {
         for (int g = 0; g < a.groups; ++g) {
             float w[EPL];
             float m = row_max;
+            const long long k0 = static_cast<long long>(g) * a.group + lane * EPL;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
-                w[e] = load(static_cast<long long>(g) * a.group + lane * EPL + e);
+                w[e] = load(k0 + e);
                 if (a.weight_groups) m = fmaxf(m, fabsf(w[e]));
             }
             if (a.weight_groups) {
@@ -145,14 +147,15 @@ __global__ void quantize_weights_kernel(const QPackArgs a) {
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            int8_t* dst = a.q + r * a.kpad + static_cast<long long>(g) * a.group + lane * EPL;
+            int8_t* dst = a.q + (tile * a.nstages + (k0 >> 6)) * 8192 + quant_tile_offset(p, static_cast<int>(k0 & 63));
             if (EPL == 8) *reinterpret_cast<uint64_t*>(dst) = bytes;
             else if (EPL == 4) *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(bytes);
             else if (EPL == 2) *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
             else *reinterpret_cast<uint8_t*>(dst) = static_cast<uint8_t>(bytes);
             if (lane == 0) {
-                a.scales[(2LL * g) * a.rows + r] = s;
-                a.scales[(2LL * g + 1) * a.rows + r] = __fmul_rn(s, static_cast<float>(sum));
+                float* sc = a.scales + (tile * a.groups + g) * 256;
+                sc[p] = s;
+                sc[128 + p] = __fmul_rn(s, static_cast<float>(sum));
             }
         }
     }
@@ -324,35 +327,19 @@ int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_
     p->group = q.group;
     p->groups = static_cast<int>((k_logical + q.group - 1) / q.group);
     p->kpad = static_cast<int64_t>(p->groups) * q.group;
-    if (gated) {
-        const int64_t halfpad = round_up(half, kRowPad);
-        p->npad = 2 * halfpad;
-        p->rows_total = 2 * halfpad;
-        p->b1_row = halfpad;
-    } else {
-        p->npad = round_up(n_logical, kRowPad);
-        p->rows_total = p->npad;
-    }
-    p->bytes = static_cast<size_t>(p->rows_total * p->kpad) + static_cast<size_t>(2 * p->groups * p->rows_total * 4);
-    SDB_CUDA(cudaMalloc(&p->data, static_cast<size_t>(p->rows_total * p->kpad)));
-    SDB_CUDA(cudaMalloc(&p->qscales, static_cast<size_t>(2 * p->groups * p->rows_total * 4)));
+    const int nstages = (p->groups * (q.group / 32) + 1) / 2;
+    p->tiles = static_cast<int>(gated ? (half + 63) / 64 : (n_logical + 127) / 128);
+    p->rows_total = static_cast<int64_t>(p->tiles) * 128;
+    p->npad = p->rows_total;
+    const size_t q_bytes = static_cast<size_t>(p->tiles) * nstages * 8192;
+    const size_t s_bytes = static_cast<size_t>(p->tiles) * p->groups * 1024;
+    p->bytes = q_bytes + s_bytes;
+    SDB_CUDA(cudaMalloc(&p->data, q_bytes));
+    SDB_CUDA(cudaMalloc(&p->qscales, s_bytes));
+    // Bytes no group covers (the second half of an item's last stage with
+    // groups of 32) are never read; zero them all the same.
+    SDB_CUDA(cudaMemsetAsync(p->data, 0, q_bytes, stream));
     SDB_CUDA(cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming));
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(p->kpad), static_cast<uint64_t>(p->rows_total)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(p->kpad)};
-        const uint32_t box[2] = {64, 64};
-        if (encode_tensor_map(&p->qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->data, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_64B) != CUDA_SUCCESS)
-            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for quantized weights");
-    }
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(p->rows_total), static_cast<uint64_t>(2 * p->groups)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(p->rows_total) * 4};
-        const uint32_t box[2] = {64, 2};
-        if (encode_tensor_map(&p->qsmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p->qscales, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
-            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for quantized weight scales");
-    }
     QPackArgs a{};
     a.src = static_cast<const uint8_t*>(w->data);
     a.type = w->type;
@@ -361,13 +348,12 @@ int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_
     a.n = gated ? half : n_logical;
     a.k = k_logical;
     a.gated = gated ? 1 : 0;
-    a.halfpad = p->b1_row;
     a.rows = p->rows_total;
     a.group = q.group;
     a.groups = p->groups;
+    a.nstages = nstages;
     a.wmax = q.wmax;
     a.weight_groups = q.weight_groups ? 1 : 0;
-    a.kpad = p->kpad;
     a.q = static_cast<int8_t*>(p->data);
     a.scales = static_cast<float*>(p->qscales);
     const int blocks = static_cast<int>(std::min<long long>((a.rows + 7) / 8, 148LL * 8));

@@ -51,13 +51,14 @@ struct Packed {
     CUtensorMap map128{};     // box {64, 128}
     CUtensorMap map192{};     // box {64, 192}
     CUtensorMap map256{};     // box {64, 256}
-    // Quantized layouts: data is int8 [rows_total][kpad], kpad = groups * group;
-    // qscales FP32 [2 * groups][rows_total]: row 2g the scales of group g, 2g + 1
-    // the offsets (scale * sum of the group's integers).
+    // Quantized layouts, in the quantized GEMM's tiles of 128 rows (quant.cuh):
+    // data int8 [tiles][nstages][8 KiB], each block 64 bytes of k of the
+    // tile's rows in the 64-byte swizzle; qscales FP32 [tiles][groups][2][128],
+    // the rows' scales then their offsets (scale * sum of the group's
+    // integers).  A tile's rows: 128 consecutive columns, or (gated) 64 x
+    // columns then the matching 64 gate columns.
     void* qscales = nullptr;
-    int group = 0, groups = 0;
-    CUtensorMap qmap{};       // int8, box {64, 64}, 64-byte swizzle
-    CUtensorMap qsmap{};      // FP32, box {64, 2}
+    int group = 0, groups = 0, tiles = 0;
     cudaEvent_t ready = nullptr;
     bool done = false;        // the packing was seen complete
     bool owned_by_store = true;
