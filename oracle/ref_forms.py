@@ -80,7 +80,7 @@ def mul_mat(w16: np.ndarray, x: np.ndarray) -> np.ndarray:
     """w16 (N, K) float16, x (M, K) float32 -> (M, N) float32 (mul_mat.cc's form)."""
     w16 = np.ascontiguousarray(w16, dtype=np.float16)
     x = np.ascontiguousarray(x, dtype=np.float32)
-    n, k = w32.shape
+    n, k = w16.shape
     m = x.shape[0]
     y = np.empty((m, n), dtype=np.float32)
     load().rf_mul_mat(_p(w16), n, k, _p(x), m, _p(y))
