@@ -135,6 +135,61 @@ def conv2d_exact(w, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1)):
     return exact, magnitude
 
 
+# ---------------------------------------------------------------- Winograd
+
+# F(2x2, 3x3): winograd.cc:14-22.  F(4x4, 3x3), points 0, 1, -1, 2, -1/2, inf:
+# winograd.cc:1155-1190 (B^T, A^T) and 1259-1264 (G, as the reference's float
+# constants).
+WINO_BT2 = np.array([[1, 0, -1, 0], [0, 1, 1, 0], [0, -1, 1, 0], [0, 1, 0, -1]], np.float32)
+WINO_G2 = np.array([[1, 0, 0], [0.5, 0.5, 0.5], [0.5, -0.5, 0.5], [0, 0, 1]], np.float32)
+WINO_AT2 = np.array([[1, 1, 1, 0], [0, 1, -1, -1]], np.float32)
+WINO_BT4 = np.array([[1, 1.5, -2, -1.5, 1, 0], [0, -1, -2.5, -0.5, 1, 0], [0, 1, 0.5, -2.5, 1, 0],
+                     [0, -0.5, -1, 0.5, 1, 0], [0, 2, -1, -2, 1, 0], [0, 1, 1.5, -2, -1.5, 1]], np.float32)
+WINO_G4 = np.array([[1, 0, 0], [np.float32(-1.0) / np.float32(3)] * 3,
+                    [np.float32(1.0) / np.float32(3), np.float32(-1.0) / np.float32(3), np.float32(1.0) / np.float32(3)],
+                    [np.float32(1.0) / np.float32(15), np.float32(2.0) / np.float32(15), np.float32(4.0) / np.float32(15)],
+                    [np.float32(-16.0) / np.float32(15), np.float32(8.0) / np.float32(15), np.float32(-4.0) / np.float32(15)],
+                    [0, 0, 1]], np.float32)
+WINO_AT4 = np.array([[1, 1, 1, 1, 1, 0], [0, 1, -1, 2, -0.5, 0], [0, 1, 1, 4, 0.25, 0],
+                     [0, 1, -1, 8, -0.125, 1]], np.float32)
+
+
+def winograd_f32(w, x, padding=(1, 1), f: int = 4):
+    """The reference's single-precision Winograd form of a 3x3, stride-1 convolution.
+
+    Y = A^T [sum over ic of (G g G^T) (.) (B^T d B)] A per tile of f x f outputs
+    (winograd.cc:9-31, 1148-1190), every transform and the channel sums in
+    float32 as the reference computes them (transform_weights4 winograd.cc:1266-1300:
+    G g then (G g) G^T; the inputs' B^T d B and the outputs' A^T M A likewise).
+    The summation order of the channel sums is numpy's, not the micro-kernel's;
+    the result's error against conv2d_exact is the size of the reference's own
+    (F(4x4): about 7e-7 of the magnitudes at worst, winograd.cc:1165-1168).
+    w (OC, IC, 3, 3), x (N, IC, H, W) -> (N, OC, OH, OW).
+    """
+    bt, g, at = (WINO_BT2, WINO_G2, WINO_AT2) if f == 2 else (WINO_BT4, WINO_G4, WINO_AT4)
+    a = bt.shape[0]
+    x32 = np.asarray(x, dtype=np.float32)
+    w32 = np.asarray(w, dtype=np.float32)
+    n, ic, h, wd = x32.shape
+    oc = w32.shape[0]
+    p0, p1 = padding
+    oh, ow = h + 2 * p1 - 2, wd + 2 * p0 - 2
+    th, tw = -(-oh // f), -(-ow // f)
+    xp = np.zeros((n, ic, th * f + 2, tw * f + 2), np.float32)
+    hh, ww = min(h, th * f + 2 - p1), min(wd, tw * f + 2 - p0)
+    xp[:, :, p1:p1 + hh, p0:p0 + ww] = x32[:, :, :hh, :ww]
+    d = np.stack([np.stack([xp[:, :, i * f:i * f + a, j * f:j * f + a] for j in range(tw)], 1)
+                  for i in range(th)], 1)                      # (n, th, tw, ic, a, a)
+    v = np.einsum("ij,ntwcjk->ntwcik", bt, d, dtype=np.float32)
+    v = np.einsum("ntwcik,lk->ntwcil", v, bt, dtype=np.float32)
+    u = np.einsum("ij,ocjk->ocik", g, w32, dtype=np.float32)
+    u = np.einsum("ocik,lk->ocil", u, g, dtype=np.float32)
+    m = np.einsum("ntwcij,ocij->ntwoij", v, u, dtype=np.float32)
+    y = np.einsum("ij,ntwojk->ntwoik", at, m, dtype=np.float32)
+    y = np.einsum("ntwoik,lk->ntwoil", y, at, dtype=np.float32)
+    return y.transpose(0, 3, 1, 4, 2, 5).reshape(n, oc, th * f, tw * f)[:, :, :oh, :ow]
+
+
 # ---------------------------------------------------------------- attention
 
 def attention_exact(q, k, v, heads: int, kv_heads: int, scale: float):

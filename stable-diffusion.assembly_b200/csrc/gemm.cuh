@@ -71,6 +71,8 @@ struct GemmArgs {
     int per_split;          // k-blocks of a part
     int n;                  // columns of C (linear: output features; gated: the half)
     int b1_row;             // row offset in the packed weights of the second B operand
+    int batch_tiles;        // batched products (Winograd's xi): row tiles of one batch; 0 = one product
+    int b_batch_rows;       // packed weight rows of one batch (batch b's B rows start at b * b_batch_rows)
     uint32_t a_tx;          // bytes of one A tile (hi or lo) as TMA writes it
     int a_planes;           // 2: one TMA box brings hi and lo (a full 128-row tile); 1: one box each
     int tiles_m, tiles_n;   // output tiles along rows / columns
@@ -235,7 +237,8 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                     ay = ty * g.oht * g.s1 - g.p1;
                     az = tz * g.nt;
                 }
-                const int n0 = tn * BN;
+                // B rows of this item: its column tile, in its batch's block of weights.
+                const int n0 = tn * BN + (args.batch_tiles ? (tm / args.batch_tiles) * args.b_batch_rows : 0);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S::kStages;
                     if (!mbar_wait(&empty[s], ((it / S::kStages) & 1) ^ 1, abort, args.err)) { ok = false; break; }

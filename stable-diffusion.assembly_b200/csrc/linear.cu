@@ -15,6 +15,7 @@
 #include "runtime.cuh"
 #include "split.cuh"
 #include "store.cuh"
+#include "winograd.cuh"
 
 namespace sdb {
 
@@ -314,6 +315,138 @@ bool conv_tiles(ConvGeom& g) {
     return g.owt >= 1 && g.oht >= 1 && static_cast<long long>(g.tw) * g.th * g.tn < (1LL << 31);
 }
 
+// The form a convolution is computed in, by the reference's rule
+// (winograd.cc:2107-2123, 1204-1206): Winograd for 3x3 kernels at stride 1,
+// dilation 1 and padding 0..2 with tuning winograd != 0 and at least
+// winograd_positions outputs an image; F(4x4, 3x3) with winograd = 2 for FP16
+// kernels of at least winograd4_positions outputs an image, else F(2x2, 3x3).
+// Two rules of this build's own: Winograd for at least winograd_channels
+// input channels (fewer fill a fraction of the GEMM's 64-channel k-block),
+// and F(4x4) for 16 input channels and more -- a sum of fewer channels does
+// not average the split's rounding down, and F(4x4)'s output transform
+// (coefficients up to 64) would carry it past 1e-6 of the magnitudes.
+// Returns 0 (direct), 2 or 4.
+int winograd_form(const sdb_tensor* w, const sdb_tensor* dst, const int32_t params[6]) {
+    const Tuning& t = tuning();
+    if (t.winograd == 0 || w->ne[0] != 3 || w->ne[1] != 3) return 0;
+    if (params[0] != 1 || params[1] != 1 || params[4] != 1 || params[5] != 1) return 0;
+    if (params[2] < 0 || params[2] > 2 || params[3] < 0 || params[3] > 2) return 0;
+    const int64_t positions = dst->ne[0] * dst->ne[1];
+    if (positions < t.winograd_positions || w->ne[2] < t.winograd_channels) return 0;
+    return t.winograd == 2 && w->type == SDB_TYPE_F16 && positions >= t.winograd4_positions && w->ne[2] >= 16 ? 4
+                                                                                                           : 2;
+}
+
+// Winograd's F(f x f, 3x3) (winograd.cuh): the inputs' transform into the
+// workspace, the XI products as one batched launch of the split GEMM (three
+// FP16 products of the split transforms), the outputs' transform with the
+// chain.  Workspace: V [2][XI][Tp][icp8] FP16, M [XI][Tp][ldm] FP32, then any
+// split-K partial sums.
+int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                 const sdb_chain* chain, cudaStream_t st) {
+    std::shared_ptr<Packed> p;
+    if (int s = winograd_weights(w, f, st, &p); s != SDB_OK) return s;
+    const int xi = f == 2 ? Wino<2>::kXi : Wino<4>::kXi;
+    WinoArgs wa{};
+    wa.x = static_cast<const float*>(x->data);
+    for (int d = 0; d < 4; ++d) wa.xnb[d] = x->nb[d] / 4;
+    wa.iw = static_cast<int>(x->ne[0]);
+    wa.ih = static_cast<int>(x->ne[1]);
+    wa.ic = static_cast<int>(x->ne[2]);
+    wa.n = static_cast<int>(x->ne[3]);
+    wa.ow = static_cast<int>(dst->ne[0]);
+    wa.oh = static_cast<int>(dst->ne[1]);
+    wa.oc = static_cast<int>(dst->ne[2]);
+    wa.p0 = params[2];
+    wa.p1 = params[3];
+    wa.tw = (wa.ow + f - 1) / f;
+    wa.th = (wa.oh + f - 1) / f;
+    wa.tiles = static_cast<long long>(wa.n) * wa.th * wa.tw;
+    wa.tiles_pad = round_up(wa.tiles, kBM);
+    wa.icp8 = static_cast<int>(round_up(wa.ic, 8));
+    wa.ldm = round_up(wa.oc, 4);
+    if (wa.tiles_pad * xi >= (1LL << 30) || wa.tiles_pad * wa.icp8 >= (1LL << 31) ||
+        wa.tiles_pad * wa.oc >= (1LL << 31))
+        return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: too many Winograd tiles");
+
+    GemmArgs a{};
+    a.m = static_cast<int>(xi * wa.tiles_pad);
+    a.kblocks = static_cast<int>(p->kpad / kBK);
+    a.n = wa.oc;
+    a.b1_row = static_cast<int>(p->b1_row);
+    a.a_tx = kBM * kBK * 2;
+    a.a_planes = 2;
+    a.tiles_m = a.m / kBM;
+    a.batch_tiles = static_cast<int>(wa.tiles_pad / kBM);
+    a.b_batch_rows = static_cast<int>(p->npad / xi);
+    a.rne1 = a.m;
+    a.rne2 = 1;
+    a.ynb[0] = 1;
+    a.ynb[1] = wa.ldm;
+    a.ynb[2] = a.ynb[3] = wa.ldm * a.m;
+    a.err = device_error_word();
+    choose_ksplit(a, a.tiles_m * static_cast<int>((wa.oc + 127) / 128), kWeightSplit);
+
+    const size_t v_bytes = static_cast<size_t>(round_up(2LL * xi * wa.tiles_pad * wa.icp8 * 2, 256));
+    const size_t m_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(xi) * wa.tiles_pad * wa.ldm * 4, 256));
+    void* ws = nullptr;
+    if (int s = workspace(st, v_bytes + m_bytes + partial_bytes(a.ksplit, a.tiles_m, wa.oc, 128), &ws); s != SDB_OK)
+        return s;
+    wa.v = static_cast<__half*>(ws);
+    float* mbuf = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + v_bytes);
+    wa.m = mbuf;
+    a.y = mbuf;
+    set_partials(a, ws, v_bytes + m_bytes, a.tiles_m, 128);
+
+    // Channel pairs as one load when the image's channels are adjacent (channels-last) and even in number.
+    const bool in_pairs = wa.xnb[2] == 1 && wa.ic % 2 == 0 && (reinterpret_cast<uintptr_t>(wa.x) & 7) == 0 &&
+                          wa.xnb[0] % 2 == 0 && wa.xnb[1] % 2 == 0 && wa.xnb[3] % 2 == 0;
+    const long long in_total = wa.tiles_pad * wa.icp8 / (in_pairs ? 2 : 1);
+    const int in_blocks = static_cast<int>(std::min<long long>((in_total + 255) / 256, 148LL * 32));
+    if (f == 2) {
+        if (in_pairs) winograd_inputs_kernel<2, 2><<<in_blocks, 256, 0, st>>>(wa);
+        else winograd_inputs_kernel<2, 1><<<in_blocks, 256, 0, st>>>(wa);
+    } else {
+        if (in_pairs) winograd_inputs_kernel<4, 2><<<in_blocks, 256, 0, st>>>(wa);
+        else winograd_inputs_kernel<4, 1><<<in_blocks, 256, 0, st>>>(wa);
+    }
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+
+    // A as [plane][xi * Tp rows][icp8]: one box {64, 128, 2} brings a tile's hi and lo rows.
+    CUtensorMap amap;
+    const uint64_t dims[3] = {static_cast<uint64_t>(wa.icp8), static_cast<uint64_t>(a.m), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(wa.icp8) * 2, static_cast<uint64_t>(a.m) * wa.icp8 * 2};
+    const uint32_t box[3] = {64, 128, 2};
+    if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, wa.v, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the transformed inputs");
+    CUtensorMap ymap{};
+    if (!store_map(&ymap, mbuf, wa.oc, a.m, wa.ldm, 32))
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the Winograd products");
+    a.store = kStoreTma;
+    if (int s = launch_gemm<kModeLinear, kWeightSplit>(amap, p->map128, ymap, a, st); s != SDB_OK) return s;
+
+    wa.y = static_cast<float*>(chain && chain->redirect ? chain->redirect : dst->data);
+    for (int d = 0; d < 4; ++d) wa.ynb[d] = dst->nb[d] / 4;
+    wa.chain = make_chain(chain);
+    wa.err = a.err;
+    const bool out_pairs = wa.ynb[2] == 1 && wa.oc % 2 == 0 && (reinterpret_cast<uintptr_t>(wa.y) & 7) == 0 &&
+                           wa.ynb[0] % 2 == 0 && wa.ynb[1] % 2 == 0 && wa.ynb[3] % 2 == 0;
+    const long long out_total = wa.tiles * wa.oc / (out_pairs ? 2 : 1);
+    const int out_blocks = static_cast<int>(std::min<long long>((out_total + 255) / 256, 148LL * 32));
+    if (f == 2) {
+        if (out_pairs) winograd_outputs_kernel<2, 2><<<out_blocks, 256, 0, st>>>(wa);
+        else winograd_outputs_kernel<2, 1><<<out_blocks, 256, 0, st>>>(wa);
+    } else {
+        if (out_pairs) winograd_outputs_kernel<4, 2><<<out_blocks, 256, 0, st>>>(wa);
+        else winograd_outputs_kernel<4, 1><<<out_blocks, 256, 0, st>>>(wa);
+    }
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
 }  // namespace
 
 }  // namespace sdb
@@ -378,6 +511,7 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (!sdb_conv2d_supported(w, x, dst, params)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: not supported");
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_conv2d: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
+    if (const int f = winograd_form(w, dst, params); f != 0) return run_winograd(f, w, x, dst, params, chain, st);
     const int64_t ic = x->ne[2], oc = w->ne[3];
     const int icp = static_cast<int>(round_up(ic, 64));
     std::shared_ptr<Packed> p;

@@ -35,6 +35,9 @@ int64_t* knob(Tuning& t, const std::string& name) {
     if (name == "fuse") return &t.fuse;
     if (name == "fuse_residual") return &t.fuse_residual;
     if (name == "winograd") return &t.winograd;
+    if (name == "winograd_positions") return &t.winograd_positions;
+    if (name == "winograd4_positions") return &t.winograd4_positions;
+    if (name == "winograd_channels") return &t.winograd_channels;
     if (name == "store") return &t.store;
     if (name == "todo") return &t.todo;
     if (name == "todo_tokens") return &t.todo_tokens;

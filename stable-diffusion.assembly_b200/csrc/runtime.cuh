@@ -19,6 +19,9 @@ struct Tuning {
     int64_t fuse = 1;            // match chains after operations (shim)
     int64_t fuse_residual = 1;   // and residual additions not in place
     int64_t winograd = 2;        // 0 direct, 1 F(2x2,3x3), 2 F(4x4,3x3) where it fits
+    int64_t winograd_positions = 1024;  // the least outputs of an image Winograd is used for
+    int64_t winograd4_positions = 256;  // with winograd = 2, the least outputs of an image for F(4x4)
+    int64_t winograd_channels = 16;     // the least input channels Winograd is used for
     int64_t store = 1;           // keep packed weights between calls
     int64_t todo = 1;            // ToDo K/V downsampling factor (1 = none)
     int64_t todo_tokens = 4096;  // least tokens of a grid downsampled

@@ -13,6 +13,7 @@
 #include "ptx.cuh"
 #include "quant.cuh"
 #include "runtime.cuh"
+#include "winograd.cuh"
 
 namespace sdb {
 
@@ -363,6 +364,49 @@ int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_
         case 4: quantize_weights_kernel<4><<<blocks, 256, 0, stream>>>(a); break;
         default: quantize_weights_kernel<8><<<blocks, 256, 0, stream>>>(a); break;
     }
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    SDB_CUDA(cudaEventRecord(p->ready, stream));
+    remember(key, p);
+    *out = p;
+    return SDB_OK;
+}
+
+int winograd_weights(const sdb_tensor* w, int f, cudaStream_t stream, std::shared_ptr<Packed>* out) {
+    if (f != 2 && f != 4) return fail(SDB_INVALID, "winograd: F(2x2) or F(4x4) only");
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    const Layout layout = f == 2 ? Layout::winograd2 : Layout::winograd4;
+    const Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]},
+                  {w->nb[0], w->nb[1], w->nb[2], w->nb[3]}, static_cast<int>(layout), 0, 0, 0};
+    bool found = false;
+    if (int s = lookup(key, stream, out, &found); s != SDB_OK || found) return s;
+    const int xi = f == 2 ? Wino<2>::kXi : Wino<4>::kXi;
+    const int64_t ic = w->ne[2], oc = w->ne[3];
+    auto p = std::make_shared<Packed>();
+    p->kpad = round_up(ic, 64);
+    const int64_t ocp = round_up(oc, 128);
+    p->npad = xi * ocp;
+    p->rows_total = 2 * p->npad;
+    p->b1_row = p->npad;
+    p->split = true;
+    p->bytes = static_cast<size_t>(p->rows_total * p->kpad * 2);
+    SDB_CUDA(cudaMalloc(&p->data, p->bytes));
+    SDB_CUDA(cudaMemsetAsync(p->data, 0, p->bytes, stream));
+    SDB_CUDA(cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming));
+    if (int st = make_maps(*p); st != SDB_OK) return st;
+    const long long total = ic * oc;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    auto src = static_cast<const uint8_t*>(w->data);
+    auto dst = static_cast<__half*>(p->data);
+    if (f == 2)
+        winograd_weights_kernel<2><<<blocks, 256, 0, stream>>>(src, w->type, w->nb[0], w->nb[1], w->nb[2], w->nb[3],
+                                                               static_cast<int>(ic), static_cast<int>(oc), ocp,
+                                                               p->kpad, dst, device_error_word());
+    else
+        winograd_weights_kernel<4><<<blocks, 256, 0, stream>>>(src, w->type, w->nb[0], w->nb[1], w->nb[2], w->nb[3],
+                                                               static_cast<int>(ic), static_cast<int>(oc), ocp,
+                                                               p->kpad, dst, device_error_word());
     count_launch();
     SDB_CUDA(cudaGetLastError());
     SDB_CUDA(cudaEventRecord(p->ready, stream));

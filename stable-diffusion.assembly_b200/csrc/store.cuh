@@ -21,6 +21,8 @@ enum class Layout : int {
     gated = 2,    // GEGLU: rows [0, half) x weights, [halfpad, halfpad + half) gate weights
     quantized = 3,        // linear, quantized (quant.cuh): int8 rows n, k padded to whole groups
     quantized_gated = 4,  // GEGLU, quantized: rows as `gated`
+    winograd2 = 5,        // F(2x2, 3x3): U = G g G^T split, [plane][16 xi][ocp][kpad] (winograd.cuh)
+    winograd4 = 6,        // F(4x4, 3x3): the same with 36 xi
 };
 
 // What a quantized packing depends on (the reference's quantized_variant,
@@ -77,5 +79,12 @@ int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_
 // quantize_weights_f16/_f32 quantize (quant.cc:204-244, 366-377).
 int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_t k_logical, int64_t half,
                       const QuantSpec& q, cudaStream_t stream, std::shared_ptr<Packed>* out);
+
+// The transformed kernels of a 3x3 convolution for Winograd's F(f x f, 3x3),
+// f = 2 or 4 (winograd.cuh): from the store or transformed now on `stream`
+// (the reference keeps them too, Layout::winograd, winograd.cc:2144-2160).
+// Packed rows: xi * ocp + oc of the hi plane, then b1_row + the same of the
+// lo plane; ocp = OC rounded up to 128, kpad = IC rounded up to 64.
+int winograd_weights(const sdb_tensor* w, int f, cudaStream_t stream, std::shared_ptr<Packed>* out);
 
 }  // namespace sdb
