@@ -21,10 +21,10 @@
 // zero: one k-step's add loses up to an ulp of the running sum, always in the
 // same direction, so over hundreds of k-steps the error grows linearly (about
 // 2^-23 of the sum per k-step, measured).  The hi product, which carries the
-// sum, is therefore accumulated over one k-block (4 k-steps) at a time, into
-// one of two tensor-memory buffers in turn, and the epilogue warps add each
-// block's partial sum to FP32 registers with round-to-nearest while the next
-// block computes.  The lo product (2^-11 of the sum) accumulates over all of
+// sum, is therefore accumulated over 64 of K (4 k-steps) at a time, into
+// one of three tensor-memory buffers in turn, and the epilogue warps add each
+// partial sum to FP32 registers with round-to-nearest while the next ones
+// compute.  The lo product (2^-11 of the sum) accumulates over all of
 // the CTA's K.  The chain (bias, scale, SiLU, residual; fusion.h:51-91) is
 // applied to sum + lo 2^-11 before the store -- or, when K is split over
 // several CTAs (few output tiles, long K), each CTA writes its sum to the
@@ -47,7 +47,11 @@
 namespace sdb {
 
 enum : int { kModeLinear = 0, kModeConv = 1 };
-enum : int { kWeightHalf = 0, kWeightSplit = 1, kWeightGated = 2 };
+// kWeightSplitK32: FP32 (split) weights with stages of 32 of K in the 64-byte
+// swizzle -- half the bytes a stage, so six stages fit where three would of
+// 64; used where K is short and the loads' latency is not hidden otherwise
+// (Winograd's batched products).  Linear mode only.
+enum : int { kWeightHalf = 0, kWeightSplit = 1, kWeightGated = 2, kWeightSplitK32 = 3 };
 
 constexpr int kBM = 128;        // rows of A per tile (the MMA's M)
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of FP16
@@ -95,15 +99,22 @@ template <int WMODE>
 struct GemmShape {
     static constexpr int BN = WMODE == kWeightGated ? 64 : 128;
     static constexpr bool kHasB1 = WMODE != kWeightHalf;
-    static constexpr int kABytes = kBM * kBK * 2;  // one of hi / lo
-    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr bool kSplitW = WMODE == kWeightSplit || WMODE == kWeightSplitK32;
+    static constexpr int kStageK = WMODE == kWeightSplitK32 ? 32 : kBK;  // K of a stage
+    static constexpr int kABytes = kBM * kStageK * 2;  // one of hi / lo
+    static constexpr int kBBytes = BN * kStageK * 2;
     static constexpr int kStageBytes = 2 * kABytes + kBBytes * (kHasB1 ? 2 : 1);
     // Output staging for the TMA stores: a 32 x 32 FP32 box (4 KB) per epilogue warp.
     static constexpr int kStagingBytes = 8 * 32 * 128;
     static constexpr int kBudget = 227 * 1024 - kStagingBytes - 1024 /*align*/ - 256 /*barriers*/;
     static constexpr int kStages = kBudget / kStageBytes >= 6 ? 6 : kBudget / kStageBytes;
-    // Tensor-memory columns: hi buffers (two; gated: x0 x1 g0 g1) then lo (gated: x, g).
-    static constexpr int kHiCols = WMODE == kWeightGated ? 4 * BN : 2 * BN;
+    // The hi product is drained every kDrainStages stages (64 of K) into one of
+    // kNHi tensor-memory buffers in turn, so that the MMAs run up to two drains
+    // ahead of the epilogue.
+    static constexpr int kDrainStages = kBK / kStageK;
+    static constexpr int kNHi = 3;
+    // Tensor-memory columns: hi buffers (gated: x buffers, then gate buffers) then lo (gated: x, g).
+    static constexpr int kHiCols = WMODE == kWeightGated ? 2 * kNHi * BN : kNHi * BN;
     static constexpr int kLoCol = kHiCols;
     static constexpr int kAccCols = kHiCols + (WMODE == kWeightGated ? 2 * BN : BN);
     static constexpr int kTmemCols = 512;
@@ -167,14 +178,15 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
     using S = GemmShape<WMODE>;
     constexpr int BN = S::BN;
     constexpr bool kGated = WMODE == kWeightGated;
+    static_assert(MODE == kModeLinear || WMODE != kWeightSplitK32, "32-wide stages: linear mode only");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + S::kStages * S::kStageBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + S::kStagingBytes);
     uint64_t* empty = full + S::kStages;
-    uint64_t* hi_full = empty + S::kStages;   // [2]
-    uint64_t* hi_empty = hi_full + 2;         // [2]
-    uint64_t* lo_full = hi_empty + 2;
+    uint64_t* hi_full = empty + S::kStages;   // [kNHi]
+    uint64_t* hi_empty = hi_full + S::kNHi;   // [kNHi]
+    uint64_t* lo_full = hi_empty + S::kNHi;
     uint64_t* lo_empty = lo_full + 1;
     uint64_t* drain = lo_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -188,7 +200,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
             mbar_init(&full[s], 1);   // TMA arrive.expect_tx
             mbar_init(&empty[s], 1);  // the MMA commit
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < S::kNHi; ++b) {
             mbar_init(&hi_full[b], 1);
             mbar_init(&hi_empty[b], 8);  // the eight epilogue warps
         }
@@ -244,7 +256,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                     if (!mbar_wait(&empty[s], ((it / S::kStages) & 1) ^ 1, abort, args.err)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], tx_bytes);
                     if (MODE == kModeLinear) {
-                        tma_load_3d(stage_a(s), &amap, &full[s], kb * kBK, tm * kBM, 0);
+                        tma_load_3d(stage_a(s), &amap, &full[s], kb * S::kStageK, tm * kBM, 0);
                     } else {
                         const int tap = kb / g.cblocks;
                         const int cx0 = (kb - tap * g.cblocks) * kBK;
@@ -257,8 +269,8 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                             tma_load_5d(stage_a(s) + S::kABytes, &amap, &full[s], cx0, x, y, az, 1);
                         }
                     }
-                    tma_load_2d(stage_b0(s), &wmap, &full[s], kb * kBK, n0);
-                    if (S::kHasB1) tma_load_2d(stage_b1(s), &wmap, &full[s], kb * kBK, args.b1_row + n0);
+                    tma_load_2d(stage_b0(s), &wmap, &full[s], kb * S::kStageK, n0);
+                    if (S::kHasB1) tma_load_2d(stage_b1(s), &wmap, &full[s], kb * S::kStageK, args.b1_row + n0);
                 }
             }
             if (*abort) {
@@ -272,7 +284,11 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
             bool ok = true;
-            int it = 0, t = 0;  // k-blocks consumed, items done
+            int it = 0, t = 0, g = 0;  // stages consumed, items done, hi drains
+            // One k-step is 16 of K, 32 bytes along a swizzled row.
+            auto desc = [](uint32_t addr) {
+                return S::kStageK == 32 ? desc_kmajor_sw64(addr) : desc_kmajor_sw128(addr);
+            };
             for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x, ++t) {
                 int tm, tn, split, kb0, kb1;
                 item_range(item, tm, tn, split, kb0, kb1);
@@ -280,31 +296,38 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                 if (!mbar_wait(lo_empty, (t & 1) ^ 1, abort, args.err)) { ok = false; break; }
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S::kStages;
-                    const int b = it & 1;
+                    const int q = (kb - kb0) % S::kDrainStages;  // stage within its drain
+                    const int b = g % S::kNHi;
                     if (!mbar_wait(&full[s], (it / S::kStages) & 1, abort, args.err)) { ok = false; break; }
-                    if (!mbar_wait(&hi_empty[b], ((it >> 1) & 1) ^ 1, abort, args.err)) { ok = false; break; }
+                    if (q == 0 && !mbar_wait(&hi_empty[b], ((g / S::kNHi) & 1) ^ 1, abort, args.err)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t ahi = smem_u32(stage_a(s)), alo = ahi + S::kABytes;
                     const uint32_t b0 = smem_u32(stage_b0(s)), b1 = smem_u32(stage_b1(s));
                     const uint32_t d_hi = tmem + b * BN;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint32_t fresh = kk > 0 ? 1u : 0u;
+                    for (int kk = 0; kk < S::kStageK / 16; ++kk) {
+                        const uint32_t fresh = (q > 0 || kk > 0) ? 1u : 0u;
                         const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
-                        const uint64_t dah = desc_kmajor_sw128(ahi + kk * 32), dal = desc_kmajor_sw128(alo + kk * 32);
-                        const uint64_t db0 = desc_kmajor_sw128(b0 + kk * 32);
+                        const uint64_t dah = desc(ahi + kk * 32), dal = desc(alo + kk * 32);
+                        const uint64_t db0 = desc(b0 + kk * 32);
                         mma_f16(d_hi, dah, db0, idesc, fresh);
                         mma_f16(tmem + S::kLoCol, dal, db0, idesc, acc);
-                        if (WMODE == kWeightSplit) {
-                            mma_f16(tmem + S::kLoCol, dah, desc_kmajor_sw128(b1 + kk * 32), idesc, 1u);
+                        if (S::kSplitW) {
+                            mma_f16(tmem + S::kLoCol, dah, desc(b1 + kk * 32), idesc, 1u);
                         } else if (kGated) {
-                            const uint64_t db1 = desc_kmajor_sw128(b1 + kk * 32);
-                            mma_f16(tmem + 2 * BN + b * BN, dah, db1, idesc, fresh);
+                            const uint64_t db1 = desc(b1 + kk * 32);
+                            mma_f16(tmem + S::kNHi * BN + b * BN, dah, db1, idesc, fresh);
                             mma_f16(tmem + S::kLoCol + BN, dal, db1, idesc, acc);
                         }
                     }
                     mma_commit(&empty[s]);
-                    mma_commit(&hi_full[b]);
+                    if (q == S::kDrainStages - 1 || kb == kb1 - 1) {
+                        mma_commit(&hi_full[b]);
+                        ++g;
+                    }
                 }
                 if (ok) mma_commit(lo_full);
             }
@@ -323,20 +346,21 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
         uint8_t* box = staging + ew * (32 * 128);
         bool ok = true;
-        int it = 0, t = 0;
+        int g = 0, t = 0;  // hi drains, items done
         for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x, ++t) {
             int tm, tn, split, kb0, kb1;
             item_range(item, tm, tn, split, kb0, kb1);
+            const int drains = (kb1 - kb0 + S::kDrainStages - 1) / S::kDrainStages;
             float sum[NV], gsum[NV];
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 sum[j] = 0.0f;
                 gsum[j] = 0.0f;
             }
-            // Drain the hi product k-block by k-block.
-            for (int kb = kb0; kb < kb1; ++kb, ++it) {
-                const int b = it & 1;
-                if (!mbar_wait(&hi_full[b], (it >> 1) & 1, abort, args.err)) { ok = false; break; }
+            // Drain the hi product 64 of K at a time.
+            for (int d = 0; d < drains; ++d, ++g) {
+                const int b = g % S::kNHi;
+                if (!mbar_wait(&hi_full[b], (g / S::kNHi) & 1, abort, args.err)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < NV; c += 32) {
@@ -344,7 +368,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                     tmem_ld32(lane_addr + b * BN + half * NV + c, part);
                     if (kGated) {
                         float gpart[32];
-                        tmem_ld32(lane_addr + 2 * BN + b * BN + half * NV + c, gpart);
+                        tmem_ld32(lane_addr + S::kNHi * BN + b * BN + half * NV + c, gpart);
                         tmem_ld_wait();
 #pragma unroll
                         for (int j = 0; j < 32; ++j) gsum[c + j] += gpart[j];

@@ -371,10 +371,10 @@ int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tens
 
     GemmArgs a{};
     a.m = static_cast<int>(xi * wa.tiles_pad);
-    a.kblocks = static_cast<int>(p->kpad / kBK);
+    a.kblocks = static_cast<int>(p->kpad / GemmShape<kWeightSplitK32>::kStageK);
     a.n = wa.oc;
     a.b1_row = static_cast<int>(p->b1_row);
-    a.a_tx = kBM * kBK * 2;
+    a.a_tx = GemmShape<kWeightSplitK32>::kABytes;
     a.a_planes = 2;
     a.tiles_m = a.m / kBM;
     a.batch_tiles = static_cast<int>(wa.tiles_pad / kBM);
@@ -413,19 +413,20 @@ int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tens
     count_launch();
     SDB_CUDA(cudaGetLastError());
 
-    // A as [plane][xi * Tp rows][icp8]: one box {64, 128, 2} brings a tile's hi and lo rows.
+    // A as [plane][xi * Tp rows][icp8]: one box {32, 128, 2} (64-byte swizzle) brings a
+    // stage's hi and lo rows.
     CUtensorMap amap;
     const uint64_t dims[3] = {static_cast<uint64_t>(wa.icp8), static_cast<uint64_t>(a.m), 2};
     const uint64_t strides[2] = {static_cast<uint64_t>(wa.icp8) * 2, static_cast<uint64_t>(a.m) * wa.icp8 * 2};
-    const uint32_t box[3] = {64, 128, 2};
+    const uint32_t box[3] = {32, 128, 2};
     if (encode_tensor_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, wa.v, dims, strides, box,
-                          CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+                          CU_TENSOR_MAP_SWIZZLE_64B) != CUDA_SUCCESS)
         return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the transformed inputs");
     CUtensorMap ymap{};
     if (!store_map(&ymap, mbuf, wa.oc, a.m, wa.ldm, 32))
         return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the Winograd products");
     a.store = kStoreTma;
-    if (int s = launch_gemm<kModeLinear, kWeightSplit>(amap, p->map128, ymap, a, st); s != SDB_OK) return s;
+    if (int s = launch_gemm<kModeLinear, kWeightSplitK32>(amap, p->map128k32, ymap, a, st); s != SDB_OK) return s;
 
     wa.y = static_cast<float*>(chain && chain->redirect ? chain->redirect : dst->data);
     for (int d = 0; d < 4; ++d) wa.ynb[d] = dst->nb[d] / 4;

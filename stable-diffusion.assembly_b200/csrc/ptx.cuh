@@ -233,6 +233,20 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory descriptor of a K-major operand tile in the 64-byte swizzle:
+// rows of 64 bytes, 8-row atoms 512 bytes apart (what a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_64B writes); the tile base is 512-byte aligned and a
+// step of 32 bytes of k moves the start address.
+__device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(512 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(4) << 61;                      // swizzle: 64 B
+    return d;
+}
+
 // Instruction descriptor of kind::f16 with FP16 A and B, FP32 accumulator,
 // both operands K-major, an M x N tile.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {

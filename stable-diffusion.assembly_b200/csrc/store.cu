@@ -240,6 +240,10 @@ int make_maps(Packed& p) {
                                              CU_TENSOR_MAP_SWIZZLE_128B);
         if (r != CUDA_SUCCESS) return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for packed weights");
     }
+    const uint32_t box32[2] = {32, 128};
+    if (encode_tensor_map(&p.map128k32, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.data, dims, strides, box32,
+                          CU_TENSOR_MAP_SWIZZLE_64B) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for packed weights");
     return SDB_OK;
 }
 

@@ -53,6 +53,7 @@ struct Packed {
     CUtensorMap map128{};     // box {64, 128}
     CUtensorMap map192{};     // box {64, 192}
     CUtensorMap map256{};     // box {64, 256}
+    CUtensorMap map128k32{};  // box {32, 128}, 64-byte swizzle (kWeightSplitK32)
     // Quantized layouts, in the quantized GEMM's tiles of 128 rows (quant.cuh):
     // data int8 [tiles][nstages][8 KiB], each block 64 bytes of k of the
     // tile's rows in the 64-byte swizzle; qscales FP32 [tiles][groups][2][128],
