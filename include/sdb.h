@@ -79,6 +79,15 @@ int sdb_mul_mat_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_te
 int sdb_mul_mat(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_chain *chain,
                 void *stream);
 
+/* The same product for a first operand the graph itself writes between calls
+ * -- the k of k.q and the v of v.softmax(k.q) when stable-diffusion.cpp builds
+ * attention from MUL_MAT and SOFT_MAX (its VAE's 512-dim head, which
+ * FLASH_ATTN_EXT does not take): w is packed into the workspace on every call
+ * and never kept by the weight store.  The reference packs every operand per
+ * call by default (its store budget is none, store.h:22-30, and a node's write
+ * forgets what was kept, store.h:17-20). */
+int sdb_mul_mat_transient(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_chain *chain,
+                          void *stream);
 /* The linear layer with the gated GELU after it (GEGLU): out[m][j] =
  * y[m][j] * GELU(y[m][half + j]), y the product with its chain, half = N/2.
  * Replaces sdasm::mul_mat_gated_supported / mul_mat_compute_gated (ops.h:127-131,
@@ -142,6 +151,11 @@ int sdb_upscale_nearest(const sdb_tensor *src, const sdb_tensor *dst, void *stre
  * cos(t f_j) for j < dim/2, then sin(t f_j), f_j = max_period^(-j / (dim/2)). */
 int sdb_timestep_embedding(const sdb_tensor *timesteps, const sdb_tensor *dst, int32_t dim, int32_t max_period,
                            void *stream);
+/* GGML_OP_SOFT_MAX without a mask (ggml_soft_max_ext(x, NULL, scale, 0.0f)):
+ * each row of ne0 softmax(scale * x), the sum of the exponentials in double and
+ * one reciprocal per row, as ggml's CPU kernel computes it.  x and dst FP32 of
+ * one shape (they may be the same memory). */
+int sdb_soft_max(const sdb_tensor *x, const sdb_tensor *dst, float scale, void *stream);
 /* One Euler step of the sampler with classifier-free guidance, in place:
  * e = eps[i] + cfg (eps[n + i] - eps[i]) (unconditional half first),
  * x[i] += (sigma_next - sigma) e, and, when x_in is given, both halves of the

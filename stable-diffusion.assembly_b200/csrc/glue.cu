@@ -13,6 +13,7 @@
 #include <cstdint>
 
 #include "../../include/sdb.h"
+#include "chain.cuh"
 #include "runtime.cuh"
 
 namespace sdb {
@@ -108,6 +109,89 @@ int grid_for(long long work) {
     return static_cast<int>(std::max<long long>(1, std::min<long long>((work + 255) / 256, 148LL * 16)));
 }
 
+// GGML_OP_SOFT_MAX without a mask (ggml_soft_max_ext(x, NULL, scale, 0)),
+// row by row as ggml's CPU kernel computes it: m = max of scale x, e_j =
+// exp(scale x_j - m) summed in double, y_j = e_j * (float)(1 / sum).  The
+// exponential is the epilogues' (scalar_math.h's method).  One CTA a row;
+// with VPT > 0 a thread keeps its VPT numbers of the row in registers (rows
+// of at most 256 VPT), else the row is read three times.
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = red[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) v = fmaxf(v, red[w]);
+    __syncthreads();
+    return v;
+}
+
+__device__ __forceinline__ double block_sum(double v, double* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = red[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) v += red[w];
+    __syncthreads();
+    return v;
+}
+
+struct SoftMaxArgs {
+    const float* x;
+    float* y;
+    int ne0;
+    long long rows, ne1, ne2;
+    long long xnb[4], ynb[4];  // element strides
+    float scale;
+};
+
+template <int VPT>
+__global__ void __launch_bounds__(256) soft_max_kernel(const SoftMaxArgs a) {
+    __shared__ float red_f[8];
+    __shared__ double red_d[8];
+    for (long long r = blockIdx.x; r < a.rows; r += gridDim.x) {
+        const long long i1 = r % a.ne1, rest = r / a.ne1, i2 = rest % a.ne2, i3 = rest / a.ne2;
+        const float* xr = a.x + i1 * a.xnb[1] + i2 * a.xnb[2] + i3 * a.xnb[3];
+        float* yr = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3];
+        float m = -INFINITY;
+        if (VPT > 0) {
+            float v[VPT > 0 ? VPT : 1];
+#pragma unroll
+            for (int e = 0; e < VPT; ++e) {
+                const int j = threadIdx.x + e * 256;
+                v[e] = j < a.ne0 ? __ldg(xr + j * a.xnb[0]) * a.scale : -INFINITY;
+                m = fmaxf(m, v[e]);
+            }
+            m = block_max(m, red_f);
+            double sum = 0.0;
+#pragma unroll
+            for (int e = 0; e < VPT; ++e) {
+                const int j = threadIdx.x + e * 256;
+                v[e] = j < a.ne0 ? exponential(v[e] - m) : 0.0f;
+                sum += v[e];
+            }
+            sum = block_sum(sum, red_d);
+            const float inv = static_cast<float>(1.0 / sum);
+#pragma unroll
+            for (int e = 0; e < VPT; ++e) {
+                const int j = threadIdx.x + e * 256;
+                if (j < a.ne0) yr[j * a.ynb[0]] = v[e] * inv;
+            }
+        } else {
+            for (int j = threadIdx.x; j < a.ne0; j += blockDim.x) m = fmaxf(m, __ldg(xr + j * a.xnb[0]) * a.scale);
+            m = block_max(m, red_f);
+            double sum = 0.0;
+            for (int j = threadIdx.x; j < a.ne0; j += blockDim.x)
+                sum += exponential(__ldg(xr + j * a.xnb[0]) * a.scale - m);
+            sum = block_sum(sum, red_d);
+            const float inv = static_cast<float>(1.0 / sum);
+            for (int j = threadIdx.x; j < a.ne0; j += blockDim.x)
+                yr[j * a.ynb[0]] = exponential(__ldg(xr + j * a.xnb[0]) * a.scale - m) * inv;
+        }
+    }
+}
+
 }  // namespace
 
 }  // namespace sdb
@@ -197,6 +281,36 @@ int sdb_euler_cfg_step(const float* eps, float* x, float* x_in, int64_t n, float
     if (!eps || !x || n <= 0) return fail(SDB_INVALID, "sdb_euler_cfg_step: null buffers");
     euler_cfg_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(eps, x, x_in, n, cfg,
                                                                                   sigma_next - sigma, c_in_next);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+int sdb_soft_max(const sdb_tensor* x, const sdb_tensor* dst, float scale, void* stream) {
+    if (!f32t(x) || !f32t(dst)) return fail(SDB_NOT_SUPPORTED, "sdb_soft_max: FP32 tensors only");
+    for (int d = 0; d < 4; ++d) {
+        if (x->ne[d] != dst->ne[d] || x->ne[d] <= 0) return fail(SDB_INVALID, "sdb_soft_max: shapes differ");
+        if (x->nb[d] % 4 || dst->nb[d] % 4 || x->nb[d] < 0 || dst->nb[d] < 0)
+            return fail(SDB_NOT_SUPPORTED, "sdb_soft_max: misaligned strides");
+    }
+    if (x->ne[0] > (1 << 30)) return fail(SDB_NOT_SUPPORTED, "sdb_soft_max: rows too long");
+    SoftMaxArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.y = static_cast<float*>(dst->data);
+    a.ne0 = static_cast<int>(x->ne[0]);
+    a.ne1 = x->ne[1];
+    a.ne2 = x->ne[2];
+    a.rows = x->ne[1] * x->ne[2] * x->ne[3];
+    for (int d = 0; d < 4; ++d) {
+        a.xnb[d] = x->nb[d] / 4;
+        a.ynb[d] = dst->nb[d] / 4;
+    }
+    a.scale = scale;
+    const auto st = static_cast<cudaStream_t>(stream);
+    const int blocks = static_cast<int>(std::min<long long>(a.rows, 148LL * 64));
+    if (a.ne0 <= 1024) soft_max_kernel<4><<<blocks, 256, 0, st>>>(a);
+    else if (a.ne0 <= 4096) soft_max_kernel<16><<<blocks, 256, 0, st>>>(a);
+    else soft_max_kernel<0><<<blocks, 256, 0, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;

@@ -236,17 +236,31 @@ bool mul_mat_shapes(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* 
     return true;
 }
 
+// transient: w is packed into the workspace on every call instead of being
+// kept by the store (an operand the graph writes between calls).
 int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
-               cudaStream_t st, bool gated) {
+               cudaStream_t st, bool gated, bool transient = false) {
     const int64_t k = w->ne[0];
     const int64_t n = gated ? w->ne[1] / 2 : w->ne[1];
     const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
     if (m > (1LL << 30) || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "mul_mat: too large");
-    if (quantized_linear(m)) return run_quantized_linear(w, x, dst, chain, st, gated);
+    if (!transient && quantized_linear(m)) return run_quantized_linear(w, x, dst, chain, st, gated);
     std::shared_ptr<Packed> p;
-    const int rc = gated ? packed_weights(w, Layout::gated, 2 * n, k, 0, n, st, &p)
-                         : packed_weights(w, Layout::linear, n, k, 0, 0, st, &p);
-    if (rc != SDB_OK) return rc;
+    size_t w_bytes = 0;
+    if (transient) {
+        // The fields the plan reads; pack_transient fills the same ones once the workspace is known.
+        p = std::make_shared<Packed>();
+        p->borrowed = true;
+        p->split = w->type == SDB_TYPE_F32;
+        p->kpad = round_up(std::max<int64_t>(k, 1), 64);
+        p->npad = round_up(n, kRowPad);
+        p->b1_row = p->split ? p->npad : 0;
+        w_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(transient_bytes(w, n, k)), 256));
+    } else {
+        const int rc = gated ? packed_weights(w, Layout::gated, 2 * n, k, 0, n, st, &p)
+                             : packed_weights(w, Layout::linear, n, k, 0, 0, st, &p);
+        if (rc != SDB_OK) return rc;
+    }
     const int wmode = gated ? kWeightGated : p->split ? kWeightSplit : kWeightHalf;
     const int tiles = static_cast<int>((m + kBM - 1) / kBM);
     const int kblocks = static_cast<int>(p->kpad / kBK);
@@ -268,11 +282,16 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     const int bn = wide_bn ? (gated ? wide_bn / 2 : wide_bn) : (wmode == kWeightGated ? 64 : 128);
     if (!wide_bn) choose_ksplit(a, tiles * static_cast<int>((n + bn - 1) / bn), wmode);
 
-    // Workspace: the split rows [0, M) hi, [M, 2M) lo of kp8 FP16, then any partial sums.
+    // Workspace: a transient operand's packing, the split rows [0, M) hi, [M, 2M) lo of kp8
+    // FP16, then any partial sums.
     const int64_t kp8 = round_up(k, 8);
     const size_t a_bytes = static_cast<size_t>(round_up(2 * m * kp8 * 2, 256));
-    void* ws = nullptr;
-    if (int s = workspace(st, a_bytes + partial_bytes(a.ksplit, tiles, n, bn), &ws); s != SDB_OK) return s;
+    void* ws0 = nullptr;
+    if (int s = workspace(st, w_bytes + a_bytes + partial_bytes(a.ksplit, tiles, n, bn), &ws0); s != SDB_OK)
+        return s;
+    if (transient)
+        if (int s = pack_transient(w, n, k, ws0, st, p.get()); s != SDB_OK) return s;
+    void* ws = static_cast<uint8_t*>(ws0) + w_bytes;
     set_partials(a, ws, a_bytes, tiles, bn);
     const long long ne[4] = {x->ne[0], x->ne[1], x->ne[2], x->ne[3]};
     const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
@@ -466,6 +485,14 @@ int sdb_mul_mat(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst,
     if (!sdb_mul_mat_supported(w, x, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat: shapes not supported");
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_mul_mat: invalid chain");
     return run_linear(w, x, dst, chain, static_cast<cudaStream_t>(stream), false);
+}
+
+int sdb_mul_mat_transient(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
+                          void* stream) {
+    if (!sdb_mul_mat_supported(w, x, dst))
+        return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat_transient: shapes not supported");
+    if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_mul_mat_transient: invalid chain");
+    return run_linear(w, x, dst, chain, static_cast<cudaStream_t>(stream), false, true);
 }
 
 int sdb_mul_mat_gated_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* out) {

@@ -214,10 +214,10 @@ int lookup(const Key& key, cudaStream_t stream, std::shared_ptr<Packed>* out, bo
     if (cap != cudaStreamCaptureStatusNone) {
         if (!pk.done) return fail(SDB_INVALID, "weights first used under stream capture: call once before");
     } else if (!pk.done) {
-        const cudaError_t q = cudaEventQuery(pk.ready);
-        if (q == cudaSuccess) pk.done = true;
-        else if (q == cudaErrorNotReady) SDB_CUDA(cudaStreamWaitEvent(stream, pk.ready, 0));
-        else return cuda_fail(q, "cudaEventQuery(packed weights)");
+        // The packing's second use waits for it on the host, once: from then on the entry
+        // is known complete, and a stream capture (which may not query events) may use it.
+        SDB_CUDA(cudaEventSynchronize(pk.ready));
+        pk.done = true;
     }
     *out = it->second;
     *found = true;
@@ -251,8 +251,49 @@ int make_maps(Packed& p) {
 
 Packed::~Packed() {
     if (ready) cudaEventDestroy(ready);
+    if (borrowed) return;
     if (data) cudaFree(data);
     if (qscales) cudaFree(qscales);
+}
+
+size_t transient_bytes(const sdb_tensor* w, int64_t n_logical, int64_t k_logical) {
+    const int64_t rows = round_up(n_logical, kRowPad) * (w->type == SDB_TYPE_F32 ? 2 : 1);
+    return static_cast<size_t>(rows * round_up(std::max<int64_t>(k_logical, 1), 64) * 2);
+}
+
+int pack_transient(const sdb_tensor* w, int64_t n_logical, int64_t k_logical, void* dst, cudaStream_t stream,
+                   Packed* p) {
+    const bool split = w->type == SDB_TYPE_F32;
+    p->borrowed = true;
+    p->data = dst;
+    p->kpad = round_up(std::max<int64_t>(k_logical, 1), 64);
+    p->split = split;
+    p->npad = round_up(n_logical, kRowPad);
+    p->rows_total = split ? 2 * p->npad : p->npad;
+    p->b1_row = split ? p->npad : 0;
+    p->bytes = static_cast<size_t>(p->rows_total * p->kpad * 2);
+    if (int st = make_maps(*p); st != SDB_OK) return st;
+    PackArgs a{};
+    a.src = static_cast<const uint8_t*>(w->data);
+    a.type = w->type;
+    for (int d = 0; d < 4; ++d) a.nb[d] = w->nb[d];
+    a.layout = static_cast<int>(Layout::linear);
+    a.n = n_logical;
+    a.k = k_logical;
+    a.kw = a.kh = 1;
+    a.icp = 1;
+    a.npad = p->npad;
+    a.kpad = p->kpad;
+    a.rows = p->npad;
+    a.split = split ? 1 : 0;
+    a.out = static_cast<__half*>(dst);
+    a.err = device_error_word();
+    const long long total = a.rows * a.kpad;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    pack_weights_kernel<<<blocks, 256, 0, stream>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
 }
 
 int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_t k_logical, int icp, int64_t half,

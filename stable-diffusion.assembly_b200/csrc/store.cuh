@@ -65,6 +65,7 @@ struct Packed {
     cudaEvent_t ready = nullptr;
     bool done = false;        // the packing was seen complete
     bool owned_by_store = true;
+    bool borrowed = false;    // data is the caller's memory (a transient packing): not freed here
     ~Packed();
 };
 
@@ -80,6 +81,14 @@ int packed_weights(const sdb_tensor* w, Layout layout, int64_t n_logical, int64_
 // quantize_weights_f16/_f32 quantize (quant.cc:204-244, 366-377).
 int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_t k_logical, int64_t half,
                       const QuantSpec& q, cudaStream_t stream, std::shared_ptr<Packed>* out);
+
+// A linear layer's first operand packed as packed_weights(Layout::linear)
+// packs it, into caller memory `dst` of at least transient_bytes(w, n, k)
+// bytes, and not kept: for operands the graph itself writes between calls
+// (the k and v of an attention computed as two products).  *out borrows dst.
+size_t transient_bytes(const sdb_tensor* w, int64_t n_logical, int64_t k_logical);
+int pack_transient(const sdb_tensor* w, int64_t n_logical, int64_t k_logical, void* dst, cudaStream_t stream,
+                   Packed* out);
 
 // The transformed kernels of a 3x3 convolution for Winograd's F(f x f, 3x3),
 // f = 2 or 4 (winograd.cuh): from the store or transformed now on `stream`

@@ -34,11 +34,12 @@ STATUS_NAMES = ["OK", "NOT_SUPPORTED", "INVALID", "CUDA_ERROR", "OUT_OF_MEMORY",
 
 # Exported symbols of include/sdb.h, checked by the tests.
 EXPORTS = [
-    "sdb_mul_mat_supported", "sdb_mul_mat", "sdb_mul_mat_gated_supported", "sdb_mul_mat_gated",
+    "sdb_mul_mat_supported", "sdb_mul_mat", "sdb_mul_mat_transient", "sdb_mul_mat_gated_supported",
+    "sdb_mul_mat_gated",
     "sdb_conv2d_supported", "sdb_conv2d", "sdb_attention_supported", "sdb_attention",
     "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
-    "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step",
+    "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step", "sdb_soft_max",
 ]
 
 
@@ -82,6 +83,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     sigs = {
         "sdb_mul_mat_supported": (i, [T, T, T]),
         "sdb_mul_mat": (i, [T, T, T, C, vp]),
+        "sdb_mul_mat_transient": (i, [T, T, T, C, vp]),
+        "sdb_soft_max": (i, [T, T, ctypes.c_float, vp]),
         "sdb_mul_mat_gated_supported": (i, [T, T, T]),
         "sdb_mul_mat_gated": (i, [T, T, T, C, vp]),
         "sdb_conv2d_supported": (i, [T, T, T, ctypes.POINTER(ctypes.c_int32)]),
@@ -256,6 +259,30 @@ def mul_mat(w, x, out=None, chain: Chain | None = None, stream=None):
     return out
 
 
+def mul_mat_transient(w, x, out=None, chain: Chain | None = None, stream=None):
+    """mul_mat for a first operand written between calls (packed every call, never kept):
+    w (N, K) FP32/FP16, x (..., K) FP32 -> (..., N)."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.float32, device=x.device)
+    _check(lib.sdb_mul_mat_transient(describe(w), describe(x), describe(out), _chain_ptr(chain),
+                                     ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def soft_max(x, scale: float = 1.0, out=None, stream=None):
+    """GGML_OP_SOFT_MAX without a mask: softmax(scale * x) along the last dimension (x may be out)."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib.sdb_soft_max(describe(x), describe(out), ctypes.c_float(scale), ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
 def mul_mat_supported(w, x, out) -> bool:
     """Whether sdb_mul_mat takes these operands (under the tuning in effect)."""
     return bool(load().sdb_mul_mat_supported(describe(w), describe(x), describe(out)))
@@ -423,8 +450,9 @@ def describe_nhwc(t) -> Tensor:
 
 
 def conv2d_nhwc(w, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1), out=None, chain: Chain | None = None,
-                stream=None):
-    """ggml_conv_2d_direct on channels-last images: w (OC, IC, KH, KW), x (N, H, W, IC) -> (N, OH, OW, OC)."""
+                stream=None, out_nchw: bool = False):
+    """ggml_conv_2d_direct on channels-last images: w (OC, IC, KH, KW), x (N, H, W, IC) -> (N, OH, OW, OC),
+    or with out_nchw the output channel-major, (N, OC, OH, OW)."""
     import torch
 
     lib = load()
@@ -433,10 +461,12 @@ def conv2d_nhwc(w, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1), out=None, 
     oh = conv_out_size(h, kh, stride[1], padding[1], dilation[1])
     ow = conv_out_size(wd, kw, stride[0], padding[0], dilation[0])
     if out is None:
-        out = torch.empty(n, oh, ow, oc, dtype=torch.float32, device=x.device)
+        shape = (n, oc, oh, ow) if out_nchw else (n, oh, ow, oc)
+        out = torch.empty(*shape, dtype=torch.float32, device=x.device)
     params = (ctypes.c_int32 * 6)(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1])
     _guard_weight(w)
-    _check(lib.sdb_conv2d(describe(w), describe_nhwc(x), describe_nhwc(out), params, _chain_ptr(chain),
+    dy = describe(out) if out_nchw else describe_nhwc(out)
+    _check(lib.sdb_conv2d(describe(w), describe_nhwc(x), dy, params, _chain_ptr(chain),
                           ctypes.c_void_p(_stream_ptr(stream))))
     return out
 
