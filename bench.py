@@ -703,6 +703,40 @@ class OpClock:
         return {k: {"work": v[0], "ms": v[1], "calls": v[2]} for k, v in classes.items()}
 
 
+def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5) -> tuple[float, int]:
+    """ms of one SD 1.5 VAE decode (64 x 64 latent to 512 x 512), a CUDA-graph replay timed with
+    CUDA events on its stream (max over ranks), and its algorithmic FLOPs."""
+    import vae as V
+
+    dec = V.VAEDecoder(device=dev)
+    z = latent.clone()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            dec.decode(z)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        dec.decode(z)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        graph.replay()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        start.record(s)
+        for _ in range(reps):
+            graph.replay()
+        end.record(s)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / reps)
+    flops = dec.flops(1, z.shape[1], z.shape[2])
+    del graph, dec
+    return ms, flops
+
+
 def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
     import sdb
     import unet as U
@@ -785,6 +819,8 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_steps)
     h2d = h_lat.numel() * 4 + h_ctx.numel() * 4
     d2h = h_out.numel() * 4
+    # The VAE decode of the step's latent (one image a GPU), captured once and replayed.
+    vae_ms, vae_flops = measure_vae(torch, dev, sampler.x, barrier, max_over_ranks)
     status = sdb.device_status(clear=True)
     del sampler
     if dist is not None:
@@ -812,8 +848,14 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
                    "weights": f"random-init FP16, {net.params / 1e6:.1f}M parameters, packed once",
                    "parallelism": f"replicas x{world} (one image a GPU)",
                    "l2": "weights (1.7 GB) and activations exceed L2 every step",
-                   "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step"},
+                   "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step",
+                   "vae": "SD 1.5 decoder, the step's 64x64 latent to 512x512, random-init FP16 weights "
+                          "(49.5M parameters); vae_ms is one decode, a CUDA-graph replay; imgs_per_s counts "
+                          f"{SAMPLER_STEPS} UNet steps and one decode an image"},
         "unet_ms_per_step": ms,
+        "vae_ms": vae_ms,
+        "vae_tflops": vae_flops / (vae_ms * 1e-3) / 1e12,
+        "imgs_per_s": world * 1e3 / (SAMPLER_STEPS * ms + vae_ms),
         "imgs_per_s_unet_only": world * 1e3 / ms / SAMPLER_STEPS,
         "step_tflop": step_flops / 1e12,
         "step_frac_of_sustained_peak": step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
