@@ -288,19 +288,29 @@ __global__ void __launch_bounds__(kResidentThreads) group_resident_kernel(const 
 // ---- channels-last (NHWC) images -----------------------------------------
 //
 // x and y are [N][P positions][C], C % groups == 0 and C % 4 == 0: a group is
-// cpg contiguous channels of every position.  One cooperative launch does the
-// reference's three passes (norm.cc:100-140): every CTA takes a chunk of one
-// image's positions -- whole rows, read with float4 loads and, when they fit,
-// kept in shared memory -- and the CTAs of an image exchange their groups'
-// double partial sums through global memory at two grid barriers: sums ->
-// mean, centred sums -> variance, then the normalisation with the chain.  x is
-// read from HBM once (the chunks that do not fit re-read it from L2).
-constexpr int kClThreads = 512;
-constexpr int kClMaxCols = 2;     // float4 columns a thread may own: C <= 2 * 4 * 512
+// cpg contiguous channels of every position.  Two launches, no grid-wide wait:
+//
+//   nhwc_gn_stats_kernel  every CTA takes a chunk of one image's positions
+//       (float4 loads, a thread's rows a float4 column of channels) and sums,
+//       in double, d = x - K and d^2 per group, K the group's first number
+//       (x at position 0, the group's first channel) -- a shift that keeps
+//       the one-pass variance free of cancellation for data of any offset;
+//       the CTA's sums go to global memory, and the last CTA of the image to
+//       finish (an atomic count, reset by that CTA) folds them in chunk order
+//       into the group's float mean and 1 / sqrt(variance + eps);
+//   nhwc_gn_apply_kernel  (x - mean) * scale, then the chain, float4 in and
+//       out.
+//
+// The reference makes two passes of double sums, the mean and then the
+// squares about the float mean (norm.cc:121-129); the shifted one-pass sums
+// give the same mean and a variance within a relative (mean - K)^2 / var
+// 2^-52 of it.  x is read twice (the second time mostly from L2) and y
+// written once.
+constexpr int kClThreads = 256;
+constexpr int kClMaxCols = 3;     // float4 columns a thread may own: C <= 3 * 4 * 256
 constexpr int kClMaxGroups = 128;
 constexpr int kClMaxChannels = 3072;
 constexpr int kClMaxCsum = kClMaxChannels;   // channel sums of the CTA's row phases (rpp * C <= 4 * threads)
-constexpr int kClSmemBudget = 160 * 1024;
 
 struct NhwcArgs {
     const float* x;
@@ -311,11 +321,10 @@ struct NhwcArgs {
     int cpi;                    // CTAs per image
     int per;                    // positions per CTA
     int rpp;                    // rows (positions) a pass of the CTA covers
-    int resident;               // 1: the CTA's rows stay in shared memory between the passes
     float eps;
-    double* partial;            // [2][images][cpi][groups]
-    unsigned* bar;              // the grid barrier's counter, zero at launch
-    unsigned* err;
+    double* partial;            // [images][cpi][groups][2]: the CTAs' shifted sums
+    float* stats;               // [images][groups][2]: mean, scale
+    unsigned* count;            // [images]: CTAs of the image done (zero between launches)
     Chain chain;
 };
 
@@ -333,226 +342,200 @@ __device__ __forceinline__ int cl_columns(const NhwcArgs& a, int (&col)[kClMaxCo
     return n;
 }
 
-// All CTAs of the grid meet here (they are co-resident: a cooperative launch).
-// Bounded: after kWaitLimitCycles the CTA gives up, sets the timeout bit and
-// reports false.
-__device__ bool grid_barrier(unsigned* bar, unsigned target, unsigned* err) {
-    __shared__ int ok_s;
+__global__ void __launch_bounds__(kClThreads) nhwc_gn_stats_kernel(const NhwcArgs a) {
+    // [sum, squares][row phase * C + channel]: 2 * csum_len doubles of dynamic shared memory.
+    extern __shared__ double csum_dyn[];
+    const int csum_len = a.c4 <= kClThreads ? a.rpp * a.c : a.c;
+    double* csum[2] = {csum_dyn, csum_dyn + csum_len};
+    __shared__ float shift[kClMaxGroups];
+    __shared__ int last;
+    const int i3 = blockIdx.x / a.cpi, chunk = blockIdx.x - i3 * a.cpi;
+    const long long p0 = static_cast<long long>(chunk) * a.per;
+    const long long p1 = min(static_cast<long long>(a.positions), p0 + a.per);
+    const long long base = static_cast<long long>(i3) * a.positions * a.c4;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x) + base;
+    for (int g = threadIdx.x; g < a.groups; g += blockDim.x) shift[g] = __ldg(a.x + base * 4 + g * a.cpg);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
-        int ok = 1;
-        const long long t0 = clock64();
-        for (int it = 0;; ++it) {
-            unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-            if (v >= target) break;
-            if ((it & 63) == 63 && clock64() - t0 > kWaitLimitCycles) {
-                if (err) atomicOr(err, kErrTimeout);
-                ok = 0;
-                break;
+    int col[kClMaxCols], r0;
+    const int ncols = cl_columns(a, col, r0);
+    for (int k = 0; k < ncols; ++k) {
+        const int j = col[k];
+        const float k0 = shift[4 * j / a.cpg], k1 = shift[(4 * j + 1) / a.cpg];
+        const float k2 = shift[(4 * j + 2) / a.cpg], k3 = shift[(4 * j + 3) / a.cpg];
+        double s[4] = {0.0, 0.0, 0.0, 0.0}, q[4] = {0.0, 0.0, 0.0, 0.0};
+        const float4* src = x4 + j;
+        const int rows = static_cast<int>((p1 - p0 - r0 + a.rpp - 1) / a.rpp);
+        const long long step = static_cast<long long>(a.rpp) * a.c4;
+        src += (p0 + r0) * a.c4;
+        for (int r = 0; r < rows; r += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = r + u < rows ? __ldg(src + (r + u) * step) : make_float4(k0, k1, k2, k3);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const double d0 = static_cast<double>(v[u].x) - k0, d1 = static_cast<double>(v[u].y) - k1;
+                const double d2 = static_cast<double>(v[u].z) - k2, d3 = static_cast<double>(v[u].w) - k3;
+                s[0] += d0; s[1] += d1; s[2] += d2; s[3] += d3;
+                q[0] = fma(d0, d0, q[0]); q[1] = fma(d1, d1, q[1]);
+                q[2] = fma(d2, d2, q[2]); q[3] = fma(d3, d3, q[3]);
             }
-            __nanosleep(64);
         }
-        __threadfence();
-        ok_s = ok;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            csum[0][r0 * a.c + 4 * j + e] = s[e];
+            csum[1][r0 * a.c + 4 * j + e] = q[e];
+        }
     }
     __syncthreads();
-    return ok_s != 0;
-}
-
-// The image's per-group totals of one pass, eight threads a group, eight
-// loads in flight each.
-__device__ __forceinline__ void cl_fold(const NhwcArgs& a, const double* part, int i3, double* out) {
-    const int lanes = 8;
-    for (int base = 0; base < a.groups * lanes; base += blockDim.x) {
-        const int t = base + threadIdx.x;
+    // Each group's channels over the row phases, eight threads a group, into this CTA's partial.
+    const int phases = a.c4 <= kClThreads ? a.rpp : 1;
+    const int span = phases * a.cpg;
+    double* part = a.partial + ((static_cast<long long>(i3) * a.cpi + chunk) * a.groups) * 2;
+    for (int b0 = 0; b0 < a.groups * 8; b0 += blockDim.x) {
+        const int t = b0 + threadIdx.x;
+        const int g = t / 8, k = t % 8;
+        double sv = 0.0, qv = 0.0;
+        if (g < a.groups)
+            for (int e = k; e < span; e += 8) {
+                const int ph = e / a.cpg, ch = g * a.cpg + (e - ph * a.cpg);
+                sv += csum[0][ph * a.c + ch];
+                qv += csum[1][ph * a.c + ch];
+            }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+            sv += __shfl_xor_sync(0xffffffffu, sv, o);
+            qv += __shfl_xor_sync(0xffffffffu, qv, o);
+        }
+        if (g < a.groups && k == 0) {
+            part[2 * g] = sv;
+            part[2 * g + 1] = qv;
+        }
+    }
+    // The image's last CTA to finish folds every CTA's sums, in chunk order.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(a.count + i3, 1u) == static_cast<unsigned>(a.cpi - 1) ? 1 : 0;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const double n = static_cast<double>(a.positions) * a.cpg;
+    const double2* img = reinterpret_cast<const double2*>(a.partial) + static_cast<long long>(i3) * a.cpi * a.groups;
+    // lanes threads a group (a power of two within a warp), each folding every lanes-th CTA's
+    // sums with eight loads in flight, then the lanes in a fixed order.
+    int lanes = 32;
+    while (lanes > 1 && lanes * a.groups > static_cast<int>(blockDim.x)) lanes >>= 1;
+    for (int b0 = 0; b0 < a.groups * lanes; b0 += blockDim.x) {
+        const int t = b0 + threadIdx.x;
         const int g = t / lanes, k = t % lanes;
-        double s = 0.0;
+        double sv = 0.0, qv = 0.0;
         if (g < a.groups) {
-            const double* pp = part + static_cast<long long>(i3) * a.cpi * a.groups + g;
             int ch = k;
             for (; ch + 7 * lanes < a.cpi; ch += 8 * lanes) {
-                double v[8];
+                double2 v[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(pp + static_cast<long long>(ch + u * lanes) * a.groups);
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(img + static_cast<long long>(ch + u * lanes) * a.groups + g);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) s += v[u];
+                for (int u = 0; u < 8; ++u) {
+                    sv += v[u].x;
+                    qv += v[u].y;
+                }
             }
-            for (; ch < a.cpi; ch += lanes) s += __ldcg(pp + static_cast<long long>(ch) * a.groups);
+            for (; ch < a.cpi; ch += lanes) {
+                const double2 v = __ldcg(img + static_cast<long long>(ch) * a.groups + g);
+                sv += v.x;
+                qv += v.y;
+            }
         }
-#pragma unroll
-        for (int o = lanes / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (g < a.groups && k == 0) out[g] = s;
+        for (int o = lanes / 2; o > 0; o >>= 1) {
+            sv += __shfl_xor_sync(0xffffffffu, sv, o);
+            qv += __shfl_xor_sync(0xffffffffu, qv, o);
+        }
+        if (g < a.groups && k == 0) {
+            const double dm = sv / n;
+            const double var = fmax(qv / n - dm * dm, 0.0);
+            float* st = a.stats + (static_cast<long long>(i3) * a.groups + g) * 2;
+            st[0] = static_cast<float>(static_cast<double>(shift[g]) + dm);
+            st[1] = 1.0f / sqrtf(static_cast<float>(var) + a.eps);
+        }
     }
+    if (threadIdx.x == 0) a.count[i3] = 0u;
 }
 
 // Chain patterns the apply pass compiles on their own: the GroupNorm's scale
 // and shift (per channel), with or without the SiLU after them.
 enum : int { kChainGeneral = 0, kChainAffine = 1, kChainAffineSilu = 2, kChainNone = 3 };
 
+// SiLU of the apply pass, x / (1 + e^-x) as the reference writes it (scalar_math.h:54-58), with
+// e^-x by the same Cody-Waite reduction to |r| <= ln2 / 2 but 2^(r log2 e) from the hardware's
+// ex2 (relative error about 2^-22) in place of the degree-6 polynomial, and the quotient by the
+// hardware's reciprocal refined by one Newton step: within a few 2^-23 of the exact form, at a
+// third of the instructions -- the pass is bound by issue, not by memory.
+__device__ __forceinline__ float silu_apply(float x) {
+    // Clamped at 87.3 on both sides (the reference's upper clamp is 88.73): 2^n stays finite, so
+    // the Newton step never meets an infinity; past 87.3 the quotient is below FP32's normal range.
+    const float t = fminf(fmaxf(-x, -87.3f), 87.3f);
+    const float magic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+    const float z = fmaf(t, 1.44269504088896341f, magic);
+    const float n = z - magic;
+    float r = fmaf(n, -0.693359375f, t);
+    r = fmaf(n, 2.12194440e-4f, r);
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(r * 1.44269504088896341f));
+    e *= __uint_as_float(static_cast<uint32_t>(__float_as_int(z) - 0x4b400000 + 127) << 23);
+    const float d = 1.0f + e;
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    y = fmaf(fmaf(-d, y, 1.0f), y, y);
+    return x * y;
+}
+
 template <int PATTERN>
 __device__ __forceinline__ float chain_pattern(const Chain& ch, const float (&op)[SDB_MAX_STEPS], float v) {
     if (PATTERN == kChainNone) return v;
     if (PATTERN == kChainAffine) return fmaf(v, op[0], op[1]);
-    if (PATTERN == kChainAffineSilu) return silu(fmaf(v, op[0], op[1]));
+    if (PATTERN == kChainAffineSilu) return silu_apply(fmaf(v, op[0], op[1]));
     return apply_uniform(ch, op, v);
 }
 
 template <int PATTERN>
-__global__ void __launch_bounds__(kClThreads) nhwc_group_norm_kernel(const NhwcArgs a) {
-    extern __shared__ float4 tile[];                 // [per][c4] when resident
-    __shared__ double csum[kClMaxCsum];             // [row phase][channel]: the threads' sums
-    __shared__ double gsum[kClMaxGroups];
-    __shared__ double total[kClMaxGroups];
-    __shared__ float mean[kClMaxGroups], scale[kClMaxGroups];
+__global__ void __launch_bounds__(kClThreads) nhwc_gn_apply_kernel(const NhwcArgs a) {
     const int i3 = blockIdx.x / a.cpi, chunk = blockIdx.x - i3 * a.cpi;
     const long long p0 = static_cast<long long>(chunk) * a.per;
     const long long p1 = min(static_cast<long long>(a.positions), p0 + a.per);
     const long long base = static_cast<long long>(i3) * a.positions * a.c4;
     const float4* x4 = reinterpret_cast<const float4*>(a.x) + base;
     float4* y4 = reinterpret_cast<float4*>(a.y) + base;
-    const long long images = gridDim.x / a.cpi;
-    double* part0 = a.partial;
-    double* part1 = a.partial + images * a.cpi * a.groups;
+    const float* st = a.stats + static_cast<long long>(i3) * a.groups * 2;
     int col[kClMaxCols], r0;
     const int ncols = cl_columns(a, col, r0);
-    const double n = static_cast<double>(a.positions) * a.cpg;
-    auto row_at = [&](long long p, int j) -> float4 {
-        return a.resident ? tile[(p - p0) * a.c4 + j] : __ldcg(x4 + p * a.c4 + j);
-    };
-    // Resident: the chunk -- one contiguous run of x -- arrives by bulk copies.
-    __shared__ uint64_t landed;
-    const uint32_t bytes = static_cast<uint32_t>((p1 - p0) * a.c4 * 16);
-    if (a.resident) {
-        if (threadIdx.x == 0) {
-            mbar_init(&landed, 1);
-            fence_barrier_init();
-            mbar_arrive_expect_tx(&landed, bytes);
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(x4 + p0 * a.c4);
-            for (uint32_t off = 0; off < bytes; off += 32768u)
-                bulk_load(reinterpret_cast<uint8_t*>(tile) + off, src + off, min(32768u, bytes - off), &landed);
-        }
-        __shared__ int landed_ok, gave_up;
-        if (threadIdx.x == 0) gave_up = 0;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            landed_ok = mbar_wait(&landed, 0, &gave_up, a.err) ? 1 : 0;
-            // Gave up: the copies still land before the CTA's shared memory goes away.
-            if (!landed_ok) mbar_wait_quiet(&landed, 0, 100000000ull);
-        }
-        __syncthreads();
-        if (!landed_ok) return;
-    }
-
-    for (int phase = 0; phase < 2; ++phase) {
-        for (int k = 0; k < ncols; ++k) {
-            const int j = col[k];
-            const int g0 = 4 * j / a.cpg, g1 = (4 * j + 1) / a.cpg, g2 = (4 * j + 2) / a.cpg, g3 = (4 * j + 3) / a.cpg;
-            const float m0 = phase ? mean[g0] : 0.0f, m1 = phase ? mean[g1] : 0.0f;
-            const float m2 = phase ? mean[g2] : 0.0f, m3 = phase ? mean[g3] : 0.0f;
-            double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-#pragma unroll 4
-            for (long long p = p0 + r0; p < p1; p += a.rpp) {
-                float4 v;
-                if (phase == 0) {
-                    v = row_at(p, j);
-                    s0 += v.x;
-                    s1 += v.y;
-                    s2 += v.z;
-                    s3 += v.w;
-                } else {
-                    v = row_at(p, j);
-                    const float d0 = v.x - m0, d1 = v.y - m1, d2 = v.z - m2, d3 = v.w - m3;
-                    s0 += static_cast<double>(d0 * d0);
-                    s1 += static_cast<double>(d1 * d1);
-                    s2 += static_cast<double>(d2 * d2);
-                    s3 += static_cast<double>(d3 * d3);
-                }
-            }
-            double* cs = csum + r0 * a.c + 4 * j;
-            cs[0] = s0;
-            cs[1] = s1;
-            cs[2] = s2;
-            cs[3] = s3;
-        }
-        __syncthreads();
-        // Each group's channels over the row phases, eight threads a group.
-        {
-            const int phases = a.c4 <= kClThreads ? a.rpp : 1;
-            const int span = phases * a.cpg;
-            for (int base = 0; base < a.groups * 8; base += blockDim.x) {
-                const int t = base + threadIdx.x;
-                const int g = t / 8, k = t % 8;
-                double v = 0.0;
-                if (g < a.groups)
-                    for (int e = k; e < span; e += 8) {
-                        const int ph = e / a.cpg, ch = g * a.cpg + (e - ph * a.cpg);
-                        v += csum[ph * a.c + ch];
-                    }
-#pragma unroll
-                for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (g < a.groups && k == 0) gsum[g] = v;
-            }
-        }
-        __syncthreads();
-        double* part = phase ? part1 : part0;
-        for (int g = threadIdx.x; g < a.groups; g += blockDim.x)
-            part[(static_cast<long long>(i3) * a.cpi + chunk) * a.groups + g] = gsum[g];
-        if (!grid_barrier(a.bar, (phase + 1) * gridDim.x, a.err)) return;
-        cl_fold(a, part, i3, total);
-        __syncthreads();
-        for (int g = threadIdx.x; g < a.groups; g += blockDim.x) {
-            if (phase == 0)
-                mean[g] = static_cast<float>(total[g] / n);
-            else
-                scale[g] = 1.0f / sqrtf(static_cast<float>(total[g] / n) + a.eps);
-        }
-        __syncthreads();
-    }
-
     for (int k = 0; k < ncols; ++k) {
         const int j = col[k];
         float mu[4], sc[4], op[4][SDB_MAX_STEPS];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int g = (4 * j + e) / a.cpg;
-            mu[e] = mean[g];
-            sc[e] = scale[g];
+            mu[e] = __ldg(st + 2 * g);
+            sc[e] = __ldg(st + 2 * g + 1);
             channel_operands(a.chain, 4 * j + e, i3, op[e]);
         }
-        for (long long p = p0 + r0; p < p1; p += 2LL * a.rpp) {
-            float4 v[2];
+        const int rows = static_cast<int>((p1 - p0 - r0 + a.rpp - 1) / a.rpp);
+        const long long step = static_cast<long long>(a.rpp) * a.c4;
+        const float4* src = x4 + (p0 + r0) * a.c4 + j;
+        float4* dst = y4 + (p0 + r0) * a.c4 + j;
+        for (int r = 0; r < rows; r += 4) {
+            float4 v[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) v[u] = row_at(min(p + u * a.rpp, p1 - 1), j);
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(src + min(r + u, rows - 1) * step);
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 v[u].x = chain_pattern<PATTERN>(a.chain, op[0], (v[u].x - mu[0]) * sc[0]);
                 v[u].y = chain_pattern<PATTERN>(a.chain, op[1], (v[u].y - mu[1]) * sc[1]);
                 v[u].z = chain_pattern<PATTERN>(a.chain, op[2], (v[u].z - mu[2]) * sc[2]);
                 v[u].w = chain_pattern<PATTERN>(a.chain, op[3], (v[u].w - mu[3]) * sc[3]);
             }
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                if (p + u * a.rpp >= p1) continue;
-                if (a.resident)
-                    tile[(p + u * a.rpp - p0) * a.c4 + j] = v[u];
-                else
-                    y4[(p + u * a.rpp) * a.c4 + j] = v[u];
-            }
-        }
-    }
-    if (a.resident) {
-        // The normalised chunk back out by bulk copies.
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            uint8_t* dst = reinterpret_cast<uint8_t*>(y4 + p0 * a.c4);
-            for (uint32_t off = 0; off < bytes; off += 32768u)
-                bulk_store(dst + off, reinterpret_cast<const uint8_t*>(tile) + off, min(32768u, bytes - off));
-            bulk_commit_group();
-            bulk_wait_all();
+            for (int u = 0; u < 4; ++u)
+                if (r + u < rows) dst[(r + u) * step] = v[u];
         }
     }
 }
@@ -736,40 +719,52 @@ bool uniform_chain(const sdb_chain* c) {
     return true;
 }
 
-// Scratch of the channels-last path (the grid barrier's counter, then the
-// partial sums), grown on demand, per thread and device, outside stream
-// capture only.
-double* cl_buffer(size_t count, cudaStream_t st) {
-    static thread_local double* buf = nullptr;
-    static thread_local size_t cap = 0;
+// Scratch of the channels-last path: the CTAs' partial sums, the groups'
+// statistics and the per-image counts (zeroed when allocated; the last CTA of
+// an image resets its count), grown on demand per thread and device, outside
+// stream capture only.
+struct ClScratch {
+    double* partial;
+    float* stats;
+    unsigned* count;
+};
+
+bool cl_scratch(size_t partials, size_t stats, size_t images, cudaStream_t st, ClScratch* out) {
+    static thread_local uint8_t* buf = nullptr;
+    static thread_local size_t cap_p = 0, cap_s = 0, cap_i = 0;
     static thread_local int dev = -1;
     int d = 0;
     cudaGetDevice(&d);
-    if (count > cap || d != dev) {
+    if (partials > cap_p || stats > cap_s || images > cap_i || d != dev) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
         if (buf && d == dev) {
             cudaStreamSynchronize(st);
             cudaFree(buf);
         }
         buf = nullptr;
-        cap = 0;
-        if (cudaMalloc(&buf, count * sizeof(double)) != cudaSuccess) return nullptr;
-        cap = count;
+        cap_p = std::max(partials, cap_p);
+        cap_s = std::max(stats, cap_s);
+        cap_i = std::max(images, cap_i);
+        const size_t bytes = cap_p * sizeof(double) + cap_s * sizeof(float) + cap_i * sizeof(unsigned);
+        if (cudaMalloc(&buf, bytes) != cudaSuccess) {
+            cap_p = cap_s = cap_i = 0;
+            return false;
+        }
+        if (cudaMemsetAsync(buf, 0, bytes, st) != cudaSuccess) return false;
         dev = d;
     }
-    return buf;
+    out->partial = reinterpret_cast<double*>(buf);
+    out->stats = reinterpret_cast<float*>(buf + cap_p * sizeof(double));
+    out->count = reinterpret_cast<unsigned*>(buf + cap_p * sizeof(double) + cap_s * sizeof(float));
+    return true;
 }
 
 template <int PATTERN>
-int launch_nhwc(const NhwcArgs& a, int grid, size_t smem, cudaStream_t st) {
-    auto kern = nhwc_group_norm_kernel<PATTERN>;
-    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kClSmemBudget));
-    int per_sm = 0;
-    SDB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kClThreads, smem));
-    if (per_sm * current_sm_count() < grid) return fail(SDB_NOT_SUPPORTED, "sdb_group_norm: grid not co-resident");
-    void* args[] = {const_cast<NhwcArgs*>(&a)};
-    SDB_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(grid), dim3(kClThreads), args, smem, st));
+int launch_nhwc_apply(const NhwcArgs& a, int grid, cudaStream_t st) {
+    nhwc_gn_apply_kernel<PATTERN><<<grid, kClThreads, 0, st>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
     return SDB_OK;
 }
 
@@ -785,39 +780,38 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
     a.cpg = a.c / groups;
     a.eps = eps;
     a.chain = make_chain(chain);
-    a.err = device_error_word();
     a.rpp = a.c4 <= kClThreads ? kClThreads / a.c4 : 1;
     const int images = static_cast<int>(x->ne[3]);
     const int sms = current_sm_count();
-    // CTAs: about one per SM over all images, at least two passes of rows each;
-    // the rows stay in shared memory when a CTA's share fits.
-    const int most = std::max(1, a.positions / (2 * a.rpp));
-    a.cpi = std::max(1, std::min(most, (sms + images - 1) / images));
+    // CTAs: up to four per SM over all images, each thread at least eight rows (its fixed costs --
+    // the group of each channel, the chain's operands, the CTA's reduction -- spread over them).
+    const int most = std::max(1, a.positions / (8 * a.rpp));
+    a.cpi = std::max(1, std::min(most, (4 * sms + images - 1) / images));
     a.per = (a.positions + a.cpi - 1) / a.cpi;
     a.cpi = (a.positions + a.per - 1) / a.per;
-    const size_t tile = static_cast<size_t>(a.per) * a.c * 4;
-    a.resident = tile <= static_cast<size_t>(kClSmemBudget) ? 1 : 0;
-    const size_t smem = a.resident ? tile : 0;
     const int grid = images * a.cpi;
-    double* buf = cl_buffer(2 + 2 * static_cast<size_t>(grid) * groups, st);
-    if (!buf) return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: scratch");
-    a.bar = reinterpret_cast<unsigned*>(buf);
-    a.partial = buf + 2;
-    SDB_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), st));
-    // The chain's pattern: mul then add (then SiLU) -- the GroupNorm's affine -- compiles alone.
-    const Chain& c = a.chain;
-    int rc;
-    if (c.count == 0)
-        rc = launch_nhwc<kChainNone>(a, grid, smem, st);
-    else if (c.count >= 2 && c.kind[0] == SDB_STEP_MUL && c.kind[1] == SDB_STEP_ADD &&
-             (c.count == 2 || (c.count == 3 && c.kind[2] == SDB_STEP_SILU)))
-        rc = c.count == 2 ? launch_nhwc<kChainAffine>(a, grid, smem, st) : launch_nhwc<kChainAffineSilu>(a, grid, smem, st);
-    else
-        rc = launch_nhwc<kChainGeneral>(a, grid, smem, st);
-    if (rc != SDB_OK) return rc;
+    ClScratch sc{};
+    if (!cl_scratch(2 * static_cast<size_t>(grid) * groups, 2 * static_cast<size_t>(images) * groups,
+                    static_cast<size_t>(images), st, &sc))
+        return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: scratch (first use of a size under stream capture?)");
+    a.partial = sc.partial;
+    a.stats = sc.stats;
+    a.count = sc.count;
+    const int csum_len = a.c4 <= kClThreads ? a.rpp * a.c : a.c;
+    const size_t smem = 2 * static_cast<size_t>(csum_len) * sizeof(double);
+    SDB_CUDA(cudaFuncSetAttribute(nhwc_gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  2 * kClMaxCsum * static_cast<int>(sizeof(double))));
+    nhwc_gn_stats_kernel<<<grid, kClThreads, smem, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
-    return SDB_OK;
+    // The chain's pattern: mul then add (then SiLU) -- the GroupNorm's affine -- compiles alone.
+    const Chain& c = a.chain;
+    if (c.count == 0) return launch_nhwc_apply<kChainNone>(a, grid, st);
+    if (c.count >= 2 && c.kind[0] == SDB_STEP_MUL && c.kind[1] == SDB_STEP_ADD &&
+        (c.count == 2 || (c.count == 3 && c.kind[2] == SDB_STEP_SILU)))
+        return c.count == 2 ? launch_nhwc_apply<kChainAffine>(a, grid, st)
+                            : launch_nhwc_apply<kChainAffineSilu>(a, grid, st);
+    return launch_nhwc_apply<kChainGeneral>(a, grid, st);
 }
 
 }  // namespace
@@ -827,7 +821,7 @@ extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_
                               const sdb_chain* chain, void* stream) {
     if (f32(x) && f32(dst) && same_shape(x, dst) && groups > 0 && channels_last(x) && channels_last(dst)) {
         if (x->ne[2] % groups != 0 || x->ne[2] % 4 != 0 || x->ne[2] > kClMaxChannels ||
-            x->ne[0] * x->ne[1] > (1LL << 30) || x->ne[3] > 148 || groups > kClMaxGroups || !uniform_chain(chain) ||
+            x->ne[0] * x->ne[1] > (1LL << 30) || x->ne[3] > 4096 || groups > kClMaxGroups || !uniform_chain(chain) ||
             (reinterpret_cast<uintptr_t>(x->data) & 15) || (reinterpret_cast<uintptr_t>(dst->data) & 15))
             return fail(SDB_NOT_SUPPORTED,
                         "sdb_group_norm: channels-last needs C % groups == 0, C % 4 == 0, C <= 3072, aligned "
