@@ -38,6 +38,11 @@ __device__ __forceinline__ float exponential(float x) {
 
 __device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, 1.0f + exponential(-x)); }
 
+// The same SiLU as one out-of-line function: the tile epilogues unroll the
+// chain over every column and every step, and SiLU inlined there (rare after
+// a GEMM) would multiply their code past what the instruction cache holds.
+static __device__ __noinline__ float silu_call(float x) { return silu(x); }
+
 __device__ __forceinline__ float gelu(float x) {
     const float y = x * fmaf(0.044715f * x, x, 1.0f);
     return __fdiv_rn(x, 1.0f + exponential(-1.5957691216057308f * y));
@@ -115,7 +120,7 @@ __device__ __forceinline__ void apply_chain_cols(const Chain& c, const ChainRow&
         if (s >= c.count) break;
         if (c.kind[s] == SDB_STEP_SILU) {
 #pragma unroll
-            for (int j = 0; j < NVAL; ++j) v[j] = silu(v[j]);
+            for (int j = 0; j < NVAL; ++j) v[j] = silu_call(v[j]);
         } else {
             const float* base = c.operand[s] + r.off[s];
             const long long stride = c.nb[s][COL_DIM];

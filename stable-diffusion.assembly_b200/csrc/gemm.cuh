@@ -554,4 +554,69 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int tiles) {
     }
 }
 
+// The same reduction four columns a thread, for outputs whose columns are
+// contiguous and 16-byte aligned (linear: ynb[0] == 1; convolution:
+// channels-last, ynb[2] == 1) with N % 4 == 0: one float4 of every split's
+// partial row (part_ld is a multiple of 4) loaded four splits at a time, added
+// in split order as the scalar kernel adds them, then the chain.
+template <int MODE>
+__global__ void __launch_bounds__(256) splitk_reduce4_kernel(const GemmArgs a, int tiles) {
+    const long long rows = static_cast<long long>(tiles) * kBM;
+    const int n4 = a.n / 4;
+    const long long total = rows * n4;
+    const long long step4 = a.part_split / 4;
+    for (long long idx = blockIdx.x * 256LL + threadIdx.x; idx < total; idx += gridDim.x * 256LL) {
+        const long long row = idx / n4;
+        const int col = static_cast<int>(idx - row * n4) * 4;
+        float* out;
+        long long c0, c1, c2, c3;  // the chain's coordinates of the first column
+        if (MODE == kModeLinear) {
+            if (row >= a.m) continue;
+            const long long i1 = row % a.rne1, t = row / a.rne1, i2 = t % a.rne2, i3 = t / a.rne2;
+            out = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3] + col;
+            c0 = col; c1 = i1; c2 = i2; c3 = i3;
+        } else {
+            const ConvPos p = conv_pos(a.cg, static_cast<int>(row / kBM), static_cast<int>(row % kBM));
+            if (!p.ok) continue;
+            out = a.y + p.ox * a.ynb[0] + static_cast<long long>(p.oy) * a.ynb[1] + p.img * a.ynb[3] + col;
+            c0 = p.ox; c1 = p.oy; c2 = col; c3 = p.img;
+        }
+        const float4* src = reinterpret_cast<const float4*>(a.part + row * a.part_ld + col);
+        float4 acc = __ldg(src);
+        int s = 1;
+        for (; s + 3 < a.ksplit; s += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(src + (s + u) * step4);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                acc.x += v[u].x;
+                acc.y += v[u].y;
+                acc.z += v[u].z;
+                acc.w += v[u].w;
+            }
+        }
+        for (; s < a.ksplit; ++s) {
+            const float4 v = __ldg(src + s * step4);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        float v[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (a.chain.from_redirect) {
+            const float4 old = *reinterpret_cast<const float4*>(out);
+            v[0] = old.x + v[0];
+            v[1] = old.y + v[1];
+            v[2] = old.z + v[2];
+            v[3] = old.w + v[3];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            v[e] = MODE == kModeLinear ? apply_chain(a.chain, v[e], c0 + e, c1, c2, c3)
+                                       : apply_chain(a.chain, v[e], c0, c1, c2 + e, c3);
+        *reinterpret_cast<float4*>(out) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
 }  // namespace sdb

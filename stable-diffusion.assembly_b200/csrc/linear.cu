@@ -35,6 +35,23 @@ int partial_map(const GemmArgs& a, CUtensorMap* map) {
     return SDB_OK;
 }
 
+// The split-K reduction: four columns a thread where the output's columns
+// are contiguous and aligned, else one.
+template <int MODE>
+int launch_reduce(const GemmArgs& a, cudaStream_t st) {
+    const bool cols = MODE == kModeLinear ? a.ynb[0] == 1 && a.ynb[1] % 4 == 0
+                                          : a.ynb[2] == 1 && a.ynb[0] % 4 == 0 && a.ynb[1] % 4 == 0;
+    const bool vec = cols && a.n % 4 == 0 && a.part_ld % 4 == 0 && a.ynb[3] % 4 == 0 &&
+                     (MODE != kModeLinear || a.ynb[2] % 4 == 0) && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+    const long long total = static_cast<long long>(a.tiles_m) * kBM * a.n / (vec ? 4 : 1);
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    if (vec) splitk_reduce4_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
+    else splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
 template <int MODE, int WMODE>
 int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const CUtensorMap& ymap, GemmArgs a,
                 cudaStream_t st) {
@@ -52,13 +69,7 @@ int launch_gemm(const CUtensorMap& amap, const CUtensorMap& wmap, const CUtensor
     kern<<<grid, kGemmThreads, S::kSmemBytes, st>>>(amap, wmap, a.ksplit > 1 ? pmap : ymap, a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
-    if (a.ksplit > 1) {
-        const long long total = static_cast<long long>(a.tiles_m) * kBM * a.n;
-        const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
-        count_launch();
-        SDB_CUDA(cudaGetLastError());
-    }
+    if (a.ksplit > 1) return launch_reduce<MODE>(a, st);
     return SDB_OK;
 }
 
@@ -148,13 +159,7 @@ int launch_wide_bn(const CUtensorMap& amap, const CUtensorMap& wmap, const CUten
     kern<<<grid, kWideThreads, S::kSmemBytes, st>>>(amap, wmap, a.ksplit > 1 ? pmap : ymap, a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
-    if (a.ksplit > 1) {
-        const long long total = static_cast<long long>(a.tiles_m) * kBM * a.n;
-        const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-        splitk_reduce_kernel<MODE><<<blocks, 256, 0, st>>>(a, a.tiles_m);
-        count_launch();
-        SDB_CUDA(cudaGetLastError());
-    }
+    if (a.ksplit > 1) return launch_reduce<MODE>(a, st);
     return SDB_OK;
 }
 
