@@ -902,6 +902,7 @@ OPS = {
     "conv3x3_320x64x64x2": lambda torch, sdb, dev: _op_conv(torch, sdb, dev, 320, 320, 64, 2),
     "conv3x3_1280x16x16x2": lambda torch, sdb, dev: _op_conv(torch, sdb, dev, 1280, 1280, 16, 2),
     "attention_4096x4096_d40_b1": lambda torch, sdb, dev: _op_attention(torch, sdb, dev, 4096, 4096, 40, 1),
+    "attention_4096x77_d40_b2": lambda torch, sdb, dev: _op_attention(torch, sdb, dev, 4096, 77, 40, 2),
     "linear_8192x320x320": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 320),
     "linear_8192x320x1280": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 1280),
     "linear_2048x640x640": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 2048, 640, 640),
