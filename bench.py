@@ -737,6 +737,64 @@ def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5) -> t
     return ms, flops
 
 
+def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
+    """One SDXL sampler step at 832 x 1216 (latent 152 x 104): the UNet forward on the
+    classifier-free-guidance batch of 2 (context 2 x 77 x 2048, pooled text + size/crop conditioning
+    2 x 2816, 2.57B random-init FP16 weights) and the guidance (scale 6) + Euler update, captured once and
+    replayed; ms a step as the max over ranks."""
+    import sdb
+    import unet as U
+
+    net = U.UNet(U.SDXL, device=dev, seed=20261013)
+    g = torch.Generator(device=dev).manual_seed(77)
+    x_in = torch.randn(2, 152, 104, 4, device=dev, generator=g)
+    x = x_in[:1].clone()
+    t = torch.full((2,), 700.0, device=dev)
+    ctx = torch.randn(2, 77, 2048, device=dev, generator=g)
+    y = torch.randn(2, 2816, device=dev, generator=g)
+    out = {}
+
+    def forward():
+        out["eps"] = net.forward(x_in, t, ctx, y=y)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            forward()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        forward()
+    torch.cuda.synchronize()
+
+    def step():
+        graph.replay()
+        sdb.euler_cfg_step(out["eps"], x, x_in, 6.0, 1.0, 0.9, 0.7, stream=s)
+
+    with torch.cuda.stream(s):
+        step()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        start.record(s)
+        for _ in range(reps):
+            step()
+        end.record(s)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / reps)
+    flops = net.flops(2, 152, 104)
+    res = {"ms_per_step": ms, "step_tflop": flops / 1e12, "tflops": flops / (ms * 1e-3) / 1e12,
+           "resolution": "832x1216 (latent 152x104)", "batch": "2 (CFG 6)", "params": net.params,
+           "context": "2x77x2048 + pooled/size conditioning 2x2816",
+           "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step "
+                     "(the ancestral sampler's noise term not included)"}
+    del graph, net
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
     import sdb
     import unet as U
@@ -821,6 +879,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     d2h = h_out.numel() * 4
     # The VAE decode of the step's latent (one image a GPU), captured once and replayed.
     vae_ms, vae_flops = measure_vae(torch, dev, sampler.x, barrier, max_over_ranks)
+    sdxl = None if args.no_sdxl else measure_sdxl(torch, dev, barrier, max_over_ranks)
     status = sdb.device_status(clear=True)
     del sampler
     if dist is not None:
@@ -857,6 +916,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
         "vae_tflops": vae_flops / (vae_ms * 1e-3) / 1e12,
         "imgs_per_s": world * 1e3 / (SAMPLER_STEPS * ms + vae_ms),
         "imgs_per_s_unet_only": world * 1e3 / ms / SAMPLER_STEPS,
+        "sdxl": sdxl,
         "step_tflop": step_flops / 1e12,
         "step_frac_of_sustained_peak": step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
         "roofline": {"kernel": f"{dom} (all calls of the class in one forward)", "bound": "tensor",
@@ -971,6 +1031,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sdxl", action="store_true", help="skip the SDXL step (BASELINE config 5) measured beside SD 1.5")
     ap.add_argument("--op", choices=sorted(OPS), help="run one operation three times (profiler captures) and exit")
     ap.add_argument("--tune", default="", help="sdb_set_tuning spec for the run, e.g. bits=8 (the quantized linear layers)")
     args = ap.parse_args()

@@ -12,12 +12,18 @@ graph allows: every ResBlock's time-embedding projection is one GEMM over the
 concatenated weights, and so is every cross-attention's K/V projection of the
 (fixed) text context.
 
-The architecture is SD 1.x's (ldm UNetModel): model channels 320, multipliers
-1/2/4/4, 2 ResBlocks a level, a SpatialTransformer of depth 1 with 8 heads at
-the first three levels, context dim 768, GroupNorm 32 (eps 1e-5; 1e-6 in the
-transformers), LayerNorm eps 1e-5, GEGLU feed-forward of 4C, nearest 2x
-upsampling.  Weights are random (the benchmark's random-init FP16 weights),
-drawn from one seed on the device.
+Two configurations of the same ldm UNetModel (the benchmark's):
+  SD15: model channels 320, multipliers 1/2/4/4, 2 ResBlocks a level, a
+        SpatialTransformer of depth 1 with 8 heads at the first three levels
+        and in the middle, context dim 768;
+  SDXL: multipliers 1/2/4, transformers of depth 0/2/10 (10 in the middle)
+        with heads of 64 dims, context dim 2048, and the label embedding of
+        the pooled text embedding and the size/crop conditioning (2816 inputs)
+        added to the time embedding.
+Both: GroupNorm 32 (eps 1e-5; 1e-6 in the transformers), LayerNorm eps 1e-5,
+GEGLU feed-forward of 4C, linear proj_in / proj_out, nearest 2x upsampling.
+Weights are random (the benchmark's random-init FP16 weights), drawn from one
+seed on the device.
 """
 from __future__ import annotations
 
@@ -39,9 +45,23 @@ class UNetConfig:
     context_dim: int = 768
     groups: int = 32
     time_dim_mult: int = 4
+    transformer_depth: tuple = ()      # blocks of the transformer at each level (empty: 1 at attention_levels)
+    mid_depth: int = 1
+    head_dim: int = 0                  # dims of a head (0: `heads` heads of C / heads)
+    adm_in_channels: int = 0           # inputs of the label embedding (SDXL: pooled text + size/crop)
+
+    def depth(self, level: int) -> int:
+        if self.transformer_depth:
+            return self.transformer_depth[level]
+        return 1 if level in self.attention_levels else 0
+
+    def heads_of(self, channels: int) -> int:
+        return channels // self.head_dim if self.head_dim else self.heads
 
 
 SD15 = UNetConfig()
+SDXL = UNetConfig(channel_mult=(1, 2, 4), attention_levels=(1, 2), transformer_depth=(0, 2, 10), mid_depth=10,
+                  head_dim=64, context_dim=2048, adm_in_channels=2816)
 
 
 # ---------------------------------------------------------------- weights
@@ -96,11 +116,8 @@ class ResBlock:
 
 
 @dataclass
-class Transformer:
-    c: int
-    gn: tuple
-    proj_in: object
-    b_in: object
+class TBlock:
+    """One BasicTransformerBlock: self-attention, cross-attention on the context, GEGLU feed-forward."""
     ln1: tuple
     wqkv: object
     wo1: object
@@ -114,9 +131,19 @@ class Transformer:
     bff1: object
     wff2: object
     bff2: object
+    kv_offset: int = 0        # columns of this block's K/V in the fused context projection
+
+
+@dataclass
+class Transformer:
+    c: int
+    heads: int
+    gn: tuple
+    proj_in: object
+    b_in: object
+    blocks: list
     proj_out: object
     b_out: object
-    kv_offset: int = 0        # columns of this block's K/V in the fused context projection
 
 
 @dataclass
@@ -154,13 +181,15 @@ class UNet:
             res_blocks.append(rb)
             return rb
 
-        def transformer(ch):
-            tr = Transformer(
-                ch, (init.gamma(ch), init.beta(ch)), init.linear(ch, ch), init.bias(ch),
-                (init.gamma(ch), init.beta(ch)), init.linear(3 * ch, ch), init.linear(ch, ch), init.bias(ch),
-                (init.gamma(ch), init.beta(ch)), init.linear(ch, ch), init.linear(ch, ch), init.bias(ch),
-                (init.gamma(ch), init.beta(ch)), init.linear(8 * ch, ch), init.bias(8 * ch),
-                init.linear(ch, 4 * ch), init.bias(ch), init.linear(ch, ch), init.bias(ch))
+        def transformer(ch, depth):
+            if depth == 0:
+                return None
+            gn, proj_in, b_in = (init.gamma(ch), init.beta(ch)), init.linear(ch, ch), init.bias(ch)
+            blocks = [TBlock((init.gamma(ch), init.beta(ch)), init.linear(3 * ch, ch), init.linear(ch, ch),
+                             init.bias(ch), (init.gamma(ch), init.beta(ch)), init.linear(ch, ch), init.linear(ch, ch),
+                             init.bias(ch), (init.gamma(ch), init.beta(ch)), init.linear(8 * ch, ch),
+                             init.bias(8 * ch), init.linear(ch, 4 * ch), init.bias(ch)) for _ in range(depth)]
+            tr = Transformer(ch, c.heads_of(ch), gn, proj_in, b_in, blocks, init.linear(ch, ch), init.bias(ch))
             transformers.append(tr)
             return tr
 
@@ -173,14 +202,14 @@ class UNet:
             for _ in range(c.num_res_blocks):
                 rb = resblock(ch, mult * mc)
                 ch = mult * mc
-                level.blocks.append((rb, transformer(ch) if lvl in c.attention_levels else None))
+                level.blocks.append((rb, transformer(ch, c.depth(lvl))))
                 chans.append(ch)
             if lvl != len(c.channel_mult) - 1:
                 level.down = (init.conv(ch, ch, 3), init.bias(ch))
                 chans.append(ch)
             self.down.append(level)
         # Middle.
-        self.mid = (resblock(ch, ch), transformer(ch), resblock(ch, ch))
+        self.mid = (resblock(ch, ch), transformer(ch, c.mid_depth), resblock(ch, ch))
         # Decoder.
         self.up: list[Level] = []
         for lvl, mult in reversed(list(enumerate(c.channel_mult))):
@@ -189,12 +218,15 @@ class UNet:
                 skip = chans.pop()
                 rb = resblock(ch + skip, mult * mc)
                 ch = mult * mc
-                level.blocks.append((rb, transformer(ch) if lvl in c.attention_levels else None))
+                level.blocks.append((rb, transformer(ch, c.depth(lvl))))
             if lvl != 0:
                 level.up = (init.conv(ch, ch, 3), init.bias(ch))
             self.up.append(level)
         self.out_gn = (init.gamma(ch), init.beta(ch))
         self.conv_out, self.conv_out_b = init.conv(c.out_channels, ch, 3), init.bias(c.out_channels)
+        if c.adm_in_channels:
+            self.label_w1, self.label_b1 = init.linear(td, c.adm_in_channels), init.bias(td)
+            self.label_w2, self.label_b2 = init.linear(td, td), init.bias(td)
 
         # Fused projections: all time-embedding projections, all context K/V projections.
         off = 0
@@ -208,9 +240,10 @@ class UNet:
         off = 0
         kv_w = []
         for tr in transformers:
-            tr.kv_offset = off
-            off += 2 * tr.c
-            kv_w.append(init.linear(2 * tr.c, c.context_dim))
+            for blk in tr.blocks:
+                blk.kv_offset = off
+                off += 2 * tr.c
+                kv_w.append(init.linear(2 * tr.c, c.context_dim))
         self.kv_w = torch.cat(kv_w).contiguous() if kv_w else None
         self.res_blocks, self.transformers = res_blocks, transformers
         self.params = init.params
@@ -245,25 +278,26 @@ class UNet:
 
     def _transformer(self, x, tr: Transformer, ctx_kv):
         b, hh, ww, c = x.shape
-        heads = self.cfg.heads
+        heads = tr.heads
         scale = 1.0 / math.sqrt(c // heads)
         n = self._gn(x, tr.gn, 1e-6, False)
         t = sdb.mul_mat(tr.proj_in, n.view(b, hh * ww, c), chain=sdb.Chain().add(tr.b_in))
-        # Self-attention.
-        h1 = self._ln(t, tr.ln1)
-        qkv = sdb.mul_mat(tr.wqkv, h1)
-        a = sdb.attention_heads(qkv[:, :, :c], qkv[:, :, c:2 * c], qkv[:, :, 2 * c:], heads, heads, scale)
-        sdb.mul_mat(tr.wo1, a, out=t, chain=sdb.Chain().add(tr.bo1).redirect(t, True))
-        # Cross-attention on the text context.
-        h2 = self._ln(t, tr.ln2)
-        q2 = sdb.mul_mat(tr.wq2, h2)
-        kv = ctx_kv[:, :, tr.kv_offset:tr.kv_offset + 2 * c]
-        a2 = sdb.attention_heads(q2, kv[:, :, :c], kv[:, :, c:], heads, heads, scale)
-        sdb.mul_mat(tr.wo2, a2, out=t, chain=sdb.Chain().add(tr.bo2).redirect(t, True))
-        # GEGLU feed-forward.
-        h3 = self._ln(t, tr.ln3)
-        g = sdb.mul_mat_gated(tr.wff1, h3, chain=sdb.Chain().add(tr.bff1))
-        sdb.mul_mat(tr.wff2, g, out=t, chain=sdb.Chain().add(tr.bff2).redirect(t, True))
+        for blk in tr.blocks:
+            # Self-attention.
+            h1 = self._ln(t, blk.ln1)
+            qkv = sdb.mul_mat(blk.wqkv, h1)
+            a = sdb.attention_heads(qkv[:, :, :c], qkv[:, :, c:2 * c], qkv[:, :, 2 * c:], heads, heads, scale)
+            sdb.mul_mat(blk.wo1, a, out=t, chain=sdb.Chain().add(blk.bo1).redirect(t, True))
+            # Cross-attention on the text context.
+            h2 = self._ln(t, blk.ln2)
+            q2 = sdb.mul_mat(blk.wq2, h2)
+            kv = ctx_kv[:, :, blk.kv_offset:blk.kv_offset + 2 * c]
+            a2 = sdb.attention_heads(q2, kv[:, :, :c], kv[:, :, c:], heads, heads, scale)
+            sdb.mul_mat(blk.wo2, a2, out=t, chain=sdb.Chain().add(blk.bo2).redirect(t, True))
+            # GEGLU feed-forward.
+            h3 = self._ln(t, blk.ln3)
+            g = sdb.mul_mat_gated(blk.wff1, h3, chain=sdb.Chain().add(blk.bff1))
+            sdb.mul_mat(blk.wff2, g, out=t, chain=sdb.Chain().add(blk.bff2).redirect(t, True))
         # Back to the image, plus the block's input.
         xv = x.view(b, hh * ww, c)
         sdb.mul_mat(tr.proj_out, t, out=xv, chain=sdb.Chain().add(tr.b_out).redirect(xv, True))
@@ -271,20 +305,27 @@ class UNet:
 
     # ------------------------------------------------------------ forward
 
-    def embed(self, timesteps):
-        """SiLU(time_embed(timestep_embedding(t))) (B, 4 * model_channels), then every ResBlock's projection."""
+    def embed(self, timesteps, y=None):
+        """SiLU(time_embed(timestep_embedding(t)) [+ label_emb(y)]) (B, 4 * model_channels), then every
+        ResBlock's projection.  y (B, adm_in_channels): SDXL's pooled text embedding and size/crop
+        conditioning."""
         mc = self.cfg.model_channels
         te = sdb.timestep_embedding(timesteps, mc)
         e1 = sdb.mul_mat(self.t_w1, te, chain=sdb.Chain().add(self.t_b1).silu())
-        e2 = sdb.mul_mat(self.t_w2, e1, chain=sdb.Chain().add(self.t_b2).silu())
+        ch = sdb.Chain().add(self.t_b2)
+        if self.cfg.adm_in_channels:
+            l1 = sdb.mul_mat(self.label_w1, y, chain=sdb.Chain().add(self.label_b1).silu())
+            l2 = sdb.mul_mat(self.label_w2, l1, chain=sdb.Chain().add(self.label_b2))
+            ch.add(l2)
+        e2 = sdb.mul_mat(self.t_w2, e1, chain=ch.silu())
         return sdb.mul_mat(self.emb_w, e2, chain=sdb.Chain().add(self.emb_b))
 
     def context_kv(self, context):
         """Every cross-attention's K and V of the context (B, 77, sum of 2C)."""
         return sdb.mul_mat(self.kv_w, context)
 
-    def forward(self, x, timesteps, context, ctx_kv=None):
-        emb = self.embed(timesteps)
+    def forward(self, x, timesteps, context, ctx_kv=None, y=None):
+        emb = self.embed(timesteps, y)
         if ctx_kv is None:
             ctx_kv = self.context_kv(context)
         h = sdb.conv2d_nhwc(self.conv_in, x, (1, 1), (1, 1), chain=sdb.Chain().add(self.conv_in_b, [0, 0, 1, 0]))
@@ -328,14 +369,15 @@ class UNet:
         def conv(ic, oc, k, h, w):
             return 2 * k * k * ic * oc * h * w * batch
 
-        def tr_flops(ch, h, w):
+        def tr_flops(tr, h, w):
+            ch = tr.c
             L = h * w
             f = 2 * L * ch * ch * 2 * batch                    # proj_in, proj_out
-            f += 2 * L * ch * 3 * ch * batch + 4 * ch * L * L * batch + 2 * L * ch * ch * batch
-            f += 2 * L * ch * ch * batch + 4 * ch * L * context_len * batch + 2 * L * ch * ch * batch
-            f += 2 * batch * context_len * c.context_dim * 2 * ch    # K/V of the context
-            f += 2 * L * ch * 8 * ch * batch + 2 * L * 4 * ch * ch * batch
-            return f
+            blk = 2 * L * ch * 3 * ch * batch + 4 * ch * L * L * batch + 2 * L * ch * ch * batch
+            blk += 2 * L * ch * ch * batch + 4 * ch * L * context_len * batch + 2 * L * ch * ch * batch
+            blk += 2 * batch * context_len * c.context_dim * 2 * ch    # K/V of the context
+            blk += 2 * L * ch * 8 * ch * batch + 2 * L * 4 * ch * ch * batch
+            return f + len(tr.blocks) * blk
 
         def rb_flops(rb, h, w):
             f = conv(rb.cin, rb.cout, 3, h, w) + conv(rb.cout, rb.cout, 3, h, w)
@@ -346,22 +388,24 @@ class UNet:
         mc = c.model_channels
         td = self.time_dim
         total += 2 * batch * (mc * td + td * td)
+        if c.adm_in_channels:
+            total += 2 * batch * (c.adm_in_channels * td + td * td)
         total += conv(c.in_channels, mc, 3, height, width)
         for lvl, level in enumerate(self.down):
             h, w = hw[lvl]
             for rb, tr in level.blocks:
-                total += rb_flops(rb, h, w) + (tr_flops(tr.c, h, w) if tr else 0)
+                total += rb_flops(rb, h, w) + (tr_flops(tr, h, w) if tr else 0)
             if level.down is not None:
                 ch = level.blocks[-1][0].cout
                 total += conv(ch, ch, 3, *hw[lvl + 1])
         h, w = hw[-1]
         rb1, tr, rb2 = self.mid
-        total += rb_flops(rb1, h, w) + tr_flops(tr.c, h, w) + rb_flops(rb2, h, w)
+        total += rb_flops(rb1, h, w) + tr_flops(tr, h, w) + rb_flops(rb2, h, w)
         for i, level in enumerate(self.up):
             lvl = len(c.channel_mult) - 1 - i
             h, w = hw[lvl]
             for rb, tr in level.blocks:
-                total += rb_flops(rb, h, w) + (tr_flops(tr.c, h, w) if tr else 0)
+                total += rb_flops(rb, h, w) + (tr_flops(tr, h, w) if tr else 0)
             if level.up is not None:
                 ch = level.blocks[-1][0].cout
                 total += conv(ch, ch, 3, *hw[lvl - 1])

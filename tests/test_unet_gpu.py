@@ -82,6 +82,58 @@ def test_unet_tiny_matches_float64(cuda):
     assert np.isfinite(err) and err <= 1e-5, f"{err:.3g} of the largest output"
 
 
+# The SDXL structure made small: no attention at the first level, transformers of depth 2 (and 2 in the
+# middle) with heads of a fixed width, the label embedding added to the time embedding.
+TINY_XL = dict(model_channels=32, channel_mult=(1, 2), num_res_blocks=1, attention_levels=(1,),
+               transformer_depth=(0, 2), mid_depth=2, head_dim=16, context_dim=48, groups=8, adm_in_channels=40)
+
+
+def test_unet_tiny_sdxl_structure_matches_float64(cuda):
+    import torch
+    import unet as U
+    import unet_reference as R
+
+    net = U.UNet(U.UNetConfig(**TINY_XL), device=cuda, seed=6)
+    g = torch.Generator(device=cuda).manual_seed(9)
+    x = torch.randn(2, 16, 16, 4, device=cuda, generator=g)
+    t = torch.tensor([500.0, 500.0], device=cuda)
+    ctx = torch.randn(2, 9, 48, device=cuda, generator=g)
+    y = torch.randn(2, 40, device=cuda, generator=g)
+    got = net.forward(x, t, ctx, y=y).double()
+    torch.cuda.synchronize()
+    want = R.forward(net, x, t, ctx, y=y)
+    err = (got - want).abs().max().item() / want.abs().max().item()
+    assert np.isfinite(err) and err <= 1e-5, f"{err:.3g} of the largest output"
+
+
+def test_sdxl_unet_forward(cuda):
+    """The SDXL UNet (2.57B parameters) once at a 64 x 64 latent, batch 2: finite, graph replay bit-identical."""
+    import torch
+    import unet as U
+
+    net = U.UNet(U.SDXL, device=cuda, seed=8)
+    assert 2.5e9 < net.params < 2.65e9, net.params
+    g = torch.Generator(device=cuda).manual_seed(10)
+    x = torch.randn(2, 64, 64, 4, device=cuda, generator=g)
+    t = torch.tensor([700.0, 700.0], device=cuda)
+    ctx = torch.randn(2, 77, 2048, device=cuda, generator=g)
+    y = torch.randn(2, 2816, device=cuda, generator=g)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        eager = net.forward(x, t, ctx, y=y).clone()
+        net.forward(x, t, ctx, y=y)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        out = net.forward(x, t, ctx, y=y)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.isfinite(eager).all()
+    assert torch.equal(out, eager)
+    del graph
+
+
 def test_sd15_unet_graph_replay(cuda):
     """SD 1.5 at its benchmark shape: the captured step equals the eager forward, bit for bit."""
     import torch

@@ -42,20 +42,22 @@ def attention(q, k, v, heads):
     return (p @ v).transpose(1, 2).reshape(b, lq, c)
 
 
-def transformer(x, tr, context, heads, groups):
+def transformer(x, tr, context, groups):
     b, c, h, w = x.shape
+    heads = tr.heads
     n = gn(x, tr.gn, groups, 1e-6, False)
     t = n.permute(0, 2, 3, 1).reshape(b, h * w, c) @ _w(tr.proj_in).T + _w(tr.b_in)
-    h1 = F.layer_norm(t, (c,), _w(tr.ln1[0]), _w(tr.ln1[1]), 1e-5)
-    qkv = h1 @ _w(tr.wqkv).T
-    t = t + attention(qkv[..., :c], qkv[..., c:2 * c], qkv[..., 2 * c:], heads) @ _w(tr.wo1).T + _w(tr.bo1)
-    h2 = F.layer_norm(t, (c,), _w(tr.ln2[0]), _w(tr.ln2[1]), 1e-5)
-    kv = context @ _w(tr.kv_w).T
-    t = t + attention(h2 @ _w(tr.wq2).T, kv[..., :c], kv[..., c:], heads) @ _w(tr.wo2).T + _w(tr.bo2)
-    h3 = F.layer_norm(t, (c,), _w(tr.ln3[0]), _w(tr.ln3[1]), 1e-5)
-    y = h3 @ _w(tr.wff1).T + _w(tr.bff1)
-    g = y[..., :4 * c] * F.gelu(y[..., 4 * c:], approximate="tanh")
-    t = t + g @ _w(tr.wff2).T + _w(tr.bff2)
+    for blk in tr.blocks:
+        h1 = F.layer_norm(t, (c,), _w(blk.ln1[0]), _w(blk.ln1[1]), 1e-5)
+        qkv = h1 @ _w(blk.wqkv).T
+        t = t + attention(qkv[..., :c], qkv[..., c:2 * c], qkv[..., 2 * c:], heads) @ _w(blk.wo1).T + _w(blk.bo1)
+        h2 = F.layer_norm(t, (c,), _w(blk.ln2[0]), _w(blk.ln2[1]), 1e-5)
+        kv = context @ _w(blk.kv_w).T
+        t = t + attention(h2 @ _w(blk.wq2).T, kv[..., :c], kv[..., c:], heads) @ _w(blk.wo2).T + _w(blk.bo2)
+        h3 = F.layer_norm(t, (c,), _w(blk.ln3[0]), _w(blk.ln3[1]), 1e-5)
+        y = h3 @ _w(blk.wff1).T + _w(blk.bff1)
+        g = y[..., :4 * c] * F.gelu(y[..., 4 * c:], approximate="tanh")
+        t = t + g @ _w(blk.wff2).T + _w(blk.bff2)
     out = t @ _w(tr.proj_out).T + _w(tr.b_out)
     return x + out.view(b, h, w, c).permute(0, 3, 1, 2)
 
@@ -67,16 +69,21 @@ def timestep_embedding(t, dim, max_period=10000):
     return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
 
 
-def forward(unet, x_nhwc, timesteps, context):
-    """eps (B, H, W, C_out) in float64 for the runner's weights and inputs."""
+def forward(unet, x_nhwc, timesteps, context, y=None):
+    """eps (B, H, W, C_out) in float64 for the runner's weights and inputs (y: the label embedding's input)."""
     cfg = unet.cfg
-    groups, heads = cfg.groups, cfg.heads
+    groups = cfg.groups
     # The fused K/V weights, split back per block.
     for tr in unet.transformers:
-        tr.kv_w = unet.kv_w[tr.kv_offset:tr.kv_offset + 2 * tr.c]
+        for blk in tr.blocks:
+            blk.kv_w = unet.kv_w[blk.kv_offset:blk.kv_offset + 2 * tr.c]
     te = timestep_embedding(timesteps, cfg.model_channels)
     e = F.silu(te @ _w(unet.t_w1).T + _w(unet.t_b1))
-    e = F.silu(e @ _w(unet.t_w2).T + _w(unet.t_b2))
+    e = e @ _w(unet.t_w2).T + _w(unet.t_b2)
+    if cfg.adm_in_channels:
+        lab = F.silu(y.to(D) @ _w(unet.label_w1).T + _w(unet.label_b1))
+        e = e + lab @ _w(unet.label_w2).T + _w(unet.label_b2)
+    e = F.silu(e)
     emb = e @ _w(unet.emb_w).T + _w(unet.emb_b)
     ctx = context.to(D)
     h = F.conv2d(x_nhwc.to(D).permute(0, 3, 1, 2), _w(unet.conv_in), _w(unet.conv_in_b), padding=1)
@@ -85,21 +92,21 @@ def forward(unet, x_nhwc, timesteps, context):
         for rb, tr in level.blocks:
             h = resblock(h, rb, emb, groups)
             if tr is not None:
-                h = transformer(h, tr, ctx, heads, groups)
+                h = transformer(h, tr, ctx, groups)
             hs.append(h)
         if level.down is not None:
             h = F.conv2d(h, _w(level.down[0]), _w(level.down[1]), stride=2, padding=1)
             hs.append(h)
     rb1, tr, rb2 = unet.mid
     h = resblock(h, rb1, emb, groups)
-    h = transformer(h, tr, ctx, heads, groups)
+    h = transformer(h, tr, ctx, groups)
     h = resblock(h, rb2, emb, groups)
     for level in unet.up:
         for rb, tr in level.blocks:
             h = torch.cat([h, hs.pop()], dim=1)
             h = resblock(h, rb, emb, groups)
             if tr is not None:
-                h = transformer(h, tr, ctx, heads, groups)
+                h = transformer(h, tr, ctx, groups)
         if level.up is not None:
             h = F.interpolate(h, scale_factor=2, mode="nearest")
             h = F.conv2d(h, _w(level.up[0]), _w(level.up[1]), padding=1)
