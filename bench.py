@@ -795,6 +795,63 @@ def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
     return res
 
 
+def run_cfg_split(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
+    """SD 1.5 with classifier-free guidance split over GPU pairs (--cfg-split): each rank runs the UNet on one
+    half of the guidance batch (batch 1), the pair all-gathers its eps each step (NCCL), both take the same
+    update.  value = images a step x steps/s over the job (world / 2 images)."""
+    import sdb
+    import unet as U
+
+    if world % 2:
+        raise SystemExit("--cfg-split needs an even number of ranks")
+    groups = U.pair_groups(dist, world)
+    net = U.UNet(U.SD15, device=dev, seed=20261011)
+    sampler = U.PairSampler(net, dist, groups[rank // 2], rank % 2, 64, 64, steps=SAMPLER_STEPS)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank // 2)
+    latent = torch.randn(1, 64, 64, 4, device=dev, generator=g)
+    context = torch.randn(2, 77, 768, device=dev, generator=g)
+    sampler.x.copy_(latent * sampler.sigmas[0])
+    sampler.context.copy_(context[rank % 2:rank % 2 + 1])
+    sampler.set_step(0)
+    sampler.capture(warmup=max(3, args.warmup))
+    for i in range(args.warmup):
+        sampler.step(i % SAMPLER_STEPS)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(sampler.stream)
+        for i in range(args.steps):
+            sampler.step(i % SAMPLER_STEPS)
+        end.record(sampler.stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    # Both ranks of a pair hold the same latent after every step.
+    both = torch.empty(2, *sampler.x.shape[1:], device=dev)
+    U.gather_guidance(dist, groups[rank // 2], sampler.x, both)
+    same = torch.tensor([1.0 if torch.equal(both[0], both[1]) else 0.0], device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    status = sdb.device_status(clear=True)
+    del sampler
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": UNET_METRIC, "value": (world // 2) * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": UNET_WORKLOAD + "_cfg_split", "resolution": "512x512 (latent 64x64)",
+                   "batch": "1 a rank (one guidance half), 2 a pair",
+                   "parallelism": f"guidance pairs x{world // 2} (eps all-gathered per step over NCCL)",
+                   "timing": "CUDA-graph replay of the half forward, the pair's all-gather, the update"},
+        "pair_latents_identical": bool(same.item() == 1.0),
+        "clocks": clocks.summary(), "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
     import sdb
     import unet as U
@@ -1032,6 +1089,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sdxl", action="store_true", help="skip the SDXL step (BASELINE config 5) measured beside SD 1.5")
+    ap.add_argument("--cfg-split", action="store_true",
+                    help="split classifier-free guidance over GPU pairs (needs an even number of ranks)")
     ap.add_argument("--op", choices=sorted(OPS), help="run one operation three times (profiler captures) and exit")
     ap.add_argument("--tune", default="", help="sdb_set_tuning spec for the run, e.g. bits=8 (the quantized linear layers)")
     args = ap.parse_args()
@@ -1069,7 +1128,7 @@ def main() -> None:
         if dist is not None:
             dist.barrier()
 
-    run = run_unet if args.workload == "unet" else run_hot_ops
+    run = (run_cfg_split if args.cfg_split else run_unet) if args.workload == "unet" else run_hot_ops
     run(args, torch, dev, dist, world, rank, local, barrier, lambda v: max_over_ranks(v, dist, dev))
 
 

@@ -81,3 +81,41 @@ def test_reference_arm_line():
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["unit"] == "UNet steps/s"
+
+
+def _guidance_worker(rank: int, world: int, port: int, out):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT / "stable-diffusion.assembly_b200"))
+    import unet as U
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    groups = U.pair_groups(dist, world)
+    group = groups[rank // 2]
+    half = torch.full((1, 3, 2, 4), float(10 * rank + 1))
+    full = torch.zeros(2, 3, 2, 4)
+    U.gather_guidance(dist, group, half, full)
+    out[rank] = full[:, 0, 0, 0].tolist()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_guidance_pairs_gloo():
+    """Four ranks in two guidance pairs: each pair's lower rank holds the unconditional half, its higher
+    rank the conditional one, and after the exchange both hold [unconditional, conditional] -- their own
+    pair's, never the other pair's."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    out = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_guidance_worker, args=(r, 4, port, out)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    assert out[0] == out[1] == [1.0, 11.0]
+    assert out[2] == out[3] == [21.0, 31.0]
