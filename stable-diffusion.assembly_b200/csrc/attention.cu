@@ -792,18 +792,14 @@ int prepare_tiles(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const s
     a.qs = base;
     a.ks = base + 2 * a.q_plane;
     a.vs = base + 2 * (a.q_plane + a.k_plane);
-    if (int s = split_tiles(q->data, 0, qne, qnb, a.dp, kAttnQ, const_cast<uint16_t*>(
-                                reinterpret_cast<const uint16_t*>(a.qs)), a.err, st); s != SDB_OK)
-        return s;
-    if (int s = split_tiles(k->data, k->type == SDB_TYPE_F16, kne, knb, a.dp, BK,
-                            const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.ks)), a.err, st);
-        s != SDB_OK)
-        return s;
-    if (int s = split_tiles(v->data, v->type == SDB_TYPE_F16, vne, vnb, a.dvs, BK,
-                            const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.vs)), a.err, st);
-        s != SDB_OK)
-        return s;
-    return SDB_OK;
+    // Q, K and V split in one launch.
+    const SplitTilesJob jobs[3] = {
+        split_tiles_job(q->data, 0, qne, qnb, a.dp, kAttnQ, const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.qs))),
+        split_tiles_job(k->data, k->type == SDB_TYPE_F16, kne, knb, a.dp, BK,
+                        const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.ks))),
+        split_tiles_job(v->data, v->type == SDB_TYPE_F16, vne, vnb, a.dvs, BK,
+                        const_cast<uint16_t*>(reinterpret_cast<const uint16_t*>(a.vs)))};
+    return split_tiles_many(jobs, 3, a.err, st);
 }
 
 template <int BK, int DVC, int NO>

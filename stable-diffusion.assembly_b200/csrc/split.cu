@@ -71,9 +71,10 @@ __global__ void split_rows_half_kernel(const __half* __restrict__ x, long long n
 
 // One thread per 8 values of a row of a tile.
 template <typename I>
-__global__ void split_tiles_kernel(const void* __restrict__ x, int half, I ne0, I ne1, I ne2, I heads,
-                                   long long xnb0, long long xnb1, long long xnb2, long long xnb3, I ld, int tile,
-                                   I ntiles, uint16_t* __restrict__ out, long long plane, unsigned* err) {
+__device__ __forceinline__ void split_tiles_body(const void* __restrict__ x, int half, I ne0, I ne1, I ne2, I heads,
+                                                 long long xnb0, long long xnb1, long long xnb2, long long xnb3, I ld,
+                                                 int tile, I ntiles, uint16_t* __restrict__ out, long long plane,
+                                                 unsigned* err) {
     const I chunks = ld / 8;
     const I rows_pad = ntiles * tile;
     const I total = heads * rows_pad * chunks;
@@ -112,6 +113,22 @@ __global__ void split_tiles_kernel(const void* __restrict__ x, int half, I ne0, 
         *reinterpret_cast<uint4*>(out + plane / 2 + at) = lo;
     }
     if (over) atomicOr(err, kErrRange);
+}
+
+template <typename I>
+__global__ void split_tiles_kernel(const void* __restrict__ x, int half, I ne0, I ne1, I ne2, I heads,
+                                   long long xnb0, long long xnb1, long long xnb2, long long xnb3, I ld, int tile,
+                                   I ntiles, uint16_t* __restrict__ out, long long plane, unsigned* err) {
+    split_tiles_body<I>(x, half, ne0, ne1, ne2, heads, xnb0, xnb1, xnb2, xnb3, ld, tile, ntiles, out, plane, err);
+}
+
+// Several split_tiles jobs in one launch: blockIdx.y picks the job.
+template <typename I>
+__global__ void split_tiles_many_kernel(const SplitTilesJobs jobs, unsigned* err) {
+    const SplitTilesJob& j = jobs.job[blockIdx.y];
+    split_tiles_body<I>(j.x, j.half, static_cast<I>(j.ne0), static_cast<I>(j.ne1), static_cast<I>(j.ne2),
+                        static_cast<I>(j.heads), j.xnb[0], j.xnb[1], j.xnb[2], j.xnb[3], static_cast<I>(j.ld), j.tile,
+                        static_cast<I>(j.ntiles), j.out, j.plane, err);
 }
 
 // Channels-last through shared memory: a block takes 64 channels x 32
@@ -233,6 +250,43 @@ int split_tiles(const void* x, int half, const long long ne[4], const long long 
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
+}
+
+int split_tiles_many(const SplitTilesJob* jobs, int count, unsigned* err, cudaStream_t stream) {
+    if (count <= 0 || count > kSplitTilesJobs) return fail(SDB_INVALID, "split_tiles_many: 1..3 jobs");
+    SplitTilesJobs all{};
+    long long most = 0;
+    for (int i = 0; i < count; ++i) {
+        SplitTilesJob j = jobs[i];
+        most = std::max(most, j.heads * j.ntiles * j.tile * (j.ld / 8));
+        all.job[i] = j;
+    }
+    const int blocks = static_cast<int>(std::min<long long>((most + 255) / 256, 148LL * 32));
+    if (blocks == 0) return SDB_OK;
+    const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(count));
+    if (most * 8 < (1LL << 31)) split_tiles_many_kernel<unsigned><<<grid, 256, 0, stream>>>(all, err);
+    else split_tiles_many_kernel<long long><<<grid, 256, 0, stream>>>(all, err);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+SplitTilesJob split_tiles_job(const void* x, int half, const long long ne[4], const long long xnb[4], long long ld,
+                              int tile, uint16_t* out) {
+    SplitTilesJob j{};
+    j.x = x;
+    j.half = half;
+    j.ne0 = ne[0];
+    j.ne1 = ne[1];
+    j.ne2 = ne[2];
+    j.heads = ne[2] * ne[3];
+    for (int d = 0; d < 4; ++d) j.xnb[d] = xnb[d];
+    j.ld = ld;
+    j.tile = tile;
+    j.ntiles = (ne[1] + tile - 1) / tile;
+    j.out = out;
+    j.plane = split_tiles_plane(ne, ld, tile);
+    return j;
 }
 
 int split_nhwc(const float* x, const long long ne[4], const long long xnb[4], long long cp, uint16_t* out,

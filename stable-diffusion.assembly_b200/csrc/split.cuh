@@ -43,6 +43,27 @@ int split_rows_half(const uint16_t* x, const long long ne[4], const long long xn
 // Writes the hi plane, then the lo plane right after it.
 int split_tiles(const void* x, int half, const long long ne[4], const long long xnb[4], long long ld, int tile,
                 uint16_t* out, unsigned* err, cudaStream_t stream);
+// One split_tiles job, and up to three of them in one launch (attention's Q, K
+// and V): the same output as three split_tiles calls.
+struct SplitTilesJob {
+    const void* x;
+    int half;
+    long long ne0, ne1, ne2, heads;
+    long long xnb[4];
+    long long ld;
+    int tile;
+    long long ntiles;
+    uint16_t* out;
+    long long plane;
+};
+constexpr int kSplitTilesJobs = 3;
+struct SplitTilesJobs {
+    SplitTilesJob job[kSplitTilesJobs];
+};
+SplitTilesJob split_tiles_job(const void* x, int half, const long long ne[4], const long long xnb[4], long long ld,
+                              int tile, uint16_t* out);
+int split_tiles_many(const SplitTilesJob* jobs, int count, unsigned* err, cudaStream_t stream);
+
 // Bytes of one plane of split_tiles' output.
 inline long long split_tiles_plane(const long long ne[4], long long ld, int tile) {
     return ne[2] * ne[3] * ((ne[1] + tile - 1) / tile) * tile * ld * 2;
