@@ -178,3 +178,118 @@ def qfold(xq, wq, group: int = 64, y0: np.ndarray | None = None) -> np.ndarray:
     load().rf_qfold(_p(qx), _p(sx), _p(ox), m, _p(qw), _p(sw), _p(ow), n, groups, group, _p(y),
                     1 if y0 is not None else 0)
     return y
+
+
+def _quantize_weights_spans(w, group, wmax, weight_groups, span):
+    """quantize_weights with per-row scales over stretches of `span` numbers of k (a multiple of the
+    group): each stretch quantized as a row of its own (quant.cc quantize_panel_weights over the
+    stretch the caller passes)."""
+    k = w.shape[1]
+    if weight_groups or span is None or span >= k:
+        return quantize_weights(w, group, wmax, weight_groups)
+    parts = [quantize_weights(w[:, k0:k0 + span], group, wmax, False) for k0 in range(0, k, span)]
+    return tuple(np.concatenate([p[i] for p in parts], axis=1) for i in range(3))
+
+
+def im2col(x: np.ndarray, kh: int, kw: int, stride=(1, 1), padding=(0, 0), dilation=(1, 1)) -> np.ndarray:
+    """The columns of a direct convolution, float32: x (N, IC, H, W) -> (N * OH * OW, IC * KH * KW), the
+    positions ow fastest, k = (ic, ky, kx) kx fastest, taps outside the image 0 (conv2d.cc:231-316)."""
+    x = np.asarray(x, np.float32)
+    n, ic, h, wd = x.shape
+    s0, s1 = stride
+    p0, p1 = padding
+    d0, d1 = dilation
+    oh = (h + 2 * p1 - d1 * (kh - 1) - 1) // s1 + 1
+    ow = (wd + 2 * p0 - d0 * (kw - 1) - 1) // s0 + 1
+    xp = np.zeros((n, ic, h + 2 * p1 + d1 * kh + s1, wd + 2 * p0 + d0 * kw + s0), np.float32)
+    xp[:, :, p1:p1 + h, p0:p0 + wd] = x
+    cols = np.empty((n, oh, ow, ic, kh, kw), np.float32)
+    for ky in range(kh):
+        for kx in range(kw):
+            patch = xp[:, :, ky * d1:ky * d1 + s1 * (oh - 1) + 1:s1, kx * d0:kx * d0 + s0 * (ow - 1) + 1:s0]
+            cols[:, :, :, :, ky, kx] = patch.transpose(0, 2, 3, 1)
+    return cols.reshape(n * oh * ow, ic * kh * kw), (n, oh, ow)
+
+
+def qconv2d(w, x, stride=(1, 1), padding=(0, 0), dilation=(1, 1), group: int = 64, levels: int = 255,
+            wmax: int = 127, weight_groups: bool = True) -> np.ndarray:
+    """The reference's quantized direct convolution (conv2d.cc:338-470): the kernel as (OC, IC*KH*KW)
+    rows, each output position's columns quantized in groups of k, folded as the quantized linear
+    layer.  w (OC, IC, KH, KW), x (N, IC, H, W) -> (N, OC, OH, OW) float32, before any chain."""
+    oc, ic, kh, kw = w.shape
+    cols, (n, oh, ow) = im2col(x, kh, kw, stride, padding, dilation)
+    wm = np.asarray(w, np.float32).reshape(oc, ic * kh * kw)
+    y = qmul_mat(wm, cols, group, levels, wmax, weight_groups)
+    return y.reshape(n, oh, ow, oc).transpose(0, 3, 1, 2).copy()
+
+
+def winograd2_weights(w) -> np.ndarray:
+    """U = G g G^T of every kernel in FP32, the reference's order (winograd.cc:681-729): -> (16, OC, IC)."""
+    g = np.asarray(w, np.float32)
+    half = np.float32(0.5)
+    t = []
+    for j in range(3):
+        g0, g1, g2 = g[:, :, 0, j], g[:, :, 1, j], g[:, :, 2, j]
+        t.append((g0, half * ((g0 + g1) + g2), half * ((g0 - g1) + g2), g2))
+    u = []
+    for i in range(4):
+        a, b, d = t[0][i], t[1][i], t[2][i]
+        u += [a, half * ((a + b) + d), half * ((a - b) + d), d]
+    return np.stack(u)
+
+
+def winograd2_inputs(x, padding):
+    """B^T d B of every tile in FP32, the reference's order (winograd.cc:440-500, 640-665): the rows of
+    the tile by row s of B^T first, then combined by row r; -> ((16, N * TH * TW, IC), (n, th, tw, oh, ow))."""
+    x = np.asarray(x, np.float32)
+    n, ic, h, wd = x.shape
+    p0, p1 = padding
+    oh, ow = h + 2 * p1 - 2, wd + 2 * p0 - 2
+    th, tw = (oh + 1) // 2, (ow + 1) // 2
+    xp = np.zeros((n, ic, 2 * th + 2, 2 * tw + 2), np.float32)
+    hh, ww = min(h, 2 * th + 2 - p1), min(wd, 2 * tw + 2 - p0)
+    xp[:, :, p1:p1 + hh, p0:p0 + ww] = x[:, :, :hh, :ww]
+    d = np.empty((n, ic, th, tw, 4, 4), np.float32)
+    for i in range(4):
+        for j in range(4):
+            d[..., i, j] = xp[:, :, i:i + 2 * th:2, j:j + 2 * tw:2]
+
+    def trow(i, s):
+        r = d[..., i, :]
+        return [r[..., 0] - r[..., 2], r[..., 1] + r[..., 2], r[..., 2] - r[..., 1], r[..., 1] - r[..., 3]][s]
+
+    v = []
+    for r in range(4):
+        for s in range(4):
+            rows = [trow(i, s) for i in range(4)]
+            e = [rows[0] - rows[2], rows[1] + rows[2], rows[2] - rows[1], rows[1] - rows[3]][r]
+            v.append(e.transpose(0, 2, 3, 1).reshape(n * th * tw, ic))
+    return np.stack(v), (n, th, tw, oh, ow)
+
+
+def winograd2_outputs(m, shape) -> np.ndarray:
+    """Y = A^T M A in FP32, the reference's order (winograd.cc:540-560): m (16, tiles, OC) -> (N, OC, OH, OW)."""
+    n, th, tw, oh, ow = shape
+    oc = m.shape[2]
+    mm = m.reshape(4, 4, n, th, tw, oc)
+    a0 = [(mm[0, j] + mm[1, j]) + mm[2, j] for j in range(4)]
+    a1 = [(mm[1, j] - mm[2, j]) - mm[3, j] for j in range(4)]
+    y = np.empty((n, th, 2, tw, 2, oc), np.float32)
+    y[:, :, 0, :, 0] = (a0[0] + a0[1]) + a0[2]
+    y[:, :, 0, :, 1] = (a0[1] - a0[2]) - a0[3]
+    y[:, :, 1, :, 0] = (a1[0] + a1[1]) + a1[2]
+    y[:, :, 1, :, 1] = (a1[1] - a1[2]) - a1[3]
+    y = y.reshape(n, 2 * th, 2 * tw, oc)[:, :oh, :ow]
+    return y.transpose(0, 3, 1, 2).copy()
+
+
+def qwinograd2(w, x, padding=(1, 1), group: int = 64, levels: int = 255, wmax: int = 127,
+               weight_groups: bool = True, span: int | None = None) -> np.ndarray:
+    """The reference's quantized F(2x2, 3x3) (winograd.cc:1826-2100): each xi's transformed kernels
+    quantized per output channel in groups of input channels (per-row scales over stretches of `span`
+    channels), each tile's transformed inputs likewise, folded, then A^T M A.  -> (N, OC, OH, OW)."""
+    u = winograd2_weights(w)
+    v, shape = winograd2_inputs(x, padding)
+    m = np.stack([qfold(quantize_inputs(v[i], group, levels),
+                        _quantize_weights_spans(u[i], group, wmax, weight_groups, span), group) for i in range(16)])
+    return winograd2_outputs(m, shape)

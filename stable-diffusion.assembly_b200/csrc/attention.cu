@@ -36,6 +36,7 @@
 #include "../../include/sdb.h"
 #include "chain.cuh"
 #include "ptx.cuh"
+#include "quant.cuh"
 #include "runtime.cuh"
 #include "split.cuh"
 
@@ -907,6 +908,8 @@ extern "C" int sdb_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb
     if (chain && (chain->count < 0 || chain->count > SDB_MAX_STEPS || chain->redirect))
         return fail(SDB_INVALID, "sdb_attention: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
+    // Integer products for self-attention over 256 keys or more (attention.cc:612-618, 858-862).
+    if (quantized_attention(k->ne[1])) return run_quantized_attention(q, k, v, dst, scale, chain, st);
     AttnArgs a{};
     a.out = static_cast<float*>(dst->data);
     for (int i = 0; i < 4; ++i) a.onb[i] = dst->nb[i] / 4;

@@ -544,6 +544,11 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     if (!sdb_conv2d_supported(w, x, dst, params)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: not supported");
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_conv2d: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
+    if (quantized_conv()) {
+        // Integer products (conv2d.cc:843-844, winograd.cc:2237-2244): the reference's own choice of form.
+        if (quantized_winograd(w, dst, params)) return run_quantized_winograd(w, x, dst, params, chain, st);
+        return run_quantized_conv(w, x, dst, params, chain, st);
+    }
     if (const int f = winograd_form(w, dst, params); f != 0) return run_winograd(f, w, x, dst, params, chain, st);
     const int64_t ic = x->ne[2], oc = w->ne[3];
     const int icp = static_cast<int>(round_up(ic, 64));

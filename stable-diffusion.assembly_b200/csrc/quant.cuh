@@ -88,6 +88,9 @@ struct QGemmArgs {
     int cpg;            // 32-byte chunks of k a group: group / 32
     int kchunks;        // groups * cpg
     int tiles_m, tiles_n, items;
+    int batch_tiles;    // batched products (Winograd's xi, attention's heads): row tiles of one batch, whose
+                        // weights are tiles_n tiles of their own; 0 for one product
+    int batch_rep;      // batches sharing one set of weights (heads sharing keys); 1 otherwise
     int magic;          // the sums convert exactly by the 1.5 * 2^23 trick (|sum| < 2^22)
     int store;          // kStoreTma: whole 32 x 16 boxes through the output map; else direct
     float* y;
@@ -276,12 +279,13 @@ qgemm_kernel(const __grid_constant__ CUtensorMap ymap, const QGemmArgs args) {
         produced[1] = g;
         const int item = blockIdx.x + (g / args.groups) * gridDim.x, gi = g % args.groups;
         const int tm = item % args.tiles_m, tn = item / args.tiles_m;
+        const int tw = args.batch_tiles ? tn + (tm / args.batch_tiles / args.batch_rep) * args.tiles_n : tn;
         const int slot = g % kQRing;
         if (!mbar_wait(&sempty[slot], ((g / kQRing) & 1) ^ 1, abort, args.err)) return false;
         float* sc = scales + slot * kQScaleFloats;
         mbar_arrive_expect_tx(&sfull[slot], kQScaleFloats * 4);
         bulk_load(sc, args.as + (static_cast<long long>(tm) * args.groups + gi) * 256, 1024, &sfull[slot]);
-        bulk_load(sc + 256, args.ws + (static_cast<long long>(tn) * args.groups + gi) * 256, 1024, &sfull[slot]);
+        bulk_load(sc + 256, args.ws + (static_cast<long long>(tw) * args.groups + gi) * 256, 1024, &sfull[slot]);
         const int base = (g / args.groups) * nstages;
         for (int ls = need(gi - 1); ls < need(gi); ++ls) {
             const int st_count = base + ls, s = st_count % kQStages;
@@ -289,7 +293,7 @@ qgemm_kernel(const __grid_constant__ CUtensorMap ymap, const QGemmArgs args) {
             uint8_t* st = smem + s * kQStageBytes;
             mbar_arrive_expect_tx(&full[s], kQStageBytes);
             bulk_load(st, args.a + (static_cast<long long>(tm) * nstages + ls) * kQABytes, kQABytes, &full[s]);
-            bulk_load(st + kQABytes, args.w + (static_cast<long long>(tn) * nstages + ls) * kQBBytes, kQBBytes,
+            bulk_load(st + kQABytes, args.w + (static_cast<long long>(tw) * nstages + ls) * kQBBytes, kQBBytes,
                       &full[s]);
         }
         return true;
@@ -512,5 +516,14 @@ qgemm_kernel(const __grid_constant__ CUtensorMap ymap, const QGemmArgs args) {
 bool quantized_linear(int64_t rows);
 int run_quantized_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
                          cudaStream_t st, bool gated);
+bool quantized_conv();
+int run_quantized_conv(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                       const sdb_chain* chain, cudaStream_t st);
+bool quantized_winograd(const sdb_tensor* w, const sdb_tensor* dst, const int32_t params[6]);
+bool quantized_attention(int64_t lk);
+int run_quantized_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, const sdb_tensor* dst,
+                            float scale, const sdb_chain* chain, cudaStream_t st);
+int run_quantized_winograd(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                           const sdb_chain* chain, cudaStream_t st);
 
 }  // namespace sdb

@@ -38,6 +38,9 @@ int64_t* knob(Tuning& t, const std::string& name) {
     if (name == "winograd_positions") return &t.winograd_positions;
     if (name == "winograd4_positions") return &t.winograd4_positions;
     if (name == "winograd_channels") return &t.winograd_channels;
+    if (name == "winograd_small_tiles") return &t.winograd_small_tiles;
+    if (name == "winograd_kc") return &t.winograd_kc;
+    if (name == "winograd_small_kc") return &t.winograd_small_kc;
     if (name == "store") return &t.store;
     if (name == "todo") return &t.todo;
     if (name == "todo_tokens") return &t.todo_tokens;

@@ -22,6 +22,9 @@ struct Tuning {
     int64_t winograd_positions = 1024;  // the least outputs of an image Winograd is used for
     int64_t winograd4_positions = 256;  // with winograd = 2, the least outputs of an image for F(4x4)
     int64_t winograd_channels = 16;     // the least input channels Winograd is used for
+    int64_t winograd_small_tiles = 256; // quantized: Winograd also for images of at most this many tiles in all
+    int64_t winograd_kc = 256;          // quantized, per-row weight scales: the input channels a scale spans
+    int64_t winograd_small_kc = 128;    //   and for images of few tiles
     int64_t store = 1;           // keep packed weights between calls
     int64_t todo = 1;            // ToDo K/V downsampling factor (1 = none)
     int64_t todo_tokens = 4096;  // least tokens of a grid downsampled
@@ -29,7 +32,7 @@ struct Tuning {
     int64_t input_bits = 8;      // the inputs' bits, 2..8, unsigned with a zero point
     int64_t group = 64;          // numbers of k sharing a scale: 32, 64, 128 or 256
     int64_t weight_group = 1;    // the weights' scale per group: 1; per whole row: 0
-    int64_t quantize = 7;        // with bits, what is quantized: 1 linear layers (2, 4: not taken here)
+    int64_t quantize = 7;        // with bits, what is quantized: 1 linear layers, 2 convolutions, 4 attention
     int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
     int64_t attention_wg = 1;    // 1: two-warpgroup attention where it fits; 0: the pair kernel
 };

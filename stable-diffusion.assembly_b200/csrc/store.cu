@@ -80,35 +80,26 @@ __global__ void pack_weights_kernel(const PackArgs p) {
 // -wmax, wmax); the group's scale s and offset s * sum(q).  One warp a row;
 // every operation rounds as the reference's scalar one does.  Written in the
 // quantized GEMM's tiles (store.cuh, Packed).
-struct QPackArgs {
-    const uint8_t* src;
-    int type;
-    long long nb0, nb1;   // source strides in bytes (k, row)
-    long long n;          // logical rows (gated: of one half)
-    long long k;
-    int gated;
-    long long rows;       // packed rows: tiles * 128
-    int group, groups, nstages, wmax, weight_groups;
-    int8_t* q;
-    float* scales;
-};
 
 template <int EPL>
 __global__ void quantize_weights_kernel(const QPackArgs a) {
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    const long long per_batch = a.rows / a.batches;
     for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < a.rows;
          r += warps) {
         const long long tile = r >> 7;
         const int p = static_cast<int>(r & 127);
+        const long long bi = r / per_batch, rr = r - bi * per_batch;
         long long src_row = -1;
         if (!a.gated) {
-            if (r < a.n) src_row = r;
+            if (rr < a.n) src_row = rr;
         } else {
-            const long long c = tile * 64 + (p & 63);
+            const long long c = (rr >> 7) * 64 + (p & 63);
             if (c < a.n) src_row = p < 64 ? c : a.n + c;
         }
-        const uint8_t* row = src_row >= 0 ? a.src + src_row * a.nb1 : nullptr;
+        const uint8_t* row =
+            src_row >= 0 ? a.src + (bi / a.bdiv) * a.bnb_hi + (bi % a.bdiv) * a.bnb_lo + src_row * a.nb1 : nullptr;
         auto load = [&](long long kk) -> float {
             if (row == nullptr || kk >= a.k) return 0.0f;
             const uint8_t* ptr = row + kk * a.nb0;
@@ -116,12 +107,16 @@ __global__ void quantize_weights_kernel(const QPackArgs a) {
                                           : *reinterpret_cast<const float*>(ptr);
         };
         float row_max = 0.0f;
-        if (!a.weight_groups) {
-            for (long long kk = lane; kk < a.k; kk += 32) row_max = fmaxf(row_max, fabsf(load(kk)));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, o));
-        }
         for (int g = 0; g < a.groups; ++g) {
+            if (!a.weight_groups && static_cast<long long>(g) * a.group % a.span == 0) {
+                // The largest magnitude of the span of k this group begins.
+                const long long k1 = min(a.k, static_cast<long long>(g) * a.group + a.span);
+                row_max = 0.0f;
+                for (long long kk = static_cast<long long>(g) * a.group + lane; kk < k1; kk += 32)
+                    row_max = fmaxf(row_max, fabsf(load(kk)));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, o));
+            }
             float w[EPL];
             float m = row_max;
             const long long k0 = static_cast<long long>(g) * a.group + lane * EPL;
@@ -148,11 +143,22 @@ __global__ void quantize_weights_kernel(const QPackArgs a) {
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            int8_t* dst = a.q + (tile * a.nstages + (k0 >> 6)) * 8192 + quant_tile_offset(p, static_cast<int>(k0 & 63));
-            if (EPL == 8) *reinterpret_cast<uint64_t*>(dst) = bytes;
-            else if (EPL == 4) *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(bytes);
-            else if (EPL == 2) *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
-            else *reinterpret_cast<uint8_t*>(dst) = static_cast<uint8_t>(bytes);
+            if (EPL == 1 || EPL == 2 || EPL == 4 || EPL == 8) {
+                int8_t* dst =
+                    a.q + (tile * a.nstages + (k0 >> 6)) * 8192 + quant_tile_offset(p, static_cast<int>(k0 & 63));
+                if (EPL == 8) *reinterpret_cast<uint64_t*>(dst) = bytes;
+                else if (EPL == 4) *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(bytes);
+                else if (EPL == 2) *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(bytes);
+                else *reinterpret_cast<uint8_t*>(dst) = static_cast<uint8_t>(bytes);
+            } else {
+                // Runs of 3 or 5 bytes may cross a 16-byte chunk: byte by byte.
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) {
+                    const long long kk = k0 + e;
+                    a.q[(tile * a.nstages + (kk >> 6)) * 8192 + quant_tile_offset(p, static_cast<int>(kk & 63))] =
+                        static_cast<int8_t>(static_cast<uint8_t>(bytes >> (8 * e)));
+                }
+            }
             if (lane == 0) {
                 float* sc = a.scales + (tile * a.groups + g) * 256;
                 sc[p] = s;
@@ -400,17 +406,102 @@ int quantized_weights(const sdb_tensor* w, bool gated, int64_t n_logical, int64_
     a.nstages = nstages;
     a.wmax = q.wmax;
     a.weight_groups = q.weight_groups ? 1 : 0;
+    a.span = p->kpad;
+    a.batches = 1;
+    a.bdiv = 1;
     a.q = static_cast<int8_t*>(p->data);
     a.scales = static_cast<float*>(p->qscales);
+    launch_quantize_weights(a, stream);
+    SDB_CUDA(cudaGetLastError());
+    SDB_CUDA(cudaEventRecord(p->ready, stream));
+    remember(key, p);
+    *out = p;
+    return SDB_OK;
+}
+
+void launch_quantize_weights(const QPackArgs& a, cudaStream_t stream) {
     const int blocks = static_cast<int>(std::min<long long>((a.rows + 7) / 8, 148LL * 8));
-    switch (q.group / 32) {
+    switch (a.group / 32) {
         case 1: quantize_weights_kernel<1><<<blocks, 256, 0, stream>>>(a); break;
         case 2: quantize_weights_kernel<2><<<blocks, 256, 0, stream>>>(a); break;
+        case 3: quantize_weights_kernel<3><<<blocks, 256, 0, stream>>>(a); break;
         case 4: quantize_weights_kernel<4><<<blocks, 256, 0, stream>>>(a); break;
+        case 5: quantize_weights_kernel<5><<<blocks, 256, 0, stream>>>(a); break;
         default: quantize_weights_kernel<8><<<blocks, 256, 0, stream>>>(a); break;
     }
     count_launch();
+}
+
+// F(2x2)'s transformed kernels quantized, xi by xi: U = G g G^T in FP32
+// (winograd2_weights_f32_kernel, into a buffer freed after), then each xi's
+// (oc, ic) matrix quantized like a linear layer's weights into tiles
+// [xi][tiles][nstages][8 KiB] and scales [xi][tiles][groups][2][128]
+// (winograd.cc:1907-1936).  span: with per-row scales, the input channels
+// one scale covers (the reference's stretch of channels).
+int quantized_winograd_weights(const sdb_tensor* w, const QuantSpec& q, int64_t span, cudaStream_t stream,
+                               std::shared_ptr<Packed>* out) {
+    if (q.group % 32 != 0 || q.group < 32 || q.group > 256)
+        return fail(SDB_NOT_SUPPORTED, "quantized products: group must be 32, 64, 128 or 256");
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    const int64_t ic = w->ne[2], oc = w->ne[3];
+    const Key key{dev, w->data, w->type, {w->ne[0], w->ne[1], w->ne[2], w->ne[3]},
+                  {w->nb[0], w->nb[1], w->nb[2], w->nb[3]}, static_cast<int>(Layout::quantized_winograd2), 0,
+                  q.weight_groups ? 0 : span, q.variant()};
+    bool found = false;
+    if (int s = lookup(key, stream, out, &found); s != SDB_OK || found) return s;
+
+    constexpr int xi = 16;
+    auto p = std::make_shared<Packed>();
+    p->group = q.group;
+    p->groups = static_cast<int>((ic + q.group - 1) / q.group);
+    p->kpad = static_cast<int64_t>(p->groups) * q.group;
+    const int nstages = (p->groups * (q.group / 32) + 1) / 2;
+    p->tiles = static_cast<int>((oc + 127) / 128);
+    p->rows_total = static_cast<int64_t>(p->tiles) * 128;
+    p->npad = p->rows_total;
+    const size_t q_xi = static_cast<size_t>(p->tiles) * nstages * 8192;
+    const size_t s_xi = static_cast<size_t>(p->tiles) * p->groups * 1024;
+    p->bytes = xi * (q_xi + s_xi);
+    SDB_CUDA(cudaMalloc(&p->data, xi * q_xi));
+    SDB_CUDA(cudaMalloc(&p->qscales, xi * s_xi));
+    SDB_CUDA(cudaMemsetAsync(p->data, 0, xi * q_xi, stream));
+    SDB_CUDA(cudaEventCreateWithFlags(&p->ready, cudaEventDisableTiming));
+    float* u = nullptr;
+    const size_t u_bytes = static_cast<size_t>(xi) * oc * ic * 4;
+    SDB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&u), u_bytes, stream));
+    const long long total = ic * oc;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    winograd2_weights_f32_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(w->data), w->type, w->nb[0],
+                                                             w->nb[1], w->nb[2], w->nb[3], static_cast<int>(ic),
+                                                             static_cast<int>(oc), u);
+    count_launch();
     SDB_CUDA(cudaGetLastError());
+    QPackArgs a{};
+    a.type = SDB_TYPE_F32;
+    a.nb0 = 4;
+    a.nb1 = 4 * ic;
+    a.n = oc;
+    a.k = ic;
+    a.gated = 0;
+    a.rows = p->rows_total;
+    a.group = q.group;
+    a.groups = p->groups;
+    a.nstages = nstages;
+    a.wmax = q.wmax;
+    a.weight_groups = q.weight_groups ? 1 : 0;
+    a.span = q.weight_groups ? p->kpad : span;
+    // The sixteen xi as batches of the one launch: batch x reads U's plane x.
+    a.src = reinterpret_cast<const uint8_t*>(u);
+    a.batches = xi;
+    a.bdiv = 1;
+    a.bnb_hi = static_cast<long long>(oc) * ic * 4;
+    a.rows = xi * p->rows_total;
+    a.q = static_cast<int8_t*>(p->data);
+    a.scales = static_cast<float*>(p->qscales);
+    launch_quantize_weights(a, stream);
+    SDB_CUDA(cudaGetLastError());
+    SDB_CUDA(cudaFreeAsync(u, stream));
     SDB_CUDA(cudaEventRecord(p->ready, stream));
     remember(key, p);
     *out = p;

@@ -23,6 +23,7 @@ enum class Layout : int {
     quantized_gated = 4,  // GEGLU, quantized: rows as `gated`
     winograd2 = 5,        // F(2x2, 3x3): U = G g G^T split, [plane][16 xi][ocp][kpad] (winograd.cuh)
     winograd4 = 6,        // F(4x4, 3x3): the same with 36 xi
+    quantized_winograd2 = 7,  // F(2x2, 3x3) quantized: 16 xi of quantized rows oc (k = ic), as `quantized`
 };
 
 // What a quantized packing depends on (the reference's quantized_variant,
@@ -95,6 +96,29 @@ int pack_transient(const sdb_tensor* w, int64_t n_logical, int64_t k_logical, vo
 // (the reference keeps them too, Layout::winograd, winograd.cc:2144-2160).
 // Packed rows: xi * ocp + oc of the hi plane, then b1_row + the same of the
 // lo plane; ocp = OC rounded up to 128, kpad = IC rounded up to 64.
+// The arguments of the weight quantizer (store.cu quantize_weights_kernel):
+// `batches` matrices of n logical rows each, packed tiles of 128 rows
+// (rows / batches of them a batch, one after another); matrix bi at
+// src + (bi / bdiv) * bnb_hi + (bi % bdiv) * bnb_lo.
+struct QPackArgs {
+    const uint8_t* src;
+    int type;
+    long long nb0, nb1;   // source strides in bytes (k, row)
+    long long n;          // logical rows of a batch (gated: of one half)
+    long long k;
+    int gated;
+    long long rows;       // packed rows in all: batches * tiles a batch * 128
+    int group, groups, nstages, wmax, weight_groups;
+    long long span;       // per-row scales (weight_groups 0): the numbers of k one scale covers, a multiple of group
+    int batches, bdiv;
+    long long bnb_hi, bnb_lo;
+    int8_t* q;
+    float* scales;
+};
+void launch_quantize_weights(const QPackArgs& a, cudaStream_t stream);
+
+int quantized_winograd_weights(const sdb_tensor* w, const QuantSpec& q, int64_t span, cudaStream_t stream,
+                               std::shared_ptr<Packed>* out);
 int winograd_weights(const sdb_tensor* w, int f, cudaStream_t stream, std::shared_ptr<Packed>* out);
 
 }  // namespace sdb

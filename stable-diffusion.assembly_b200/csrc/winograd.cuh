@@ -352,4 +352,98 @@ __global__ void __launch_bounds__(256) winograd_outputs_kernel(const WinoArgs a)
     }
 }
 
+// ---------------------------------------------------------------- quantized
+//
+// F(2x2, 3x3) with integer products (winograd.cc:1826-2100): the transforms in
+// single precision, each xi's product quantized -- the transformed kernels a
+// scale per output channel per group of input channels, the transformed inputs
+// a scale and zero point per tile per group of input channels.  The quantized
+// bytes depend on every bit of the transforms, so both follow the reference's
+// C++ order of operations exactly.
+
+// U = G g G^T in FP32 as transform_weights computes it (winograd.cc:681-729):
+// G g a column of g at a time, then (G g) G^T a row at a time, each sum of
+// three left to right and halved after.  Out: [16 xi][oc][ic], xi = 4 i + j
+// (i the row of the transformed kernel).
+static __global__ void winograd2_weights_f32_kernel(const uint8_t* __restrict__ src, int type, long long nb0, long long nb1,
+                                                    long long nb2, long long nb3, int ic, int oc, float* __restrict__ out) {
+    const long long total = static_cast<long long>(oc) * ic;
+    const long long plane = total;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long o = idx / ic;
+        const long long c = idx - o * ic;
+        float g[3][3];  // g[row][column]
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+                const uint8_t* ptr = src + q * nb0 + r * nb1 + c * nb2 + o * nb3;
+                g[r][q] = type == SDB_TYPE_F16 ? __half2float(*reinterpret_cast<const __half*>(ptr))
+                                               : *reinterpret_cast<const float*>(ptr);
+            }
+        float t[4][3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const float g0 = g[0][j], g1 = g[1][j], g2 = g[2][j];
+            t[0][j] = g0;
+            t[1][j] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(g0, g1), g2));
+            t[2][j] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(g0, g1), g2));
+            t[3][j] = g2;
+        }
+        float* dst = out + o * ic + c;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = t[i][0], b = t[i][1], d = t[i][2];
+            dst[(i * 4 + 0) * plane] = a;
+            dst[(i * 4 + 1) * plane] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(a, b), d));
+            dst[(i * 4 + 2) * plane] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(a, b), d));
+            dst[(i * 4 + 3) * plane] = d;
+        }
+    }
+}
+
+// The transformed input of row xi * tiles_pad + t (tile t), input channel kk,
+// for the input quantizer: B^T d B as the reference packs it
+// (winograd.cc:440-500, 640-665): each of the tile's rows transformed by row s
+// of B^T first, then those rows combined by row r, xi = 4 r + s.  Tiles past
+// the last are zeros.
+struct Wino2QuantLoader {
+    const float* x;
+    long long xnb[4];
+    int iw, ih, p0, p1, tw, th;
+    long long tiles, tiles_pad;
+    __device__ __forceinline__ float operator()(long long row, long long kk) const {
+        const int xi = static_cast<int>(row / tiles_pad);
+        const long long t = row - xi * tiles_pad;
+        if (t >= tiles) return 0.0f;
+        const int r = xi >> 2, s = xi & 3;
+        const int tx = static_cast<int>(t % tw);
+        const long long rest = t / tw;
+        const int ty = static_cast<int>(rest % th);
+        const long long img = rest / th;
+        const int y0 = 2 * ty - p1, x0 = 2 * tx - p0;
+        const float* plane = x + img * xnb[3] + kk * xnb[2];
+        auto at = [&](int i, int j) -> float {
+            const int y = y0 + i, xx = x0 + j;
+            return (y >= 0 && y < ih && xx >= 0 && xx < iw) ? __ldg(plane + y * xnb[1] + xx * xnb[0]) : 0.0f;
+        };
+        // Row i of the tile transformed by row s of B^T (bt(), winograd.cc:321-333): the two inputs it takes.
+        auto trow = [&](int i) -> float {
+            switch (s) {
+                case 0: return __fsub_rn(at(i, 0), at(i, 2));
+                case 1: return __fadd_rn(at(i, 1), at(i, 2));
+                case 2: return __fsub_rn(at(i, 2), at(i, 1));
+                default: return __fsub_rn(at(i, 1), at(i, 3));
+            }
+        };
+        switch (r) {
+            case 0: return __fsub_rn(trow(0), trow(2));
+            case 1: return __fadd_rn(trow(1), trow(2));
+            case 2: return __fsub_rn(trow(2), trow(1));
+            default: return __fsub_rn(trow(1), trow(3));
+        }
+    }
+};
+
 }  // namespace sdb
