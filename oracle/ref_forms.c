@@ -432,3 +432,10 @@ void rf_qmul_mat(const float *w, int N, int K, const float *x, int M, float *y, 
     free(sx);
     free(ox);
 }
+
+/* The C library's single-precision exp, element by element: the reference's
+ * std::exp(float) for the keys past its vector kernel's last eight
+ * (attention.cc:287-301). */
+void rf_expf(const float *x, float *y, long n) {
+    for (long i = 0; i < n; ++i) y[i] = expf(x[i]);
+}

@@ -58,6 +58,7 @@ def load() -> ctypes.CDLL:
         lib.rf_quantize_weights.argtypes = [P, i, i, i, i, i, P, P, P]
         lib.rf_quantize_inputs.argtypes = [P, i, i, i, i, P, P, P]
         lib.rf_qfold.argtypes = [P, P, P, i, P, P, P, i, i, i, P, i]
+        lib.rf_expf.argtypes = [P, P, ctypes.c_long]
         lib.rf_threads.restype = i
         lib.rf_set_threads.argtypes = [i]
         _lib = lib
@@ -293,3 +294,52 @@ def qwinograd2(w, x, padding=(1, 1), group: int = 64, levels: int = 255, wmax: i
     m = np.stack([qfold(quantize_inputs(v[i], group, levels),
                         _quantize_weights_spans(u[i], group, wmax, weight_groups, span), group) for i in range(16)])
     return winograd2_outputs(m, shape)
+
+
+def expf(x: np.ndarray) -> np.ndarray:
+    """The C library's expf of every element (float32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    load().rf_expf(_p(x), _p(y), x.size)
+    return y
+
+
+def qattention(q, k, v, heads: int, kv_heads: int, scale: float, group: int = 64, levels: int = 255,
+               wmax: int = 127) -> np.ndarray:
+    """The reference's attention with integer products (attention.cc:596-844).
+
+    q (B, LQ, H*D), k (B, LK, HK*D), v (B, LK, HK*DV) -> (B, LQ, H*DV) float32.  Per head: the queries
+    quantized (unsigned, zero point) and the keys (signed), each over its D numbers as one group of
+    4 ceil(D/4), the queries' scales and offsets times the softmax's scale (FP32); the scores their fold;
+    each query's exponentials of its scores less their greatest -- the reference's exponential for the
+    keys before the last LK % 8, the C library's expf for those -- summed in double; the exponentials
+    quantized per group of keys, the values per dimension per group of keys; their fold times
+    float(1 / sum).  Head h reads key head h / (H / HK).
+    """
+    import oracle
+
+    f32 = np.float32
+    b, lq, hd = q.shape
+    lk = k.shape[1]
+    d = hd // heads
+    dv = v.shape[2] // kv_heads
+    gd = 4 * (-(-d // 4))
+    tail0 = lk - lk % 8
+    out = np.empty((b, lq, heads * dv), f32)
+    for bi in range(b):
+        for h in range(heads):
+            hk = h // (heads // kv_heads)
+            qm = np.ascontiguousarray(q[bi, :, h * d:(h + 1) * d], dtype=f32)
+            km = np.ascontiguousarray(k[bi, :, hk * d:(hk + 1) * d], dtype=f32)
+            vm = np.ascontiguousarray(v[bi, :, hk * dv:(hk + 1) * dv], dtype=f32)
+            qx, sx, ox = quantize_inputs(qm, gd, levels)
+            sx, ox = (sx * f32(scale)).astype(f32), (ox * f32(scale)).astype(f32)
+            s = qfold((qx, sx, ox), quantize_weights(km, gd, wmax, True), gd)
+            x = (s - s.max(axis=1, keepdims=True)).astype(f32)
+            e = np.empty_like(x)
+            e[:, :tail0] = oracle.exponential(x[:, :tail0])
+            e[:, tail0:] = expf(x[:, tail0:])
+            rec = (1.0 / e.astype(np.float64).sum(axis=1)).astype(f32)
+            o = qfold(quantize_inputs(e, group, levels), quantize_weights(vm.T, group, wmax, True), group)
+            out[bi, :, h * dv:(h + 1) * dv] = (o * rec[:, None]).astype(f32)
+    return out

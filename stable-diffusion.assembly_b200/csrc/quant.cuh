@@ -327,7 +327,9 @@ qgemm_kernel(const __grid_constant__ CUtensorMap ymap, const QGemmArgs args) {
                 // group alone in an item's last stage twice.
                 mma_commit(&empty[s]);
                 if ((c & 1) == 0 && c == args.kchunks - 1) mma_commit(&empty[s]);
-            } else if ((c & 1) == 1) {
+            } else if ((c & 1) == 1 || c == args.kchunks - 1) {
+                // A stage is released after its second chunk, or after its only
+                // one (an item of an odd number of chunks: groups of 96 or 160).
                 mma_commit(&empty[s]);
             }
         }
