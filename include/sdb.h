@@ -147,6 +147,13 @@ int sdb_concat(const sdb_tensor *a, const sdb_tensor *b, const sdb_tensor *dst, 
 /* GGML_OP_UPSCALE, nearest, by integer factors of W and H; channels-last images
  * [W, H, C, N] with C % 4 == 0. */
 int sdb_upscale_nearest(const sdb_tensor *src, const sdb_tensor *dst, void *stream);
+/* ToDo's coarser grid of an image's tokens (stable-diffusion.cpp patch 0004,
+ * sdasm_coarser_tokens: a VIEW of every factor-th token of every factor-th row,
+ * made contiguous): src [C, W, H, N] with contiguous channels -> dst
+ * [C, ceil(W / factor), ceil(H / factor), N] dense, dst[c, i, j, n] =
+ * src[c, factor i, factor j, n].  The keys' and values' projections of a
+ * self-attention take these tokens when sdb_token_downsampling() > 1. */
+int sdb_coarser_tokens(const sdb_tensor *src, const sdb_tensor *dst, int32_t factor, void *stream);
 /* GGML_OP_TIMESTEP_EMBEDDING: timesteps [N] FP32 -> dst [>= dim, N]:
  * cos(t f_j) for j < dim/2, then sin(t f_j), f_j = max_period^(-j / (dim/2)). */
 int sdb_timestep_embedding(const sdb_tensor *timesteps, const sdb_tensor *dst, int32_t dim, int32_t max_period,

@@ -62,6 +62,28 @@ __global__ void concat_rows_kernel(const float* a, const float* b, float* d, lon
 
 // Channels-last nearest upscale by integer factors: dst position (x, y) of
 // image n takes source position (x / fx, y / fy); c floats a position.
+// ToDo's coarser grid of tokens (the reference's stable-diffusion.cpp patch
+// 0004, sdasm_coarser_tokens): dst[c, i, j, n] = src[c, f i, f j, n], the
+// token nearest each point of the coarser grid; VEC consecutive channels a
+// thread (cv of them a token), strides in floats.
+template <int VEC>
+__global__ void coarser_tokens_kernel(const float* __restrict__ src, float* __restrict__ dst, long long snb1,
+                                      long long snb2, long long snb3, int cv, int w2, int h2, int f,
+                                      long long total) {
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(idx % cv);
+        long long rest = idx / cv;
+        const int i = static_cast<int>(rest % w2);
+        rest /= w2;
+        const int j = static_cast<int>(rest % h2);
+        const long long n = rest / h2;
+        const float* s = src + n * snb3 + static_cast<long long>(j) * f * snb2 + static_cast<long long>(i) * f * snb1;
+        if (VEC == 4) reinterpret_cast<float4*>(dst)[idx] = __ldg(reinterpret_cast<const float4*>(s + 4 * c));
+        else dst[idx] = __ldg(s + c);
+    }
+}
+
 __global__ void upscale_cl_kernel(const float* s, float* d, int c4, int dw, int dh, int fx, int fy, long long total4) {
     const int sw = dw / fx, sh = dh / fy;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total4;
@@ -236,6 +258,35 @@ int sdb_concat(const sdb_tensor* a, const sdb_tensor* b, const sdb_tensor* dst, 
     concat_rows_kernel<<<grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const float*>(a->data), static_cast<const float*>(b->data), static_cast<float*>(dst->data), rows,
         static_cast<int>(ua), static_cast<int>(ub), vec);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+int sdb_coarser_tokens(const sdb_tensor* src, const sdb_tensor* dst, int32_t factor, void* stream) {
+    if (!f32t(src) || !f32t(dst) || factor < 1) return fail(SDB_NOT_SUPPORTED, "sdb_coarser_tokens: FP32 tensors");
+    const int64_t c = src->ne[0], w = src->ne[1], h = src->ne[2], n = src->ne[3];
+    const int64_t w2 = (w + factor - 1) / factor, h2 = (h + factor - 1) / factor;
+    if (dst->ne[0] != c || dst->ne[1] != w2 || dst->ne[2] != h2 || dst->ne[3] != n)
+        return fail(SDB_INVALID, "sdb_coarser_tokens: dst must be [C, ceil(W / f), ceil(H / f), N]");
+    const int order[4] = {0, 1, 2, 3};
+    if (src->nb[0] != 4 || !dense(dst, order)) return fail(SDB_NOT_SUPPORTED, "sdb_coarser_tokens: contiguous channels");
+    for (int d = 1; d < 4; ++d)
+        if (src->nb[d] % 4 != 0) return fail(SDB_NOT_SUPPORTED, "sdb_coarser_tokens: strides of whole floats");
+    const bool vec = c % 4 == 0 && src->nb[1] % 16 == 0 && src->nb[2] % 16 == 0 && src->nb[3] % 16 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(src->data) | reinterpret_cast<uintptr_t>(dst->data)) & 15) == 0;
+    const int cv = static_cast<int>(vec ? c / 4 : c);
+    const long long total = static_cast<long long>(cv) * w2 * h2 * n;
+    const auto st = static_cast<cudaStream_t>(stream);
+    const long long e = 4;
+    if (vec)
+        coarser_tokens_kernel<4><<<grid_for(total), 256, 0, st>>>(
+            static_cast<const float*>(src->data), static_cast<float*>(dst->data), src->nb[1] / e, src->nb[2] / e,
+            src->nb[3] / e, cv, static_cast<int>(w2), static_cast<int>(h2), factor, total);
+    else
+        coarser_tokens_kernel<1><<<grid_for(total), 256, 0, st>>>(
+            static_cast<const float*>(src->data), static_cast<float*>(dst->data), src->nb[1] / e, src->nb[2] / e,
+            src->nb[3] / e, cv, static_cast<int>(w2), static_cast<int>(h2), factor, total);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;

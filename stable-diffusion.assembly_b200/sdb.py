@@ -40,6 +40,7 @@ EXPORTS = [
     "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
     "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step", "sdb_soft_max",
+    "sdb_coarser_tokens",
 ]
 
 
@@ -104,6 +105,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_launch_count": (ctypes.c_uint64, []),
         "sdb_concat": (i, [T, T, T, ctypes.c_int32, vp]),
         "sdb_upscale_nearest": (i, [T, T, vp]),
+        "sdb_coarser_tokens": (i, [T, T, ctypes.c_int32, vp]),
         "sdb_timestep_embedding": (i, [T, T, ctypes.c_int32, ctypes.c_int32, vp]),
         "sdb_euler_cfg_step": (i, [vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                    ctypes.c_float, vp]),
@@ -509,6 +511,25 @@ def upscale_nearest_nhwc(x, factor: int = 2, out=None, stream=None):
     if out is None:
         out = torch.empty(n, h * factor, w * factor, c, dtype=torch.float32, device=x.device)
     _check(lib.sdb_upscale_nearest(describe_nhwc(x), describe_nhwc(out), ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def coarser_tokens(x, width: int, height: int, factor: int, out=None, stream=None):
+    """ToDo's keys' and values' tokens: x (N, height * width, C) tokens of a grid, row after row ->
+    (N, ceil(height / f) * ceil(width / f), C), every f-th token of every f-th row."""
+    import torch
+
+    lib = load()
+    n, l, c = x.shape
+    if l != width * height:
+        raise SdbError(INVALID, "coarser_tokens: the tokens are not the grid's")
+    w2, h2 = -(-width // factor), -(-height // factor)
+    if out is None:
+        out = torch.empty(n, h2 * w2, c, dtype=torch.float32, device=x.device)
+    s = [v * 4 for v in x.stride()]
+    src = describe(x, [c, width, height, n], [s[2], s[1], s[1] * width, s[0]])
+    dst = describe(out, [c, w2, h2, n], [4, 4 * c, 4 * c * w2, 4 * c * w2 * h2])
+    _check(lib.sdb_coarser_tokens(src, dst, factor, ctypes.c_void_p(_stream_ptr(stream))))
     return out
 
 

@@ -132,6 +132,8 @@ class TBlock:
     wff2: object
     bff2: object
     kv_offset: int = 0        # columns of this block's K/V in the fused context projection
+    wq: object = None         # wqkv's query rows, and its key and value rows (ToDo projects them apart):
+    wkv: object = None        #   views made once, so that the weight store keeps one packing of each
 
 
 @dataclass
@@ -189,6 +191,8 @@ class UNet:
                              init.bias(ch), (init.gamma(ch), init.beta(ch)), init.linear(ch, ch), init.linear(ch, ch),
                              init.bias(ch), (init.gamma(ch), init.beta(ch)), init.linear(8 * ch, ch),
                              init.bias(8 * ch), init.linear(ch, 4 * ch), init.bias(ch)) for _ in range(depth)]
+            for blk in blocks:
+                blk.wq, blk.wkv = blk.wqkv[:ch], blk.wqkv[ch:]
             tr = Transformer(ch, c.heads_of(ch), gn, proj_in, b_in, blocks, init.linear(ch, ch), init.bias(ch))
             transformers.append(tr)
             return tr
@@ -282,11 +286,19 @@ class UNet:
         scale = 1.0 / math.sqrt(c // heads)
         n = self._gn(x, tr.gn, 1e-6, False)
         t = sdb.mul_mat(tr.proj_in, n.view(b, hh * ww, c), chain=sdb.Chain().add(tr.b_in))
+        # ToDo (the reference's stable-diffusion.cpp patch 0004): self-attention's keys and values from
+        # every f-th token of every f-th row when the tuning asks for it on a grid this large.
+        f = sdb.token_downsampling(ww, hh)
         for blk in tr.blocks:
             # Self-attention.
             h1 = self._ln(t, blk.ln1)
-            qkv = sdb.mul_mat(blk.wqkv, h1)
-            a = sdb.attention_heads(qkv[:, :, :c], qkv[:, :, c:2 * c], qkv[:, :, 2 * c:], heads, heads, scale)
+            if f > 1:
+                q = sdb.mul_mat(blk.wq, h1)
+                kv = sdb.mul_mat(blk.wkv, sdb.coarser_tokens(h1, ww, hh, f))
+                a = sdb.attention_heads(q, kv[:, :, :c], kv[:, :, c:], heads, heads, scale)
+            else:
+                qkv = sdb.mul_mat(blk.wqkv, h1)
+                a = sdb.attention_heads(qkv[:, :, :c], qkv[:, :, c:2 * c], qkv[:, :, 2 * c:], heads, heads, scale)
             sdb.mul_mat(blk.wo1, a, out=t, chain=sdb.Chain().add(blk.bo1).redirect(t, True))
             # Cross-attention on the text context.
             h2 = self._ln(t, blk.ln2)

@@ -153,3 +153,45 @@ def test_sd15_unet_graph_replay(cuda):
     assert torch.isfinite(eager).all()
     assert torch.equal(eager, replay)
     assert eager.abs().max().item() < 1e4
+
+
+@pytest.mark.parametrize("factor", [2, 3])
+def test_unet_tiny_todo_matches_float64(cuda, factor):
+    """ToDo (todo=2 or 3): self-attention's keys and values from every f-th token of every f-th row
+    of the transformers' 8 x 8 grids (todo_tokens lowered to 64); against the float64 restatement with
+    the same rule."""
+    import sdb
+    import torch
+    import unet as U
+    import unet_reference as R
+
+    net = U.UNet(U.UNetConfig(**TINY), device=cuda, seed=5)
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn(2, 16, 16, 4, device=cuda, generator=g)
+    t = torch.tensor([981.0, 981.0], device=cuda)
+    ctx = torch.randn(2, 8, 32, device=cuda, generator=g)
+    sdb.set_tuning(f"todo={factor},todo_tokens=64")
+    try:
+        assert sdb.token_downsampling(8, 8) == factor and sdb.token_downsampling(7, 9) == 1
+        got = net.forward(x, t, ctx).double()
+        torch.cuda.synchronize()
+    finally:
+        sdb.set_tuning("todo=1,todo_tokens=4096")
+    want = R.forward(net, x, t, ctx, todo=(factor, 64))
+    plain = R.forward(net, x, t, ctx)
+    err = (got - want).abs().max().item() / want.abs().max().item()
+    assert np.isfinite(err) and err <= 1e-5, f"{err:.3g} of the largest output"
+    # And it is not the full attention.
+    assert (plain - want).abs().max().item() > 1e3 * (got - want).abs().max().item()
+
+
+def test_coarser_tokens(cuda):
+    """sdb_coarser_tokens against slicing, a grid of odd size (ceil), channels of no multiple of 4."""
+    import sdb
+    import torch
+
+    for c in (8, 6):
+        x = torch.randn(2, 7 * 5, c, device=cuda)
+        y = sdb.coarser_tokens(x, 5, 7, 2)
+        want = x.view(2, 7, 5, c)[:, ::2, ::2, :].reshape(2, -1, c)
+        assert torch.equal(y, want)

@@ -42,15 +42,21 @@ def attention(q, k, v, heads):
     return (p @ v).transpose(1, 2).reshape(b, lq, c)
 
 
-def transformer(x, tr, context, groups):
+def transformer(x, tr, context, groups, todo=(1, 4096)):
+    """todo (factor, least tokens): ToDo's keys and values from every factor-th token of every
+    factor-th row of grids of at least that many tokens (stable-diffusion.cpp patch 0004)."""
     b, c, h, w = x.shape
     heads = tr.heads
+    f = todo[0] if todo[0] >= 2 and h * w >= todo[1] else 1
     n = gn(x, tr.gn, groups, 1e-6, False)
     t = n.permute(0, 2, 3, 1).reshape(b, h * w, c) @ _w(tr.proj_in).T + _w(tr.b_in)
     for blk in tr.blocks:
         h1 = F.layer_norm(t, (c,), _w(blk.ln1[0]), _w(blk.ln1[1]), 1e-5)
-        qkv = h1 @ _w(blk.wqkv).T
-        t = t + attention(qkv[..., :c], qkv[..., c:2 * c], qkv[..., 2 * c:], heads) @ _w(blk.wo1).T + _w(blk.bo1)
+        wqkv = _w(blk.wqkv).T
+        src = h1.view(b, h, w, c)[:, ::f, ::f, :].reshape(b, -1, c) if f > 1 else h1
+        kv = src @ wqkv[:, c:]
+        a = attention(h1 @ wqkv[:, :c], kv[..., :c], kv[..., c:], heads)
+        t = t + a @ _w(blk.wo1).T + _w(blk.bo1)
         h2 = F.layer_norm(t, (c,), _w(blk.ln2[0]), _w(blk.ln2[1]), 1e-5)
         kv = context @ _w(blk.kv_w).T
         t = t + attention(h2 @ _w(blk.wq2).T, kv[..., :c], kv[..., c:], heads) @ _w(blk.wo2).T + _w(blk.bo2)
@@ -69,8 +75,9 @@ def timestep_embedding(t, dim, max_period=10000):
     return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
 
 
-def forward(unet, x_nhwc, timesteps, context, y=None):
-    """eps (B, H, W, C_out) in float64 for the runner's weights and inputs (y: the label embedding's input)."""
+def forward(unet, x_nhwc, timesteps, context, y=None, todo=(1, 4096)):
+    """eps (B, H, W, C_out) in float64 for the runner's weights and inputs (y: the label embedding's input;
+    todo: ToDo's factor and least tokens, as the tuning's todo and todo_tokens)."""
     cfg = unet.cfg
     groups = cfg.groups
     # The fused K/V weights, split back per block.
@@ -92,21 +99,21 @@ def forward(unet, x_nhwc, timesteps, context, y=None):
         for rb, tr in level.blocks:
             h = resblock(h, rb, emb, groups)
             if tr is not None:
-                h = transformer(h, tr, ctx, groups)
+                h = transformer(h, tr, ctx, groups, todo)
             hs.append(h)
         if level.down is not None:
             h = F.conv2d(h, _w(level.down[0]), _w(level.down[1]), stride=2, padding=1)
             hs.append(h)
     rb1, tr, rb2 = unet.mid
     h = resblock(h, rb1, emb, groups)
-    h = transformer(h, tr, ctx, groups)
+    h = transformer(h, tr, ctx, groups, todo)
     h = resblock(h, rb2, emb, groups)
     for level in unet.up:
         for rb, tr in level.blocks:
             h = torch.cat([h, hs.pop()], dim=1)
             h = resblock(h, rb, emb, groups)
             if tr is not None:
-                h = transformer(h, tr, ctx, groups)
+                h = transformer(h, tr, ctx, groups, todo)
         if level.up is not None:
             h = F.interpolate(h, scale_factor=2, mode="nearest")
             h = F.conv2d(h, _w(level.up[0]), _w(level.up[1]), padding=1)
