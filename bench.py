@@ -703,12 +703,12 @@ class OpClock:
         return {k: {"work": v[0], "ms": v[1], "calls": v[2]} for k, v in classes.items()}
 
 
-def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5) -> tuple[float, int]:
-    """ms of one SD 1.5 VAE decode (64 x 64 latent to 512 x 512), a CUDA-graph replay timed with
-    CUDA events on its stream (max over ranks), and its algorithmic FLOPs."""
+def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5, config=None) -> tuple[float, int]:
+    """ms of one VAE decode (SD 1.5's by default: 64 x 64 latent to 512 x 512), a CUDA-graph replay timed
+    with CUDA events on its stream (max over ranks), and its algorithmic FLOPs."""
     import vae as V
 
-    dec = V.VAEDecoder(device=dev)
+    dec = V.VAEDecoder(config or V.SD15_VAE, device=dev)
     z = latent.clone()
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
@@ -740,8 +740,9 @@ def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5) -> t
 def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
     """One SDXL sampler step at 832 x 1216 (latent 152 x 104): the UNet forward on the
     classifier-free-guidance batch of 2 (context 2 x 77 x 2048, pooled text + size/crop conditioning
-    2 x 2816, 2.57B random-init FP16 weights) and the guidance (scale 6) + Euler update, captured once and
-    replayed; ms a step as the max over ranks."""
+    2 x 2816, 2.57B random-init FP16 weights) and the guidance (scale 6) + ancestral Euler update (each
+    step's fresh noise drawn before the timing), captured once and replayed; ms a step as the max over
+    ranks.  Then the SDXL VAE decode of the latent to 832 x 1216."""
     import sdb
     import unet as U
 
@@ -768,19 +769,21 @@ def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
         forward()
     torch.cuda.synchronize()
 
-    def step():
+    noise = torch.randn(reps + 1, 152, 104, 4, device=dev, generator=g)
+
+    def step(k):
         graph.replay()
-        sdb.euler_cfg_step(out["eps"], x, x_in, 6.0, 1.0, 0.9, 0.7, stream=s)
+        sdb.euler_ancestral_cfg_step(out["eps"], x, x_in, noise[k], 6.0, 1.0, 0.9, 0.7, stream=s)
 
     with torch.cuda.stream(s):
-        step()
+        step(reps)
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(s):
         start.record(s)
-        for _ in range(reps):
-            step()
+        for k in range(reps):
+            step(k)
         end.record(s)
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / reps)
@@ -788,9 +791,16 @@ def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
     res = {"ms_per_step": ms, "step_tflop": flops / 1e12, "tflops": flops / (ms * 1e-3) / 1e12,
            "resolution": "832x1216 (latent 152x104)", "batch": "2 (CFG 6)", "params": net.params,
            "context": "2x77x2048 + pooled/size conditioning 2x2816",
-           "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step "
-                     "(the ancestral sampler's noise term not included)"}
+           "timing": "CUDA-graph replay of the UNet forward + the guidance/ancestral-Euler kernel per step"}
     del graph, net
+    torch.cuda.empty_cache()
+    import vae as V
+
+    vae_ms, vae_flops = measure_vae(torch, dev, x.clone(), barrier, max_over_ranks, reps=3, config=V.SDXL_VAE)
+    res.update({"vae_ms": vae_ms, "vae_tflops": vae_flops / (vae_ms * 1e-3) / 1e12,
+                "imgs_per_s": 1000.0 / (20 * ms + vae_ms),
+                "vae": "SDXL decoder (SD's first-stage decoder, latents scaled by 0.13025), 152x104 latent to "
+                       "1216x832, random-init FP16 weights; imgs_per_s counts 20 steps and one decode"})
     torch.cuda.empty_cache()
     return res
 

@@ -169,6 +169,14 @@ int sdb_soft_max(const sdb_tensor *x, const sdb_tensor *dst, float scale, void *
  * next model input x_in[i] = x_in[n + i] = x[i] * c_in_next. */
 int sdb_euler_cfg_step(const float *eps, float *x, float *x_in, int64_t n, float cfg, float sigma, float sigma_next,
                        float c_in_next, void *stream);
+/* The ancestral Euler step (k-diffusion's sample_euler_ancestral, eta 1, the
+ * sampler stable-diffusion.cpp runs as euler_a): with the guidance e as above,
+ * sigma_up = min(sigma_next, sqrt(sigma_next^2 (sigma^2 - sigma_next^2) / sigma^2)),
+ * sigma_down = sqrt(sigma_next^2 - sigma_up^2), x[i] += (sigma_down - sigma) e
+ * + sigma_up noise[i] (no noise at sigma_next = 0); x_in as above.  noise [n]
+ * is the step's fresh N(0, 1) draw. */
+int sdb_euler_ancestral_cfg_step(const float *eps, float *x, float *x_in, const float *noise, int64_t n, float cfg,
+                                 float sigma, float sigma_next, float c_in_next, void *stream);
 
 /* ---- the weight store (store.h:58-120, store.cc:202-266) ----------------
  * Weights are repacked once into the layout the kernels read and kept on the

@@ -112,13 +112,15 @@ __global__ void timestep_kernel(const float* t, float* d, int dim, int n, float 
     }
 }
 
+// noise (may be null): the ancestral sampler's fresh noise, added times s_up.
 __global__ void euler_cfg_kernel(const float* eps, float* x, float* x_in, long long n, float cfg, float dt,
-                                 float c_in) {
+                                 float c_in, const float* noise, float s_up) {
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const float u = eps[i], c = eps[n + i];
         const float e = u + cfg * (c - u);
-        const float xn = x[i] + dt * e;
+        float xn = x[i] + dt * e;
+        if (noise) xn += s_up * noise[i];
         x[i] = xn;
         if (x_in) {
             x_in[i] = xn * c_in;
@@ -331,7 +333,25 @@ int sdb_euler_cfg_step(const float* eps, float* x, float* x_in, int64_t n, float
                        float c_in_next, void* stream) {
     if (!eps || !x || n <= 0) return fail(SDB_INVALID, "sdb_euler_cfg_step: null buffers");
     euler_cfg_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(eps, x, x_in, n, cfg,
-                                                                                  sigma_next - sigma, c_in_next);
+                                                                                  sigma_next - sigma, c_in_next,
+                                                                                  nullptr, 0.0f);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+int sdb_euler_ancestral_cfg_step(const float* eps, float* x, float* x_in, const float* noise, int64_t n, float cfg,
+                                 float sigma, float sigma_next, float c_in_next, void* stream) {
+    if (!eps || !x || !noise || n <= 0) return fail(SDB_INVALID, "sdb_euler_ancestral_cfg_step: null buffers");
+    if (!(sigma > 0.0f) || sigma_next < 0.0f || sigma_next > sigma)
+        return fail(SDB_INVALID, "sdb_euler_ancestral_cfg_step: 0 <= sigma_next <= sigma, sigma > 0");
+    // get_ancestral_step with eta 1 (k-diffusion, as stable-diffusion.cpp's euler_a samples).
+    const double s = sigma, sn = sigma_next;
+    const double up = std::min(sn, std::sqrt(sn * sn * (s * s - sn * sn) / (s * s)));
+    const double down = std::sqrt(sn * sn - up * up);
+    euler_cfg_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        eps, x, x_in, n, cfg, static_cast<float>(down - s), c_in_next, sn > 0.0 ? noise : nullptr,
+        static_cast<float>(up));
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;

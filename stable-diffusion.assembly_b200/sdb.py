@@ -40,7 +40,7 @@ EXPORTS = [
     "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
     "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step", "sdb_soft_max",
-    "sdb_coarser_tokens",
+    "sdb_coarser_tokens", "sdb_euler_ancestral_cfg_step",
 ]
 
 
@@ -109,6 +109,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_timestep_embedding": (i, [T, T, ctypes.c_int32, ctypes.c_int32, vp]),
         "sdb_euler_cfg_step": (i, [vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                    ctypes.c_float, vp]),
+        "sdb_euler_ancestral_cfg_step": (i, [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float,
+                                             ctypes.c_float, ctypes.c_float, vp]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(lib, name)
@@ -543,6 +545,17 @@ def timestep_embedding(t, dim: int, max_period: int = 10000, out=None, stream=No
     _check(lib.sdb_timestep_embedding(describe(t), describe(out), dim, max_period,
                                       ctypes.c_void_p(_stream_ptr(stream))))
     return out
+
+
+def euler_ancestral_cfg_step(eps, x, x_in, noise, cfg: float, sigma: float, sigma_next: float, c_in_next: float,
+                             stream=None):
+    """The ancestral Euler step with guidance: x += (sigma_down - sigma) e + sigma_up noise (see sdb.h)."""
+    lib = load()
+    _check(lib.sdb_euler_ancestral_cfg_step(ctypes.c_void_p(eps.data_ptr()), ctypes.c_void_p(x.data_ptr()),
+                                            ctypes.c_void_p(x_in.data_ptr() if x_in is not None else 0),
+                                            ctypes.c_void_p(noise.data_ptr()), ctypes.c_int64(x.numel()),
+                                            ctypes.c_float(cfg), ctypes.c_float(sigma), ctypes.c_float(sigma_next),
+                                            ctypes.c_float(c_in_next), ctypes.c_void_p(_stream_ptr(stream))))
 
 
 def euler_cfg_step(eps, x, x_in, cfg: float, sigma: float, sigma_next: float, c_in_next: float, stream=None):

@@ -46,6 +46,8 @@ class VAEConfig:
 
 
 SD15_VAE = VAEConfig()
+# SDXL's first-stage decoder: the same network, its latents scaled by 0.13025.
+SDXL_VAE = VAEConfig(scale_factor=0.13025)
 
 
 @dataclass

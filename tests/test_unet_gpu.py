@@ -61,6 +61,31 @@ def test_euler_cfg_step(cuda):
     torch.testing.assert_close(x_in[1], want * 0.25, rtol=1e-6, atol=1e-5)
 
 
+@pytest.mark.parametrize("sigma,sigma_next", [(14.6, 11.2), (0.9, 0.0)])
+def test_euler_ancestral_cfg_step(cuda, sigma, sigma_next):
+    """The ancestral step (k-diffusion's sample_euler_ancestral, eta 1) against its formula in double:
+    sigma_up, sigma_down, the deterministic part to sigma_down and the fresh noise times sigma_up (none
+    at the last step)."""
+    import sdb
+    import torch
+
+    g = torch.Generator(device=cuda).manual_seed(4)
+    n = 4 * 152 * 104
+    eps = torch.randn(2, n, device=cuda, generator=g)
+    x = torch.randn(n, device=cuda, generator=g)
+    noise = torch.randn(n, device=cuda, generator=g)
+    x_in = torch.empty(2, n, device=cuda)
+    x0 = x.clone()
+    sdb.euler_ancestral_cfg_step(eps, x, x_in, noise, 6.0, sigma, sigma_next, 0.5)
+    up = min(sigma_next, math.sqrt(sigma_next ** 2 * (sigma ** 2 - sigma_next ** 2) / sigma ** 2))
+    down = math.sqrt(sigma_next ** 2 - up ** 2)
+    e = eps[0].double() + 6.0 * (eps[1].double() - eps[0].double())
+    want = x0.double() + (down - sigma) * e + up * noise.double()
+    assert (x.double() - want).abs().max().item() <= 1e-5 * max(1.0, want.abs().max().item())
+    torch.testing.assert_close(x_in[0], x * 0.5, rtol=0, atol=0)
+    torch.testing.assert_close(x_in[1], x * 0.5, rtol=0, atol=0)
+
+
 TINY = dict(model_channels=32, channel_mult=(1, 2), num_res_blocks=1, attention_levels=(1,), heads=2,
             context_dim=32, groups=8)
 

@@ -152,3 +152,35 @@ def test_sd15_vae_decode_graph(cuda):
     assert bool(torch.isfinite(eager).all())
     assert torch.equal(out, eager)
     assert sdb.device_status(clear=False) == 0
+
+
+def test_sdxl_vae_attention_full_size(cuda):
+    """The SDXL decoder's attention block at 832 x 1216 (152 x 104 positions, one 512-dim head) against
+    float64."""
+    import torch
+    import vae as vae_mod
+    import vae_reference
+
+    dec = vae_mod.VAEDecoder(vae_mod.SDXL_VAE, device=cuda)
+    at = dec.mid[1]
+    g = torch.Generator(device=cuda).manual_seed(9)
+    x = torch.randn(1, 152, 104, 512, device=cuda, generator=g)
+    want = vae_reference.attention(x.double().permute(0, 3, 1, 2), at, 32, 1e-6).permute(0, 2, 3, 1)
+    got = dec._attention(x.clone(), at)
+    err = (got.double() - want).abs().max().item()
+    assert err <= 1e-5 * want.abs().max().item(), err
+
+
+def test_sdxl_vae_decode_full_size(cuda):
+    """SDXL's decode, 152 x 104 latent to a 1216 x 832 image: finite, the latent's 1/0.13025 applied."""
+    import torch
+    import vae as vae_mod
+
+    dec = vae_mod.VAEDecoder(vae_mod.SDXL_VAE, device=cuda)
+    assert abs(dec.inv_scale.item() - 1 / 0.13025) <= 1e-6 / 0.13025
+    g = torch.Generator(device=cuda).manual_seed(10)
+    z = torch.randn(1, 152, 104, 4, device=cuda, generator=g)
+    img = dec.decode(z)
+    torch.cuda.synchronize()
+    assert tuple(img.shape) == (1, 1216, 832, 3)
+    assert bool(torch.isfinite(img).all())
