@@ -80,6 +80,44 @@ __device__ __forceinline__ void store_quant_bytes(uint8_t* q, long long tm, int 
 // post multiplies each group's scale and offset after they are made (the
 // scale of attention's softmax, folded into the queries' as the reference
 // folds it, attention.cc:748-757); 1 elsewhere, which changes nothing.
+// One warp's group of a row: v[EPL] a lane (numbers at k0 + e >= k are past
+// the row's end), quantized and stored with the group's scale and offset.
+template <int EPL>
+__device__ __forceinline__ void quantize_group(const float (&v)[EPL], long long k0, long long k, int levels, float post,
+                                               long long row, int g, int groups, int nstages, uint8_t* q,
+                                               float* scales, int lane) {
+    float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        lo = fminf(lo, v[e]);
+        hi = fmaxf(hi, v[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    const float top = static_cast<float>(levels);
+    const float s = __fdiv_rn(__fsub_rn(hi, lo), top);
+    const float inverse = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+    const float zero = rintf(__fmul_rn(-lo, inverse));
+    uint64_t bytes = 0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const float qv = k0 + e < k ? fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(v[e], inverse)), zero), 0.0f), top)
+                                    : zero;
+        bytes |= static_cast<uint64_t>(static_cast<uint8_t>(qv)) << (8 * e);
+    }
+    const long long tm = row >> 7;
+    const int r = static_cast<int>(row & 127);
+    store_quant_bytes<EPL>(q, tm, nstages, r, k0, bytes);
+    if (lane == 0) {
+        float* sc = scales + (tm * groups + g) * 256;
+        sc[r] = __fmul_rn(s, post);
+        sc[128 + r] = __fmul_rn(__fmul_rn(s, zero), post);
+    }
+}
+
 template <int EPL, class Loader>
 __global__ void quantize_inputs_kernel(Loader load, long long m, long long k, int group, int groups,
                                        int nstages, int levels, float post, uint8_t* __restrict__ q,
@@ -93,37 +131,9 @@ __global__ void quantize_inputs_kernel(Loader load, long long m, long long k, in
         const int g = static_cast<int>(w - row * groups);
         const long long k0 = static_cast<long long>(g) * group + lane * EPL;
         float v[EPL];
-        float lo = 0.0f, hi = 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-            v[e] = k0 + e < k ? load(row, k0 + e) : 0.0f;
-            lo = fminf(lo, v[e]);
-            hi = fmaxf(hi, v[e]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-            hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-        }
-        const float top = static_cast<float>(levels);
-        const float s = __fdiv_rn(__fsub_rn(hi, lo), top);
-        const float inverse = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
-        const float zero = rintf(__fmul_rn(-lo, inverse));
-        uint64_t bytes = 0;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-            const float qv = k0 + e < k ? fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(v[e], inverse)), zero), 0.0f), top)
-                                        : zero;
-            bytes |= static_cast<uint64_t>(static_cast<uint8_t>(qv)) << (8 * e);
-        }
-        const long long tm = row >> 7;
-        const int r = static_cast<int>(row & 127);
-        store_quant_bytes<EPL>(q, tm, nstages, r, k0, bytes);
-        if (lane == 0) {
-            float* sc = scales + (tm * groups + g) * 256;
-            sc[r] = __fmul_rn(s, post);
-            sc[128 + r] = __fmul_rn(__fmul_rn(s, zero), post);
-        }
+        for (int e = 0; e < EPL; ++e) v[e] = k0 + e < k ? load(row, k0 + e) : 0.0f;
+        quantize_group<EPL>(v, k0, k, levels, post, row, g, groups, nstages, q, scales, lane);
     }
 }
 
@@ -148,6 +158,67 @@ void launch_quantize(const Loader& load, long long m, long long k, int group, in
     count_launch();
 }
 
+// F(2x2)'s transformed inputs quantized: one warp a (tile, group of input
+// channels), EPL channels a lane.  Each channel's 4 x 4 inputs are read once
+// and all sixteen B^T d B made from them as the reference packs them
+// (winograd.cc:440-500, 640-665): the tile's rows by row s of B^T (bt(),
+// winograd.cc:321-333) first, then combined by row r, xi = 4 r + s; then each
+// xi's group quantized as row xi * tiles_pad + tile.  Tiles past the last are
+// zeros.
+template <int EPL>
+__global__ void wino2_quantize_kernel(const Wino2QuantLoader a, int ic, int group, int groups, int nstages, int levels,
+                                      uint8_t* __restrict__ q, float* __restrict__ scales) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    const long long total = a.tiles_pad * groups;
+    for (long long w = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+         w += warps) {
+        const long long t = w / groups;
+        const int g = static_cast<int>(w - t * groups);
+        const long long k0 = static_cast<long long>(g) * group + lane * EPL;
+        float v[16][EPL];
+        const bool live = t < a.tiles;
+        const int tx = live ? static_cast<int>(t % a.tw) : 0;
+        const long long rest = live ? t / a.tw : 0;
+        const int ty = static_cast<int>(rest % a.th);
+        const long long img = rest / a.th;
+        const int y0 = 2 * ty - a.p1, x0 = 2 * tx - a.p0;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            const long long c = k0 + e;
+            float d[4][4];
+            const float* plane = a.x + img * a.xnb[3] + c * a.xnb[2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int y = y0 + i, xx = x0 + j;
+                    d[i][j] = (live && c < ic && y >= 0 && y < a.ih && xx >= 0 && xx < a.iw)
+                                  ? __ldg(plane + y * a.xnb[1] + xx * a.xnb[0])
+                                  : 0.0f;
+                }
+            float tr[4][4];  // tr[i][s]: row i by row s of B^T
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                tr[i][0] = __fsub_rn(d[i][0], d[i][2]);
+                tr[i][1] = __fadd_rn(d[i][1], d[i][2]);
+                tr[i][2] = __fsub_rn(d[i][2], d[i][1]);
+                tr[i][3] = __fsub_rn(d[i][1], d[i][3]);
+            }
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+                v[0 * 4 + s4][e] = __fsub_rn(tr[0][s4], tr[2][s4]);
+                v[1 * 4 + s4][e] = __fadd_rn(tr[1][s4], tr[2][s4]);
+                v[2 * 4 + s4][e] = __fsub_rn(tr[2][s4], tr[1][s4]);
+                v[3 * 4 + s4][e] = __fsub_rn(tr[1][s4], tr[3][s4]);
+            }
+        }
+#pragma unroll
+        for (int x = 0; x < 16; ++x)
+            quantize_group<EPL>(v[x], k0, ic, levels, 1.0f, x * a.tiles_pad + t, g, groups, nstages, q, scales, lane);
+    }
+}
+
 // Attention's queries (b, h, query), each head's rows padded to lq_pad (a
 // multiple of 128): row (b H + h) lq_pad + i, number kk of the head's d.
 struct QueryLoader {
@@ -164,45 +235,55 @@ struct QueryLoader {
     }
 };
 
-// A query's exponentials of its scores less its greatest (attention.cc:287-301):
-// the keys before `tail0` by the reference's exponential (its vector kernel's,
-// eight keys at a time), those after by the C library's exp.
-struct ExpLoader {
-    const float* s;     // scores [rows][lds]
-    long long lds;
-    const float* top;   // each row's greatest score
-    int tail0;
-    __device__ __forceinline__ float operator()(long long row, long long kk) const {
-        const float x = __fsub_rn(__ldg(s + row * lds + kk), __ldg(top + row));
-        return kk >= tail0 ? expf(x) : exponential(x);
-    }
-};
-
-// Each row's greatest score over its lk keys, and the reciprocal of the sum
-// of its exponentials, summed in double and rounded once
-// (attention.cc:767-790, 838-841).  One warp a row.
-__global__ void softmax_stats_kernel(const float* __restrict__ s, long long rows, long long lds, int lk, int tail0,
-                                     float* __restrict__ top, float* __restrict__ rec) {
+// A query's exponentials of its scores less its greatest (attention.cc:287-301,
+// 767-800): the keys before `tail0` by the reference's exponential (its
+// vector kernel's, eight keys at a time), those after by the C library's exp;
+// summed in double, the reciprocal of the sum rounded once (838-841); and
+// quantized, unsigned, in groups of keys.  One warp a row: the row's greatest
+// score first, then each group's exponentials made once, summed and
+// quantized.
+template <int EPL>
+__global__ void softmax_quantize_kernel(const float* __restrict__ s, long long rows, long long lds, int lk, int tail0,
+                                        int group, int groups, int nstages, int levels, uint8_t* __restrict__ q,
+                                        float* __restrict__ scales, float* __restrict__ rec) {
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
     for (long long row = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
          row += warps) {
         const float* sr = s + row * lds;
         float mx = -INFINITY;
-        for (int j = lane; j < lk; j += 32) mx = fmaxf(mx, __ldg(sr + j));
+        if ((lds & 3) == 0) {
+            const int l4 = lk >> 2;
+            for (int j = lane; j < l4; j += 32) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(sr) + j);
+                mx = fmaxf(fmaxf(mx, t.x), fmaxf(t.y, fmaxf(t.z, t.w)));
+            }
+            for (int j = 4 * l4 + lane; j < lk; j += 32) mx = fmaxf(mx, __ldg(sr + j));
+        } else {
+            for (int j = lane; j < lk; j += 32) mx = fmaxf(mx, __ldg(sr + j));
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         double sum = 0.0;
-        for (int j = lane; j < lk; j += 32) {
-            const float x = __fsub_rn(__ldg(sr + j), mx);
-            sum += static_cast<double>(j >= tail0 ? expf(x) : exponential(x));
+        for (int g = 0; g < groups; ++g) {
+            const long long k0 = static_cast<long long>(g) * group + lane * EPL;
+            float v[EPL];
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                const long long j = k0 + e;
+                if (j < lk) {
+                    const float x = __fsub_rn(__ldg(sr + j), mx);
+                    v[e] = j >= tail0 ? expf(x) : exponential(x);
+                    sum += static_cast<double>(v[e]);
+                } else {
+                    v[e] = 0.0f;
+                }
+            }
+            quantize_group<EPL>(v, k0, lk, levels, 1.0f, row, g, groups, nstages, q, scales, lane);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-            top[row] = mx;
-            rec[row] = static_cast<float>(1.0 / sum);
-        }
+        if (lane == 0) rec[row] = static_cast<float>(1.0 / sum);
     }
 }
 
@@ -437,7 +518,7 @@ bool quantized_winograd(const sdb_tensor* w, const sdb_tensor* dst, const int32_
 
 // F(2x2, 3x3) quantized (winograd.cc:1826-2100): the transformed kernels
 // quantized by the store; the transformed inputs of every tile made and
-// quantized in one pass (Wino2QuantLoader), rows xi * tiles_pad + tile; the
+// quantized in one pass (wino2_quantize_kernel), rows xi * tiles_pad + tile; the
 // sixteen products as one batched qgemm into M [16][tiles_pad][ldm]; then
 // Y = A^T M A and the chain (winograd_outputs_kernel).  The reference folds a
 // stretch of input channels at a time into its FP32 products, each a whole
@@ -502,7 +583,20 @@ int run_quantized_winograd(const sdb_tensor* w, const sdb_tensor* x, const sdb_t
     load.th = wa.th;
     load.tiles = wa.tiles;
     load.tiles_pad = wa.tiles_pad;
-    launch_quantize(load, m, ic, spec.group, groups, nstages, levels, qa, sa, st);
+    {
+        const long long warps = wa.tiles_pad * groups;
+        const int blocks = static_cast<int>(std::min<long long>((warps + 7) / 8, 148LL * 16));
+#define SDB_WINO_Q(E) wino2_quantize_kernel<E><<<blocks, 256, 0, st>>>(load, static_cast<int>(ic), spec.group, groups, \
+                                                                       nstages, levels, qa, sa)
+        switch (spec.group / 32) {
+            case 1: SDB_WINO_Q(1); break;
+            case 2: SDB_WINO_Q(2); break;
+            case 4: SDB_WINO_Q(4); break;
+            default: SDB_WINO_Q(8); break;
+        }
+#undef SDB_WINO_Q
+        count_launch();
+    }
     SDB_CUDA(cudaGetLastError());
 
     QGemmArgs a{};
@@ -566,9 +660,9 @@ bool quantized_attention(int64_t lk) {
 //     into their scales and offsets;
 //   * the scores, a fold of one group, into S [rows][lds] FP32 -- rows
 //     (image, head, query), each head's queries padded to a multiple of 128;
-//   * each query's greatest score and the reciprocal of its exponentials'
-//     sum (softmax_stats_kernel); the exponentials quantized unsigned in
-//     groups of keys (ExpLoader); the values signed, a scale each dimension
+//   * each query's greatest score, its exponentials quantized unsigned in
+//     groups of keys and the reciprocal of their sum (softmax_quantize_kernel,
+//     one pass over the exponentials); the values signed, a scale each dimension
 //     per group of keys; their fold into O [rows][ldo];
 //   * out = O * reciprocal, and the chain (attention_finish_kernel).
 // A group covering d dimensions is laid out as round_up(d, 32) bytes: the
@@ -598,12 +692,12 @@ int run_quantized_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb_
     auto part = [](int64_t bytes) { return static_cast<size_t>((bytes + 255) / 256 * 256); };
     const size_t b_qq = part(tiles_m * st_d * kQABytes), b_qs = part(tiles_m * 1024);
     const size_t b_kq = part(b * hk * lk_tiles * st_d * kQBBytes), b_ks = part(b * hk * lk_tiles * 1024);
-    const size_t b_s = part(rows * lds * 4), b_top = part(rows * 4), b_rec = part(rows * 4);
+    const size_t b_s = part(rows * lds * 4), b_rec = part(rows * 4);
     const size_t b_pq = part(tiles_m * st_k * kQABytes), b_ps = part(tiles_m * kgroups * 1024);
     const size_t b_vq = part(b * hk * dv_tiles * st_k * kQBBytes), b_vs = part(b * hk * dv_tiles * kgroups * 1024);
     const size_t b_o = part(rows * ldo * 4);
     void* ws = nullptr;
-    if (int s = workspace(st, b_qq + b_qs + b_kq + b_ks + b_s + b_top + b_rec + b_pq + b_ps + b_vq + b_vs + b_o, &ws);
+    if (int s = workspace(st, b_qq + b_qs + b_kq + b_ks + b_s + b_rec + b_pq + b_ps + b_vq + b_vs + b_o, &ws);
         s != SDB_OK)
         return s;
     uint8_t* at = static_cast<uint8_t*>(ws);
@@ -613,7 +707,6 @@ int run_quantized_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb_
     int8_t* kq = reinterpret_cast<int8_t*>(take(b_kq));
     float* ks = reinterpret_cast<float*>(take(b_ks));
     float* sbuf = reinterpret_cast<float*>(take(b_s));
-    float* top = reinterpret_cast<float*>(take(b_top));
     float* rec = reinterpret_cast<float*>(take(b_rec));
     uint8_t* pq = take(b_pq);
     float* ps = reinterpret_cast<float*>(take(b_ps));
@@ -687,17 +780,22 @@ int run_quantized_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb_
     a.store = store_map(&smap, sbuf, lk, rows, lds, 16) ? kStoreTma : kStoreDirect;
     if (int s = launch_qgemm<false>(smap, a, st); s != SDB_OK) return s;
 
-    // The softmax's statistics and the quantized exponentials.  The
-    // reference's vector kernel takes the keys of each stretch eight at a
-    // time and the C library's exp the rest: with stretches of a multiple of
-    // eight keys, the last lk % 8 keys.
+    // The softmax and its quantized exponentials.  The reference's vector
+    // kernel takes the keys of each stretch eight at a time and the C
+    // library's exp the rest: with stretches of a multiple of eight keys, the
+    // last lk % 8 keys.
     const int tail0 = static_cast<int>(lk - lk % 8);
     const int sblocks = static_cast<int>(std::min<long long>((rows + 7) / 8, 148LL * 16));
-    softmax_stats_kernel<<<sblocks, 256, 0, st>>>(sbuf, rows, lds, static_cast<int>(lk), tail0, top, rec);
+#define SDB_SOFTMAX_Q(E) softmax_quantize_kernel<E><<<sblocks, 256, 0, st>>>(sbuf, rows, lds, static_cast<int>(lk), \
+        tail0, gk, static_cast<int>(kgroups), st_k, levels, pq, ps, rec)
+    switch (gk / 32) {
+        case 1: SDB_SOFTMAX_Q(1); break;
+        case 2: SDB_SOFTMAX_Q(2); break;
+        case 4: SDB_SOFTMAX_Q(4); break;
+        default: SDB_SOFTMAX_Q(8); break;
+    }
+#undef SDB_SOFTMAX_Q
     count_launch();
-    SDB_CUDA(cudaGetLastError());
-    launch_quantize(ExpLoader{sbuf, lds, top, tail0}, rows, lk, gk, static_cast<int>(kgroups), st_k, levels, pq, ps,
-                    st);
     SDB_CUDA(cudaGetLastError());
 
     // Values: (image, key head) matrices of dv rows (dimensions) of lk keys.

@@ -403,47 +403,14 @@ static __global__ void winograd2_weights_f32_kernel(const uint8_t* __restrict__ 
     }
 }
 
-// The transformed input of row xi * tiles_pad + t (tile t), input channel kk,
-// for the input quantizer: B^T d B as the reference packs it
-// (winograd.cc:440-500, 640-665): each of the tile's rows transformed by row s
-// of B^T first, then those rows combined by row r, xi = 4 r + s.  Tiles past
-// the last are zeros.
+// Where the quantized F(2x2) finds its inputs (quant.cu wino2_quantize_kernel):
+// the image, its element strides, padding and tiles; the transformed inputs
+// of tile t are rows xi * tiles_pad + t, tiles past the last zeros.
 struct Wino2QuantLoader {
     const float* x;
     long long xnb[4];
     int iw, ih, p0, p1, tw, th;
     long long tiles, tiles_pad;
-    __device__ __forceinline__ float operator()(long long row, long long kk) const {
-        const int xi = static_cast<int>(row / tiles_pad);
-        const long long t = row - xi * tiles_pad;
-        if (t >= tiles) return 0.0f;
-        const int r = xi >> 2, s = xi & 3;
-        const int tx = static_cast<int>(t % tw);
-        const long long rest = t / tw;
-        const int ty = static_cast<int>(rest % th);
-        const long long img = rest / th;
-        const int y0 = 2 * ty - p1, x0 = 2 * tx - p0;
-        const float* plane = x + img * xnb[3] + kk * xnb[2];
-        auto at = [&](int i, int j) -> float {
-            const int y = y0 + i, xx = x0 + j;
-            return (y >= 0 && y < ih && xx >= 0 && xx < iw) ? __ldg(plane + y * xnb[1] + xx * xnb[0]) : 0.0f;
-        };
-        // Row i of the tile transformed by row s of B^T (bt(), winograd.cc:321-333): the two inputs it takes.
-        auto trow = [&](int i) -> float {
-            switch (s) {
-                case 0: return __fsub_rn(at(i, 0), at(i, 2));
-                case 1: return __fadd_rn(at(i, 1), at(i, 2));
-                case 2: return __fsub_rn(at(i, 2), at(i, 1));
-                default: return __fsub_rn(at(i, 1), at(i, 3));
-            }
-        };
-        switch (r) {
-            case 0: return __fsub_rn(trow(0), trow(2));
-            case 1: return __fadd_rn(trow(1), trow(2));
-            case 2: return __fsub_rn(trow(2), trow(1));
-            default: return __fsub_rn(trow(1), trow(3));
-        }
-    }
 };
 
 }  // namespace sdb
