@@ -45,10 +45,12 @@ HOT_WORKLOAD = "sd15_hot_ops"
 HOT_METRIC = "SD1.5 UNet hot-path op set (BASELINE configs 1-3) steps/s"
 HOT_UNIT = "steps/s"
 UNET_WORKLOAD = "sd15_unet_step"
-UNET_METRIC = ("UNet ms/step (SD1.5 512x512, CFG batch 2, Euler): whole-job UNet steps/s; "
-               "ms_per_step is the UNet ms/step")
-UNET_UNIT = "UNet steps/s"
+UNET_METRIC = ("UNet ms/step + VAE ms (SD1.5 512x512, CFG 7, Euler; the 8-image batch over the GPUs): whole-job "
+               "image-steps/s (an image-step: one image's UNet step on its CFG batch of 2); ms_per_step is the "
+               "job's UNet step")
+UNET_UNIT = "image-steps/s"
 SAMPLER_STEPS = 20
+IMAGES = 8        # batches of 8 images, sharded by image over 1/2/4/8 GPUs
 
 
 # ---------------------------------------------------------------- peaks
@@ -469,7 +471,8 @@ def run_reference(args) -> None:
     metric, unit, workload = (UNET_METRIC, UNET_UNIT, UNET_WORKLOAD) if unet else (HOT_METRIC, HOT_UNIT, HOT_WORKLOAD)
     line = {"metric": metric, "value": best["value"], "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 / best["value"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "scaling": "strong" if unet else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
             "config": {"workload": workload, "sample": best["sample"]},
             "cpu_baseline": {k: best[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": best["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -704,8 +707,9 @@ class OpClock:
 
 
 def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5, config=None) -> tuple[float, int]:
-    """ms of one VAE decode (SD 1.5's by default: 64 x 64 latent to 512 x 512), a CUDA-graph replay timed
-    with CUDA events on its stream (max over ranks), and its algorithmic FLOPs."""
+    """ms of one VAE decode of the latents (N, h, w, 4) (SD 1.5's decoder by default: 64 x 64 latents to
+    512 x 512), a CUDA-graph replay timed with CUDA events on its stream (max over ranks), and its
+    algorithmic FLOPs."""
     import vae as V
 
     dec = V.VAEDecoder(config or V.SD15_VAE, device=dev)
@@ -732,7 +736,7 @@ def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5, conf
         end.record(s)
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / reps)
-    flops = dec.flops(1, z.shape[1], z.shape[2])
+    flops = dec.flops(z.shape[0], z.shape[1], z.shape[2])
     del graph, dec
     return ms, flops
 
@@ -867,10 +871,12 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     import unet as U
 
     net = U.UNet(U.SD15, device=dev, seed=20261011)
-    sampler = U.Sampler(net, 64, 64, steps=SAMPLER_STEPS)
+    # This rank's images of the 8-image batch (one a rank past 8 GPUs).
+    per = max(1, IMAGES // world)
+    sampler = U.Sampler(net, 64, 64, steps=SAMPLER_STEPS, images=per)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    latent = torch.randn(1, 64, 64, 4, device=dev, generator=g)
-    context = torch.randn(2, 77, 768, device=dev, generator=g)
+    latent = torch.randn(per, 64, 64, 4, device=dev, generator=g)
+    context = torch.randn(2 * per, 77, 768, device=dev, generator=g)
     sampler.x.copy_(latent * sampler.sigmas[0])
     sampler.context.copy_(context)
     sampler.set_step(0)
@@ -884,7 +890,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
 
     def step(i: int) -> None:
         j = i % SAMPLER_STEPS
-        sampler.t.copy_(ts[j:j + 1].expand(2))
+        sampler.t.copy_(ts[j:j + 1].expand(2 * per))
         eps = sampler.step_forward()
         sdb.euler_cfg_step(eps, sampler.x, sampler.x_in, sampler.cfg_scale, sampler.sigmas[j],
                            sampler.sigmas[j + 1], c_in[(j + 1) % SAMPLER_STEPS])
@@ -925,7 +931,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     # the updated latent back to the host.
     h_lat = latent.cpu().pin_memory()
     h_ctx = context.cpu().pin_memory()
-    h_out = torch.empty(1, 64, 64, 4).pin_memory()
+    h_out = torch.empty(per, 64, 64, 4).pin_memory()
     e2e_steps = max(3, min(args.steps, 20))
 
     def e2e_step(i: int) -> None:
@@ -944,11 +950,37 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_steps)
     h2d = h_lat.numel() * 4 + h_ctx.numel() * 4
     d2h = h_out.numel() * 4
-    # The VAE decode of the step's latent (one image a GPU), captured once and replayed.
+    # The VAE decode of this rank's latents, captured once and replayed.
     vae_ms, vae_flops = measure_vae(torch, dev, sampler.x, barrier, max_over_ranks)
+    del sampler
+    torch.cuda.empty_cache()
+    # One image's latency: the same step on a CFG batch of 2 alone.
+    ms1 = ms
+    if per > 1:
+        one = U.Sampler(net, 64, 64, steps=SAMPLER_STEPS, images=1)
+        one.x.copy_(latent[:1] * one.sigmas[0])
+        one.context.copy_(context[:2])
+        one.set_step(0)
+        one.capture(warmup=3)
+        with torch.cuda.stream(torch.cuda.current_stream()):
+            for _ in range(3):
+                one.step_forward()
+        barrier()
+        torch.cuda.synchronize()
+        s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s1.record()
+        for i in range(10):
+            one.t.copy_(ts[i:i + 1].expand(2))
+            eps1 = one.step_forward()
+            sdb.euler_cfg_step(eps1, one.x, one.x_in, one.cfg_scale, one.sigmas[i], one.sigmas[i + 1],
+                               c_in[i + 1])
+        e1.record()
+        torch.cuda.synchronize()
+        ms1 = max_over_ranks(s1.elapsed_time(e1) / 10)
+        del one
+        torch.cuda.empty_cache()
     sdxl = None if args.no_sdxl else measure_sdxl(torch, dev, barrier, max_over_ranks)
     status = sdb.device_status(clear=True)
-    del sampler
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -956,7 +988,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
         return
 
     peaks = measured_peaks()
-    step_flops = net.flops(2, 64, 64)
+    step_flops = net.flops(2 * per, 64, 64)
     dom = max((k for k in classes if CLASSES[k] == "tensor"), key=lambda k: classes[k]["ms"])
     d = classes[dom]
     achieved = d["work"] / (d["ms"] * 1e-3) / 1e12
@@ -965,24 +997,28 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     if tfile.exists():
         traffic = json.loads(tfile.read_text()).get(dom)
     line = {
-        "metric": UNET_METRIC, "value": world * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "metric": UNET_METRIC, "value": world * per * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if world * per == IMAGES else "weak",
         "vs_baseline": None, "dtype": "f32" if not args.tune else f"f32 ({args.tune})", "data": "synthetic",
-        "config": {"workload": UNET_WORKLOAD, "resolution": "512x512 (latent 64x64)", "batch": "2 (CFG)",
+        "config": {"workload": UNET_WORKLOAD, "resolution": "512x512 (latent 64x64)",
+                   "images": f"{IMAGES}-image batch, {per} a GPU",
+                   "batch": f"{2 * per} a GPU ({per} image(s) x CFG 2)",
                    "tuning": args.tune or "default (FP32-accurate products)",
                    "context": "2x77x768", "sampler": f"Euler, {SAMPLER_STEPS} steps, CFG 7",
                    "weights": f"random-init FP16, {net.params / 1e6:.1f}M parameters, packed once",
-                   "parallelism": f"replicas x{world} (one image a GPU)",
+                   "parallelism": f"images over {world} GPU(s): {per} a GPU, no data-path collective",
                    "l2": "weights (1.7 GB) and activations exceed L2 every step",
                    "timing": "CUDA-graph replay of the UNet forward + the guidance/Euler kernel per step",
-                   "vae": "SD 1.5 decoder, the step's 64x64 latent to 512x512, random-init FP16 weights "
-                          "(49.5M parameters); vae_ms is one decode, a CUDA-graph replay; imgs_per_s counts "
-                          f"{SAMPLER_STEPS} UNet steps and one decode an image"},
+                   "vae": "SD 1.5 decoder, a GPU's 64x64 latents to 512x512 images, random-init FP16 weights "
+                          "(49.5M parameters); vae_ms is one decode of them, a CUDA-graph replay; imgs_per_s "
+                          f"counts {SAMPLER_STEPS} UNet steps and the decode"},
         "unet_ms_per_step": ms,
+        "unet_ms_per_step_one_image": ms1,
         "vae_ms": vae_ms,
         "vae_tflops": vae_flops / (vae_ms * 1e-3) / 1e12,
-        "imgs_per_s": world * 1e3 / (SAMPLER_STEPS * ms + vae_ms),
-        "imgs_per_s_unet_only": world * 1e3 / ms / SAMPLER_STEPS,
+        "imgs_per_s": world * per * 1e3 / (SAMPLER_STEPS * ms + vae_ms),
+        "imgs_per_s_unet_only": world * per * 1e3 / ms / SAMPLER_STEPS,
         "sdxl": sdxl,
         "step_tflop": step_flops / 1e12,
         "step_frac_of_sustained_peak": step_flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
@@ -995,7 +1031,8 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
         "classes_tflops": {k: round(v["work"] / (v["ms"] * 1e-3) / 1e12, 1) for k, v in classes.items()
                            if CLASSES[k] == "tensor"},
         "top_shapes": shapes,
-        "e2e": {"value": world * 1e3 / e2e_ms, "unit": UNET_UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": world * per * 1e3 / e2e_ms, "unit": UNET_UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "device_status": status,

@@ -465,21 +465,22 @@ def sigma_to_t(sigma: float) -> float:
 
 
 class Sampler:
-    """Euler sampling with classifier-free guidance: per step one UNet forward on the batch
-    [unconditional, conditional] and one fused guidance + Euler update (sdb_euler_cfg_step).
-    The per-step forward is captured once as a CUDA graph and replayed."""
+    """Euler sampling with classifier-free guidance of `images` images at once: per step one UNet forward
+    on the batch [the images unconditional, the images conditional] and one fused guidance + Euler update
+    (sdb_euler_cfg_step, whose halves are those two).  The per-step forward is captured once as a CUDA
+    graph and replayed."""
 
     def __init__(self, unet: UNet, height: int = 64, width: int = 64, steps: int = 20, cfg_scale: float = 7.0,
-                 context_len: int = 77):
+                 context_len: int = 77, images: int = 1):
         torch = unet.torch
-        self.unet, self.steps, self.cfg_scale = unet, steps, cfg_scale
+        self.unet, self.steps, self.cfg_scale, self.images = unet, steps, cfg_scale, images
         dev = unet.device
         c = unet.cfg
         self.sigmas = discrete_sigmas(steps)
-        self.x = torch.zeros(1, height, width, c.in_channels, device=dev)
-        self.x_in = torch.zeros(2, height, width, c.in_channels, device=dev)
-        self.t = torch.zeros(2, device=dev)
-        self.context = torch.zeros(2, context_len, c.context_dim, device=dev)
+        self.x = torch.zeros(images, height, width, c.in_channels, device=dev)
+        self.x_in = torch.zeros(2 * images, height, width, c.in_channels, device=dev)
+        self.t = torch.zeros(2 * images, device=dev)
+        self.context = torch.zeros(2 * images, context_len, c.context_dim, device=dev)
         self.eps = None
         self.graph = None
 
@@ -515,10 +516,12 @@ class Sampler:
     def set_step(self, i: int):
         sigma = self.sigmas[i]
         self.t.fill_(sigma_to_t(sigma))
-        self.x_in.copy_(self.x.expand(2, -1, -1, -1) / math.sqrt(sigma * sigma + 1.0))
+        self.x_in.view(2, *self.x.shape).copy_(self.x.unsqueeze(0).expand(2, *self.x.shape) /
+                                               math.sqrt(sigma * sigma + 1.0))
 
     def sample(self, latent, context):
-        """latent (1, H, W, 4) N(0, 1), context (2, 77, 768) [uncond, cond] -> the final latent."""
+        """latent (images, H, W, 4) N(0, 1), context (2 images, 77, 768) [the images' unconditional, their
+        conditional] -> the final latents."""
         self.x.copy_(latent * self.sigmas[0])
         self.context.copy_(context)
         for i in range(self.steps):

@@ -80,7 +80,7 @@ def test_reference_arm_line():
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
-    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["unit"] == "UNet steps/s"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["unit"] == "image-steps/s"
 
 
 def _guidance_worker(rank: int, world: int, port: int, out):

@@ -220,3 +220,25 @@ def test_coarser_tokens(cuda):
         y = sdb.coarser_tokens(x, 5, 7, 2)
         want = x.view(2, 7, 5, c)[:, ::2, ::2, :].reshape(2, -1, c)
         assert torch.equal(y, want)
+
+
+def test_sd15_unet_eight_images(cuda):
+    """The bench's per-GPU batch at one GPU: SD 1.5's UNet on 8 images' guidance batch (16) gives each
+    image's pair what the pair alone gives (within 1e-5 of the largest output: only the GEMMs' plans,
+    split by the row count, differ)."""
+    import torch
+    import unet as U
+
+    net = U.UNet(U.SD15, device=cuda, seed=20261011)
+    g = torch.Generator(device=cuda).manual_seed(21)
+    x = torch.randn(16, 64, 64, 4, device=cuda, generator=g)
+    t = torch.full((16,), 500.0, device=cuda)
+    ctx = torch.randn(16, 77, 768, device=cuda, generator=g)
+    eps = net.forward(x, t, ctx)
+    for i in (0, 5):
+        rows = [i, 8 + i]
+        pair = net.forward(x[rows].contiguous(), t[rows].contiguous(), ctx[rows].contiguous())
+        err = (eps[rows] - pair).abs().max().item() / pair.abs().max().item()
+        assert err <= 1e-5, f"image {i}: {err:.3g}"
+    del net
+    torch.cuda.empty_cache()
