@@ -995,7 +995,10 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
+        # Captured on the UNet's launch of one image's guidance pair; DRAM bytes grow with the images a
+        # launch processes (every launch streams its own activations), so scale by this GPU's images.
         traffic = json.loads(tfile.read_text()).get(dom)
+        traffic = traffic * per if traffic is not None else None
     line = {
         "metric": UNET_METRIC, "value": world * per * 1e3 / ms, "unit": UNET_UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
