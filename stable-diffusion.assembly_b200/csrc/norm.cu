@@ -604,62 +604,92 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(const RowArgs a) {
     }
 }
 
-// One warp per row with the row in registers (rows of up to 32 * kLnPer
+// One warp per R rows with the rows in registers (rows of up to 32 * kLnPer
 // elements, contiguous): x is read from memory once, both statistics and the
-// normalisation come from the registers.
+// normalisation come from the registers.  The R rows' dependent chains (double
+// sums, warp reductions) interleave, which hides their latency where a row is
+// short; each row's arithmetic is the same, in the same order, for any R.
 constexpr int kLnPer = 40;   // the widest row kept in registers: 32 x 40 elements
 
-template <int kLnPer>
+template <int PER, int R>
 __global__ void __launch_bounds__(256) norm_rows_reg_kernel(const RowArgs a) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * R;
     const int lane = threadIdx.x & 31;
-    if (row >= a.rows) return;
-    const long long i1 = row % a.ne1;
-    const long long i2 = (row / a.ne1) % a.ne2;
-    const long long i3 = row / (a.ne1 * a.ne2);
-    const float* xr = a.x + i1 * a.xnb[1] + i2 * a.xnb[2] + i3 * a.xnb[3];
-    float* yr = a.y + i1 * a.ynb[1] + i2 * a.ynb[2] + i3 * a.ynb[3];
+    if (row0 >= a.rows) return;
     const int n = static_cast<int>(a.ne0);
-    float v[kLnPer];
+    bool live[R];
+    long long i1[R], i2[R], i3[R];
+    float v[R][PER];
 #pragma unroll
-    for (int k = 0; k < kLnPer; ++k) v[k] = lane + 32 * k < n ? __ldg(xr + lane + 32 * k) : 0.0f;
-    double s = 0.0;
+    for (int r = 0; r < R; ++r) {
+        live[r] = row0 + r < a.rows;
+        const long long row = live[r] ? row0 + r : row0;
+        i1[r] = row % a.ne1;
+        i2[r] = (row / a.ne1) % a.ne2;
+        i3[r] = row / (a.ne1 * a.ne2);
+        const float* xr = a.x + i1[r] * a.xnb[1] + i2[r] * a.xnb[2] + i3[r] * a.xnb[3];
 #pragma unroll
-    for (int k = 0; k < kLnPer; ++k) s += static_cast<double>(v[k]);
-    s = warp_sum(s);
-    const float mean = static_cast<float>(s / static_cast<double>(n));
-    double q = 0.0;
+        for (int k = 0; k < PER; ++k) v[r][k] = live[r] && lane + 32 * k < n ? __ldg(xr + lane + 32 * k) : 0.0f;
+    }
+    double s[R];
 #pragma unroll
-    for (int k = 0; k < kLnPer; ++k) {
+    for (int r = 0; r < R; ++r) s[r] = 0.0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k)
+#pragma unroll
+        for (int r = 0; r < R; ++r) s[r] += static_cast<double>(v[r][k]);
+    float mean[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        s[r] = warp_sum(s[r]);
+        mean[r] = static_cast<float>(s[r] / static_cast<double>(n));
+    }
+    double q[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) q[r] = 0.0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
         if (lane + 32 * k < n) {
-            const float d = v[k] - mean;
-            q += static_cast<double>(d * d);
-        }
-    }
-    q = warp_sum(q);
-    const float scale = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(n)) + a.eps);
 #pragma unroll
-    for (int k = 0; k < kLnPer; ++k) v[k] = (v[k] - mean) * scale;
-    ChainRow cr;
-    row_offsets(a.chain, cr, 0, i1, i2, i3);
-#pragma unroll
-    for (int st = 0; st < SDB_MAX_STEPS; ++st) {
-        if (st >= a.chain.count) break;
-        if (a.chain.kind[st] == SDB_STEP_SILU) {
-#pragma unroll
-            for (int k = 0; k < kLnPer; ++k) v[k] = silu(v[k]);
-        } else {
-            float o[kLnPer];
-#pragma unroll
-            for (int k = 0; k < kLnPer; ++k)
-                o[k] = __ldg(a.chain.operand[st] + cr.off[st] + min(lane + 32 * k, n - 1) * a.chain.nb[st][0]);
-#pragma unroll
-            for (int k = 0; k < kLnPer; ++k) v[k] = a.chain.kind[st] == SDB_STEP_ADD ? v[k] + o[k] : v[k] * o[k];
+            for (int r = 0; r < R; ++r) {
+                const float d = v[r][k] - mean[r];
+                q[r] += static_cast<double>(d * d);
+            }
         }
     }
 #pragma unroll
-    for (int k = 0; k < kLnPer; ++k)
-        if (lane + 32 * k < n) yr[(lane + 32 * k) * a.ynb[0]] = v[k];
+    for (int r = 0; r < R; ++r) {
+        q[r] = warp_sum(q[r]);
+        const float scale = 1.0f / sqrtf(static_cast<float>(q[r] / static_cast<double>(n)) + a.eps);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) v[r][k] = (v[r][k] - mean[r]) * scale;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        ChainRow cr;
+        row_offsets(a.chain, cr, 0, i1[r], i2[r], i3[r]);
+#pragma unroll
+        for (int st = 0; st < SDB_MAX_STEPS; ++st) {
+            if (st >= a.chain.count) break;
+            if (a.chain.kind[st] == SDB_STEP_SILU) {
+#pragma unroll
+                for (int k = 0; k < PER; ++k) v[r][k] = silu(v[r][k]);
+            } else {
+                float o[PER];
+#pragma unroll
+                for (int k = 0; k < PER; ++k)
+                    o[k] = __ldg(a.chain.operand[st] + cr.off[st] + min(lane + 32 * k, n - 1) * a.chain.nb[st][0]);
+#pragma unroll
+                for (int k = 0; k < PER; ++k)
+                    v[r][k] = a.chain.kind[st] == SDB_STEP_ADD ? v[r][k] + o[k] : v[r][k] * o[k];
+            }
+        }
+        if (!live[r]) continue;
+        float* yr = a.y + i1[r] * a.ynb[1] + i2[r] * a.ynb[2] + i3[r] * a.ynb[3];
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (lane + 32 * k < n) yr[(lane + 32 * k) * a.ynb[0]] = v[r][k];
+    }
 }
 
 bool f32(const sdb_tensor* t) { return t && t->type == SDB_TYPE_F32 && t->data; }
@@ -891,15 +921,16 @@ extern "C" int sdb_norm(const sdb_tensor* x, const sdb_tensor* dst, float eps, c
     a.chain = make_chain(chain);
     const long long threads = a.rows * 32;
     const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+    const unsigned blocks2 = static_cast<unsigned>(((a.rows + 1) / 2 * 32 + 255) / 256);   // two rows a warp
     const int per = static_cast<int>((a.ne0 + 31) / 32);
     if (a.xnb[0] == 1 && per <= 8)
-        norm_rows_reg_kernel<8><<<blocks, 256, 0, st>>>(a);
+        norm_rows_reg_kernel<8, 2><<<blocks2, 256, 0, st>>>(a);
     else if (a.xnb[0] == 1 && per <= 12)
-        norm_rows_reg_kernel<12><<<blocks, 256, 0, st>>>(a);
+        norm_rows_reg_kernel<12, 2><<<blocks2, 256, 0, st>>>(a);
     else if (a.xnb[0] == 1 && per <= 20)
-        norm_rows_reg_kernel<20><<<blocks, 256, 0, st>>>(a);
+        norm_rows_reg_kernel<20, 1><<<blocks, 256, 0, st>>>(a);
     else if (a.xnb[0] == 1 && per <= kLnPer)
-        norm_rows_reg_kernel<kLnPer><<<blocks, 256, 0, st>>>(a);
+        norm_rows_reg_kernel<kLnPer, 1><<<blocks, 256, 0, st>>>(a);
     else
         norm_rows_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(a);
     count_launch();
