@@ -386,16 +386,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnAr
                 const float recip = static_cast<float>(1.0 / total);
                 const long long ob = static_cast<long long>(head) * a.onb[1] + static_cast<long long>(qi) * a.onb[2] +
                                      static_cast<long long>(batch) * a.onb[3];
+                // Whole 16-column chunks of a row with unit stride leave as four float4s.
+                const bool vec = a.onb[0] == 1 && dv0 % 4 == 0 && (reinterpret_cast<uintptr_t>(a.out + ob) & 15) == 0;
 #pragma unroll
                 for (int c = 0; c < OMINE; ++c) {
                     const int ch = 2 * c + half;
                     if (ch < OCH) {
+                        const int d0c = dv0 + ch * 16;
+                        if (vec && d0c + 16 <= a.dv) {
+                            float w[16];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int dcol = dv0 + ch * 16 + i;
-                            if (dcol < a.dv) {
-                                const float v = apply_chain(a.chain, o[c * 16 + i] * recip, dcol, head, qi, batch);
-                                a.out[ob + dcol * a.onb[0]] = v;
+                            for (int i = 0; i < 16; ++i)
+                                w[i] = apply_chain(a.chain, o[c * 16 + i] * recip, d0c + i, head, qi, batch);
+#pragma unroll
+                            for (int i = 0; i < 16; i += 4)
+                                *reinterpret_cast<float4*>(a.out + ob + d0c + i) = make_float4(w[i], w[i + 1], w[i + 2],
+                                                                                                w[i + 3]);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int dcol = d0c + i;
+                                if (dcol < a.dv) {
+                                    const float v = apply_chain(a.chain, o[c * 16 + i] * recip, dcol, head, qi, batch);
+                                    a.out[ob + dcol * a.onb[0]] = v;
+                                }
                             }
                         }
                     }
@@ -734,10 +748,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
                 for (int c = 0; c < DVC; c += 16) apply_chain_cols<0, 16>(a.chain, cr, o + c, dv0 + c, a.dv - 1);
                 float* orow = a.out + static_cast<long long>(head) * a.onb[1] + static_cast<long long>(qi) * a.onb[2] +
                               static_cast<long long>(batch) * a.onb[3];
-                if (a.onb[0] == 1 && ncols == DVC && ((reinterpret_cast<uintptr_t>(orow + dv0)) & 15) == 0) {
+                if (a.onb[0] == 1 && ncols % 4 == 0 && ((reinterpret_cast<uintptr_t>(orow + dv0)) & 15) == 0) {
+                    // Whole float4s up to the value dims the row holds (40 of a 48-wide chunk, say).
 #pragma unroll
                     for (int i = 0; i < DVC; i += 4)
-                        *reinterpret_cast<float4*>(orow + dv0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                        if (i < ncols)
+                            *reinterpret_cast<float4*>(orow + dv0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
                 } else {
 #pragma unroll
                     for (int i = 0; i < DVC; ++i)
