@@ -127,12 +127,13 @@ int sdb_norm(const sdb_tensor *x, const sdb_tensor *dst, float eps, const sdb_ch
 /* GroupNorm that allocates nothing, for callers that may not call cudaMalloc
  * (memory owned by another allocator, code running under stream capture, loops
  * that may not take the driver's allocation lock).  No counterpart in the
- * reference, whose CPU ops allocate from the host.  Same arguments and result
- * as sdb_group_norm; its partial sums live in a fixed 512 KiB device array that
- * every GPU loading this library holds until exit, so images x groups must be
- * <= 32768 (else SDB_INVALID).  The first call on a device looks the array up
- * (make it before any stream capture).  Calls share the array: calls that
- * overlap on the GPU race. */
+ * reference, whose CPU ops allocate from the host.  The arguments and result of
+ * sdb_group_norm, for the contiguous (channel-major [W, H, C, N]) layout only:
+ * channels-last images return SDB_NOT_SUPPORTED.  Its partial sums live in a
+ * fixed 512 KiB device array that every GPU loading this library holds until
+ * exit, so images x groups must be <= 32768 (else SDB_INVALID).  The first call
+ * on a device looks the array up (make it before any stream capture).  Calls
+ * share the array: calls that overlap on the GPU race. */
 int sdb_group_norm_no_alloc(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps,
                             const sdb_chain *chain, void *stream);
 

@@ -1,6 +1,9 @@
 """Builds oracle/_ref/libsdasm_ref.so from the reference's own x86-64 kernels -- TEST INFRASTRUCTURE ONLY.
 
-    python oracle/ref_asm.py [--reference /root/reference]
+    python oracle/ref_asm.py [--reference DIR]
+
+DIR defaults to reference_dir(): $SDB_REFERENCE_DIR, else a directory named
+"reference" beside this repository's root, where the reference's sources are.
 
 The reference (stable-diffusion.assembly) cannot be built here as a whole: it
 needs Clang >= 23, C++26 and the ggml / stable-diffusion.cpp sources, which
@@ -24,6 +27,7 @@ linear layers and convolutions; nothing in the product links it.
 from __future__ import annotations
 
 import argparse
+import os
 import re
 import struct
 import subprocess
@@ -32,6 +36,20 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
+
+
+def reference_dir() -> Path:
+    """Where the reference's sources are: $SDB_REFERENCE_DIR, else ../reference
+    beside the repository's root.  The directory may not exist (a GPU box gets
+    only the repository and the libraries built from it)."""
+    env = os.environ.get("SDB_REFERENCE_DIR")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
+def reference_kernels_present() -> bool:
+    return (reference_dir() / "sources" / "x86_64").is_dir()
+
+
 KERNELS = ["gemm_avx2", "activation_avx2", "softmax_avx2", "quant_avx512", "quantize_avx2"]
 HEXFLOAT = re.compile(r"(?<![\w.])(-?0x[0-9a-fA-F]+(?:\.[0-9a-fA-F]*)?p[+-]?\d+)")
 
@@ -56,7 +74,8 @@ def rewrite(src: str) -> str:
     return "\n".join(out) + "\n"
 
 
-def build(reference: Path = Path("/root/reference")) -> Path:
+def build(reference: Path | None = None) -> Path:
+    reference = reference_dir() if reference is None else reference
     src_dir = reference / "sources" / "x86_64"
     if not src_dir.is_dir():
         raise FileNotFoundError(f"{src_dir}: the reference is not here")
@@ -76,6 +95,6 @@ def build(reference: Path = Path("/root/reference")) -> Path:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=str(reference_dir()))
     print(build(Path(ap.parse_args().reference)))
     sys.exit(0)

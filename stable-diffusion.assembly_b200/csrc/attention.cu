@@ -32,6 +32,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/sdb.h"
 #include "chain.cuh"
@@ -892,6 +895,116 @@ int launch_bk(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_t
     return fail(SDB_NOT_SUPPORTED, "sdb_attention: head too wide");
 }
 
+// ---------------------------------------------------------------- wide heads
+// Heads of more than 160 dims (the VAE's one head of 512, attention.cc:828-845
+// takes any width) do not fit the fused kernels' shared and tensor memory: a
+// 128-query tile of Q alone, split, is 128 x 512 x 4 B = 256 KB.  They run per
+// (image, head) as the product, the softmax and the product again, which is the
+// reference's own two-pass order (attention.cc:9-27): S = Q K^T by the linear
+// layers' split GEMM (three FP16 products of the FP32 operands), the rows of S
+// through softmax(scale S) with its exponentials summed in double and one
+// reciprocal a row (sdb_soft_max), and O = P V by the same GEMM.  The head's
+// rows are gathered into dense matrices first (V transposed, so that keys run
+// along the GEMM's K), and O is scattered into dst.
+
+__global__ void gather2d_kernel(const void* src, int f16, long long s0, long long s1, long long n0, long long n1,
+                                float* dst, long long d0, long long d1) {
+    const long long total = n0 * n1;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long i = e / n1, j = e - i * n1;
+        const long long at = i * s0 + j * s1;
+        const float v = f16 ? __half2float(static_cast<const __half*>(src)[at]) : static_cast<const float*>(src)[at];
+        dst[i * d0 + j * d1] = v;
+    }
+}
+
+// Device memory of the wide path, per (device, stream), apart from the GEMM's
+// workspace; grows outside stream capture only.
+int wide_scratch(cudaStream_t st, size_t bytes, float** out) {
+    static std::mutex lock;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> spaces;
+    int dev = 0;
+    SDB_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> guard(lock);
+    auto& s = spaces[{dev, st}];
+    if (s.second < bytes) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        SDB_CUDA(cudaStreamIsCapturing(st, &cap));
+        if (cap != cudaStreamCaptureStatusNone)
+            return fail(SDB_INVALID, "sdb_attention: scratch must grow under stream capture: run it once before");
+        if (s.first) {
+            SDB_CUDA(cudaStreamSynchronize(st));
+            SDB_CUDA(cudaFree(s.first));
+            s = {nullptr, 0};
+        }
+        SDB_CUDA(cudaMalloc(&s.first, bytes));
+        s.second = bytes;
+    }
+    *out = static_cast<float*>(s.first);
+    return SDB_OK;
+}
+
+int gather2d(const void* src, bool f16, long long s0, long long s1, long long n0, long long n1, float* dst,
+             long long d0, long long d1, cudaStream_t st) {
+    const long long total = n0 * n1;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    gather2d_kernel<<<blocks, 256, 0, st>>>(src, f16 ? 1 : 0, s0, s1, n0, n1, dst, d0, d1);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
+sdb_tensor dense(float* data, long long ne0, long long ne1) {
+    sdb_tensor t{};
+    t.type = SDB_TYPE_F32;
+    t.ne[0] = ne0; t.ne[1] = ne1; t.ne[2] = 1; t.ne[3] = 1;
+    t.nb[0] = 4; t.nb[1] = 4 * ne0; t.nb[2] = t.nb[1] * ne1; t.nb[3] = t.nb[2];
+    t.data = data;
+    return t;
+}
+
+int run_wide_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, const sdb_tensor* dst,
+                       float scale, cudaStream_t st) {
+    const long long d = q->ne[0], lq = q->ne[1], h = q->ne[2], b = q->ne[3];
+    const long long lk = k->ne[1], hk = k->ne[2], dv = v->ne[0];
+    const int ke = esize(k), ve = esize(v);
+    const long long qn = lq * d, kn = lk * d, vn = dv * lk, sn = lq * lk, on = lq * dv;
+    float* base = nullptr;
+    const auto pad = [](long long n) { return (n + 63) / 64 * 64; };
+    const size_t bytes = 4 * static_cast<size_t>(pad(qn) + pad(kn) + pad(vn) + pad(sn) + pad(on));
+    if (int s = wide_scratch(st, bytes, &base); s != SDB_OK) return s;
+    float* qc = base;
+    float* kc = qc + pad(qn);
+    float* vt = kc + pad(kn);
+    float* sc = vt + pad(vn);
+    float* oc = sc + pad(sn);
+    for (long long bi = 0; bi < b; ++bi) {
+        for (long long hi = 0; hi < h; ++hi) {
+            const long long khi = hi / (h / hk);
+            const char* qh = static_cast<const char*>(q->data) + bi * q->nb[3] + hi * q->nb[2];
+            const char* kh = static_cast<const char*>(k->data) + bi * k->nb[3] + khi * k->nb[2];
+            const char* vh = static_cast<const char*>(v->data) + bi * v->nb[3] + khi * v->nb[2];
+            if (int s = gather2d(qh, false, q->nb[1] / 4, q->nb[0] / 4, lq, d, qc, d, 1, st); s != SDB_OK) return s;
+            if (int s = gather2d(kh, ke == 2, k->nb[1] / ke, k->nb[0] / ke, lk, d, kc, d, 1, st); s != SDB_OK)
+                return s;
+            if (int s = gather2d(vh, ve == 2, v->nb[0] / ve, v->nb[1] / ve, dv, lk, vt, lk, 1, st); s != SDB_OK)
+                return s;
+            const sdb_tensor tq = dense(qc, d, lq), tk = dense(kc, d, lk), ts = dense(sc, lk, lq),
+                             tv = dense(vt, lk, dv), to = dense(oc, dv, lq);
+            if (int s = sdb_mul_mat_transient(&tk, &tq, &ts, nullptr, st); s != SDB_OK) return s;
+            if (int s = sdb_soft_max(&ts, &ts, scale, st); s != SDB_OK) return s;
+            if (int s = sdb_mul_mat_transient(&tv, &ts, &to, nullptr, st); s != SDB_OK) return s;
+            char* oh = static_cast<char*>(dst->data) + bi * dst->nb[3] + hi * dst->nb[1];
+            if (int s = gather2d(oc, false, dv, 1, lq, dv, reinterpret_cast<float*>(oh), dst->nb[2] / 4,
+                                 dst->nb[0] / 4, st);
+                s != SDB_OK)
+                return s;
+        }
+    }
+    return SDB_OK;
+}
+
 }  // namespace
 
 }  // namespace sdb
@@ -909,10 +1022,11 @@ extern "C" int sdb_attention_supported(const sdb_tensor* q, const sdb_tensor* k,
     if (k->ne[0] != d || v->ne[1] != lk || v->ne[2] != hk || k->ne[3] != b || v->ne[3] != b) return 0;
     if (hk <= 0 || h % hk != 0 || d <= 0 || dv <= 0 || lq <= 0 || lk <= 0) return 0;
     if (dst->ne[0] != dv || dst->ne[1] != h || dst->ne[2] != lq || dst->ne[3] != b) return 0;
-    if (d > 160 || dv > 512) return 0;
     for (const sdb_tensor* t : {q, k, v, dst})
         for (int i = 0; i < 4; ++i)
             if (t->nb[i] % esize(t) != 0 || t->nb[i] < 0) return 0;
+    // Heads wider than the fused kernels take: by the product, softmax, product path.
+    if (d > 160 || dv > 512) return d <= (1 << 16) && dv <= (1 << 16) && lk <= (1 << 24) && lq <= (1 << 30);
     // TMA row coordinates are 32-bit (hi and lo planes).
     if (2 * b * h * lq >= (1LL << 31) || 2 * b * hk * lk >= (1LL << 31)) return 0;
     return h * ((dv + 79) / 80) <= 65535 && b <= 65535;
@@ -924,8 +1038,15 @@ extern "C" int sdb_attention(const sdb_tensor* q, const sdb_tensor* k, const sdb
     if (chain && (chain->count < 0 || chain->count > SDB_MAX_STEPS || chain->redirect))
         return fail(SDB_INVALID, "sdb_attention: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
-    // Integer products for self-attention over 256 keys or more (attention.cc:612-618, 858-862).
-    if (quantized_attention(k->ne[1])) return run_quantized_attention(q, k, v, dst, scale, chain, st);
+    // Integer products for self-attention over 256 keys or more (attention.cc:612-618, 858-862);
+    // heads wider than 160 dims stay in single precision.
+    const bool wide = q->ne[0] > 160 || v->ne[0] > 512;
+    if (!wide && quantized_attention(k->ne[1])) return run_quantized_attention(q, k, v, dst, scale, chain, st);
+    if (wide) {
+        if (chain && (chain->count > 0 || chain->from_redirect))
+            return fail(SDB_NOT_SUPPORTED, "sdb_attention: heads over 160 dims take no chain");
+        return run_wide_attention(q, k, v, dst, scale, st);
+    }
     AttnArgs a{};
     a.out = static_cast<float*>(dst->data);
     for (int i = 0; i < 4; ++i) a.onb[i] = dst->nb[i] / 4;

@@ -4,7 +4,8 @@ Cases: the reference's (tests/ops_test.cc:925-938) -- SD 1.5's self- and
 cross-attention made smaller, heads of 80 and 160, the VAE's single head of
 512, dims and keys of no multiple of a panel with heads sharing keys, FP16
 keys and values -- and BASELINE config 3 (8 heads x 40, Lq = Lk = 4096 and
-Lk = 77), with and without the residual add fused.  Q, K, V ~ U(-1, 1)
+Lk = 77), with and without the residual add fused; heads wider than 160 dims
+(the VAE's 512) at full size, with shared FP16 keys and an odd width.  Q, K, V ~ U(-1, 1)
 (ops_test.cc:478-483); bound: the ops_test metric <= 1e-6.
 """
 from __future__ import annotations
@@ -65,11 +66,28 @@ def run(cuda, d, lq, lk, h, hk, b, kvtype, seed=oracle.SEED, normal=False, resid
 def test_attention_reference_cases(cuda, case):
     import sdb
 
-    d = case[0]
-    if d > 160:
-        pytest.xfail("heads wider than 160 are not taken yet (the caller computes them)")
     err = run(cuda, *case)
     assert err <= oracle.K_B200, f"error {err:.3g}"
+
+
+@pytest.mark.parametrize("case", [(512, 4096, 4096, 1, 1, 2, np.float32), (256, 77, 130, 3, 1, 2, np.float16),
+                                  (200, 33, 64, 2, 2, 1, np.float32)],
+                         ids=["vae_512x4096_b2", "d256_shared_kv_f16", "d200"])
+def test_attention_wide_heads(cuda, case):
+    """Heads over 160 dims (the product, softmax, product path): the SD 1.5 VAE's full-size
+    block (one 512-dim head over 4096 positions), heads sharing FP16 keys, an odd width."""
+    err = run(cuda, *case)
+    assert err <= oracle.K_B200, f"error {err:.3g}"
+
+
+def test_attention_wide_heads_take_no_chain(cuda):
+    import sdb
+    import torch
+
+    q = torch.zeros((1, 40, 512), device=cuda)
+    out = torch.empty_like(q)
+    with pytest.raises(sdb.SdbError, match="take no chain"):
+        sdb.attention_heads(q, q, q, 1, 1, 1.0, out=out, chain=sdb.Chain().add(q, nb=[1, 512, 512, 40 * 512]))
 
 
 @pytest.mark.parametrize("lk,residual", [(4096, False), (77, False), (4096, True), (77, True)])

@@ -1,4 +1,5 @@
-"""CPU checks of the C ABI: the library loads and exports every symbol include/sdb.h declares.
+"""CPU checks of the C ABI: the library loads and exports every symbol include/*.h declares
+(sdb.h, the op-level entry points; sdasm.h, the reference's hook surface).
 
 No compute call is made here (there is no GPU on the CPU runner).
 """
@@ -14,10 +15,10 @@ ROOT = Path(__file__).resolve().parent.parent
 LIB = ROOT / "stable-diffusion.assembly_b200" / "libsdb.so"
 
 
-def declared_functions(header: Path) -> list[str]:
+def declared_functions(header: Path, prefix: str = "sdb_") -> list[str]:
     text = header.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(sdb_[a-z0-9_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(" + prefix + r"[a-z0-9_]+)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")
@@ -32,6 +33,28 @@ def test_header_declarations_are_exported(lib):
     assert names, "no declarations found"
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, f"not exported: {missing}"
+
+
+def test_hook_surface_is_exported(lib):
+    """The reference's sdasm.h functions (sources/sdasm.h:38-78), all nine."""
+    names = declared_functions(ROOT / "include" / "sdasm.h", "sdasm_")
+    assert len(names) == 9, names
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_hook_surface_answers_without_a_device(lib):
+    """Calls that need no GPU: a node of an operation not taken, the work size, ToDo's factor."""
+    import ggml_graph as gg
+
+    g = gg.Graph("host")
+    a = g.new_f32((8, 4), fill=1.0)
+    node = g.scale(a, 2.0)
+    size = ctypes.c_size_t(7)
+    assert not lib.sdasm_work_size(ctypes.byref(node.s), 1, ctypes.byref(size))
+    assert size.value == 7
+    assert gg.compute_nodes(lib, [node], 0) == 0
+    assert lib.sdasm_token_downsampling(ctypes.c_int64(64), ctypes.c_int64(64)) == 1
 
 
 def test_binding_lists_every_export():

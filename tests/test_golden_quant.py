@@ -21,6 +21,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+import ref_asm
 import ref_forms
 
 HERE = Path(__file__).resolve().parent
@@ -60,7 +61,7 @@ def test_reference_product_accumulating_pins_the_oracle():
 
 
 def test_quant_fixture_reproduces_from_the_reference():
-    if not Path("/root/reference/sources/x86_64").is_dir() or not mg.has_vnni512():
+    if not ref_asm.reference_kernels_present() or not mg.has_vnni512():
         pytest.skip("the reference's sources or AVX512-VNNI are not on this machine")
     lib = mg.load_ref()
     for i, (k, n, m, group) in enumerate(CASES):

@@ -1,11 +1,18 @@
-"""sdb_group_norm_no_alloc, the GroupNorm that allocates no device memory, against sdb_group_norm.
+"""sdb_group_norm_no_alloc, the GroupNorm that allocates no device memory.
+
+Some callers cannot allocate device memory: a host whose device memory is owned
+by another allocator, work recorded under stream capture, a loop that must not
+take the driver's allocation lock.  The entry point serves them with a fixed
+static scratch array; these tests check it against sdb_group_norm (the entry
+point that does allocate) and against the float64-summed CPU restatement of the
+reference's GroupNorm (oracle.group_norm_ref, norm.cc:100-140).
 
 Collected last (file name) so that it runs both after the other tests and, with
 `pytest tests/test_zz_no_alloc.py`, alone in a fresh process.  Each case makes
 two calls in a row through the C ABI with different inputs (the second call
 finds the first call's partial sums in the shared static array) and holds both
-to the GroupNorm tests' bound: within 1e-6 of the largest output of
-sdb_group_norm on the same input.
+to the GroupNorm tests' bound: within 1e-6 of the largest output, against
+sdb_group_norm on the same input and against the oracle.
 """
 from __future__ import annotations
 
@@ -28,14 +35,21 @@ def close(got, want, bound=oracle.K_FUSED_APART):
 
 
 def inputs(shape, seed, cuda):
+    """x on the device, its chain (scale, shift, SiLU), and what the oracle makes of them."""
     import sdb
 
     g = rng(seed)
     x = oracle.uniform(g, shape, 3.0) + np.float32(seed % 5)
     c = shape[1]
-    gamma = cuda_tensor(oracle.uniform(g, (1, c, 1, 1), 1.0), cuda)
-    beta = cuda_tensor(oracle.uniform(g, (1, c, 1, 1), 1.0), cuda)
-    return cuda_tensor(x, cuda), sdb.Chain().mul(gamma).add(beta).silu()
+    gamma = oracle.uniform(g, (1, c, 1, 1), 1.0)
+    beta = oracle.uniform(g, (1, c, 1, 1), 1.0)
+    chain = sdb.Chain().mul(cuda_tensor(gamma, cuda)).add(cuda_tensor(beta, cuda)).silu()
+    return cuda_tensor(x, cuda), chain, (x, [("mul", gamma), ("add", beta), ("silu", None)])
+
+
+def oracle_group_norm(host_inputs, groups, eps=1e-5):
+    x, steps = host_inputs
+    return oracle.apply_chain(oracle.group_norm_ref(x, groups, eps), steps)
 
 
 @pytest.mark.parametrize("first,second,groups", [
@@ -48,13 +62,15 @@ def test_no_alloc_matches_group_norm_twice(cuda, first, second, groups):
     import torch
 
     for call, shape in enumerate((first, second)):
-        x, chain = inputs(shape, oracle.SEED + call, cuda)
+        x, chain, on_host = inputs(shape, oracle.SEED + call, cuda)
         got = canary_like(shape, cuda)
         want = canary_like(shape, cuda)
         sdb.group_norm_no_alloc(x, groups, 1e-5, out=got, chain=chain)
         sdb.group_norm(x, groups, 1e-5, out=want, chain=chain)
         torch.cuda.synchronize()
         close(host(got), host(want))
+        if np.prod(shape) <= (1 << 21):   # the oracle's Python loop over groups stays in seconds
+            close(host(got), oracle_group_norm(on_host, groups))
 
 
 def test_no_alloc_repeat_allocates_nothing(cuda):
@@ -62,7 +78,7 @@ def test_no_alloc_repeat_allocates_nothing(cuda):
     import sdb
     import torch
 
-    x, chain = inputs((1, 640, 32, 32), oracle.SEED, cuda)
+    x, chain, _ = inputs((1, 640, 32, 32), oracle.SEED, cuda)
     out = canary_like(x.shape, cuda)
     sdb.group_norm_no_alloc(x, 32, 1e-5, out=out, chain=chain)
     torch.cuda.synchronize()
@@ -81,3 +97,14 @@ def test_no_alloc_rejects_sizes_beyond_its_scratch(cuda):
     out = canary_like(x.shape, cuda)
     with pytest.raises(sdb.SdbError, match="exceeds the static scratch limit"):
         sdb.group_norm_no_alloc(x, 16384, 1e-5, out=out)
+
+
+def test_no_alloc_rejects_channels_last_images(cuda):
+    """Only the contiguous (channel-major) layout is taken; sdb_group_norm also takes channels-last."""
+    import sdb
+    import torch
+
+    x = torch.zeros((1, 64, 8, 8), dtype=torch.float32, device=cuda).to(memory_format=torch.channels_last)
+    out = torch.empty_like(x)
+    with pytest.raises(sdb.SdbError, match="not supported"):
+        sdb.group_norm_no_alloc(x, 32, 1e-5, out=out)
