@@ -50,7 +50,7 @@ def reference_kernels_present() -> bool:
     return (reference_dir() / "sources" / "x86_64").is_dir()
 
 
-KERNELS = ["gemm_avx2", "activation_avx2", "softmax_avx2", "quant_avx512", "quantize_avx2"]
+KERNELS = ["gemm_avx2", "gemm_avx512", "activation_avx2", "softmax_avx2", "quant_avx512", "quantize_avx2"]
 HEXFLOAT = re.compile(r"(?<![\w.])(-?0x[0-9a-fA-F]+(?:\.[0-9a-fA-F]*)?p[+-]?\d+)")
 
 
@@ -88,7 +88,7 @@ def build(reference: Path | None = None) -> Path:
         subprocess.run(["as", "--64", "-o", str(o), str(s)], check=True, capture_output=True)
         objs.append(str(o))
     lib = OUT / "libsdasm_ref.so"
-    subprocess.run(["gcc", "-O2", "-fopenmp", "-shared", "-fPIC", "-mavx2", "-mfma", "-mf16c", "-o", str(lib),
+    subprocess.run(["gcc", "-O3", "-fopenmp", "-shared", "-fPIC", "-mavx2", "-mfma", "-mf16c", "-o", str(lib),
                     str(HERE / "ref_driver.c"), *objs, "-lm", "-Wl,-z,noexecstack"], check=True, capture_output=True)
     return lib
 

@@ -29,6 +29,9 @@
 enum { KC = 256, MR = 6, NR = 16 };
 
 void sdasm_gemm_6x16_avx2(int64_t kc, const float *a, const float *b, float *c, int64_t ldc, int64_t accumulate);
+void sdasm_gemm_6x16_avx512(int64_t kc, const float *a, const float *b, float *c, int64_t ldc, int64_t accumulate);
+void sdasm_gemm_6x32_avx512(int64_t kc, const float *a, const float *b, int64_t b_next, float *c, int64_t ldc,
+                            int64_t accumulate);
 void sdasm_gated_gelu_avx2(float *out, const float *x, const float *gate, int64_t n);
 void sdasm_exponentials_avx2(float *s, int64_t n, const float *max, double *total);
 
@@ -167,6 +170,33 @@ int refk_threads(void) {
 #endif
 }
 
+/* The threads the products use: the caller names them (the host's cores), so
+ * that a launcher's OMP_NUM_THREADS does not decide it. */
+void refk_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+/* The micro-kernel the reference picks for the host (cpu.cc:302, Tuning::wide):
+ * on AVX-512 the tile of 6 x 32 columns from two adjacent panels
+ * (sdasm_gemm_6x32_avx512, gemm_avx512.S) and 6 x 16 at an odd last panel;
+ * else AVX2's 6 x 16.  refk_set_isa(0) forces AVX2 (for the golden fixtures). */
+static int use_avx512 = -1;
+
+void refk_set_isa(int avx512) { use_avx512 = avx512; }
+
+int refk_isa(void) {
+    if (use_avx512 < 0) {
+        __builtin_cpu_init();
+        use_avx512 = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512vl") &&
+                     __builtin_cpu_supports("avx512bw") && __builtin_cpu_supports("avx512dq");
+    }
+    return use_avx512;
+}
+
 static int refk_threads_internal(void) { return refk_threads(); }
 
 /* Widened weight panels are kept between calls, keyed by the weights' address
@@ -226,17 +256,39 @@ static float *widen_panels(const uint16_t *w16, int N, int K) {
  * panels [p0, p1) (all when p1 <= 0). */
 static void block_product_cols(const float *ap, const float *wp, int N, int K, int k0, int kc, int rows_total,
                                float *y, float *tile, int p0, int p1) {
+    const int wide = refk_isa();
+    void (*tile16)(int64_t, const float *, const float *, float *, int64_t, int64_t) =
+        wide ? sdasm_gemm_6x16_avx512 : sdasm_gemm_6x16_avx2;
     for (int p = p0; p < p1; ++p) {
         const float *b = wp + ((size_t)p * K + k0) * NR;
         const int cols = N - p * NR < NR ? N - p * NR : NR;
+        /* Two full panels: the 6 x 32 tile over both, rows of whole tiles. */
+        if (wide && p + 1 < p1 && N - (p + 1) * NR >= NR) {
+            const int64_t b_next = (int64_t)K * NR * 4;
+            int i0 = 0;
+            for (; i0 + MR <= rows_total; i0 += MR)
+                sdasm_gemm_6x32_avx512(kc, ap + (size_t)(i0 / MR) * kc * MR, b, b_next, y + (size_t)i0 * N + p * NR,
+                                       (int64_t)N * 4, k0 > 0);
+            for (int q = p; q <= p + 1 && i0 < rows_total; ++q) {
+                const float *bq = wp + ((size_t)q * K + k0) * NR;
+                const int rows = rows_total - i0;
+                float *c = y + (size_t)i0 * N + q * NR;
+                tile16(kc, ap + (size_t)(i0 / MR) * kc * MR, bq, tile, NR * 4, 0);
+                for (int i = 0; i < rows; ++i)
+                    for (int j = 0; j < NR; ++j)
+                        c[(size_t)i * N + j] = k0 > 0 ? c[(size_t)i * N + j] + tile[i * NR + j] : tile[i * NR + j];
+            }
+            ++p;
+            continue;
+        }
         for (int i0 = 0; i0 < rows_total; i0 += MR) {
             const float *a = ap + (size_t)(i0 / MR) * kc * MR;
             const int rows = rows_total - i0 < MR ? rows_total - i0 : MR;
             float *c = y + (size_t)i0 * N + p * NR;
             if (rows == MR && cols == NR) {
-                sdasm_gemm_6x16_avx2(kc, a, b, c, (int64_t)N * 4, k0 > 0);
+                tile16(kc, a, b, c, (int64_t)N * 4, k0 > 0);
             } else {
-                sdasm_gemm_6x16_avx2(kc, a, b, tile, NR * 4, 0);
+                tile16(kc, a, b, tile, NR * 4, 0);
                 for (int i = 0; i < rows; ++i)
                     for (int j = 0; j < cols; ++j)
                         c[(size_t)i * N + j] = k0 > 0 ? c[(size_t)i * N + j] + tile[i * NR + j] : tile[i * NR + j];
@@ -253,8 +305,15 @@ static void block_product(const float *ap, const float *wp, int N, int K, int k0
 /* Work items: blocks of 48 rows, each split over column-panel chunks when the
  * rows alone would leave threads idle (the reference's queue hands out tiles). */
 static int column_chunks(int mblocks, int npanels) {
+    const int pairs = (npanels + 1) / 2;
     const int want = (4 * refk_threads_internal() + mblocks - 1) / mblocks;
-    return want < 1 ? 1 : (want > npanels ? npanels : want);
+    return want < 1 ? 1 : (want > pairs ? pairs : want);
+}
+
+/* Panels per chunk, even, so that a chunk's 6 x 32 tiles pair its own panels. */
+static int chunk_panels(int npanels, int chunks) {
+    const int per = (npanels + chunks - 1) / chunks;
+    return (per + 1) / 2 * 2;
 }
 
 /* y (M, N) = x (M, K) w16 (N, K)^T on all threads. */
@@ -266,7 +325,7 @@ int refk_mul_mat_mt(const uint16_t *w16, int N, int K, const float *x, int M, fl
         keep_panels(w16, N, K, 0, wp);
     }
     const int mblocks = (M + 47) / 48, npanels = (N + NR - 1) / NR;
-    const int chunks = column_chunks(mblocks, npanels), per = (npanels + chunks - 1) / chunks;
+    const int chunks = column_chunks(mblocks, npanels), per = chunk_panels(npanels, chunks);
     int bad = 0;
 #pragma omp parallel
     {
@@ -330,7 +389,7 @@ int refk_conv2d_mt(const uint16_t *w16, int OC, int IC, int KH, int KW, const fl
                 xl[(((size_t)n * H + iy) * W + ix) * IC + ic] = x[(((size_t)n * IC + ic) * H + iy) * W + ix];
     }
     const int mblocks = (M + 47) / 48;
-    const int chunks = column_chunks(mblocks, npanels), per = (npanels + chunks - 1) / chunks;
+    const int chunks = column_chunks(mblocks, npanels), per = chunk_panels(npanels, chunks);
     int bad = 0;
 #pragma omp parallel
     {
@@ -446,11 +505,11 @@ int refk_attention_mt(const float *q, const float *k, const float *v, float *out
                         row[key] *= scale;
                         mx = row[key] > mx ? row[key] : mx;
                     }
+                    /* The exponentials in one loop the compiler vectorises (the reference's own are
+                     * sdasm_exponentials_*, vector code too), their sum in double in another. */
+                    for (int key = 0; key < LK; ++key) row[key] = c_exponential(row[key] - mx);
                     double t = 0.0;
-                    for (int key = 0; key < LK; ++key) {
-                        row[key] = c_exponential(row[key] - mx);
-                        t += row[key];
-                    }
+                    for (int key = 0; key < LK; ++key) t += row[key];
                     sum[i] = t;
                 }
                 /* O = P V over K = LK, stretch by stretch. */
@@ -481,5 +540,213 @@ int refk_attention_mt(const float *q, const float *k, const float *v, float *out
     }
     free(kp);
     free(vp);
+    return bad;
+}
+
+/* ------------------------------------------------------------------ Winograd
+ * The reference sends a 3x3 stride-1 convolution to Winograd when an image has
+ * at least winograd_positions (1024) outputs or all images together few tiles
+ * (winograd.cc:194-196, 2107-2123), as F(4x4, 3x3) from winograd4_positions
+ * (256) outputs an image with FP16 weights, else F(2x2, 3x3)
+ * (winograd.cc:1204-1206, 2230-2272).  Its transforms are hand-written
+ * (winograd4_avx512.S); here they are C over channels-last rows (the compiler
+ * vectorises the channel loops), with the published transform matrices of
+ * Lavin and Gray (F(2x2): points 0, +-1; F(4x4): 0, +-1, +-2), and each of the
+ * (F+2)^2 products runs on the reference's micro-kernel as the linear layers'
+ * do.  The transformed weights U are kept between calls as its store keeps
+ * packed weights.  x [N][IC][H][W], y [position][OC]; padding `pad` on all
+ * sides; the outputs OH x OW = H + 2 pad - 2 by W + 2 pad - 2.
+ * TEST INFRASTRUCTURE (the CPU baseline's timing), not the product. */
+
+static void bt_f4(const float *d, float *t, int n, size_t step, size_t ostep) {
+    /* t_i = sum_j BT[i][j] d_j for the 6 x 6 BT of F(4x4), n lanes, element j at d + j*step. */
+    for (int c = 0; c < n; ++c) {
+        const float d0 = d[c], d1 = d[step + c], d2 = d[2 * step + c], d3 = d[3 * step + c], d4 = d[4 * step + c],
+                    d5 = d[5 * step + c];
+        t[c] = 4 * d0 - 5 * d2 + d4;
+        t[ostep + c] = -4 * d1 - 4 * d2 + d3 + d4;
+        t[2 * ostep + c] = 4 * d1 - 4 * d2 - d3 + d4;
+        t[3 * ostep + c] = -2 * d1 - d2 + 2 * d3 + d4;
+        t[4 * ostep + c] = 2 * d1 - d2 - 2 * d3 + d4;
+        t[5 * ostep + c] = 4 * d1 - 5 * d3 + d5;
+    }
+}
+
+static void bt_f2(const float *d, float *t, int n, size_t step, size_t ostep) {
+    for (int c = 0; c < n; ++c) {
+        const float d0 = d[c], d1 = d[step + c], d2 = d[2 * step + c], d3 = d[3 * step + c];
+        t[c] = d0 - d2;
+        t[ostep + c] = d1 + d2;
+        t[2 * ostep + c] = d2 - d1;
+        t[3 * ostep + c] = d1 - d3;
+    }
+}
+
+static void at_f4(const float *m, float *o, int n, size_t step, size_t ostep) {
+    for (int c = 0; c < n; ++c) {
+        const float m0 = m[c], m1 = m[step + c], m2 = m[2 * step + c], m3 = m[3 * step + c], m4 = m[4 * step + c],
+                    m5 = m[5 * step + c];
+        o[c] = m0 + m1 + m2 + m3 + m4;
+        o[ostep + c] = m1 - m2 + 2 * m3 - 2 * m4;
+        o[2 * ostep + c] = m1 + m2 + 4 * m3 + 4 * m4;
+        o[3 * ostep + c] = m1 - m2 + 8 * m3 - 8 * m4 + m5;
+    }
+}
+
+static void at_f2(const float *m, float *o, int n, size_t step, size_t ostep) {
+    for (int c = 0; c < n; ++c) {
+        const float m0 = m[c], m1 = m[step + c], m2 = m[2 * step + c], m3 = m[3 * step + c];
+        o[c] = m0 + m1 + m2;
+        o[ostep + c] = m1 - m2 - m3;
+    }
+}
+
+/* U[xi] = G g G^T of each (oc, ic) kernel, as [xi][panel][ic][16] panels. */
+static float *winograd_weights(const uint16_t *w16, int OC, int IC, int F) {
+    const int T = F + 2, np = (OC + NR - 1) / NR;
+    static const float g4[6][3] = {{0.25f, 0, 0},
+                                   {-1.0f / 6, -1.0f / 6, -1.0f / 6},
+                                   {-1.0f / 6, 1.0f / 6, -1.0f / 6},
+                                   {1.0f / 24, 1.0f / 12, 1.0f / 6},
+                                   {1.0f / 24, -1.0f / 12, 1.0f / 6},
+                                   {0, 0, 1}};
+    static const float g2[4][3] = {{1, 0, 0}, {0.5f, 0.5f, 0.5f}, {0.5f, -0.5f, 0.5f}, {0, 0, 1}};
+    float *u = aligned(sizeof(float) * (size_t)T * T * np * NR * IC);
+    if (!u) return NULL;
+#pragma omp parallel for schedule(static)
+    for (int oc = 0; oc < np * NR; ++oc)
+        for (int ic = 0; ic < IC; ++ic) {
+            float g[3][3], t[6][3], r[6][6];
+            for (int a = 0; a < 3; ++a)
+                for (int b = 0; b < 3; ++b)
+                    g[a][b] = oc < OC ? half_to_float(w16[(((size_t)oc * IC + ic) * 3 + a) * 3 + b]) : 0.0f;
+            for (int i = 0; i < T; ++i)
+                for (int b = 0; b < 3; ++b) {
+                    float s = 0;
+                    for (int a = 0; a < 3; ++a) s += (F == 4 ? g4[i][a] : g2[i][a]) * g[a][b];
+                    t[i][b] = s;
+                }
+            for (int i = 0; i < T; ++i)
+                for (int j = 0; j < T; ++j) {
+                    float s = 0;
+                    for (int b = 0; b < 3; ++b) s += t[i][b] * (F == 4 ? g4[j][b] : g2[j][b]);
+                    r[i][j] = s;
+                }
+            const int p = oc / NR, lane = oc % NR;
+            for (int xi = 0; xi < T * T; ++xi)
+                u[(((size_t)xi * np + p) * IC + ic) * NR + lane] = r[xi / T][xi % T];
+        }
+    return u;
+}
+
+int refk_winograd_mt(const uint16_t *w16, int OC, int IC, const float *x, int NI, int H, int W, int pad, int F,
+                     float *y) {
+    const int T = F + 2, XI = T * T;
+    const int OH = H + 2 * pad - 2, OW = W + 2 * pad - 2;
+    const int TH = (OH + F - 1) / F, TW = (OW + F - 1) / F, tiles = NI * TH * TW;
+    const int np = (OC + NR - 1) / NR;
+    float *u = cached_panels(w16, OC, IC, 100 + F);
+    if (!u) {
+        u = winograd_weights(w16, OC, IC, F);
+        if (!u) return 1;
+        keep_panels(w16, OC, IC, 100 + F, u);
+    }
+    /* Channels-last padded image, V [xi][tile][IC], M [xi][tile][OC]. */
+    const int PH = TH * F + 2, PW = TW * F + 2;
+    float *xp = aligned(sizeof(float) * (size_t)NI * PH * PW * IC);
+    float *v = aligned(sizeof(float) * (size_t)XI * tiles * IC);
+    float *m = aligned(sizeof(float) * (size_t)XI * tiles * OC);
+    if (!xp || !v || !m) return 1;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < NI * PH; ++r) {
+        const int n = r / PH, iy = r % PH - pad;
+        for (int ix = 0; ix < PW; ++ix) {
+            float *dst = xp + ((size_t)r * PW + ix) * IC;
+            const int sx = ix - pad;
+            if (iy < 0 || iy >= H || sx < 0 || sx >= W) {
+                memset(dst, 0, sizeof(float) * IC);
+                continue;
+            }
+            for (int ic = 0; ic < IC; ++ic) dst[ic] = x[(((size_t)n * IC + ic) * H + iy) * W + sx];
+        }
+    }
+    /* Inputs: V = B^T d B per tile, the channels as lanes. */
+#pragma omp parallel
+    {
+        float *rows = aligned(sizeof(float) * 36 * (size_t)IC), *vt = aligned(sizeof(float) * 36 * (size_t)IC);
+#pragma omp for schedule(static)
+        for (int t = 0; t < tiles; ++t) {
+            const int n = t / (TH * TW), ty = (t / TW) % TH, tx = t % TW;
+            const float *patch = xp + (((size_t)n * PH + ty * F) * PW + tx * F) * IC;
+            for (int i = 0; i < T; ++i) /* columns of each row of the patch */
+                (F == 4 ? bt_f4 : bt_f2)(patch + (size_t)i * PW * IC, rows + (size_t)i * T * IC, IC, IC, IC);
+            for (int j = 0; j < T; ++j) /* then down the columns */
+                (F == 4 ? bt_f4 : bt_f2)(rows + (size_t)j * IC, vt + (size_t)j * IC, IC, (size_t)T * IC,
+                                         (size_t)T * IC);
+            for (int xi = 0; xi < XI; ++xi)
+                memcpy(v + ((size_t)xi * tiles + t) * IC, vt + (size_t)xi * IC, sizeof(float) * IC);
+        }
+        free(rows);
+        free(vt);
+    }
+    /* The products M[xi] = V[xi] U[xi]^T: blocks of 48 tiles of one xi. */
+    const int mblocks = (tiles + 47) / 48;
+    const int chunks = column_chunks(mblocks * XI, np), per = chunk_panels(np, chunks);
+    int bad = 0;
+#pragma omp parallel
+    {
+        float *ap = aligned(sizeof(float) * 48 * KC);
+        float tile[MR * NR] __attribute__((aligned(64)));
+        if (!ap) bad = 1;
+#pragma omp for schedule(dynamic)
+        for (int w = 0; w < XI * mblocks * chunks; ++w) {
+            if (!ap) continue;
+            const int xi = w / (mblocks * chunks), rest = w % (mblocks * chunks);
+            const int mb = rest / chunks, p0 = (rest % chunks) * per, p1 = p0 + per < np ? p0 + per : np;
+            const int m0 = mb * 48, rowsn = tiles - m0 < 48 ? tiles - m0 : 48;
+            const float *vx = v + (size_t)xi * tiles * IC;
+            const float *ux = u + (size_t)xi * np * NR * IC;
+            for (int k0 = 0; k0 < IC; k0 += KC) {
+                const int kc = IC - k0 < KC ? IC - k0 : KC;
+                for (int i0 = 0; i0 < rowsn; i0 += MR)
+                    for (int k = 0; k < kc; ++k)
+                        for (int i = 0; i < MR; ++i)
+                            ap[((size_t)(i0 / MR) * kc + k) * MR + i] =
+                                i0 + i < rowsn ? vx[(size_t)(m0 + i0 + i) * IC + k0 + k] : 0.0f;
+                block_product_cols(ap, ux, OC, IC, k0, kc, rowsn, m + ((size_t)xi * tiles + m0) * OC, tile, p0, p1);
+            }
+        }
+        free(ap);
+    }
+    /* Outputs: Y = A^T M A per tile, the output channels as lanes. */
+#pragma omp parallel
+    {
+        float *mt = aligned(sizeof(float) * 36 * (size_t)OC), *half = aligned(sizeof(float) * 24 * (size_t)OC);
+        float *out = aligned(sizeof(float) * 16 * (size_t)OC);
+#pragma omp for schedule(static)
+        for (int t = 0; t < tiles; ++t) {
+            const int n = t / (TH * TW), ty = (t / TW) % TH, tx = t % TW;
+            for (int xi = 0; xi < XI; ++xi)
+                memcpy(mt + (size_t)xi * OC, m + ((size_t)xi * tiles + t) * OC, sizeof(float) * OC);
+            for (int i = 0; i < T; ++i) /* along each row of M */
+                (F == 4 ? at_f4 : at_f2)(mt + (size_t)i * T * OC, half + (size_t)i * F * OC, OC, OC, OC);
+            for (int j = 0; j < F; ++j) /* then down its columns */
+                (F == 4 ? at_f4 : at_f2)(half + (size_t)j * OC, out + (size_t)j * OC, OC, (size_t)F * OC,
+                                         (size_t)F * OC);
+            for (int a = 0; a < F; ++a)
+                for (int b = 0; b < F; ++b) {
+                    const int oy = ty * F + a, ox = tx * F + b;
+                    if (oy < OH && ox < OW)
+                        memcpy(y + (((size_t)n * OH + oy) * OW + ox) * OC, out + ((size_t)a * F + b) * OC,
+                               sizeof(float) * OC);
+                }
+        }
+        free(mt);
+        free(half);
+        free(out);
+    }
+    free(xp);
+    free(v);
+    free(m);
     return bad;
 }

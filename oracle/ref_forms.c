@@ -308,6 +308,31 @@ void rf_group_norm(const float *x, float *y, int N, int C, long HW, int groups, 
         }
 }
 
+/* Layer normalisation of rows of C numbers (norm.cc:148-175): mean and variance
+ * summed in double, then gamma and beta per column (when given). */
+void rf_norm(const float *x, float *y, long rows, int C, float eps, const float *gamma, const float *beta) {
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) {
+        const float *xr = x + (size_t)r * C;
+        float *yr = y + (size_t)r * C;
+        double sum = 0.0;
+        for (int i = 0; i < C; ++i) sum += (double)xr[i];
+        const float mean = (float)(sum / (double)C);
+        double sq = 0.0;
+        for (int i = 0; i < C; ++i) {
+            const float d = xr[i] - mean;
+            sq += (double)(d * d);
+        }
+        const float scale = 1.0f / sqrtf((float)(sq / (double)C) + eps);
+        for (int i = 0; i < C; ++i) {
+            float v = (xr[i] - mean) * scale;
+            if (gamma) v = v * gamma[i];
+            if (beta) v = v + beta[i];
+            yr[i] = v;
+        }
+    }
+}
+
 /* ---- the quantized linear layer (bits = 8), quant.h / quant.cc ---------------
  * The inputs: per row, per group of `group` numbers of k (the last group
  * short, its missing numbers standing for zeros): the least and the greatest

@@ -59,6 +59,7 @@ def load() -> ctypes.CDLL:
         lib.rf_quantize_inputs.argtypes = [P, i, i, i, i, P, P, P]
         lib.rf_qfold.argtypes = [P, P, P, i, P, P, P, i, i, i, P, i]
         lib.rf_expf.argtypes = [P, P, ctypes.c_long]
+        lib.rf_norm.argtypes = [P, P, ctypes.c_long, i, ctypes.c_float, P, P]
         lib.rf_threads.restype = i
         lib.rf_set_threads.argtypes = [i]
         _lib = lib
@@ -128,6 +129,17 @@ def group_norm(x, groups: int, eps: float, gamma=None, beta=None, silu=False) ->
     b = np.ascontiguousarray(beta, dtype=np.float32) if beta is not None else None
     load().rf_group_norm(_p(x), _p(y), n, c, hw, groups, eps, _p(g) if g is not None else None,
                          _p(b) if b is not None else None, 1 if silu else 0)
+    return y
+
+
+def norm(x, eps: float, gamma=None, beta=None, out=None) -> np.ndarray:
+    """Rows (the last dimension) of x float32 normalised, then gamma and beta (norm.cc's form)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x) if out is None else out
+    g = np.ascontiguousarray(gamma, dtype=np.float32) if gamma is not None else None
+    b = np.ascontiguousarray(beta, dtype=np.float32) if beta is not None else None
+    load().rf_norm(_p(x), _p(y), x.size // x.shape[-1], x.shape[-1], eps, _p(g) if g is not None else None,
+                   _p(b) if b is not None else None)
     return y
 
 
