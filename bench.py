@@ -161,30 +161,42 @@ class HotOps:
         self.ops = self._ops()
 
     def _ops(self):
-        """(name, work, bound, fn(set)) -- work in FLOPs (tensor) or bytes (hbm), the reference's convention."""
+        """(name, work, bound, fn(set)) -- BASELINE configs 1-3, work in FLOPs (tensor) or the least bytes
+        moved (hbm), by the reference's convention (bench.cc:82-124, profile.cc:65-81)."""
         sdb = self.sdb
         ops = []
-        ops.append(("linear_4096x320x1280_bias", 4096 * 1280 * 4 + 4096 * 320 * 4 + 1280 * 320 * 2, "hbm",
+        ops.append(("config1_linear_4096x320x1280_bias", 4096 * 1280 * 4 + 4096 * 320 * 4 + 1280 * 320 * 2 + 1280 * 4,
+                    "hbm",
                     lambda s: sdb.mul_mat(self.w_lin, s["x_lin"], s["y_lin"], chain=sdb.Chain().add(self.b_lin))))
-        for i, cv in enumerate(self.convs):
+        for i, (tag, cv) in enumerate(zip("abc", self.convs)):
             c, hw = cv["c"], cv["hw"]
             flops = 2 * 9 * c * c * hw * hw
-            ops.append((f"conv3x3_{c}x{hw}x{hw}_bias", flops, "tensor",
-                        lambda s, i=i, cv=cv: sdb.conv2d(cv["w"], s[f"x_conv{i}"], (1, 1), (1, 1), (1, 1),
-                                                         out=s[f"y_conv{i}"], chain=sdb.Chain().add(cv["b"]))))
-            gn_bytes = 2 * c * hw * hw * 4
-            ops.append((f"groupnorm32_silu_{c}x{hw}x{hw}", gn_bytes, "hbm",
-                        lambda s, i=i, cv=cv: sdb.group_norm(s[f"y_conv{i}"], 32, 1e-5, out=s[f"z_conv{i}"],
-                                                             chain=sdb.Chain().mul(cv["gamma"]).add(cv["beta"]).silu())))
-        for lk in (4096, 77):
+            # 8x8: the weights' bytes bound it (SURVEY config 2c: 63 FLOP/B).
+            work, bound = (flops, "tensor") if hw > 8 else (c * c * 9 * 2 + 2 * c * hw * hw * 4, "hbm")
+
+            def conv_gn(s, i=i, cv=cv):
+                sdb.conv2d(cv["w"], s[f"x_conv{i}"], (1, 1), (1, 1), (1, 1), out=s[f"y_conv{i}"],
+                           chain=sdb.Chain().add(cv["b"]))
+                sdb.group_norm(s[f"y_conv{i}"], 32, 1e-5, out=s[f"z_conv{i}"],
+                               chain=sdb.Chain().mul(cv["gamma"]).add(cv["beta"]).silu())
+
+            ops.append((f"config2{tag}_conv3x3_{c}x{hw}x{hw}_bias_gn32_silu", work, bound, conv_gn))
+        for tag, lk in (("a", 4096), ("b", 77)):
             flops = 4 * 40 * 8 * 4096 * lk
-            ops.append((f"attention_h8d40_q4096_k{lk}_residual", flops, "tensor" if lk > 256 else "hbm",
-                        lambda s, lk=lk: sdb.attention_heads(
-                            s[f"q{lk}"], s[f"k{lk}"], s[f"v{lk}"], 8, 8, 40 ** -0.5, out=s[f"o{lk}"],
-                            chain=sdb.Chain().add(s[f"r{lk}"], nb=[1, 40, 320, 4096 * 320]))))
-        # Memory-bound attention's work is its bytes: q, k, v, residual in, out.
-        name, _, bound, fn = ops[-1]
-        ops[-1] = (name, (4096 * 320 * 3 + 77 * 320 * 2) * 4, bound, fn)
+            for residual in (False, True):
+                if lk > 256:
+                    work, bound = flops, "tensor"
+                else:   # cross-attention: q, k, v (and the residual) in, the output out
+                    work, bound = (4096 * 320 * (3 if residual else 2) + 2 * 77 * 320) * 4, "hbm"
+
+                def attn(s, lk=lk, residual=residual):
+                    ch = sdb.Chain().add(s[f"r{lk}"], nb=[1, 40, 320, 4096 * 320]) if residual else None
+                    sdb.attention_heads(s[f"q{lk}"], s[f"k{lk}"], s[f"v{lk}"], 8, 8, 40 ** -0.5, out=s[f"o{lk}"],
+                                        chain=ch)
+
+                kind = "self" if lk > 256 else "cross"
+                ops.append((f"config3{tag}_{kind}_attention_h8d40_q4096_k{lk}" + ("_residual" if residual else ""),
+                            work, bound, attn))
         return ops
 
     def step(self, i: int, events=None):
@@ -611,6 +623,55 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def hot_op_configs(torch, dev, reps: int = 30) -> dict:
+    """BASELINE configs 1-3 timed op by op on this GPU (CUDA-graph replays over three rotating input
+    sets larger than L2), each against its roofline: tensor-bound ops by the reference's FLOP count over
+    the measured bf16 burst peak, memory-bound ones by their least bytes over the measured HBM copy rate
+    (MEASURED_PEAKS.json)."""
+    work = HotOps(dev, seed=1234)
+    cap = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(cap):
+        for i in range(3):
+            work.step(i)
+    torch.cuda.synchronize()
+    graphs = []
+    for _, _, _, fn in work.ops:
+        gs = []
+        for sidx in range(work.SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                fn(work.sets[sidx])
+            gs.append(g)
+        graphs.append(gs)
+    torch.cuda.synchronize()
+    peaks = measured_peaks()
+    profiles = {p.stem: str(p.relative_to(ROOT)) for p in (ROOT / "profiles").glob("*.md")}
+    out = {}
+    for (name, units, bound, _), gs in zip(work.ops, graphs):
+        for i in range(3):
+            gs[i % work.SETS].replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            gs[i % work.SETS].replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if bound == "tensor":
+            achieved, peak, unit = units / (ms * 1e-3) / 1e12, peaks["bf16_tflops"], "TFLOP/s"
+        else:
+            achieved, peak, unit = units / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+        key = name.split("_", 1)[0]
+        prof = [v for k, v in profiles.items() if k.startswith(key)]
+        out[name] = {"ms": round(ms, 5), "bound": bound, "work": units, "achieved": round(achieved, 1),
+                     "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+                     "peak_source": peaks["source"] + " (burst)" if bound == "tensor" else peaks["source"],
+                     "profile": prof[0] if prof else None}
+    del graphs
+    torch.cuda.synchronize()
+    return out
+
+
 def run_hot_ops(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks) -> None:
     import sdb
 
@@ -747,8 +808,9 @@ class OpClock:
     replays (device time only).  Each call has its class and algorithmic work (FLOPs in the
     reference's convention for products, bytes read + written for the rest)."""
 
-    NAMES = ("conv2d_nhwc", "mul_mat", "mul_mat_gated", "attention_heads", "group_norm_nhwc", "norm",
-             "concat_channels_nhwc", "upscale_nearest_nhwc", "timestep_embedding")
+    NAMES = ("conv2d_nhwc", "conv2d_nhwc_normed", "mul_mat", "mul_mat_normed", "mul_mat_gated", "attention_heads",
+             "group_norm_nhwc", "group_norm_stats", "norm", "concat_channels_nhwc", "upscale_nearest_nhwc",
+             "timestep_embedding")
 
     def __init__(self, sdb, torch):
         self.sdb, self.torch = sdb, torch
@@ -757,14 +819,17 @@ class OpClock:
 
     @staticmethod
     def work(name, args, out):
-        if name == "conv2d_nhwc":
+        if name in ("conv2d_nhwc", "conv2d_nhwc_normed"):
             w = args[0]
             oc, ic, kh, kw = w.shape
             n, oh, ow, _ = out.shape
-            stride = args[2] if len(args) > 2 else (1, 1)
+            stride = args[3 if name == "conv2d_nhwc_normed" else 2] if len(args) > (3 if name == "conv2d_nhwc_normed"
+                                                                                    else 2) else (1, 1)
             cls = "conv1x1" if kh == 1 else ("conv3x3_s2" if stride[0] == 2 else "conv3x3")
             return cls, 2 * kh * kw * ic * oc * oh * ow * n
-        if name in ("mul_mat", "mul_mat_gated"):
+        if name == "group_norm_stats":
+            return "groupnorm", 4 * args[0].numel()
+        if name in ("mul_mat", "mul_mat_gated", "mul_mat_normed"):
             w, x = args[0], args[1]
             k = w.shape[1]
             m = x.numel() // k
@@ -797,10 +862,10 @@ class OpClock:
 
     @staticmethod
     def shape_key(name, args, out) -> str:
-        if name == "conv2d_nhwc":
+        if name in ("conv2d_nhwc", "conv2d_nhwc_normed"):
             w, x = args[0], args[1]
             return f"conv {w.shape[1]}->{w.shape[0]} k{w.shape[2]} @{x.shape[1]}x{x.shape[2]}x{x.shape[0]}"
-        if name in ("mul_mat", "mul_mat_gated"):
+        if name in ("mul_mat", "mul_mat_gated", "mul_mat_normed"):
             w, x = args[0], args[1]
             return f"{'geglu' if name == 'mul_mat_gated' else 'linear'} M{x.numel() // w.shape[1]} K{w.shape[1]} N{w.shape[0]}"
         if name == "attention_heads":
@@ -1086,6 +1151,25 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     d2h = h_out.numel() * 4
     # The VAE decode of this rank's latents, captured once and replayed.
     vae_ms, vae_flops = measure_vae(torch, dev, sampler.x, barrier, max_over_ranks)
+    # The job's final latents to rank 0 (NCCL over NVLink): the gather BASELINE config 4's image sharding
+    # ends with, timed on the device as the max over ranks.
+    gather = None
+    if dist is not None and world > 1:
+        lat_all = torch.empty(world * per, *sampler.x.shape[1:], device=dev) if rank == 0 else None
+        for _ in range(2):
+            dist.gather(sampler.x.contiguous(), [lat_all[i * per:(i + 1) * per] for i in range(world)]
+                        if rank == 0 else None, dst=0)
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        dist.gather(sampler.x.contiguous(), [lat_all[i * per:(i + 1) * per] for i in range(world)]
+                    if rank == 0 else None, dst=0)
+        g1.record()
+        torch.cuda.synchronize()
+        gather = {"ms": max_over_ranks(g0.elapsed_time(g1)), "bytes": world * sampler.x.numel() * 4,
+                  "how": "torch.distributed.gather over NCCL of every rank's latents to rank 0"}
+        del lat_all
     del sampler
     torch.cuda.empty_cache()
     # One image's latency: the same step on a CFG batch of 2 alone.
@@ -1121,6 +1205,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     if rank != 0:
         return
 
+    configs = hot_op_configs(torch, dev)
     peaks = measured_peaks()
     step_flops = net.flops(2 * per, 64, 64)
     dom = max((k for k in classes if CLASSES[k] == "tensor"), key=lambda k: classes[k]["ms"])
@@ -1141,6 +1226,8 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
         "config": unet_config(world, args.tune),
         "unet_ms_per_step": ms,
         "unet_ms_per_step_one_image": ms1,
+        "configs": configs,
+        "latent_gather": gather,
         "vae_ms": vae_ms,
         "vae_tflops": vae_flops / (vae_ms * 1e-3) / 1e12,
         "imgs_per_s": world * per * 1e3 / (SAMPLER_STEPS * ms + vae_ms),

@@ -137,6 +137,38 @@ int sdb_norm(const sdb_tensor *x, const sdb_tensor *dst, float eps, const sdb_ch
 int sdb_group_norm_no_alloc(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps,
                             const sdb_chain *chain, void *stream);
 
+/* ---- GroupNorm fused into the operation that reads its output -----------
+ * An extension of the reference, which computes GROUP_NORM as a node of its
+ * own (norm.cc:100-140) between a convolution and the next: here the group
+ * statistics are computed once (sdb_group_norm_stats: warp-shuffle and
+ * cross-CTA reductions in double, the image's last CTA folding them) and the
+ * normalisation (x - mean) * scale * gamma + beta, then SiLU, is applied as
+ * the next operation reads its input -- in the Winograd input transform or
+ * the split of the activations -- so the normalised tensor is never written.
+ * The numbers the operation sees are those sdb_group_norm would have written
+ * for a channels-last image with the chain (gamma, beta[, SiLU]).
+ *
+ * stats: [N][groups][2] FP32 -- mean, 1 / sqrt(variance + eps) per image and
+ * group of C / groups consecutive channels (C % groups == 0). */
+typedef struct sdb_norm_in {
+    const float *stats;
+    const float *gamma;  /* [C] and beta [C], or both NULL */
+    const float *beta;
+    int32_t groups;
+    int32_t silu;
+} sdb_norm_in;
+/* The statistics of x, a channels-last image [W, H, C, N] (nb[2] = 4), into
+ * stats (device memory of N * groups * 2 floats). */
+int sdb_group_norm_stats(const sdb_tensor *x, int32_t groups, float eps, float *stats, void *stream);
+/* sdb_conv2d of the normalised x (channels-last, or any layout on the Winograd
+ * path), then the chain. */
+int sdb_conv2d_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const int32_t params[6],
+                      const sdb_norm_in *norm, const sdb_chain *chain, void *stream);
+/* sdb_mul_mat of the normalised x: x [C, P, N] -- P positions (rows) of each of
+ * N images, C channels along a row. */
+int sdb_mul_mat_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_norm_in *norm,
+                       const sdb_chain *chain, void *stream);
+
 /* ---- the graph's data-movement nodes (device-resident runner) -----------
  * The reference takes only CONV_2D, MUL_MAT, FLASH_ATTN_EXT, GROUP_NORM and
  * NORM and leaves every other node of stable-diffusion.cpp's UNet graph to

@@ -445,6 +445,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnAr
 // O = O0 2^(m0 - m) + O1 2^(m1 - m), l likewise, then O / l with the chain.
 // A block's weights are summed in FP32 as a pairwise tree (at most log2(BK)
 // roundings), blocks in double.
+//
+// Each product lands in ONE accumulator: its lo products (hi.lo and lo.hi,
+// whose lo operands carry the split's 2^11) are issued first, then the first
+// hi.hi product with tcgen05.mma's input scale 2^-11 (mma_f16_scale_lo), the
+// others plain -- hi.hi + (hi.lo + lo.hi) 2^-11 with no second accumulator to
+// read and no combining instruction.  S keeps one accumulator per 64 dims
+// (the first also holding the lo sum), the output one per block.  Tensor
+// memory: 2 NSC BK + 2 DVC columns (224 for 40-dim heads).
 struct AttnWgLayout {
     int q_hi, q_lo, stage0, stage_bytes, k_lo, v_hi, v_lo, p0, p_bytes, merge_o, merge_m, merge_l, bars, total;
     __host__ __device__ AttnWgLayout(int dp, int dvc, int bk) {
@@ -458,7 +466,7 @@ struct AttnWgLayout {
         v_lo = 2 * kb + vb;
         stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
         p_bytes = 2 * kAttnQ * bk * 2;                     // hi then lo plane of one warpgroup's P
-        p0 = stage0 + kStagesKV * stage_bytes;           // [2] buffers
+        p0 = (stage0 + kStagesKV * stage_bytes + 1023) / 1024 * 1024;   // [2] buffers, 1024-aligned (swizzle)
         merge_o = p0 + 2 * p_bytes;                      // [128][dvc] floats of warpgroup 1
         merge_m = merge_o + kAttnQ * dvc * 4;            // [128] floats
         merge_l = merge_m + kAttnQ * 4;                  // [128] doubles
@@ -467,9 +475,18 @@ struct AttnWgLayout {
     }
 };
 
+// Tensor-memory columns an allocation takes: a power of two, at least 32.
+__host__ __device__ constexpr int tmem_columns(int used) {
+    return used <= 32 ? 32 : used <= 64 ? 64 : used <= 128 ? 128 : used <= 256 ? 256 : 512;
+}
+
 template <int BK, int NSC, int DVC>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const AttnArgs a) {
     constexpr int OCH = DVC / 16;
+    constexpr int kCols = tmem_columns(2 * NSC * BK + 2 * DVC);
+    // P (the A operand of P V) in the 128-byte swizzle when a row of it is 128 bytes (64 keys): the
+    // tensor core reads swizzled rows at full shared-memory width, no-swizzle core matrices slower.
+    constexpr bool kPSwizzle = BK == 64;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const AttnWgLayout L(a.dp, DVC, BK);
@@ -494,7 +511,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
     const int batch = blockIdx.z;
     const int khead = head / (a.h / a.hk);
     const int nblk = (a.lk + BK - 1) / BK;
-    constexpr int sbuf = (NSC + 1) * BK;              // tensor-memory columns of one S buffer
+    constexpr int sbuf = NSC * BK;                    // tensor-memory columns of one S buffer
     const uint32_t base = smem_u32(smem);
 
     if (threadIdx.x == 0) {
@@ -513,13 +530,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
         *abort = 0;
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    if (warp == 1) tmem_alloc(tmem_slot, kCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto t_o_hi = [&](int wg) { return tmem + 2 * sbuf + wg * 2 * DVC; };
-    auto t_o_lo = [&](int wg) { return tmem + 2 * sbuf + wg * 2 * DVC + DVC; };
+    auto t_o = [&](int wg) { return tmem + 2 * sbuf + wg * DVC; };
 
     if (warp == 0) {
         // ------------------------------------------------ bulk-copy producer
@@ -562,14 +578,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
                 const int s = j % kStagesKV;
                 const uint32_t st = base + L.stage0 + s * L.stage_bytes;
                 const uint32_t sb = tmem + (j & 1) * sbuf;
+                // The lo products into the first accumulator, ...
                 for (int kk = 0; kk < a.dp / 16; ++kk) {
                     const uint64_t qh = desc_noswizzle(base + L.q_hi + kk * 2 * q_lbo, q_lbo, 128);
                     const uint64_t ql = desc_noswizzle(base + L.q_lo + kk * 2 * q_lbo, q_lbo, 128);
                     const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, kv_sbo);
                     const uint64_t kl = desc_noswizzle(st + L.k_lo + kk * 2 * k_lbo, k_lbo, kv_sbo);
-                    mma_f16(sb + (kk >> 2) * BK, qh, kh, id_s, (kk & 3) ? 1u : 0u);
-                    mma_f16(sb + NSC * BK, qh, kl, id_s, kk > 0 ? 1u : 0u);
-                    mma_f16(sb + NSC * BK, ql, kh, id_s, 1u);
+                    mma_f16(sb, qh, kl, id_s, kk > 0 ? 1u : 0u);
+                    mma_f16(sb, ql, kh, id_s, 1u);
+                }
+                // ... then hi.hi, 64 dims an accumulator, the first scaling the lo sum by 2^-11.
+                for (int kk = 0; kk < a.dp / 16; ++kk) {
+                    const uint64_t qh = desc_noswizzle(base + L.q_hi + kk * 2 * q_lbo, q_lbo, 128);
+                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, kv_sbo);
+                    if (kk == 0) mma_f16_scale_lo(sb, qh, kh, id_s);
+                    else mma_f16(sb + (kk >> 2) * BK, qh, kh, id_s, (kk & 3) ? 1u : 0u);
                 }
                 mma_commit(&s_full[j & 1]);
             };
@@ -594,15 +617,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
                 const int s = j % kStagesKV;
                 const uint32_t st = base + L.stage0 + s * L.stage_bytes;
                 const uint32_t pb = base + L.p0 + wg * L.p_bytes;
+                // The block's P V into the warpgroup's fresh accumulator: lo products, then hi.hi.
                 for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ph = desc_noswizzle(pb + kk * 256, 128, p_sbo);
-                    const uint64_t pl = desc_noswizzle(pb + kAttnQ * BK * 2 + kk * 256, 128, p_sbo);
+                    const uint64_t ph = kPSwizzle ? desc_kmajor_sw128(pb + kk * 32) : desc_noswizzle(pb + kk * 256, 128, p_sbo);
+                    const uint64_t pl = kPSwizzle ? desc_kmajor_sw128(pb + kAttnQ * BK * 2 + kk * 32)
+                                                  : desc_noswizzle(pb + kAttnQ * BK * 2 + kk * 256, 128, p_sbo);
                     const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
                     const uint64_t vl = desc_noswizzle(st + L.v_lo + kk * 256, 128, BK * 16);
-                    const uint32_t acc = kk > 0 ? 1u : 0u;
-                    mma_f16(t_o_hi(wg), ph, vh, id_pv, acc);
-                    mma_f16(t_o_lo(wg), ph, vl, id_pv, acc);
-                    mma_f16(t_o_lo(wg), pl, vh, id_pv, 1u);
+                    mma_f16(t_o(wg), ph, vl, id_pv, kk > 0 ? 1u : 0u);
+                    mma_f16(t_o(wg), pl, vh, id_pv, 1u);
+                }
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t ph = kPSwizzle ? desc_kmajor_sw128(pb + kk * 32) : desc_noswizzle(pb + kk * 256, 128, p_sbo);
+                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
+                    if (kk == 0) mma_f16_scale_lo(t_o(wg), ph, vh, id_pv);
+                    else mma_f16(t_o(wg), ph, vh, id_pv, 1u);
                 }
                 mma_commit(&o_full[wg]);
                 mma_commit(&kv_empty[s]);
@@ -635,12 +664,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
             tc_fence_after();
 #pragma unroll
             for (int ch = 0; ch < OCH; ++ch) {
-                float oh[16], ol[16];
-                tmem_ld16(t_o_hi(wg) + lane_off + ch * 16, oh);
-                tmem_ld16(t_o_lo(wg) + lane_off + ch * 16, ol);
+                float oh[16];
+                tmem_ld16(t_o(wg) + lane_off + ch * 16, oh);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[ch * 16 + i] += fmaf(ol[i], kLoUnscale, oh[i]);
+                for (int i = 0; i < 16; ++i) o[ch * 16 + i] += oh[i];
             }
             return true;
         };
@@ -651,16 +679,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
             tc_fence_after();
             const uint32_t sb = tmem + wg * sbuf + lane_off;
             float s[BK];
+            // The block's scores, every 16 keys' load issued before the one wait.
 #pragma unroll
-            for (int c = 0; c < BK; c += 16) {
-                // The lo accumulator and the hi ones of these 16 keys, one wait.
-                float lo[16], h0[16], h1[16];
-                tmem_ld16(sb + NSC * BK + c, lo);
-                tmem_ld16(sb + c, h0);
-                if (NSC > 1) tmem_ld16(sb + BK + c, h1);
+            for (int c = 0; c < BK; c += 16) tmem_ld16(sb + c, *reinterpret_cast<float(*)[16]>(s + c));
+            if (NSC > 1) {
+                float h1[BK];
+#pragma unroll
+                for (int c = 0; c < BK; c += 16) tmem_ld16(sb + BK + c, *reinterpret_cast<float(*)[16]>(h1 + c));
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) s[c + i] = fmaf(lo[i], kLoUnscale, NSC > 1 ? h0[i] + h1[i] : h0[i]);
+                for (int i = 0; i < BK; ++i) s[i] += h1[i];
+            } else {
+                tmem_ld_wait();
             }
             const int valid = min(BK, a.lk - j * BK);
             const bool full = valid == BK;
@@ -703,7 +733,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
                 for (int i = 0; i < 8; ++i) p8[i] = s[c * 8 + i];
                 uint4 h4, l4;
                 split8_inrange(p8, h4, l4);
-                const uint32_t off = static_cast<uint32_t>((r >> 3) * (BK * 16) + c * 128 + (r & 7) * 16);
+                // Rows of 64 keys (128 bytes) in the 128-byte swizzle (16-byte chunk c of row r at
+                // chunk c ^ (r mod 8)), else the no-swizzle core matrices of 8 rows x 16 bytes.
+                const uint32_t off = kPSwizzle ? static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 +
+                                                                       ((c ^ (r & 7)) * 16))
+                                               : static_cast<uint32_t>((r >> 3) * (BK * 16) + c * 128 + (r & 7) * 16);
                 st_shared_v4(pbuf + off, h4);
                 st_shared_v4(pbuf + kAttnQ * BK * 2 + off, l4);
             }
@@ -771,7 +805,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc(tmem, kCols);
     }
 }
 
@@ -860,7 +894,7 @@ int launch_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_t
     *taken = false;
     const int nsc = (a.dp + 63) / 64;
     auto fits = [&](int bk) {
-        return 2 * (nsc + 1) * bk + 4 * DVC <= 512 && AttnWgLayout(a.dp, DVC, bk).total + 1024 <= 227 * 1024;
+        return 2 * nsc * bk + 2 * DVC <= 512 && AttnWgLayout(a.dp, DVC, bk).total + 1024 <= 227 * 1024;
     };
     if (nsc == 1 && fits(64)) {
         *taken = true;

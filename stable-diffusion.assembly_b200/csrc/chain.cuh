@@ -48,6 +48,74 @@ __device__ __forceinline__ float gelu(float x) {
     return __fdiv_rn(x, 1.0f + exponential(-1.5957691216057308f * y));
 }
 
+// SiLU of the GroupNorm apply pass and its prologue form, x / (1 + e^-x) as the reference writes it (scalar_math.h:54-58), with
+// e^-x by the same Cody-Waite reduction to |r| <= ln2 / 2 but 2^(r log2 e) from the hardware's
+// ex2 (relative error about 2^-22) in place of the degree-6 polynomial, and the quotient by the
+// hardware's reciprocal refined by one Newton step: within a few 2^-23 of the exact form, at a
+// third of the instructions -- the pass is bound by issue, not by memory.
+__device__ __forceinline__ float silu_apply(float x) {
+    // Clamped at 87.3 on both sides (the reference's upper clamp is 88.73): 2^n stays finite, so
+    // the Newton step never meets an infinity; past 87.3 the quotient is below FP32's normal range.
+    const float t = fminf(fmaxf(-x, -87.3f), 87.3f);
+    const float magic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+    const float z = fmaf(t, 1.44269504088896341f, magic);
+    const float n = z - magic;
+    float r = fmaf(n, -0.693359375f, t);
+    r = fmaf(n, 2.12194440e-4f, r);
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(r * 1.44269504088896341f));
+    e *= __uint_as_float(static_cast<uint32_t>(__float_as_int(z) - 0x4b400000 + 127) << 23);
+    const float d = 1.0f + e;
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    y = fmaf(fmaf(-d, y, 1.0f), y, y);
+    return x * y;
+}
+
+
+// GroupNorm read in place of its output (a prologue of the operation that
+// consumes it: the Winograd input transform, the split of a convolution's or
+// linear layer's activations): x' = (x - mean) * scale, then gamma and beta
+// by one fmaf, then SiLU -- the apply pass's arithmetic (norm.cu,
+// nhwc_gn_apply_kernel), so the fused operation sees the very numbers the
+// GroupNorm node would have written.  stats [images][groups][2] (mean,
+// 1 / sqrt(variance + eps)); stats null: no prologue.
+struct GnIn {
+    const float* stats;
+    const float* gamma;   // [C], with beta, or both null
+    const float* beta;
+    int cpg;              // channels per group
+    int groups;
+    int silu;
+    long long positions;  // rows (positions) of an image, for row-wise consumers
+};
+
+// The normalisation of one value whose channel's mean m, scale s, gamma ga and beta gb are known.
+__device__ __forceinline__ float gn_apply(const GnIn& g, float x, float m, float s, float ga, float gb) {
+    float v = (x - m) * s;
+    if (g.gamma) v = fmaf(v, ga, gb);
+    return g.silu ? silu_apply(v) : v;
+}
+
+// A channel's four numbers (consumers load them once for all the values of a channel they read).
+struct GnCoef {
+    float m, s, ga, gb;
+};
+
+__device__ __forceinline__ GnCoef gn_coef(const GnIn& g, int c, long long img) {
+    const float* st = g.stats + (img * g.groups + c / g.cpg) * 2;
+    GnCoef k{__ldg(st), __ldg(st + 1), 1.0f, 0.0f};
+    if (g.gamma) {
+        k.ga = __ldg(g.gamma + c);
+        k.gb = __ldg(g.beta + c);
+    }
+    return k;
+}
+
+__device__ __forceinline__ float gn_in(const GnIn& g, float x, const GnCoef& k) {
+    return gn_apply(g, x, k.m, k.s, k.ga, k.gb);
+}
+
 // The chain as kernels take it (by value, in the launch parameters).
 struct Chain {
     int count;

@@ -244,12 +244,15 @@ bool mul_mat_shapes(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* 
 // transient: w is packed into the workspace on every call instead of being
 // kept by the store (an operand the graph writes between calls).
 int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
-               cudaStream_t st, bool gated, bool transient = false) {
+               cudaStream_t st, bool gated, bool transient = false, const GnIn* gn = nullptr) {
     const int64_t k = w->ne[0];
     const int64_t n = gated ? w->ne[1] / 2 : w->ne[1];
     const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
     if (m > (1LL << 30) || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "mul_mat: too large");
-    if (!transient && quantized_linear(m)) return run_quantized_linear(w, x, dst, chain, st, gated);
+    if (!transient && quantized_linear(m)) {
+        if (gn) return fail(SDB_NOT_SUPPORTED, "mul_mat: no GroupNorm prologue on integer products");
+        return run_quantized_linear(w, x, dst, chain, st, gated);
+    }
     std::shared_ptr<Packed> p;
     size_t w_bytes = 0;
     if (transient) {
@@ -300,7 +303,8 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     set_partials(a, ws, a_bytes, tiles, bn);
     const long long ne[4] = {x->ne[0], x->ne[1], x->ne[2], x->ne[3]};
     const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
-    if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err, st);
+    if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err, st,
+                           gn);
         s != SDB_OK)
         return s;
     // A as [plane][row][k]: one box {64, 128, 2} brings a tile's hi and lo rows.
@@ -367,7 +371,7 @@ int winograd_form(const sdb_tensor* w, const sdb_tensor* dst, const int32_t para
 // chain.  Workspace: V [2][XI][Tp][icp8] FP16, M [XI][Tp][ldm] FP32, then any
 // split-K partial sums.
 int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
-                 const sdb_chain* chain, cudaStream_t st) {
+                 const sdb_chain* chain, cudaStream_t st, const GnIn* gn = nullptr) {
     std::shared_ptr<Packed> p;
     if (int s = winograd_weights(w, f, st, &p); s != SDB_OK) return s;
     const int xi = f == 2 ? Wino<2>::kXi : Wino<4>::kXi;
@@ -427,7 +431,16 @@ int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tens
                           wa.xnb[0] % 2 == 0 && wa.xnb[1] % 2 == 0 && wa.xnb[3] % 2 == 0;
     const long long in_total = wa.tiles_pad * wa.icp8 / (in_pairs ? 2 : 1);
     const int in_blocks = static_cast<int>(std::min<long long>((in_total + 255) / 256, 148LL * 32));
-    if (f == 2) {
+    if (gn) {
+        wa.gn = *gn;
+        if (f == 2) {
+            if (in_pairs) winograd_inputs_kernel<2, 2, true><<<in_blocks, 256, 0, st>>>(wa);
+            else winograd_inputs_kernel<2, 1, true><<<in_blocks, 256, 0, st>>>(wa);
+        } else {
+            if (in_pairs) winograd_inputs_kernel<4, 2, true><<<in_blocks, 256, 0, st>>>(wa);
+            else winograd_inputs_kernel<4, 1, true><<<in_blocks, 256, 0, st>>>(wa);
+        }
+    } else if (f == 2) {
         if (in_pairs) winograd_inputs_kernel<2, 2><<<in_blocks, 256, 0, st>>>(wa);
         else winograd_inputs_kernel<2, 1><<<in_blocks, 256, 0, st>>>(wa);
     } else {
@@ -477,6 +490,28 @@ int run_winograd(int f, const sdb_tensor* w, const sdb_tensor* x, const sdb_tens
 }  // namespace sdb
 
 using namespace sdb;
+
+namespace sdb {
+// sdb_conv2d's body, with an optional GroupNorm prologue on x (chain.cuh GnIn).
+int conv2d_impl(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                const sdb_chain* chain, void* stream, const GnIn* gn);
+
+// The prologue's parameters from the C ABI's sdb_norm_in, for an input of C channels and
+// `positions` positions an image; SDB_OK or SDB_INVALID.
+int make_gn_in(const sdb_norm_in* in, long long channels, long long positions, GnIn* out) {
+    if (!in || !in->stats || in->groups <= 0 || channels % in->groups != 0 || positions <= 0 ||
+        (in->gamma == nullptr) != (in->beta == nullptr))
+        return fail(SDB_INVALID, "GroupNorm prologue: stats, groups dividing the channels, gamma with beta");
+    out->stats = in->stats;
+    out->gamma = in->gamma;
+    out->beta = in->beta;
+    out->groups = in->groups;
+    out->cpg = static_cast<int>(channels / in->groups);
+    out->silu = in->silu ? 1 : 0;
+    out->positions = positions;
+    return SDB_OK;
+}
+}  // namespace sdb
 
 extern "C" {
 
@@ -541,15 +576,44 @@ int sdb_conv2d_supported(const sdb_tensor* w, const sdb_tensor* x, const sdb_ten
 
 int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
                const sdb_chain* chain, void* stream) {
+    return conv2d_impl(w, x, dst, params, chain, stream, nullptr);
+}
+
+int sdb_conv2d_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                      const sdb_norm_in* norm, const sdb_chain* chain, void* stream) {
+    if (!sdb_conv2d_supported(w, x, dst, params)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d_normed: not supported");
+    GnIn gn{};
+    if (int s = make_gn_in(norm, x->ne[2], x->ne[0] * x->ne[1], &gn); s != SDB_OK) return s;
+    return conv2d_impl(w, x, dst, params, chain, stream, &gn);
+}
+
+int sdb_mul_mat_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_norm_in* norm,
+                       const sdb_chain* chain, void* stream) {
+    if (!sdb_mul_mat_supported(w, x, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat_normed: shapes not supported");
+    if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_mul_mat_normed: invalid chain");
+    GnIn gn{};
+    if (int s = make_gn_in(norm, x->ne[0], x->ne[1], &gn); s != SDB_OK) return s;
+    return run_linear(w, x, dst, chain, static_cast<cudaStream_t>(stream), false, false, &gn);
+}
+
+}  // extern "C"
+
+namespace sdb {
+
+int conv2d_impl(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const int32_t params[6],
+                const sdb_chain* chain, void* stream, const GnIn* gn) {
     if (!sdb_conv2d_supported(w, x, dst, params)) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: not supported");
     if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_conv2d: invalid chain");
     const auto st = static_cast<cudaStream_t>(stream);
     if (quantized_conv()) {
+        if (gn) return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: no GroupNorm prologue on integer products");
         // Integer products (conv2d.cc:843-844, winograd.cc:2237-2244): the reference's own choice of form.
         if (quantized_winograd(w, dst, params)) return run_quantized_winograd(w, x, dst, params, chain, st);
         return run_quantized_conv(w, x, dst, params, chain, st);
     }
-    if (const int f = winograd_form(w, dst, params); f != 0) return run_winograd(f, w, x, dst, params, chain, st);
+    if (const int f = winograd_form(w, dst, params); f != 0) return run_winograd(f, w, x, dst, params, chain, st, gn);
+    if (gn && !channels_last(x))
+        return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: a GroupNorm prologue needs a channels-last image");
     const int64_t ic = x->ne[2], oc = w->ne[3];
     const int icp = static_cast<int>(round_up(ic, 64));
     std::shared_ptr<Packed> p;
@@ -594,7 +658,8 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
         // Already channels-last: the split is a split of rows (positions).
         const long long ne[4] = {ic, W, H, N};
         const long long nb[4] = {1, ic, W * ic, H * W * ic};
-        if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st);
+        if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, cp8, static_cast<uint16_t*>(ws), a.err, st,
+                               gn);
             s != SDB_OK)
             return s;
     } else {
@@ -629,4 +694,4 @@ int sdb_conv2d(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     return dispatch<kModeConv>(amap, *p, wmode, ymap, a, st);
 }
 
-}  // extern "C"
+}  // namespace sdb

@@ -465,30 +465,6 @@ __global__ void __launch_bounds__(kClThreads) nhwc_gn_stats_kernel(const NhwcArg
 // and shift (per channel), with or without the SiLU after them.
 enum : int { kChainGeneral = 0, kChainAffine = 1, kChainAffineSilu = 2, kChainNone = 3 };
 
-// SiLU of the apply pass, x / (1 + e^-x) as the reference writes it (scalar_math.h:54-58), with
-// e^-x by the same Cody-Waite reduction to |r| <= ln2 / 2 but 2^(r log2 e) from the hardware's
-// ex2 (relative error about 2^-22) in place of the degree-6 polynomial, and the quotient by the
-// hardware's reciprocal refined by one Newton step: within a few 2^-23 of the exact form, at a
-// third of the instructions -- the pass is bound by issue, not by memory.
-__device__ __forceinline__ float silu_apply(float x) {
-    // Clamped at 87.3 on both sides (the reference's upper clamp is 88.73): 2^n stays finite, so
-    // the Newton step never meets an infinity; past 87.3 the quotient is below FP32's normal range.
-    const float t = fminf(fmaxf(-x, -87.3f), 87.3f);
-    const float magic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
-    const float z = fmaf(t, 1.44269504088896341f, magic);
-    const float n = z - magic;
-    float r = fmaf(n, -0.693359375f, t);
-    r = fmaf(n, 2.12194440e-4f, r);
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(r * 1.44269504088896341f));
-    e *= __uint_as_float(static_cast<uint32_t>(__float_as_int(z) - 0x4b400000 + 127) << 23);
-    const float d = 1.0f + e;
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
-    y = fmaf(fmaf(-d, y, 1.0f), y, y);
-    return x * y;
-}
-
 template <int PATTERN>
 __device__ __forceinline__ float chain_pattern(const Chain& ch, const float (&op)[SDB_MAX_STEPS], float v) {
     if (PATTERN == kChainNone) return v;
@@ -798,18 +774,16 @@ int launch_nhwc_apply(const NhwcArgs& a, int grid, cudaStream_t st) {
     return SDB_OK;
 }
 
-int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps, const sdb_chain* chain,
-                    cudaStream_t st) {
-    NhwcArgs a{};
+// The statistics pass alone, into `stats` (the caller's [N][groups][2]) or, with stats null, the scratch's.
+int nhwc_stats(NhwcArgs& a, const sdb_tensor* x, int32_t groups, float eps, float* stats, cudaStream_t st,
+               int* grid_out) {
     a.x = static_cast<const float*>(x->data);
-    a.y = static_cast<float*>(dst->data);
     a.positions = static_cast<int>(x->ne[0] * x->ne[1]);
     a.c = static_cast<int>(x->ne[2]);
     a.c4 = a.c / 4;
     a.groups = groups;
     a.cpg = a.c / groups;
     a.eps = eps;
-    a.chain = make_chain(chain);
     a.rpp = a.c4 <= kClThreads ? kClThreads / a.c4 : 1;
     const int images = static_cast<int>(x->ne[3]);
     const int sms = current_sm_count();
@@ -825,7 +799,7 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
                     static_cast<size_t>(images), st, &sc))
         return fail(SDB_OUT_OF_MEMORY, "sdb_group_norm: scratch (first use of a size under stream capture?)");
     a.partial = sc.partial;
-    a.stats = sc.stats;
+    a.stats = stats ? stats : sc.stats;
     a.count = sc.count;
     const int csum_len = a.c4 <= kClThreads ? a.rpp * a.c : a.c;
     const size_t smem = 2 * static_cast<size_t>(csum_len) * sizeof(double);
@@ -834,6 +808,17 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
     nhwc_gn_stats_kernel<<<grid, kClThreads, smem, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
+    *grid_out = grid;
+    return SDB_OK;
+}
+
+int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps, const sdb_chain* chain,
+                    cudaStream_t st) {
+    NhwcArgs a{};
+    a.y = static_cast<float*>(dst->data);
+    a.chain = make_chain(chain);
+    int grid = 0;
+    if (int s = nhwc_stats(a, x, groups, eps, nullptr, st, &grid); s != SDB_OK) return s;
     // The chain's pattern: mul then add (then SiLU) -- the GroupNorm's affine -- compiles alone.
     const Chain& c = a.chain;
     if (c.count == 0) return launch_nhwc_apply<kChainNone>(a, grid, st);
@@ -846,6 +831,18 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
 
 }  // namespace
 }  // namespace sdb
+
+extern "C" int sdb_group_norm_stats(const sdb_tensor* x, int32_t groups, float eps, float* stats, void* stream) {
+    if (!f32(x) || !channels_last(x) || groups <= 0 || x->ne[2] % groups != 0 || x->ne[2] % 4 != 0 ||
+        x->ne[2] > kClMaxChannels || groups > kClMaxGroups || x->ne[0] * x->ne[1] > (1LL << 30) || x->ne[3] > 4096 ||
+        (reinterpret_cast<uintptr_t>(x->data) & 15) || stats == nullptr)
+        return fail(SDB_NOT_SUPPORTED,
+                    "sdb_group_norm_stats: a channels-last image with C % groups == 0, C % 4 == 0, C <= 3072, "
+                    "aligned, and a stats buffer");
+    NhwcArgs a{};
+    int grid = 0;
+    return nhwc_stats(a, x, groups, eps, stats, static_cast<cudaStream_t>(stream), &grid);
+}
 
 extern "C" int sdb_group_norm(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, float eps,
                               const sdb_chain* chain, void* stream) {

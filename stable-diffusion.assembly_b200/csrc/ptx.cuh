@@ -267,6 +267,18 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
         : "memory");
 }
 
+// D = A B + D 2^-11: the product into an accumulator that holds the lo
+// products of a split (each lo operand carries the split's 2^11), scaled to
+// the hi product's units as the product is added (tcgen05.mma's scale of the
+// input D, kind::f16).  So hi.hi + (hi.lo + lo.hi) 2^-11 lands in one
+// accumulator: the lo products are issued first, then the first hi product
+// with this scale, the rest plain.
+__device__ __forceinline__ void mma_f16_scale_lo(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1, 11;" ::"r"(tmem_d), "l"(adesc),
+                 "l"(bdesc), "r"(idesc)
+                 : "memory");
+}
+
 // Arrives on `bar` once every tcgen05 operation this thread issued before has
 // completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {

@@ -8,6 +8,7 @@
 #include <mutex>
 #include <utility>
 
+#include "chain.cuh"
 #include "ptx.cuh"
 #include "runtime.cuh"
 
@@ -26,10 +27,12 @@ std::map<std::pair<int, cudaStream_t>, Space> g_spaces;
 // One thread per 8 consecutive values of a row: two float4 loads when the
 // row is contiguous and aligned, one 16-byte store of hi and one of lo.
 // I: the index type, 32-bit when every index fits (cheaper division).
-template <typename I>
+// GN: the rows are an image's positions (channels along the row) read through
+// a GroupNorm prologue (chain.cuh gn_in): the split of the normalised values.
+template <typename I, bool GN = false>
 __global__ void split_rows_kernel(const float* __restrict__ x, I ne0, I ne1, I ne2, I rows, long long xnb0,
                                   long long xnb1, long long xnb2, long long xnb3, I ld,
-                                  uint16_t* __restrict__ out, unsigned* err, int vec) {
+                                  uint16_t* __restrict__ out, unsigned* err, int vec, GnIn gn = GnIn{}) {
     const I chunks = ld / 8;
     const I total = rows * chunks;
     bool over = false;
@@ -47,6 +50,12 @@ __global__ void split_rows_kernel(const float* __restrict__ x, I ne0, I ne1, I n
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = c0 + i < ne0 ? __ldg(src + (c0 + i) * xnb0) : 0.0f;
+        }
+        if (GN) {
+            const long long img = static_cast<long long>(r) / gn.positions;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (c0 + i < ne0) v[i] = gn_in(gn, v[i], gn_coef(gn, static_cast<int>(c0 + i), img));
         }
         uint4 hi, lo;
         over |= split8(v, hi, lo);
@@ -198,14 +207,25 @@ int workspace(cudaStream_t stream, size_t bytes, void** out) {
 }
 
 int split_rows(const float* x, const long long ne[4], const long long xnb[4], long long ld, uint16_t* out,
-               unsigned* err, cudaStream_t stream) {
+               unsigned* err, cudaStream_t stream, const GnIn* gn) {
     const long long rows = ne[1] * ne[2] * ne[3];
     const long long total = rows * (ld / 8);
     const int vec = xnb[0] == 1 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && xnb[1] % 4 == 0 &&
                     xnb[2] % 4 == 0 && xnb[3] % 4 == 0;
     const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 32));
     if (blocks == 0) return SDB_OK;
-    if (2 * total * 8 < (1LL << 31))
+    const bool small = 2 * total * 8 < (1LL << 31);
+    if (gn && gn->stats) {
+        if (small)
+            split_rows_kernel<unsigned, true><<<blocks, 256, 0, stream>>>(
+                x, static_cast<unsigned>(ne[0]), static_cast<unsigned>(ne[1]), static_cast<unsigned>(ne[2]),
+                static_cast<unsigned>(rows), xnb[0], xnb[1], xnb[2], xnb[3], static_cast<unsigned>(ld), out, err, vec,
+                *gn);
+        else
+            split_rows_kernel<long long, true><<<blocks, 256, 0, stream>>>(x, ne[0], ne[1], ne[2], rows, xnb[0],
+                                                                           xnb[1], xnb[2], xnb[3], ld, out, err, vec,
+                                                                           *gn);
+    } else if (small)
         split_rows_kernel<unsigned><<<blocks, 256, 0, stream>>>(
             x, static_cast<unsigned>(ne[0]), static_cast<unsigned>(ne[1]), static_cast<unsigned>(ne[2]),
             static_cast<unsigned>(rows), xnb[0], xnb[1], xnb[2], xnb[3], static_cast<unsigned>(ld), out, err, vec);

@@ -28,8 +28,11 @@ int workspace(cudaStream_t stream, size_t bytes, void** out);
 // strides xnb, rows enumerated (i3, i2, i1) -> r = (i3 * ne2 + i2) * ne1 + i1.
 // Writes hi rows [0, R) then lo rows [R, 2R) of `ld` FP16 each (ld >= ne0,
 // a multiple of 8; columns past ne0 are zero).  R = ne1 * ne2 * ne3.
+// With gn (stats not null), each row is an image's position, its values
+// channels 0 .. ne0 - 1, read through the GroupNorm prologue (chain.cuh).
+struct GnIn;
 int split_rows(const float* x, const long long ne[4], const long long xnb[4], long long ld, uint16_t* out,
-               unsigned* err, cudaStream_t stream);
+               unsigned* err, cudaStream_t stream, const GnIn* gn = nullptr);
 // The same for an FP16 source (hi = the value, lo = 0).
 int split_rows_half(const uint16_t* x, const long long ne[4], const long long xnb[4], long long ld, uint16_t* out,
                     cudaStream_t stream);

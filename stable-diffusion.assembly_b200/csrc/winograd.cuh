@@ -108,6 +108,7 @@ struct WinoArgs {
     long long ynb[4];
     Chain chain;
     unsigned* err;
+    GnIn gn;                 // the inputs read through a GroupNorm prologue (gn.stats not null)
 };
 
 // The kernels' transform U = G g G^T of output channel o and input channel c,
@@ -161,8 +162,10 @@ __global__ void winograd_weights_kernel(const uint8_t* __restrict__ src, int typ
 // split; rows of padded tiles and channels past IC are zeros.  Consecutive
 // threads take consecutive channels.  B^T d is formed a column of d at a
 // time, then each row of (B^T d) B is split and stored as it is made.
-template <int F, int VEC>
-__global__ void __launch_bounds__(256) winograd_inputs_kernel(const WinoArgs a) {
+// GN: the image read through the GroupNorm prologue (gn_in) -- inside the
+// image only; the padding stays zero, as the normalised image's would.
+template <int F, int VEC, bool GN = false>
+__global__ void __launch_bounds__(256, GN ? 2 : 1) winograd_inputs_kernel(const WinoArgs a) {
     using W = Wino<F>;
     constexpr int A = W::kA;
     const int groups = a.icp8 / VEC;  // channel groups of a tile row
@@ -174,16 +177,21 @@ __global__ void __launch_bounds__(256) winograd_inputs_kernel(const WinoArgs a) 
         const int t = idx / groups;
         const int c = (idx - t * groups) * VEC;
         const bool live = t < tiles && c < a.ic;
-        int x0 = 0, y0 = 0;
+        int x0 = 0, y0 = 0, img = 0;
         const float* base = a.x;
         if (live) {
             const int tx = t % a.tw;
             const int rest = t / a.tw;
             const int ty = rest % a.th;
-            const int img = rest / a.th;
+            img = rest / a.th;
             x0 = tx * F - a.p0;
             y0 = ty * F - a.p1;
             base = a.x + c * a.xnb[2] + img * a.xnb[3];
+        }
+        GnCoef gk[VEC];
+        if (GN && live) {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) gk[e] = gn_coef(a.gn, c + e, img);
         }
         float s[VEC][A][A];  // B^T d
 #pragma unroll
@@ -197,11 +205,15 @@ __global__ void __launch_bounds__(256) winograd_inputs_kernel(const WinoArgs a) 
                 const bool ok = col_ok && yy >= 0 && yy < a.ih;
                 const float* p = base + xx * a.xnb[0] + yy * a.xnb[1];
                 if (VEC == 2) {
-                    const float2 v = ok ? __ldg(reinterpret_cast<const float2*>(p)) : make_float2(0.0f, 0.0f);
+                    float2 v = ok ? __ldg(reinterpret_cast<const float2*>(p)) : make_float2(0.0f, 0.0f);
+                    if (GN && ok) {
+                        v.x = gn_in(a.gn, v.x, gk[0]);
+                        v.y = gn_in(a.gn, v.y, gk[VEC - 1]);
+                    }
                     d[0][k] = v.x;
                     d[VEC - 1][k] = v.y;
                 } else {
-                    d[0][k] = ok ? __ldg(p) : 0.0f;
+                    d[0][k] = ok ? (GN ? gn_in(a.gn, __ldg(p), gk[0]) : __ldg(p)) : 0.0f;
                 }
             }
 #pragma unroll

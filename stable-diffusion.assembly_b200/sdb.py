@@ -40,7 +40,8 @@ EXPORTS = [
     "sdb_group_norm", "sdb_group_norm_no_alloc", "sdb_norm", "sdb_forget", "sdb_store_stats", "sdb_token_downsampling",
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
     "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step", "sdb_soft_max",
-    "sdb_coarser_tokens", "sdb_euler_ancestral_cfg_step",
+    "sdb_coarser_tokens", "sdb_euler_ancestral_cfg_step", "sdb_group_norm_stats", "sdb_conv2d_normed",
+    "sdb_mul_mat_normed",
 ]
 
 
@@ -58,6 +59,11 @@ class Tensor(ctypes.Structure):
 
 class Step(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int32), ("operand", ctypes.c_void_p), ("nb", ctypes.c_int64 * 4)]
+
+
+class NormIn(ctypes.Structure):
+    _fields_ = [("stats", ctypes.c_void_p), ("gamma", ctypes.c_void_p), ("beta", ctypes.c_void_p),
+                ("groups", ctypes.c_int32), ("silu", ctypes.c_int32)]
 
 
 class ChainStruct(ctypes.Structure):
@@ -107,6 +113,9 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_upscale_nearest": (i, [T, T, vp]),
         "sdb_coarser_tokens": (i, [T, T, ctypes.c_int32, vp]),
         "sdb_timestep_embedding": (i, [T, T, ctypes.c_int32, ctypes.c_int32, vp]),
+        "sdb_group_norm_stats": (i, [T, ctypes.c_int32, ctypes.c_float, vp, vp]),
+        "sdb_conv2d_normed": (i, [T, T, T, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(NormIn), C, vp]),
+        "sdb_mul_mat_normed": (i, [T, T, T, ctypes.POINTER(NormIn), C, vp]),
         "sdb_euler_cfg_step": (i, [vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                    ctypes.c_float, vp]),
         "sdb_euler_ancestral_cfg_step": (i, [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float,
@@ -489,6 +498,61 @@ def group_norm_nhwc(x, groups: int, eps: float, out=None, chain: Chain | None = 
         out = torch.empty_like(x)
     _check(lib.sdb_group_norm(describe_nhwc(x), describe_nhwc(out), groups, ctypes.c_float(eps), _chain_ptr(chain),
                               ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+class GroupNormIn:
+    """A GroupNorm (+ SiLU) that the next operation applies as it reads its input (sdb_norm_in):
+    the statistics of x (group_norm_stats), gamma and beta (C,) or None, groups, SiLU."""
+
+    def __init__(self, stats, groups: int, gamma=None, beta=None, silu: bool = False):
+        self.stats, self.groups, self.gamma, self.beta, self.silu = stats, groups, gamma, beta, silu
+        self.c = NormIn(stats.data_ptr(), gamma.data_ptr() if gamma is not None else None,
+                        beta.data_ptr() if beta is not None else None, groups, 1 if silu else 0)
+
+
+def group_norm_stats(x, groups: int, eps: float, out=None, stream=None):
+    """Mean and 1 / sqrt(variance + eps) per image and group of a channels-last image (N, H, W, C):
+    (N, groups, 2) FP32 (sdb_group_norm_stats)."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty(x.shape[0], groups, 2, dtype=torch.float32, device=x.device)
+    _check(lib.sdb_group_norm_stats(describe_nhwc(x), groups, ctypes.c_float(eps), ctypes.c_void_p(out.data_ptr()),
+                                    ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def conv2d_nhwc_normed(w, x, norm: GroupNormIn, stride=(1, 1), padding=(0, 0), dilation=(1, 1), out=None,
+                       chain: Chain | None = None, stream=None):
+    """conv2d_nhwc of GroupNorm(x) [+ SiLU], the normalisation applied as the convolution reads x."""
+    import torch
+
+    lib = load()
+    oc, _, kh, kw = w.shape
+    n, h, wd, _ = x.shape
+    oh = conv_out_size(h, kh, stride[1], padding[1], dilation[1])
+    ow = conv_out_size(wd, kw, stride[0], padding[0], dilation[0])
+    if out is None:
+        out = torch.empty(n, oh, ow, oc, dtype=torch.float32, device=x.device)
+    params = (ctypes.c_int32 * 6)(stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1])
+    _guard_weight(w)
+    _check(lib.sdb_conv2d_normed(describe(w), describe_nhwc(x), describe_nhwc(out), params, ctypes.byref(norm.c),
+                                 _chain_ptr(chain), ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def mul_mat_normed(w, x, norm: GroupNormIn, out=None, chain: Chain | None = None, stream=None):
+    """mul_mat of GroupNorm(x) [+ SiLU]: x (N, P, C), the P positions of each of N images."""
+    import torch
+
+    lib = load()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.float32, device=x.device)
+    _guard_weight(w)
+    _check(lib.sdb_mul_mat_normed(describe(w), describe(x), describe(out), ctypes.byref(norm.c), _chain_ptr(chain),
+                                  ctypes.c_void_p(_stream_ptr(stream))))
     return out
 
 

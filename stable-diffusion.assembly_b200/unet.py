@@ -251,6 +251,9 @@ class UNet:
         self.kv_w = torch.cat(kv_w).contiguous() if kv_w else None
         self.res_blocks, self.transformers = res_blocks, transformers
         self.params = init.params
+        # GroupNorm fused into the convolution or linear layer that reads it (sdb_conv2d_normed,
+        # sdb_mul_mat_normed); False runs it as the reference's separate node (the same numbers).
+        self.fuse_gn = True
 
     # ------------------------------------------------------------ pieces
 
@@ -260,21 +263,31 @@ class UNet:
             ch.silu()
         return sdb.group_norm_nhwc(x, self.cfg.groups, eps, out=out, chain=ch)
 
+    def _gn_in(self, x, gn, eps, silu):
+        """The GroupNorm (+ SiLU) of x as a prologue of the operation that reads it (fuse_gn): its
+        statistics now, the normalisation as the next convolution or linear layer loads x."""
+        return sdb.GroupNormIn(sdb.group_norm_stats(x, self.cfg.groups, eps), self.cfg.groups, gn[0], gn[1], silu)
+
+    def _conv_gn(self, w, x, gn, eps, chain, out=None):
+        """3x3 convolution of SiLU(GroupNorm(x)): fused (the statistics, then the convolution normalising
+        its input as it reads it) or as the reference's separate nodes.  Fused where the convolution
+        reads each input once (the direct path's split: images under 1024 positions); in front of a
+        Winograd convolution, whose input transform reads each input (F + 2)^2 / F^2 = 2.25 times, the
+        normalisation and SiLU run once as a pass of their own (measured faster there)."""
+        winograd = w.shape[2] == 3 and x.shape[1] * x.shape[2] >= 1024
+        if self.fuse_gn and not winograd:
+            return sdb.conv2d_nhwc_normed(w, x, self._gn_in(x, gn, eps, True), (1, 1), (1, 1), out=out, chain=chain)
+        return sdb.conv2d_nhwc(w, self._gn(x, gn, eps, True), (1, 1), (1, 1), out=out, chain=chain)
+
     def _resblock(self, x, rb: ResBlock, emb):
-        torch = self.torch
-        b, hh, ww, _ = x.shape
-        t1 = self._gn(x, rb.gn1, 1e-5, True)
         emb_view = emb[:, rb.emb_offset:rb.emb_offset + rb.cout]
-        h = sdb.conv2d_nhwc(rb.conv1, t1, (1, 1), (1, 1), chain=sdb.Chain()
-                            .add(rb.b1, [0, 0, 1, 0]).add(emb_view, [0, 0, 1, emb.shape[1]]))
-        t2 = self._gn(h, rb.gn2, 1e-5, True, out=t1 if rb.cin == rb.cout else None)
+        h = self._conv_gn(rb.conv1, x, rb.gn1, 1e-5,
+                          sdb.Chain().add(rb.b1, [0, 0, 1, 0]).add(emb_view, [0, 0, 1, emb.shape[1]]))
         if rb.skip is None:
             xs = (x.stride(2), x.stride(1), x.stride(3), x.stride(0))  # ggml order [W, H, C, N]
-            return sdb.conv2d_nhwc(rb.conv2, t2, (1, 1), (1, 1), out=h,
-                                   chain=sdb.Chain().add(rb.b2, [0, 0, 1, 0]).add(x, list(xs)))
+            return self._conv_gn(rb.conv2, h, rb.gn2, 1e-5, sdb.Chain().add(rb.b2, [0, 0, 1, 0]).add(x, list(xs)))
         out = sdb.conv2d_nhwc(rb.skip, x, chain=sdb.Chain().add(rb.bskip, [0, 0, 1, 0]))
-        sdb.conv2d_nhwc(rb.conv2, t2, (1, 1), (1, 1), out=h,
-                        chain=sdb.Chain().add(rb.b2, [0, 0, 1, 0]).redirect(out, True))
+        self._conv_gn(rb.conv2, h, rb.gn2, 1e-5, sdb.Chain().add(rb.b2, [0, 0, 1, 0]).redirect(out, True))
         return out
 
     def _ln(self, x, ln):
@@ -284,8 +297,12 @@ class UNet:
         b, hh, ww, c = x.shape
         heads = tr.heads
         scale = 1.0 / math.sqrt(c // heads)
-        n = self._gn(x, tr.gn, 1e-6, False)
-        t = sdb.mul_mat(tr.proj_in, n.view(b, hh * ww, c), chain=sdb.Chain().add(tr.b_in))
+        if self.fuse_gn:
+            t = sdb.mul_mat_normed(tr.proj_in, x.view(b, hh * ww, c), self._gn_in(x, tr.gn, 1e-6, False),
+                                   chain=sdb.Chain().add(tr.b_in))
+        else:
+            n = self._gn(x, tr.gn, 1e-6, False)
+            t = sdb.mul_mat(tr.proj_in, n.view(b, hh * ww, c), chain=sdb.Chain().add(tr.b_in))
         # ToDo (the reference's stable-diffusion.cpp patch 0004): self-attention's keys and values from
         # every f-th token of every f-th row when the tuning asks for it on a grid this large.
         f = sdb.token_downsampling(ww, hh)
@@ -365,8 +382,7 @@ class UNet:
             if level.up is not None:
                 h = sdb.upscale_nearest_nhwc(h, 2)
                 h = sdb.conv2d_nhwc(level.up[0], h, (1, 1), (1, 1), chain=sdb.Chain().add(level.up[1], [0, 0, 1, 0]))
-        t = self._gn(h, self.out_gn, 1e-5, True)
-        return sdb.conv2d_nhwc(self.conv_out, t, (1, 1), (1, 1), chain=sdb.Chain().add(self.conv_out_b, [0, 0, 1, 0]))
+        return self._conv_gn(self.conv_out, h, self.out_gn, 1e-5, sdb.Chain().add(self.conv_out_b, [0, 0, 1, 0]))
 
     def flops(self, batch: int, height: int, width: int, context_len: int = 77) -> int:
         """Algorithmic FLOPs of one forward in the reference's convention (profile.cc:65-81):

@@ -72,15 +72,22 @@ def test_reference_arm_other_ranks_print_nothing():
 
 @pytest.mark.skipif(not (ROOT / "oracle" / "_ref" / "libsdasm_ref.so").exists(), reason="reference kernels not built")
 def test_reference_arm_line():
-    """Rank 0's reference line: the driver contract's keys, the arm's kind and a positive rate."""
-    env = dict(os.environ, RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", OMP_NUM_THREADS=os.environ.get("OMP_NUM_THREADS", "4"))
-    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3"],
-                       env=env, capture_output=True, text=True, timeout=600)
+    """Rank 0's reference line: the driver contract's keys, the arm's kind, a positive rate, the GPU
+    arm's config, and every host core in use although the launcher's OMP_NUM_THREADS says 1 (torchrun
+    sets it so): the arm sets its thread count from the process's CPU affinity."""
+    env = dict(os.environ, RANK="0", WORLD_SIZE="2", LOCAL_RANK="0", OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2", "--steps", "1",
+                        "--warmup", "0"], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["unit"] == "image-steps/s"
+    assert line["steps"] == 1 and abs(line["ms_per_step"] - 1e3 / line["value"]) < 1e-6 * line["ms_per_step"]
+    import bench
+
+    assert line["config"] == bench.unet_config(2, "")
 
 
 def _guidance_worker(rank: int, world: int, port: int, out):
