@@ -809,8 +809,8 @@ class OpClock:
     reference's convention for products, bytes read + written for the rest)."""
 
     NAMES = ("conv2d_nhwc", "conv2d_nhwc_normed", "mul_mat", "mul_mat_normed", "mul_mat_gated", "attention_heads",
-             "group_norm_nhwc", "group_norm_stats", "norm", "concat_channels_nhwc", "upscale_nearest_nhwc",
-             "timestep_embedding")
+             "group_norm_nhwc", "group_norm_stats", "norm", "mul_mat_layer_normed", "concat_channels_nhwc",
+             "upscale_nearest_nhwc", "timestep_embedding")
 
     def __init__(self, sdb, torch):
         self.sdb, self.torch = sdb, torch
@@ -829,6 +829,10 @@ class OpClock:
             return cls, 2 * kh * kw * ic * oc * oh * ow * n
         if name == "group_norm_stats":
             return "groupnorm", 4 * args[0].numel()
+        if name == "mul_mat_layer_normed":
+            w, x = args[0], args[1]
+            k = w.shape[1]
+            return ("geglu" if out.shape[-1] * 2 == w.shape[0] else "linear"), 2 * (x.numel() // k) * w.shape[0] * k
         if name in ("mul_mat", "mul_mat_gated", "mul_mat_normed"):
             w, x = args[0], args[1]
             k = w.shape[1]
@@ -865,9 +869,10 @@ class OpClock:
         if name in ("conv2d_nhwc", "conv2d_nhwc_normed"):
             w, x = args[0], args[1]
             return f"conv {w.shape[1]}->{w.shape[0]} k{w.shape[2]} @{x.shape[1]}x{x.shape[2]}x{x.shape[0]}"
-        if name in ("mul_mat", "mul_mat_gated", "mul_mat_normed"):
+        if name in ("mul_mat", "mul_mat_gated", "mul_mat_normed", "mul_mat_layer_normed"):
             w, x = args[0], args[1]
-            return f"{'geglu' if name == 'mul_mat_gated' else 'linear'} M{x.numel() // w.shape[1]} K{w.shape[1]} N{w.shape[0]}"
+            gated = name == "mul_mat_gated" or (name == "mul_mat_layer_normed" and out.shape[-1] * 2 == w.shape[0])
+            return f"{'geglu' if gated else 'linear'} M{x.numel() // w.shape[1]} K{w.shape[1]} N{w.shape[0]}"
         if name == "attention_heads":
             q, k, heads = args[0], args[1], args[3]
             return f"attention L{q.shape[1]}x{k.shape[1]} d{q.shape[2] // heads} b{q.shape[0]}"

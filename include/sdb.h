@@ -169,6 +169,18 @@ int sdb_conv2d_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor
 int sdb_mul_mat_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_norm_in *norm,
                        const sdb_chain *chain, void *stream);
 
+/* LayerNorm fused into the linear layer that reads it (an extension of the
+ * reference, whose NORM node writes its output, norm.cc:148-175): each row of
+ * x is normalised -- mean and variance in double -- with the LayerNorm's chain
+ * (norm_chain: its gamma and beta) as sdb_norm computes it, inside the split
+ * of the linear layer's rows, and never written.  The result equals sdb_norm
+ * followed by sdb_mul_mat (or sdb_mul_mat_gated) bit for bit.  Rows of at most
+ * 1280 numbers. */
+int sdb_mul_mat_layer_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, float eps,
+                             const sdb_chain *norm_chain, const sdb_chain *chain, void *stream);
+int sdb_mul_mat_gated_layer_normed(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *out, float eps,
+                                   const sdb_chain *norm_chain, const sdb_chain *chain, void *stream);
+
 /* ---- the graph's data-movement nodes (device-resident runner) -----------
  * The reference takes only CONV_2D, MUL_MAT, FLASH_ATTN_EXT, GROUP_NORM and
  * NORM and leaves every other node of stable-diffusion.cpp's UNet graph to

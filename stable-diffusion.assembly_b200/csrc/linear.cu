@@ -244,13 +244,14 @@ bool mul_mat_shapes(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* 
 // transient: w is packed into the workspace on every call instead of being
 // kept by the store (an operand the graph writes between calls).
 int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
-               cudaStream_t st, bool gated, bool transient = false, const GnIn* gn = nullptr) {
+               cudaStream_t st, bool gated, bool transient = false, const GnIn* gn = nullptr,
+               const LnIn* ln = nullptr) {
     const int64_t k = w->ne[0];
     const int64_t n = gated ? w->ne[1] / 2 : w->ne[1];
     const int64_t m = x->ne[1] * x->ne[2] * x->ne[3];
     if (m > (1LL << 30) || k > (1 << 24)) return fail(SDB_NOT_SUPPORTED, "mul_mat: too large");
     if (!transient && quantized_linear(m)) {
-        if (gn) return fail(SDB_NOT_SUPPORTED, "mul_mat: no GroupNorm prologue on integer products");
+        if (gn || ln) return fail(SDB_NOT_SUPPORTED, "mul_mat: no normalisation prologue on integer products");
         return run_quantized_linear(w, x, dst, chain, st, gated);
     }
     std::shared_ptr<Packed> p;
@@ -303,10 +304,14 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     set_partials(a, ws, a_bytes, tiles, bn);
     const long long ne[4] = {x->ne[0], x->ne[1], x->ne[2], x->ne[3]};
     const long long nb[4] = {x->nb[0] / 4, x->nb[1] / 4, x->nb[2] / 4, x->nb[3] / 4};
-    if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err, st,
-                           gn);
-        s != SDB_OK)
+    if (ln) {
+        if (int s = layer_norm_split(x, ln->eps, ln->chain, kp8, static_cast<uint16_t*>(ws), a.err, st); s != SDB_OK)
+            return s;
+    } else if (int s = split_rows(static_cast<const float*>(x->data), ne, nb, kp8, static_cast<uint16_t*>(ws), a.err,
+                                  st, gn);
+               s != SDB_OK) {
         return s;
+    }
     // A as [plane][row][k]: one box {64, 128, 2} brings a tile's hi and lo rows.
     CUtensorMap amap;
     const uint64_t dims[3] = {static_cast<uint64_t>(kp8), static_cast<uint64_t>(m), 2};
@@ -585,6 +590,24 @@ int sdb_conv2d_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor
     GnIn gn{};
     if (int s = make_gn_in(norm, x->ne[2], x->ne[0] * x->ne[1], &gn); s != SDB_OK) return s;
     return conv2d_impl(w, x, dst, params, chain, stream, &gn);
+}
+
+int sdb_mul_mat_layer_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, float eps,
+                             const sdb_chain* norm_chain, const sdb_chain* chain, void* stream) {
+    if (!sdb_mul_mat_supported(w, x, dst)) return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat_layer_normed: not supported");
+    if (!valid_chain(chain)) return fail(SDB_INVALID, "sdb_mul_mat_layer_normed: invalid chain");
+    const LnIn ln{eps, norm_chain};
+    return run_linear(w, x, dst, chain, static_cast<cudaStream_t>(stream), false, false, nullptr, &ln);
+}
+
+int sdb_mul_mat_gated_layer_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* out, float eps,
+                                   const sdb_chain* norm_chain, const sdb_chain* chain, void* stream) {
+    if (!sdb_mul_mat_gated_supported(w, x, out))
+        return fail(SDB_NOT_SUPPORTED, "sdb_mul_mat_gated_layer_normed: not supported");
+    if (!valid_chain(chain) || (chain && (chain->redirect || chain->from_redirect)))
+        return fail(SDB_INVALID, "sdb_mul_mat_gated_layer_normed: invalid chain");
+    const LnIn ln{eps, norm_chain};
+    return run_linear(w, x, out, chain, static_cast<cudaStream_t>(stream), true, false, nullptr, &ln);
 }
 
 int sdb_mul_mat_normed(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_norm_in* norm,

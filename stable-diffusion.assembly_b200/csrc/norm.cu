@@ -13,6 +13,7 @@
 // double partial sums through global memory: the first pass writes per-CTA
 // partials, the second kernel finishes the statistics and normalises.  No CTA
 // waits on another (two launches instead of a grid barrier).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -830,6 +831,117 @@ int group_norm_nhwc(const sdb_tensor* x, const sdb_tensor* dst, int32_t groups, 
 }
 
 }  // namespace
+}  // namespace sdb
+
+namespace sdb {
+namespace {
+
+// ---- LayerNorm fused into the split of a linear layer's rows ----------------
+//
+// A transformer's LayerNorm feeds a linear layer, whose pre-pass splits every
+// FP32 row into FP16 hi and lo rows (split.cuh split_rows).  One warp a row
+// does both: the row in registers (element lane + 32 k, as norm_rows_reg_kernel
+// holds it), its mean and variance in double in the same order, (x - mean) *
+// scale, the LayerNorm's chain (its gamma and beta) step by step as the
+// LayerNorm kernel applies it -- the very numbers sdb_norm writes -- then
+// split into the hi and lo rows the GEMM reads.  The normalised row is never
+// written.
+template <int PER>
+__global__ void __launch_bounds__(256) norm_split_kernel(const RowArgs a, long long ld, uint16_t* __restrict__ out,
+                                                         unsigned* err) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= a.rows) return;
+    const int n = static_cast<int>(a.ne0);
+    const long long i1 = row % a.ne1, i2 = (row / a.ne1) % a.ne2, i3 = row / (a.ne1 * a.ne2);
+    const float* xr = a.x + i1 * a.xnb[1] + i2 * a.xnb[2] + i3 * a.xnb[3];
+    float v[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) v[k] = lane + 32 * k < n ? __ldg(xr + (lane + 32 * k) * a.xnb[0]) : 0.0f;
+    double s = 0.0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) s += static_cast<double>(v[k]);
+    s = warp_sum(s);
+    const float mean = static_cast<float>(s / static_cast<double>(n));
+    double q = 0.0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        if (lane + 32 * k < n) {
+            const float d = v[k] - mean;
+            q += static_cast<double>(d * d);
+        }
+    }
+    q = warp_sum(q);
+    const float scale = 1.0f / sqrtf(static_cast<float>(q / static_cast<double>(n)) + a.eps);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) v[k] = (v[k] - mean) * scale;
+    ChainRow cr;
+    row_offsets(a.chain, cr, 0, i1, i2, i3);
+#pragma unroll
+    for (int st = 0; st < SDB_MAX_STEPS; ++st) {
+        if (st >= a.chain.count) break;
+        if (a.chain.kind[st] == SDB_STEP_SILU) {
+#pragma unroll
+            for (int k = 0; k < PER; ++k) v[k] = silu(v[k]);
+        } else {
+            float o[PER];
+#pragma unroll
+            for (int k = 0; k < PER; ++k)
+                o[k] = __ldg(a.chain.operand[st] + cr.off[st] + min(lane + 32 * k, n - 1) * a.chain.nb[st][0]);
+#pragma unroll
+            for (int k = 0; k < PER; ++k) v[k] = a.chain.kind[st] == SDB_STEP_ADD ? v[k] + o[k] : v[k] * o[k];
+        }
+    }
+    bool over = false;
+    __half* hi = reinterpret_cast<__half*>(out) + row * ld;
+    __half* lo = reinterpret_cast<__half*>(out) + (a.rows + row) * ld;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int e = lane + 32 * k;
+        if (e < n) {
+            __half h, l;
+            split_half(v[k], h, l);
+            over |= !(fabsf(v[k]) <= kHalfLimit);
+            hi[e] = h;
+            lo[e] = l;
+        } else if (e < ld) {
+            hi[e] = __float2half_rn(0.0f);
+            lo[e] = __float2half_rn(0.0f);
+        }
+    }
+    for (int e = 32 * PER + lane; e < ld; e += 32) {
+        hi[e] = __float2half_rn(0.0f);
+        lo[e] = __float2half_rn(0.0f);
+    }
+    if (over) atomicOr(err, kErrRange);
+}
+
+}  // namespace
+
+// LayerNorm of x's rows with its chain, split into out: hi rows [0, R), lo rows [R, 2R) of ld FP16.
+int layer_norm_split(const sdb_tensor* x, float eps, const sdb_chain* chain, long long ld, uint16_t* out,
+                     unsigned* err, cudaStream_t st) {
+    if (!f32(x) || x->nb[0] % 4 || x->nb[1] % 4 || x->nb[2] % 4 || x->nb[3] % 4 || ld < x->ne[0])
+        return fail(SDB_NOT_SUPPORTED, "LayerNorm prologue: not supported");
+    if (chain && (chain->count > SDB_MAX_STEPS || chain->redirect || chain->from_redirect))
+        return fail(SDB_INVALID, "LayerNorm prologue: invalid chain");
+    RowArgs a{};
+    a.x = static_cast<const float*>(x->data);
+    a.ne0 = x->ne[0]; a.ne1 = x->ne[1]; a.ne2 = x->ne[2];
+    a.rows = x->ne[1] * x->ne[2] * x->ne[3];
+    for (int d = 0; d < 4; ++d) a.xnb[d] = x->nb[d] / 4;
+    a.eps = eps;
+    a.chain = make_chain(chain);
+    const unsigned blocks = static_cast<unsigned>((a.rows * 32 + 255) / 256);
+    const int per = static_cast<int>((a.ne0 + 31) / 32);
+    if (per <= 10) norm_split_kernel<10><<<blocks, 256, 0, st>>>(a, ld, out, err);
+    else if (per <= 20) norm_split_kernel<20><<<blocks, 256, 0, st>>>(a, ld, out, err);
+    else if (per <= 40) norm_split_kernel<40><<<blocks, 256, 0, st>>>(a, ld, out, err);
+    else return fail(SDB_NOT_SUPPORTED, "LayerNorm prologue: rows of at most 1280");
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
 }  // namespace sdb
 
 extern "C" int sdb_group_norm_stats(const sdb_tensor* x, int32_t groups, float eps, float* stats, void* stream) {

@@ -33,6 +33,14 @@ int workspace(cudaStream_t stream, size_t bytes, void** out);
 struct GnIn;
 int split_rows(const float* x, const long long ne[4], const long long xnb[4], long long ld, uint16_t* out,
                unsigned* err, cudaStream_t stream, const GnIn* gn = nullptr);
+// The rows of x through a LayerNorm (norm.cc:148-175) with its chain (gamma,
+// beta) first, as sdb_norm computes them, then split the same way (norm.cu).
+int layer_norm_split(const sdb_tensor* x, float eps, const sdb_chain* chain, long long ld, uint16_t* out,
+                     unsigned* err, cudaStream_t stream);
+struct LnIn {
+    float eps;
+    const sdb_chain* chain;
+};
 // The same for an FP16 source (hi = the value, lo = 0).
 int split_rows_half(const uint16_t* x, const long long ne[4], const long long xnb[4], long long ld, uint16_t* out,
                     cudaStream_t stream);

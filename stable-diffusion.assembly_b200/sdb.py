@@ -41,7 +41,7 @@ EXPORTS = [
     "sdb_set_tuning", "sdb_get_tuning", "sdb_device_status", "sdb_last_error", "sdb_launch_count",
     "sdb_concat", "sdb_upscale_nearest", "sdb_timestep_embedding", "sdb_euler_cfg_step", "sdb_soft_max",
     "sdb_coarser_tokens", "sdb_euler_ancestral_cfg_step", "sdb_group_norm_stats", "sdb_conv2d_normed",
-    "sdb_mul_mat_normed",
+    "sdb_mul_mat_normed", "sdb_mul_mat_layer_normed", "sdb_mul_mat_gated_layer_normed",
 ]
 
 
@@ -116,6 +116,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         "sdb_group_norm_stats": (i, [T, ctypes.c_int32, ctypes.c_float, vp, vp]),
         "sdb_conv2d_normed": (i, [T, T, T, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(NormIn), C, vp]),
         "sdb_mul_mat_normed": (i, [T, T, T, ctypes.POINTER(NormIn), C, vp]),
+        "sdb_mul_mat_layer_normed": (i, [T, T, T, ctypes.c_float, C, C, vp]),
+        "sdb_mul_mat_gated_layer_normed": (i, [T, T, T, ctypes.c_float, C, C, vp]),
         "sdb_euler_cfg_step": (i, [vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                    ctypes.c_float, vp]),
         "sdb_euler_ancestral_cfg_step": (i, [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_float, ctypes.c_float,
@@ -553,6 +555,23 @@ def mul_mat_normed(w, x, norm: GroupNormIn, out=None, chain: Chain | None = None
     _guard_weight(w)
     _check(lib.sdb_mul_mat_normed(describe(w), describe(x), describe(out), ctypes.byref(norm.c), _chain_ptr(chain),
                                   ctypes.c_void_p(_stream_ptr(stream))))
+    return out
+
+
+def mul_mat_layer_normed(w, x, eps: float, norm_chain: Chain | None = None, out=None, chain: Chain | None = None,
+                         gated: bool = False, stream=None):
+    """mul_mat (or mul_mat_gated) of LayerNorm(x) with its chain (gamma, beta), the normalisation done in
+    the linear layer's split of the rows: x (..., K) -> (..., N) (N / 2 gated)."""
+    import torch
+
+    lib = load()
+    if out is None:
+        n = w.shape[0] // 2 if gated else w.shape[0]
+        out = torch.empty(*x.shape[:-1], n, dtype=torch.float32, device=x.device)
+    _guard_weight(w)
+    fn = lib.sdb_mul_mat_gated_layer_normed if gated else lib.sdb_mul_mat_layer_normed
+    _check(fn(describe(w), describe(x), describe(out), ctypes.c_float(eps), _chain_ptr(norm_chain), _chain_ptr(chain),
+              ctypes.c_void_p(_stream_ptr(stream))))
     return out
 
 

@@ -254,6 +254,8 @@ class UNet:
         # GroupNorm fused into the convolution or linear layer that reads it (sdb_conv2d_normed,
         # sdb_mul_mat_normed); False runs it as the reference's separate node (the same numbers).
         self.fuse_gn = True
+        # LayerNorm fused into the linear layer that reads it (sdb_mul_mat_layer_normed); False: separate.
+        self.fuse_ln = True
 
     # ------------------------------------------------------------ pieces
 
@@ -293,6 +295,14 @@ class UNet:
     def _ln(self, x, ln):
         return sdb.norm(x, 1e-5, chain=sdb.Chain().mul(ln[0]).add(ln[1]))
 
+    def _ln_linear(self, w, x, ln, chain=None, gated=False):
+        """The linear layer (or GEGLU) of LayerNorm(x): fused, the normalisation inside the layer's split of
+        its rows (fuse_ln), or as the reference's separate NORM node."""
+        if self.fuse_ln:
+            return sdb.mul_mat_layer_normed(w, x, 1e-5, sdb.Chain().mul(ln[0]).add(ln[1]), chain=chain, gated=gated)
+        h = self._ln(x, ln)
+        return sdb.mul_mat_gated(w, h, chain=chain) if gated else sdb.mul_mat(w, h, chain=chain)
+
     def _transformer(self, x, tr: Transformer, ctx_kv):
         b, hh, ww, c = x.shape
         heads = tr.heads
@@ -308,24 +318,22 @@ class UNet:
         f = sdb.token_downsampling(ww, hh)
         for blk in tr.blocks:
             # Self-attention.
-            h1 = self._ln(t, blk.ln1)
             if f > 1:
+                h1 = self._ln(t, blk.ln1)
                 q = sdb.mul_mat(blk.wq, h1)
                 kv = sdb.mul_mat(blk.wkv, sdb.coarser_tokens(h1, ww, hh, f))
                 a = sdb.attention_heads(q, kv[:, :, :c], kv[:, :, c:], heads, heads, scale)
             else:
-                qkv = sdb.mul_mat(blk.wqkv, h1)
+                qkv = self._ln_linear(blk.wqkv, t, blk.ln1)
                 a = sdb.attention_heads(qkv[:, :, :c], qkv[:, :, c:2 * c], qkv[:, :, 2 * c:], heads, heads, scale)
             sdb.mul_mat(blk.wo1, a, out=t, chain=sdb.Chain().add(blk.bo1).redirect(t, True))
             # Cross-attention on the text context.
-            h2 = self._ln(t, blk.ln2)
-            q2 = sdb.mul_mat(blk.wq2, h2)
+            q2 = self._ln_linear(blk.wq2, t, blk.ln2)
             kv = ctx_kv[:, :, blk.kv_offset:blk.kv_offset + 2 * c]
             a2 = sdb.attention_heads(q2, kv[:, :, :c], kv[:, :, c:], heads, heads, scale)
             sdb.mul_mat(blk.wo2, a2, out=t, chain=sdb.Chain().add(blk.bo2).redirect(t, True))
             # GEGLU feed-forward.
-            h3 = self._ln(t, blk.ln3)
-            g = sdb.mul_mat_gated(blk.wff1, h3, chain=sdb.Chain().add(blk.bff1))
+            g = self._ln_linear(blk.wff1, t, blk.ln3, chain=sdb.Chain().add(blk.bff1), gated=True)
             sdb.mul_mat(blk.wff2, g, out=t, chain=sdb.Chain().add(blk.bff2).redirect(t, True))
         # Back to the image, plus the block's input.
         xv = x.view(b, hh * ww, c)

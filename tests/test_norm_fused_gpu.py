@@ -1,5 +1,5 @@
-"""GroupNorm fused into the operation that reads its output (sdb_group_norm_stats, sdb_conv2d_normed,
-sdb_mul_mat_normed), against the reference's separate nodes.
+"""GroupNorm and LayerNorm fused into the operation that reads their output (sdb_group_norm_stats,
+sdb_conv2d_normed, sdb_mul_mat_normed; sdb_mul_mat_layer_normed), against the reference's separate nodes.
 
 The reference computes GROUP_NORM as a node of its own (norm.cc:100-140) between a convolution and the
 next.  The fused path computes the group statistics once and normalises the input as the next
@@ -147,3 +147,29 @@ def test_config2_block_fused_within_bound(cuda, c, hw):
     # The first convolution's own error (<= its bound, relative to its magnitudes) passes through the
     # normalisation (scale 1/std) and the second convolution: a few times 1e-6 of the magnitudes.
     assert err <= 5e-6, f"error {err:.3g}"
+
+
+@pytest.mark.parametrize("rows,k,n,gated", [(2 * 4096, 320, 960, False), (77, 640, 640, False), (300, 1280, 2 * 1280, True),
+                                            (33, 40, 24, False)])
+def test_linear_layer_normed_equals_separate_nodes(cuda, rows, k, n, gated):
+    """LayerNorm (eps 1e-5, gamma and beta) fused into the split of the next linear layer (or GEGLU) equals
+    sdb_norm followed by the layer, bit for bit."""
+    import sdb
+    import torch
+
+    g = rng(14)
+    x = torch.from_numpy(oracle.uniform(g, (rows, k), 3.0) + np.float32(0.25)).cuda()
+    w = torch.from_numpy(oracle.uniform(g, (n, k), 0.25 / np.sqrt(k), np.float16)).cuda()
+    b = torch.from_numpy(oracle.uniform(g, (n,), 0.1)).cuda()
+    gamma, beta = affine(k, g)
+    ln = sdb.Chain().mul(gamma).add(beta)
+    fused = sdb.mul_mat_layer_normed(w, x, 1e-5, ln, chain=sdb.Chain().add(b), gated=gated)
+    h = sdb.norm(x, 1e-5, chain=ln)
+    apart = (sdb.mul_mat_gated if gated else sdb.mul_mat)(w, h, chain=sdb.Chain().add(b))
+    torch.cuda.synchronize()
+    assert torch.isfinite(fused).all()
+    assert torch.equal(fused, apart)
+    # And the separate LayerNorm is the reference's (norm.cc:148-175) within 1e-6 of its largest output.
+    want = oracle.apply_chain(oracle.norm_ref(x.cpu().numpy()[:64], 1e-5),
+                              [("mul", gamma.cpu().numpy()), ("add", beta.cpu().numpy())])
+    assert np.abs(h.cpu().numpy()[:64] - want).max() <= 1e-6 * np.abs(want).max()

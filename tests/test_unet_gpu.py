@@ -244,10 +244,11 @@ def test_sd15_unet_eight_images(cuda):
     torch.cuda.empty_cache()
 
 
-def test_sd15_unet_fused_groupnorm_equals_separate_nodes(cuda):
-    """SD 1.5's forward with every GroupNorm fused into the convolution or linear layer that reads it
-    (sdb_group_norm_stats + sdb_conv2d_normed / sdb_mul_mat_normed) equals the forward with the
-    reference's separate GROUP_NORM nodes, bit for bit."""
+def test_sd15_unet_fused_norms_equal_separate_nodes(cuda):
+    """SD 1.5's forward with its GroupNorms and LayerNorms fused into the convolution or linear layer
+    that reads them (sdb_group_norm_stats + sdb_conv2d_normed / sdb_mul_mat_normed,
+    sdb_mul_mat_layer_normed) equals the forward with the reference's separate GROUP_NORM and NORM
+    nodes, bit for bit."""
     import torch
     import unet as U
 
@@ -256,11 +257,11 @@ def test_sd15_unet_fused_groupnorm_equals_separate_nodes(cuda):
     x = torch.randn(2, 64, 64, 4, device=cuda, generator=g)
     t = torch.tensor([600.0, 600.0], device=cuda)
     ctx = torch.randn(2, 77, 768, device=cuda, generator=g)
-    net.fuse_gn = True
+    net.fuse_gn = net.fuse_ln = True
     fused = net.forward(x, t, ctx).clone()
-    net.fuse_gn = False
+    net.fuse_gn = net.fuse_ln = False
     apart = net.forward(x, t, ctx).clone()
-    net.fuse_gn = True
+    net.fuse_gn = net.fuse_ln = True
     torch.cuda.synchronize()
     assert torch.isfinite(fused).all()
     assert torch.equal(fused, apart)
