@@ -73,7 +73,7 @@ typedef enum sdb_status {
 /* ---- linear layers: GGML_OP_MUL_MAT of a weight matrix ------------------
  * dst[m][n] = sum_k x[m][k] * w[n][k] (+ chain), for w FP16 or FP32 [K, N]
  * and x, dst FP32 with rows m over dimensions 1..3 (mul_mat.cc:9-18).
- * Replaces sdasm::mul_mat_supported / mul_mat_compute (ops.h:124-126,
+ * Replaces sdasm::mul_mat_supported / mul_mat_compute (ops.h:40-42,
  * mul_mat.cc:181-194, 1175-1196). */
 int sdb_mul_mat_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst);
 int sdb_mul_mat(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const sdb_chain *chain,
@@ -90,7 +90,7 @@ int sdb_mul_mat_transient(const sdb_tensor *w, const sdb_tensor *x, const sdb_te
                           void *stream);
 /* The linear layer with the gated GELU after it (GEGLU): out[m][j] =
  * y[m][j] * GELU(y[m][half + j]), y the product with its chain, half = N/2.
- * Replaces sdasm::mul_mat_gated_supported / mul_mat_compute_gated (ops.h:127-131,
+ * Replaces sdasm::mul_mat_gated_supported / mul_mat_compute_gated (ops.h:43-47,
  * fusion.h:110-129, mul_mat.cc:934-1058). */
 int sdb_mul_mat_gated_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *out);
 int sdb_mul_mat_gated(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *out, const sdb_chain *chain,
@@ -100,7 +100,7 @@ int sdb_mul_mat_gated(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor
  * w [KW, KH, IC, OC] FP16 or FP32, x [W, H, IC, N] FP32, dst [OW, OH, OC, N]
  * FP32; params = {s0, s1, p0, p1, d0, d1} as ggml_conv_2d_direct's op_params.
  * 3x3 stride-1 cases go to Winograd when the tuning allows.  Replaces
- * sdasm::conv2d_* and winograd_* (ops.h:110-120, conv2d.cc:837-858,
+ * sdasm::conv2d_* and winograd_* (ops.h:26-36, conv2d.cc:837-858,
  * winograd.cc:2107-2272). */
 int sdb_conv2d_supported(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const int32_t params[6]);
 int sdb_conv2d(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, const int32_t params[6],
@@ -109,7 +109,7 @@ int sdb_conv2d(const sdb_tensor *w, const sdb_tensor *x, const sdb_tensor *dst, 
 /* ---- attention: GGML_OP_FLASH_ATTN_EXT without a mask --------------------
  * q [D, LQ, H, B], k [D, LK, HK, B], v [DV, LK, HK, B] (FP32, or FP16 k/v),
  * dst [DV, H, LQ, B] FP32: softmax(scale q k^T) v per head, H % HK == 0.
- * Replaces sdasm::attention_supported / attention_compute (ops.h:133-138,
+ * Replaces sdasm::attention_supported / attention_compute (ops.h:49-54,
  * attention.cc:828-1064).  With a chain (residual add: an extension of the
  * reference, which fuses nothing into attention) the chain is applied to dst. */
 int sdb_attention_supported(const sdb_tensor *q, const sdb_tensor *k, const sdb_tensor *v, const sdb_tensor *dst);
@@ -118,7 +118,7 @@ int sdb_attention(const sdb_tensor *q, const sdb_tensor *k, const sdb_tensor *v,
 
 /* ---- normalisation: GGML_OP_GROUP_NORM and GGML_OP_NORM -----------------
  * Mean and variance in double precision, two passes, then the chain
- * (norm.cc:100-175).  Replaces sdasm::group_norm_* / norm_* (ops.h:140-146). */
+ * (norm.cc:100-175).  Replaces sdasm::group_norm_* / norm_* (ops.h:56-62). */
 int sdb_group_norm(const sdb_tensor *x, const sdb_tensor *dst, int32_t groups, float eps, const sdb_chain *chain,
                    void *stream);
 /* (x and dst may also be channels-last images -- [W, H, C, N] with nb[2] = 4 --
