@@ -809,6 +809,372 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
     }
 }
 
+// ---- both A operands in tensor memory, two CTAs an SM ----------------------
+//
+// For heads up to 64 dims (value chunks up to 64).  Q and P, the A operands of
+// the two products, live in tensor memory, so the tensor core reads only K and
+// V from shared memory, and a CTA takes 256 columns, so that two CTAs share an
+// SM.  One CTA's products issue at ~47 cycles each whatever their width up to
+// N = 64; the two CTAs' streams overlap (measured: M = 128, N = 48, K = 16
+// products at 4200 FLOP/cycle for one CTA, 8100 for two; with A in shared
+// memory the operand reads fill shared memory's ~128 B/cycle and the second
+// stream gains little).
+// Warp 0 loads the K/V stages; warp 1 issues the products; warps 2-5 (one
+// query row a thread) first write their Q rows into tensor memory, then per
+// block of 64 keys read S, take the weights against the reference maximum
+// (raised as in the kernels above), write P -- the FP16 pairs of split8_inrange,
+// so the same products -- over S's columns, and add the previous block's P V
+// into their registers before publishing P.  The next block's S is issued
+// before this block's P V, into the other buffer.
+// Tensor memory (columns): S / P buffers [0, 64) and [64, 128) (P hi in the
+// first 32 columns of a buffer, lo in the next 32); O [128, 128 + DVC); Q hi
+// then lo from 128 + DVC, dp / 2 columns each.
+constexpr int kAttnTmThreads = 192;
+constexpr int kAttnTmBK = 64;
+constexpr int kAttnTmMaxStages = 4;
+
+struct AttnTmLayout {
+    int stage_bytes, k_lo, v_hi, v_lo, stages, bars, total;
+    __host__ __device__ AttnTmLayout(int dp, int dvc) {
+        const int kb = kAttnTmBK * dp * 2, vb = kAttnTmBK * dvc * 2;
+        k_lo = kb;
+        v_hi = 2 * kb;
+        v_lo = 2 * kb + vb;
+        stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
+        // Stages within 96 KB, so that two CTAs fit an SM's shared memory.
+        const int fit = (96 * 1024) / stage_bytes;
+        stages = fit < kAttnTmMaxStages ? fit : kAttnTmMaxStages;
+        bars = stages * stage_bytes;
+        total = bars + 256;
+    }
+};
+
+__host__ __device__ constexpr bool attention_tm_fits(int dp, int dvc) {
+    return 2 * kAttnTmBK + dvc + dp <= 256 && dp <= 64 && dvc <= 64;
+}
+
+// max (scale >= 0) or min (scale < 0) of a block's scores: the one whose
+// scaled value is the block's largest.
+template <bool kMin>
+__device__ __forceinline__ float extreme64(const float (&s)[kAttnTmBK]) {
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = s[i];
+#pragma unroll
+    for (int i = 4; i < kAttnTmBK; i += 8) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (i + 2 * t + 1 < kAttnTmBK)
+                e[t] = kMin ? -fmax3(-e[t], -s[i + 2 * t], -s[i + 2 * t + 1]) : fmax3(e[t], s[i + 2 * t], s[i + 2 * t + 1]);
+        }
+    }
+    return kMin ? fminf(fminf(e[0], e[1]), fminf(e[2], e[3])) : fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3]));
+}
+
+// The softmax warpgroup of attention_tm_kernel (warps 2-5, thread = query row).
+template <int DVC>
+__device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const AttnTmLayout& L, uint32_t tmem,
+                                                     uint32_t t_o, uint32_t t_qh, uint32_t t_ql, uint64_t* q_full,
+                                                     uint64_t* s_full, uint64_t* p_full, uint64_t* o_full,
+                                                     volatile int* abort, int q0, int head, int dv0, int batch,
+                                                     int nblk) {
+    constexpr int BK = kAttnTmBK;
+    constexpr int OCH = DVC / 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = warp & 3;  // lane quarter of tensor memory this warp may access
+    const int r = q * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, a.err) ? 1 : 0) != 0;
+    };
+
+    // Row r of the Q tile (hi, then lo: 16-byte chunks of 8 dims, [chunk][row][8]) into tensor memory.
+    {
+        const uint8_t* qt =
+            a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + blockIdx.x) * (kAttnQ * a.dp * 2);
+        for (int plane = 0; plane < 2; ++plane) {
+            const uint8_t* src = qt + plane * a.q_plane;
+            const uint32_t dst = (plane ? t_ql : t_qh) + lane_off;
+            for (int c0 = 0; c0 < a.dp / 8; c0 += 2) {
+                const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(src + (c0 * kAttnQ + r) * 16));
+                const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(src + ((c0 + 1) * kAttnQ + r) * 16));
+                const uint32_t w[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+                tmem_st8_bits(dst + c0 * 4, w);
+            }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
+    }
+
+    const bool neg = a.scale2 < 0.0f;
+    const float masked = neg ? INFINITY : -INFINITY;
+    const uint64_t scale2 = pack2(a.scale2, a.scale2);
+    float m_ref = -INFINITY;
+    double l = 0.0;
+    float o[DVC];
+#pragma unroll
+    for (int i = 0; i < DVC; ++i) o[i] = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+        if (!warp_wait(&s_full[j & 1], (j >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sb = tmem + (j & 1) * BK + lane_off;
+        float s[BK];
+        tmem_ld32(sb, *reinterpret_cast<float(*)[32]>(s));
+        tmem_ld32(sb + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+        tmem_ld_wait();
+        const int valid = a.lk - j * BK;
+        if (valid < BK) {
+#pragma unroll
+            for (int i = 0; i < BK; ++i)
+                if (i >= valid) s[i] = masked;
+        }
+        const float bmax = (neg ? extreme64<true>(s) : extreme64<false>(s)) * a.scale2;
+        float factor = 1.0f;
+        if (j == 0) {
+            m_ref = bmax;
+        } else if (bmax > m_ref + kRescaleAbove) {
+            factor = ex2(m_ref - bmax);
+            m_ref = bmax;
+        }
+        // The weights 2^(s scale2 - m), two keys a packed FMA.
+        const uint64_t nm = pack2(-m_ref, -m_ref);
+#pragma unroll
+        for (int i = 0; i < BK; i += 2) {
+            float x0, x1;
+            unpack2(ffma2(pack2(s[i], s[i + 1]), scale2, nm), x0, x1);
+            s[i] = ex2(x0);
+            s[i + 1] = ex2(x1);
+        }
+        // P over S's columns: hi pairs in columns [0, 32), lo pairs in [32, 64).
+#pragma unroll
+        for (int c = 0; c < BK / 16; ++c) {
+            uint32_t ph[8], pl[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) split_weights2(s[c * 16 + 2 * w], s[c * 16 + 2 * w + 1], ph[w], pl[w]);
+            tmem_st8_bits(sb + c * 8, ph);
+            tmem_st8_bits(sb + 32 + c * 8, pl);
+        }
+        // The block's weights summed pairwise, two lanes of pairs at a time.
+        uint64_t sum2[BK / 4];
+#pragma unroll
+        for (int i = 0; i < BK / 4; ++i) sum2[i] = fadd2(pack2(s[2 * i], s[2 * i + 1]), pack2(s[BK / 2 + 2 * i], s[BK / 2 + 2 * i + 1]));
+#pragma unroll
+        for (int w = BK / 8; w > 0; w >>= 1) {
+#pragma unroll
+            for (int i = 0; i < w; ++i) sum2[i] = fadd2(sum2[i], sum2[i + w]);
+        }
+        float b0, b1;
+        unpack2(sum2[0], b0, b1);
+        l = l * static_cast<double>(factor) + static_cast<double>(b0 + b1);
+        // The previous block's product (taken against the old maximum) into the registers: its
+        // accumulator is then free for this block's.
+        if (j >= 1) {
+            if (!warp_wait(o_full, (j - 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            float oh[DVC];
+#pragma unroll
+            for (int ch = 0; ch < OCH; ++ch) tmem_ld16(t_o + lane_off + ch * 16, *reinterpret_cast<float(*)[16]>(oh + ch * 16));
+            tmem_ld_wait();
+            if (factor != 1.0f) {
+#pragma unroll
+                for (int i = 0; i < DVC; ++i) o[i] = (o[i] + oh[i]) * factor;
+            } else {
+#pragma unroll
+                for (int i = 0; i < DVC; ++i) o[i] += oh[i];
+            }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!ok) return;
+    if (!warp_wait(o_full, (nblk - 1) & 1)) return;
+    tc_fence_after();
+    {
+        float oh[DVC];
+#pragma unroll
+        for (int ch = 0; ch < OCH; ++ch) tmem_ld16(t_o + lane_off + ch * 16, *reinterpret_cast<float(*)[16]>(oh + ch * 16));
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < DVC; ++i) o[i] += oh[i];
+    }
+    if (qi >= a.lq) return;
+    const float recip = static_cast<float>(1.0 / l);
+#pragma unroll
+    for (int i = 0; i < DVC; ++i) o[i] *= recip;
+    ChainRow cr;
+    row_offsets(a.chain, cr, 0, head, qi, batch);
+#pragma unroll
+    for (int c = 0; c < DVC; c += 16) apply_chain_cols<0, 16>(a.chain, cr, o + c, dv0 + c, a.dv - 1);
+    const int ncols = min(DVC, a.dv - dv0);
+    float* orow = a.out + static_cast<long long>(head) * a.onb[1] + static_cast<long long>(qi) * a.onb[2] +
+                  static_cast<long long>(batch) * a.onb[3];
+    if (a.onb[0] == 1 && ncols % 4 == 0 && ((reinterpret_cast<uintptr_t>(orow + dv0)) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < DVC; i += 4)
+            if (i < ncols) *reinterpret_cast<float4*>(orow + dv0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < DVC; ++i)
+            if (i < ncols) orow[static_cast<long long>(dv0 + i) * a.onb[0]] = o[i];
+    }
+}
+
+template <int DVC>
+__global__ void __launch_bounds__(kAttnTmThreads, 2) attention_tm_kernel(const AttnArgs a) {
+    constexpr int BK = kAttnTmBK;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    const AttnTmLayout L(a.dp, DVC);
+    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [stages]
+    uint64_t* kv_empty = kv_full + kAttnTmMaxStages;                 // [stages]
+    uint64_t* q_full = kv_empty + kAttnTmMaxStages;
+    uint64_t* s_full = q_full + 1;  // [2] per S buffer
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_full = p_full + 1;
+    uint64_t* drain = o_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kAttnQ;
+    const int head = blockIdx.y / a.dv_chunks;
+    const int dv0 = (blockIdx.y - head * a.dv_chunks) * DVC;
+    const int batch = blockIdx.z;
+    const int khead = head / (a.h / a.hk);
+    const int nblk = (a.lk + BK - 1) / BK;
+    const int stages = L.stages;
+    const uint32_t base = smem_u32(smem);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(q_full, 4);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_o = tmem + 2 * BK;
+    const uint32_t t_qh = t_o + DVC;
+    const uint32_t t_ql = t_qh + a.dp / 2;
+
+    if (warp == 0) {
+        // ------------------------------------------------ bulk-copy producer
+        if (lane == 0) {
+            const uint32_t kbytes = BK * a.dp * 2, vbytes = BK * DVC * 2;
+            const long long ktile0 = static_cast<long long>(batch * a.hk + khead) * a.ntk;
+            int issued = 0;
+            for (int j = 0; j < nblk; ++j) {
+                const int s = j % stages;
+                if (!mbar_wait(&kv_empty[s], ((j / stages) & 1) ^ 1, abort, a.err)) break;
+                uint8_t* st = smem + s * L.stage_bytes;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kbytes + 2 * vbytes);
+                const uint8_t* kt = a.ks + (ktile0 + j) * kbytes;
+                const uint8_t* vt = a.vs + (ktile0 + j) * static_cast<long long>(BK) * a.dvs * 2 +
+                                    static_cast<long long>(dv0 / 8) * BK * 16;
+                bulk_load(st, kt, kbytes, &kv_full[s]);
+                bulk_load(st + L.k_lo, kt + a.k_plane, kbytes, &kv_full[s]);
+                bulk_load(st + L.v_hi, vt, vbytes, &kv_full[s]);
+                bulk_load(st + L.v_lo, vt + a.v_plane, vbytes, &kv_full[s]);
+                ++issued;
+            }
+            if (*abort) {
+                for (int j = (issued > stages ? issued - stages : 0); j < issued; ++j)
+                    mbar_wait_quiet(&kv_full[j % stages], (j / stages) & 1, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16_f32(kAttnQ, BK);
+            const uint32_t id_pv = idesc_f16_f32_bmajor(kAttnQ, DVC, 1);
+            const uint32_t k_lbo = BK * 16;
+            // S = Q K^T into buffer j & 1: the lo products (Q.K lo, Q lo.K, each
+            // carrying 2^11) first, then Q.K hi with the input scale 2^-11.
+            auto issue_s = [&](int j) {
+                const uint32_t st = base + (j % stages) * L.stage_bytes;
+                const uint32_t sb = tmem + (j & 1) * BK;
+                for (int kk = 0; kk < a.dp / 16; ++kk) {
+                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, 128);
+                    const uint64_t kl = desc_noswizzle(st + L.k_lo + kk * 2 * k_lbo, k_lbo, 128);
+                    mma_f16_ta(sb, t_qh + kk * 8, kl, id_s, kk > 0 ? 1u : 0u);
+                    mma_f16_ta(sb, t_ql + kk * 8, kh, id_s, 1u);
+                }
+                for (int kk = 0; kk < a.dp / 16; ++kk) {
+                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, 128);
+                    if (kk == 0) mma_f16_ta_scale_lo(sb, t_qh, kh, id_s);
+                    else mma_f16_ta(sb, t_qh + kk * 8, kh, id_s, 1u);
+                }
+                mma_commit(&s_full[j & 1]);
+            };
+            // O = P V from the P that the softmax warps wrote over S(j).
+            auto issue_pv = [&](int j) {
+                const int s = j % stages;
+                const uint32_t st = base + s * L.stage_bytes;
+                const uint32_t pb = tmem + (j & 1) * BK;
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
+                    const uint64_t vl = desc_noswizzle(st + L.v_lo + kk * 256, 128, BK * 16);
+                    mma_f16_ta(t_o, pb + kk * 8, vl, id_pv, kk > 0 ? 1u : 0u);
+                    mma_f16_ta(t_o, pb + 32 + kk * 8, vh, id_pv, 1u);
+                }
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
+                    if (kk == 0) mma_f16_ta_scale_lo(t_o, pb, vh, id_pv);
+                    else mma_f16_ta(t_o, pb + kk * 8, vh, id_pv, 1u);
+                }
+                mma_commit(o_full);
+                mma_commit(&kv_empty[s]);
+            };
+            bool ok = mbar_wait(q_full, 0, abort, a.err);
+            for (int j = 0; j < nblk && ok; ++j) {
+                if (!mbar_wait(&kv_full[j % stages], (j / stages) & 1, abort, a.err)) { ok = false; break; }
+                tc_fence_after();
+                issue_s(j);
+                if (j >= 1) {
+                    if (!mbar_wait(p_full, (j - 1) & 1, abort, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv(j - 1);
+                }
+            }
+            if (ok && mbar_wait(p_full, (nblk - 1) & 1, abort, a.err)) {
+                tc_fence_after();
+                issue_pv(nblk - 1);
+            } else {
+                mma_commit(drain);
+                mbar_wait_quiet(drain, 0, 100000000ull);
+            }
+        }
+    } else {
+        attention_tm_softmax<DVC>(a, L, tmem, t_o, t_qh, t_ql, q_full, s_full, p_full, o_full, abort, q0, head,
+                                  dv0, batch, nblk);
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 bool floaty(const sdb_tensor* t) {
     return t && t->data && (t->type == SDB_TYPE_F32 || t->type == SDB_TYPE_F16);
 }
@@ -886,6 +1252,24 @@ int launch_attention_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, c
     return SDB_OK;
 }
 
+// Shared memory of at least a third of an SM's, so that no third CTA shares an
+// SM with two that hold all its tensor memory.
+template <int DVC>
+int launch_attention_tm(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    const AttnTmLayout L(a.dp, DVC);
+    const int smem = std::max(L.total + 128, 80 * 1024);
+    if (int s = prepare_tiles<kAttnTmBK, DVC>(a, q, k, v, st); s != SDB_OK) return s;
+    auto kern = attention_tm_kernel<DVC>;
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    const dim3 grid(static_cast<unsigned>((a.lq + kAttnQ - 1) / kAttnQ), static_cast<unsigned>(a.h * a.dv_chunks),
+                    static_cast<unsigned>(a.b));
+    kern<<<grid, kAttnTmThreads, smem, st>>>(a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    return SDB_OK;
+}
+
 // The two-warpgroup kernel when its S buffers and two output accumulators fit
 // tensor memory (heads up to 64 dims with 64-key blocks, up to 128 with 32).
 template <int DVC>
@@ -912,6 +1296,9 @@ int launch_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_t
 // whose S double buffer and output accumulators fit tensor memory.
 template <int DVC>
 int launch_bk(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    if constexpr (DVC <= 64) {
+        if (tuning().attention_wg == 2 && attention_tm_fits(a.dp, DVC)) return launch_attention_tm<DVC>(a, q, k, v, st);
+    }
     if (tuning().attention_wg) {
         bool taken = false;
         const int rc = launch_wg<DVC>(a, q, k, v, st, &taken);

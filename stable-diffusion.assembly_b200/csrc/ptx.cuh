@@ -279,6 +279,26 @@ __device__ __forceinline__ void mma_f16_scale_lo(uint32_t tmem_d, uint64_t adesc
                  : "memory");
 }
 
+// The same two products with the A operand in tensor memory: `a_tmem` is the
+// address of a 128-lane x 8-column block, lane m holding row m's 16 values of
+// K as FP16 pairs (column c: k = 2c in the low half, 2c + 1 in the high).
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_ta_scale_lo(uint32_t tmem_d, uint32_t a_tmem, uint64_t bdesc,
+                                                    uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1, 11;" ::"r"(tmem_d), "r"(a_tmem),
+                 "l"(bdesc), "r"(idesc)
+                 : "memory");
+}
+
 // Arrives on `bar` once every tcgen05 operation this thread issued before has
 // completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -337,6 +357,53 @@ __device__ __forceinline__ void tmem_st16(uint32_t addr, const float (&v)[16]) {
 
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 / 8 columns of 32-bit words from registers into tensor memory.
+__device__ __forceinline__ void tmem_st32_bits(uint32_t addr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8_bits(uint32_t addr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float m;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+    return m;
+}
+
+// Two softmax weights (inside FP16's range) split as split_half does, as the
+// FP16 pairs of two consecutive keys: hi = {fp16(p0), fp16(p1)} and
+// lo = {fp16((p0 - hi0) 2^11), fp16((p1 - hi1) 2^11)}, the first key in the
+// low half.  hi - p comes exact from the FP16 hi and the FP32 weight in one
+// mixed-precision subtraction; the 2^11 (negated) in one packed multiply.
+__device__ __forceinline__ void split_weights2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    float d0, d1;
+    asm("{\n\t.reg .b16 h0, h1;\n\t"
+        "cvt.rn.f16x2.f32 %0, %4, %3;\n\t"
+        "mov.b32 {h0, h1}, %0;\n\t"
+        "sub.f32.f16 %1, h0, %3;\n\t"
+        "sub.f32.f16 %2, h1, %4;\n\t}"
+        : "=r"(hi), "=f"(d0), "=f"(d1)
+        : "f"(p0), "f"(p1));
+    uint64_t d, s;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(s) : "f"(-2048.0f));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(s));
+    asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.f16x2.f32 %0, b, a;\n\t}" : "=r"(lo) : "l"(d));
 }
 
 // Descriptor of an operand tile in the no-swizzle canonical layout: 8 x 16-byte

@@ -63,7 +63,7 @@ bool valid(const std::string& name, int64_t v) {
     if (name == "quantize") return v >= 0 && v <= 7;
     if (name == "block_n") return v == 0 || v == 128 || v == 256;
     if (name == "todo") return v >= 1 && v <= 4;
-    if (name == "attention_wg") return v == 0 || v == 1;
+    if (name == "attention_wg") return v >= 0 && v <= 2;
     return v >= 0;
 }
 

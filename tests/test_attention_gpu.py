@@ -95,3 +95,40 @@ def test_attention_config3(cuda, lk, residual):
     """8 heads x 40, Lq = 4096, Q/K/V ~ N(0, 1), optional fused residual."""
     err = run(cuda, 40, 4096, lk, 8, 8, 1, np.float32, seed=5, normal=True, residual=residual)
     assert err <= oracle.K_B200, f"error {err:.3g}"
+
+
+KERNEL_CASES = [c for c in ATTN_CASES if c[0] <= 64] + [(40, 4096, 4096, 8, 8, 1, np.float32)]
+
+
+@pytest.mark.parametrize("kernel", [2, 1, 0], ids=["tensor_memory_operands", "two_warpgroups", "pairs"])
+@pytest.mark.parametrize("case", KERNEL_CASES, ids=lambda c: f"d{c[0]}_q{c[1]}_k{c[2]}_h{c[3]}_{c[4]}_b{c[5]}")
+def test_attention_kernels(cuda, case, kernel):
+    """Each fused kernel (tuning attention_wg: 2 = Q and P in tensor memory, two CTAs an SM; 1 = two
+    softmax warpgroups; 0 = warp pairs) on the reference's cases of heads up to 64 dims."""
+    import sdb
+
+    before = sdb.get_tuning("attention_wg")
+    sdb.set_tuning(f"attention_wg={kernel}")
+    try:
+        err = run(cuda, *case)
+    finally:
+        sdb.set_tuning(f"attention_wg={before}")
+    assert err <= oracle.K_B200, f"error {err:.3g}"
+
+
+@pytest.mark.parametrize("lk", [64, 65, 127, 4096])
+def test_attention_negative_scale(cuda, lk):
+    """A negative scale: the block's largest scaled score is its smallest score (full and ragged key blocks)."""
+    import sdb
+
+    g = rng(11)
+    d, lq, h, b = 40, 200, 2, 1
+    q = oracle.uniform(g, (b, lq, h * d), 1.0)
+    k = oracle.uniform(g, (b, lk, h * d), 1.0)
+    v = oracle.uniform(g, (b, lk, h * d), 1.0)
+    scale = -1.5 / math.sqrt(d)
+    out = canary_like((b, lq, h * d), cuda)
+    sdb.attention_heads(cuda_tensor(q, cuda), cuda_tensor(k, cuda), cuda_tensor(v, cuda), h, h, scale, out=out)
+    exact, mag = oracle.attention_exact(q, k, v, h, h, scale)
+    err = oracle.metric(host(out), exact, mag)
+    assert err <= oracle.K_B200, f"error {err:.3g}"
