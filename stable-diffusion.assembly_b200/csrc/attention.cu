@@ -809,49 +809,66 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_wg_kernel(const Att
     }
 }
 
-// ---- both A operands in tensor memory, two CTAs an SM ----------------------
+// ---- both A operands in tensor memory, two query tiles a CTA -------------------
 //
 // For heads up to 64 dims (value chunks up to 64).  Q and P, the A operands of
 // the two products, live in tensor memory, so the tensor core reads only K and
-// V from shared memory, and a CTA takes 256 columns, so that two CTAs share an
-// SM.  One CTA's products issue at ~47 cycles each whatever their width up to
-// N = 64; the two CTAs' streams overlap (measured: M = 128, N = 48, K = 16
-// products at 4200 FLOP/cycle for one CTA, 8100 for two; with A in shared
-// memory the operand reads fill shared memory's ~128 B/cycle and the second
-// stream gains little).
-// Warp 0 loads the K/V stages; warp 1 issues the products; warps 2-5 (one
-// query row a thread) first write their Q rows into tensor memory, then per
-// block of 64 keys read S, take the weights against the reference maximum
-// (raised as in the kernels above), write P -- the FP16 pairs of split8_inrange,
-// so the same products -- over S's columns, and add the previous block's P V
-// into their registers before publishing P.  The next block's S is issued
-// before this block's P V, into the other buffer.
-// Tensor memory (columns): S / P buffers [0, 64) and [64, 128) (P hi in the
-// first 32 columns of a buffer, lo in the next 32); O [128, 128 + DVC); Q hi
-// then lo from 128 + DVC, dp / 2 columns each.
-constexpr int kAttnTmThreads = 192;
+// V from shared memory (A in shared memory would take most of its ~128 B/cycle
+// at these widths).  A CTA holds two tiles of 128 queries of one head, which
+// share every K/V stage, so each key block crosses L2 once per 256 queries.
+// Products are issued by three threads: one for both tiles' S = Q K^T, one per
+// tile for O = P V.  One issuing thread's products run back to back at ~47-65
+// cycles each whatever their width up to N = 64, and products of different
+// issuing threads overlap (measured, M = 128, K = 16, A in tensor memory: one
+// issuer 3000-4000 FLOP/cycle, two 6000-8000, four 8100-8170 -- the tensor
+// pipe's peak), so the S products of the next block run beside this block's
+// P V products.
+//
+// Warp 0 loads the K/V stages; warp 1 issues both tiles' S products; warps 2
+// and 3 issue tile 0's and tile 1's P V products; warps 4-7 and 8-11 are the
+// softmax warpgroups of tiles 0 and 1 (one query row a thread): they write
+// their Q rows into tensor memory, then per block of 64 keys read S, take the
+// weights against the reference maximum (raised as in the kernels above),
+// write P -- the FP16 pairs of split8_inrange, so the same products -- over S's
+// columns, and add the previous block's P V into their registers before
+// publishing P.  S(j + 2) reuses the buffer of P(j): its issue waits for that
+// P V to complete.  (Buffers of their own for S and P, or two threads a row
+// sharing a block's keys, measured slower: both made the softmax warps of an
+// SM sub-partition reach their exponentials together.)
+// Tensor memory (columns), tile t at 256 t: S / P buffers [0, 64) and [64, 128)
+// (P hi in the first 32 columns of a buffer, lo in the next 32); O [128, 128 +
+// DVC); Q hi then lo from 128 + DVC, DP / 2 columns each.
+constexpr int kAttnTmThreads = 384;
 constexpr int kAttnTmBK = 64;
-constexpr int kAttnTmMaxStages = 4;
+constexpr int kAttnTmMaxStages = 8;
 
 struct AttnTmLayout {
-    int stage_bytes, k_lo, v_hi, v_lo, stages, bars, total;
-    __host__ __device__ AttnTmLayout(int dp, int dvc) {
+    int stage_bytes = 0, k_lo = 0, v_hi = 0, v_lo = 0, stages = 0, bars = 0, total = 0;
+    __host__ __device__ constexpr AttnTmLayout(int dp, int dvc) {
         const int kb = kAttnTmBK * dp * 2, vb = kAttnTmBK * dvc * 2;
         k_lo = kb;
         v_hi = 2 * kb;
         v_lo = 2 * kb + vb;
         stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
-        // Stages within 96 KB, so that two CTAs fit an SM's shared memory.
-        const int fit = (96 * 1024) / stage_bytes;
+        const int fit = (192 * 1024) / stage_bytes;
         stages = fit < kAttnTmMaxStages ? fit : kAttnTmMaxStages;
         bars = stages * stage_bytes;
-        total = bars + 256;
+        total = bars + 512;
     }
 };
 
 __host__ __device__ constexpr bool attention_tm_fits(int dp, int dvc) {
     return 2 * kAttnTmBK + dvc + dp <= 256 && dp <= 64 && dvc <= 64;
 }
+
+// The barriers of one query tile.
+struct AttnTmTile {
+    uint64_t* q_full;   // its Q rows are in tensor memory (4 warp arrivals)
+    uint64_t* s_full;   // [2] S(j) complete, per buffer
+    uint64_t* p_full;   // P(j) written and the previous product taken (4 warp arrivals)
+    uint64_t* o_full;   // P V (j) complete
+    uint64_t* pv_done;  // [2] P V (j) complete, per buffer: S(j + 2) may overwrite P(j)
+};
 
 // max (scale >= 0) or min (scale < 0) of a block's scores: the one whose
 // scaled value is the block's largest.
@@ -871,32 +888,35 @@ __device__ __forceinline__ float extreme64(const float (&s)[kAttnTmBK]) {
     return kMin ? fminf(fminf(e[0], e[1]), fminf(e[2], e[3])) : fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3]));
 }
 
-// The softmax warpgroup of attention_tm_kernel (warps 2-5, thread = query row).
-template <int DVC>
-__device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const AttnTmLayout& L, uint32_t tmem,
-                                                     uint32_t t_o, uint32_t t_qh, uint32_t t_ql, uint64_t* q_full,
-                                                     uint64_t* s_full, uint64_t* p_full, uint64_t* o_full,
-                                                     volatile int* abort, int q0, int head, int dv0, int batch,
+// A softmax warpgroup of attention_tm_kernel (thread = query row of tile `qt`).
+// `tb` is the tile's tensor memory; lane quarter from the warp index.
+template <int DP, int DVC>
+__device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, uint32_t tb, const AttnTmTile& T,
+                                                     volatile int* abort, int qt, int head, int dv0, int batch,
                                                      int nblk) {
     constexpr int BK = kAttnTmBK;
     constexpr int OCH = DVC / 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = warp & 3;  // lane quarter of tensor memory this warp may access
     const int r = q * 32 + lane;
-    const int qi = q0 + r;
+    const int qi = qt * kAttnQ + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t t_o = tb + 2 * BK;
+    const uint32_t t_qh = t_o + DVC;
+    const uint32_t t_ql = t_qh + DP / 2;
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, a.err) ? 1 : 0) != 0;
     };
 
     // Row r of the Q tile (hi, then lo: 16-byte chunks of 8 dims, [chunk][row][8]) into tensor memory.
     {
-        const uint8_t* qt =
-            a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + blockIdx.x) * (kAttnQ * a.dp * 2);
+        const uint8_t* qtile = a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + qt) * (kAttnQ * DP * 2);
+#pragma unroll
         for (int plane = 0; plane < 2; ++plane) {
-            const uint8_t* src = qt + plane * a.q_plane;
+            const uint8_t* src = qtile + plane * a.q_plane;
             const uint32_t dst = (plane ? t_ql : t_qh) + lane_off;
-            for (int c0 = 0; c0 < a.dp / 8; c0 += 2) {
+#pragma unroll
+            for (int c0 = 0; c0 < DP / 8; c0 += 2) {
                 const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(src + (c0 * kAttnQ + r) * 16));
                 const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(src + ((c0 + 1) * kAttnQ + r) * 16));
                 const uint32_t w[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
@@ -906,7 +926,7 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(q_full);
+        if (lane == 0) mbar_arrive(T.q_full);
     }
 
     const bool neg = a.scale2 < 0.0f;
@@ -919,9 +939,9 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
     for (int i = 0; i < DVC; ++i) o[i] = 0.0f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
-        if (!warp_wait(&s_full[j & 1], (j >> 1) & 1)) { ok = false; break; }
+        if (!warp_wait(&T.s_full[j & 1], (j >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sb = tmem + (j & 1) * BK + lane_off;
+        const uint32_t sb = tb + (j & 1) * BK + lane_off;
         float s[BK];
         tmem_ld32(sb, *reinterpret_cast<float(*)[32]>(s));
         tmem_ld32(sb + 32, *reinterpret_cast<float(*)[32]>(s + 32));
@@ -961,7 +981,8 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
         // The block's weights summed pairwise, two lanes of pairs at a time.
         uint64_t sum2[BK / 4];
 #pragma unroll
-        for (int i = 0; i < BK / 4; ++i) sum2[i] = fadd2(pack2(s[2 * i], s[2 * i + 1]), pack2(s[BK / 2 + 2 * i], s[BK / 2 + 2 * i + 1]));
+        for (int i = 0; i < BK / 4; ++i)
+            sum2[i] = fadd2(pack2(s[2 * i], s[2 * i + 1]), pack2(s[BK / 2 + 2 * i], s[BK / 2 + 2 * i + 1]));
 #pragma unroll
         for (int w = BK / 8; w > 0; w >>= 1) {
 #pragma unroll
@@ -973,11 +994,12 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
         // The previous block's product (taken against the old maximum) into the registers: its
         // accumulator is then free for this block's.
         if (j >= 1) {
-            if (!warp_wait(o_full, (j - 1) & 1)) { ok = false; break; }
+            if (!warp_wait(T.o_full, (j - 1) & 1)) { ok = false; break; }
             tc_fence_after();
             float oh[DVC];
 #pragma unroll
-            for (int ch = 0; ch < OCH; ++ch) tmem_ld16(t_o + lane_off + ch * 16, *reinterpret_cast<float(*)[16]>(oh + ch * 16));
+            for (int ch = 0; ch < OCH; ++ch)
+                tmem_ld16(t_o + lane_off + ch * 16, *reinterpret_cast<float(*)[16]>(oh + ch * 16));
             tmem_ld_wait();
             if (factor != 1.0f) {
 #pragma unroll
@@ -990,10 +1012,10 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(T.p_full);
     }
     if (!ok) return;
-    if (!warp_wait(o_full, (nblk - 1) & 1)) return;
+    if (!warp_wait(T.o_full, (nblk - 1) & 1)) return;
     tc_fence_after();
     {
         float oh[DVC];
@@ -1025,73 +1047,101 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, const At
     }
 }
 
-template <int DVC>
-__global__ void __launch_bounds__(kAttnTmThreads, 2) attention_tm_kernel(const AttnArgs a) {
+template <int DP, int DVC>
+__global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const AttnArgs a) {
     constexpr int BK = kAttnTmBK;
+    constexpr AttnTmLayout L(DP, DVC);
+    constexpr int stages = L.stages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    const AttnTmLayout L(a.dp, DVC);
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [stages]
     uint64_t* kv_empty = kv_full + kAttnTmMaxStages;                 // [stages]
-    uint64_t* q_full = kv_empty + kAttnTmMaxStages;
-    uint64_t* s_full = q_full + 1;  // [2] per S buffer
-    uint64_t* p_full = s_full + 2;
-    uint64_t* o_full = p_full + 1;
-    uint64_t* drain = o_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* tile_bars = kv_empty + kAttnTmMaxStages;               // [2][7]
+    uint64_t* drain = tile_bars + 14;                                // [3] per issuing thread
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * kAttnQ;
+    const int qt0 = blockIdx.x * 2;                   // first query tile
+    const int ntile = qt0 + 1 < a.ntq ? 2 : 1;        // the last CTA of a head may hold one
     const int head = blockIdx.y / a.dv_chunks;
     const int dv0 = (blockIdx.y - head * a.dv_chunks) * DVC;
     const int batch = blockIdx.z;
     const int khead = head / (a.h / a.hk);
     const int nblk = (a.lk + BK - 1) / BK;
-    const int stages = L.stages;
     const uint32_t base = smem_u32(smem);
+    AttnTmTile tiles[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        uint64_t* b = tile_bars + 7 * t;
+        tiles[t] = AttnTmTile{b, b + 1, b + 3, b + 4, b + 5};
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&kv_empty[s], ntile);  // one release per tile's P V
         }
-        mbar_init(q_full, 4);
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(p_full, 4);
-        mbar_init(o_full, 1);
-        mbar_init(drain, 1);
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(tiles[t].q_full, 4);
+            mbar_init(&tiles[t].s_full[0], 1);
+            mbar_init(&tiles[t].s_full[1], 1);
+            mbar_init(tiles[t].p_full, 4);
+            mbar_init(tiles[t].o_full, 1);
+            mbar_init(&tiles[t].pv_done[0], 1);
+            mbar_init(&tiles[t].pv_done[1], 1);
+        }
+        for (int i = 0; i < 3; ++i) mbar_init(&drain[i], 1);
         *abort = 0;
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 256);
+    // The dims past the head's last 8-dim chunk are zero in every stage: written once here, never loaded.
+    const int kch = (a.d + 7) / 8;
+    const int vch = (min(DVC, a.dv - dv0) + 7) / 8;
+    {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        constexpr int kpl = BK * DP * 2, vpl = BK * DVC * 2;  // bytes of a plane
+        const int kpad = kpl - kch * BK * 16, vpad = vpl - vch * BK * 16;
+        for (int s = 0; s < stages; ++s) {
+            uint8_t* st = smem + s * L.stage_bytes;
+            for (int o = threadIdx.x * 16; o < kpad; o += kAttnTmThreads * 16) {
+                *reinterpret_cast<uint4*>(st + kch * BK * 16 + o) = z;
+                *reinterpret_cast<uint4*>(st + L.k_lo + kch * BK * 16 + o) = z;
+            }
+            for (int o = threadIdx.x * 16; o < vpad; o += kAttnTmThreads * 16) {
+                *reinterpret_cast<uint4*>(st + L.v_hi + vch * BK * 16 + o) = z;
+                *reinterpret_cast<uint4*>(st + L.v_lo + vch * BK * 16 + o) = z;
+            }
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_o = tmem + 2 * BK;
-    const uint32_t t_qh = t_o + DVC;
-    const uint32_t t_ql = t_qh + a.dp / 2;
+    constexpr uint32_t id_s = idesc_f16_f32(kAttnQ, BK);
+    constexpr uint32_t id_pv = idesc_f16_f32_bmajor(kAttnQ, DVC, 1);
 
     if (warp == 0) {
         // ------------------------------------------------ bulk-copy producer
         if (lane == 0) {
-            const uint32_t kbytes = BK * a.dp * 2, vbytes = BK * DVC * 2;
+            constexpr uint32_t kbytes = BK * DP * 2;                     // a stored K plane tile
+            const uint32_t kload = kch * BK * 16, vload = vch * BK * 16;  // its dims that are loaded
             const long long ktile0 = static_cast<long long>(batch * a.hk + khead) * a.ntk;
             int issued = 0;
             for (int j = 0; j < nblk; ++j) {
                 const int s = j % stages;
                 if (!mbar_wait(&kv_empty[s], ((j / stages) & 1) ^ 1, abort, a.err)) break;
                 uint8_t* st = smem + s * L.stage_bytes;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * kbytes + 2 * vbytes);
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kload + 2 * vload);
                 const uint8_t* kt = a.ks + (ktile0 + j) * kbytes;
                 const uint8_t* vt = a.vs + (ktile0 + j) * static_cast<long long>(BK) * a.dvs * 2 +
                                     static_cast<long long>(dv0 / 8) * BK * 16;
-                bulk_load(st, kt, kbytes, &kv_full[s]);
-                bulk_load(st + L.k_lo, kt + a.k_plane, kbytes, &kv_full[s]);
-                bulk_load(st + L.v_hi, vt, vbytes, &kv_full[s]);
-                bulk_load(st + L.v_lo, vt + a.v_plane, vbytes, &kv_full[s]);
+                bulk_load(st, kt, kload, &kv_full[s]);
+                bulk_load(st + L.k_lo, kt + a.k_plane, kload, &kv_full[s]);
+                bulk_load(st + L.v_hi, vt, vload, &kv_full[s]);
+                bulk_load(st + L.v_lo, vt + a.v_plane, vload, &kv_full[s]);
                 ++issued;
             }
             if (*abort) {
@@ -1100,70 +1150,87 @@ __global__ void __launch_bounds__(kAttnTmThreads, 2) attention_tm_kernel(const A
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
+        // ------------------------------------------------ S = Q K^T of both tiles
         if (lane == 0) {
-            const uint32_t id_s = idesc_f16_f32(kAttnQ, BK);
-            const uint32_t id_pv = idesc_f16_f32_bmajor(kAttnQ, DVC, 1);
-            const uint32_t k_lbo = BK * 16;
-            // S = Q K^T into buffer j & 1: the lo products (Q.K lo, Q lo.K, each
-            // carrying 2^11) first, then Q.K hi with the input scale 2^-11.
-            auto issue_s = [&](int j) {
-                const uint32_t st = base + (j % stages) * L.stage_bytes;
-                const uint32_t sb = tmem + (j & 1) * BK;
-                for (int kk = 0; kk < a.dp / 16; ++kk) {
-                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, 128);
-                    const uint64_t kl = desc_noswizzle(st + L.k_lo + kk * 2 * k_lbo, k_lbo, 128);
-                    mma_f16_ta(sb, t_qh + kk * 8, kl, id_s, kk > 0 ? 1u : 0u);
-                    mma_f16_ta(sb, t_ql + kk * 8, kh, id_s, 1u);
-                }
-                for (int kk = 0; kk < a.dp / 16; ++kk) {
-                    const uint64_t kh = desc_noswizzle(st + kk * 2 * k_lbo, k_lbo, 128);
-                    if (kk == 0) mma_f16_ta_scale_lo(sb, t_qh, kh, id_s);
-                    else mma_f16_ta(sb, t_qh + kk * 8, kh, id_s, 1u);
-                }
-                mma_commit(&s_full[j & 1]);
-            };
-            // O = P V from the P that the softmax warps wrote over S(j).
-            auto issue_pv = [&](int j) {
-                const int s = j % stages;
-                const uint32_t st = base + s * L.stage_bytes;
-                const uint32_t pb = tmem + (j & 1) * BK;
-                for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
-                    const uint64_t vl = desc_noswizzle(st + L.v_lo + kk * 256, 128, BK * 16);
-                    mma_f16_ta(t_o, pb + kk * 8, vl, id_pv, kk > 0 ? 1u : 0u);
-                    mma_f16_ta(t_o, pb + 32 + kk * 8, vh, id_pv, 1u);
-                }
-                for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t vh = desc_noswizzle(st + L.v_hi + kk * 256, 128, BK * 16);
-                    if (kk == 0) mma_f16_ta_scale_lo(t_o, pb, vh, id_pv);
-                    else mma_f16_ta(t_o, pb + kk * 8, vh, id_pv, 1u);
-                }
-                mma_commit(o_full);
-                mma_commit(&kv_empty[s]);
-            };
-            bool ok = mbar_wait(q_full, 0, abort, a.err);
+            constexpr uint32_t k_lbo = BK * 16;
+            // Descriptors of stage 0; another stage's, and another k-step's, add their byte offset / 16 to
+            // the start-address field (shared addresses stay below 256 KB, so the field does not carry).
+            const uint64_t dk0 = desc_noswizzle(base, k_lbo, 128);
+            bool ok = true;
+            for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(tiles[t].q_full, 0, abort, a.err);
             for (int j = 0; j < nblk && ok; ++j) {
                 if (!mbar_wait(&kv_full[j % stages], (j / stages) & 1, abort, a.err)) { ok = false; break; }
-                tc_fence_after();
-                issue_s(j);
-                if (j >= 1) {
-                    if (!mbar_wait(p_full, (j - 1) & 1, abort, a.err)) { ok = false; break; }
+                const uint64_t dk = dk0 + static_cast<uint64_t>(((j % stages) * L.stage_bytes) >> 4);
+                for (int t = 0; t < ntile; ++t) {
+                    // Buffer j & 1 holds P(j - 2) until that block's P V completes.
+                    if (j >= 2 && !mbar_wait(&tiles[t].pv_done[j & 1], ((j - 2) >> 1) & 1, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
-                    issue_pv(j - 1);
+                    const uint32_t tb = tmem + 256 * t;
+                    const uint32_t sb = tb + (j & 1) * BK;
+                    const uint32_t t_qh = tb + 2 * BK + DVC, t_ql = t_qh + DP / 2;
+                    // The lo products (Q.K lo, Q lo.K, each carrying 2^11) first, then Q.K hi with the
+                    // input scale 2^-11.
+#pragma unroll
+                    for (int kk = 0; kk < DP / 16; ++kk) {
+                        mma_f16_ta(sb, t_qh + kk * 8, dk + ((L.k_lo + kk * 2 * k_lbo) >> 4), id_s, kk > 0 ? 1u : 0u);
+                        mma_f16_ta(sb, t_ql + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < DP / 16; ++kk) {
+                        if (kk == 0) mma_f16_ta_scale_lo(sb, t_qh, dk, id_s);
+                        else mma_f16_ta(sb, t_qh + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                    }
+                    mma_commit(&tiles[t].s_full[j & 1]);
                 }
             }
-            if (ok && mbar_wait(p_full, (nblk - 1) & 1, abort, a.err)) {
+            if (!ok) {
+                mma_commit(&drain[0]);
+                mbar_wait_quiet(&drain[0], 0, 100000000ull);
+            }
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------ O = P V of tile warp - 2
+        const int t = warp - 2;
+        if (lane == 0 && t < ntile) {
+            const AttnTmTile& T = tiles[t];
+            const uint32_t tb = tmem + 256 * t;
+            const uint32_t t_o = tb + 2 * BK;
+            const uint64_t dv0d = desc_noswizzle(base + L.v_hi, 128, BK * 16);
+            constexpr uint32_t vlo = (L.v_lo - L.v_hi) >> 4;
+            bool ok = true;
+            for (int j = 0; j < nblk; ++j) {
+                if (!mbar_wait(T.p_full, j & 1, abort, a.err)) { ok = false; break; }
                 tc_fence_after();
-                issue_pv(nblk - 1);
-            } else {
-                mma_commit(drain);
-                mbar_wait_quiet(drain, 0, 100000000ull);
+                const int s = j % stages;
+                const uint64_t dvh = dv0d + static_cast<uint64_t>((s * L.stage_bytes) >> 4);
+                const uint32_t pb = tb + (j & 1) * BK;
+                // hi.V lo and lo.V hi (each carrying 2^11) first, then hi.V hi with the input scale 2^-11.
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    mma_f16_ta(t_o, pb + kk * 8, dvh + vlo + kk * 16, id_pv, kk > 0 ? 1u : 0u);
+                    mma_f16_ta(t_o, pb + 32 + kk * 8, dvh + kk * 16, id_pv, 1u);
+                }
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    if (kk == 0) mma_f16_ta_scale_lo(t_o, pb, dvh, id_pv);
+                    else mma_f16_ta(t_o, pb + kk * 8, dvh + kk * 16, id_pv, 1u);
+                }
+                mma_commit(&kv_empty[s]);
+                mma_commit(&T.pv_done[j & 1]);
+                mma_commit(T.o_full);
+            }
+            if (!ok) {
+                mma_commit(&drain[1 + t]);
+                mbar_wait_quiet(&drain[1 + t], 0, 100000000ull);
             }
         }
     } else {
-        attention_tm_softmax<DVC>(a, L, tmem, t_o, t_qh, t_ql, q_full, s_full, p_full, o_full, abort, q0, head,
-                                  dv0, batch, nblk);
+        const int t = (warp - 4) >> 2;
+        if (t < ntile)
+            attention_tm_softmax<DP, DVC>(a, tmem + 256 * t, tiles[t], abort, qt0 + t, head, dv0, batch, nblk);
     }
 
     __syncwarp();
@@ -1171,7 +1238,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 2) attention_tm_kernel(const A
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, 512);
     }
 }
 
@@ -1252,22 +1319,31 @@ int launch_attention_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, c
     return SDB_OK;
 }
 
-// Shared memory of at least a third of an SM's, so that no third CTA shares an
-// SM with two that hold all its tensor memory.
-template <int DVC>
+// Shared memory of more than half an SM's, so that no second CTA waits on an SM
+// whose tensor memory the first holds.
+template <int DP, int DVC>
 int launch_attention_tm(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
-    const AttnTmLayout L(a.dp, DVC);
-    const int smem = std::max(L.total + 128, 80 * 1024);
+    constexpr AttnTmLayout L(DP, DVC);
+    const int smem = std::max(L.total + 128, 120 * 1024);
     if (int s = prepare_tiles<kAttnTmBK, DVC>(a, q, k, v, st); s != SDB_OK) return s;
-    auto kern = attention_tm_kernel<DVC>;
+    auto kern = attention_tm_kernel<DP, DVC>;
     SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    const dim3 grid(static_cast<unsigned>((a.lq + kAttnQ - 1) / kAttnQ), static_cast<unsigned>(a.h * a.dv_chunks),
+    const dim3 grid(static_cast<unsigned>((a.ntq + 1) / 2), static_cast<unsigned>(a.h * a.dv_chunks),
                     static_cast<unsigned>(a.b));
     kern<<<grid, kAttnTmThreads, smem, st>>>(a);
     count_launch();
     SDB_CUDA(cudaGetLastError());
     return SDB_OK;
+}
+
+template <int DVC>
+int launch_attention_tm(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
+    switch (a.dp) {
+    case 16: return launch_attention_tm<16, DVC>(a, q, k, v, st);
+    case 32: return launch_attention_tm<32, DVC>(a, q, k, v, st);
+    case 48: return launch_attention_tm<48, DVC>(a, q, k, v, st);
+    default: return launch_attention_tm<64, DVC>(a, q, k, v, st);
+    }
 }
 
 // The two-warpgroup kernel when its S buffers and two output accumulators fit

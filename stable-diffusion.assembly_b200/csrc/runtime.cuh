@@ -34,7 +34,7 @@ struct Tuning {
     int64_t weight_group = 1;    // the weights' scale per group: 1; per whole row: 0
     int64_t quantize = 7;        // with bits, what is quantized: 1 linear layers, 2 convolutions, 4 attention
     int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
-    int64_t attention_wg = 2;    // 2: Q and P in tensor memory, two CTAs an SM, where it fits; 1: two-warpgroup; 0: the pair kernel
+    int64_t attention_wg = 2;    // 2: Q and P in tensor memory, two query tiles a CTA, where it fits; 1: two-warpgroup; 0: the pair kernel
 };
 
 Tuning& tuning();
