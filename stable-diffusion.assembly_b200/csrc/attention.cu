@@ -842,23 +842,30 @@ constexpr int kAttnTmThreads = 384;
 constexpr int kAttnTmBK = 64;
 constexpr int kAttnTmMaxStages = 8;
 
+// Q in tensor memory when a tile's S / P buffers, O and Q fit its 256 columns;
+// else (heads of 80 dims) in shared memory, the S products reading it there.
+__host__ __device__ constexpr bool attention_tm_q_in_tmem(int dp, int dvc) { return 2 * kAttnTmBK + dvc + dp <= 256; }
+
 struct AttnTmLayout {
-    int stage_bytes = 0, k_lo = 0, v_hi = 0, v_lo = 0, stages = 0, bars = 0, total = 0;
+    int q_plane = 0, stage0 = 0, stage_bytes = 0, k_lo = 0, v_hi = 0, v_lo = 0, stages = 0, bars = 0, total = 0;
     __host__ __device__ constexpr AttnTmLayout(int dp, int dvc) {
+        q_plane = attention_tm_q_in_tmem(dp, dvc) ? 0 : kAttnQ * dp * 2;
+        stage0 = 4 * q_plane;  // tile 0 hi, lo, tile 1 hi, lo
         const int kb = kAttnTmBK * dp * 2, vb = kAttnTmBK * dvc * 2;
         k_lo = kb;
         v_hi = 2 * kb;
         v_lo = 2 * kb + vb;
         stage_bytes = (2 * kb + 2 * vb + 127) / 128 * 128;
-        const int fit = (192 * 1024) / stage_bytes;
+        const int fit = (200 * 1024 - stage0) / stage_bytes;
         stages = fit < kAttnTmMaxStages ? fit : kAttnTmMaxStages;
-        bars = stages * stage_bytes;
+        bars = stage0 + stages * stage_bytes;
         total = bars + 512;
     }
 };
 
 __host__ __device__ constexpr bool attention_tm_fits(int dp, int dvc) {
-    return 2 * kAttnTmBK + dvc + dp <= 256 && dp <= 64 && dvc <= 64;
+    return dp == dvc && 2 * kAttnTmBK + dvc <= 256 && dp <= 80 && AttnTmLayout(dp, dvc).stages >= 2 &&
+           AttnTmLayout(dp, dvc).total + 128 <= 227 * 1024;
 }
 
 // The barriers of one query tile.
@@ -909,7 +916,7 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, uint32_t
     };
 
     // Row r of the Q tile (hi, then lo: 16-byte chunks of 8 dims, [chunk][row][8]) into tensor memory.
-    {
+    if constexpr (attention_tm_q_in_tmem(DP, DVC)) {
         const uint8_t* qtile = a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + qt) * (kAttnQ * DP * 2);
 #pragma unroll
         for (int plane = 0; plane < 2; ++plane) {
@@ -1052,6 +1059,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
     constexpr int BK = kAttnTmBK;
     constexpr AttnTmLayout L(DP, DVC);
     constexpr int stages = L.stages;
+    constexpr bool kQt = attention_tm_q_in_tmem(DP, DVC);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [stages]
@@ -1083,7 +1091,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
             mbar_init(&kv_empty[s], ntile);  // one release per tile's P V
         }
         for (int t = 0; t < 2; ++t) {
-            mbar_init(tiles[t].q_full, 4);
+            mbar_init(tiles[t].q_full, kQt ? 4 : 1);  // the softmax warps' stores, or the producer's copies
             mbar_init(&tiles[t].s_full[0], 1);
             mbar_init(&tiles[t].s_full[1], 1);
             mbar_init(tiles[t].p_full, 4);
@@ -1103,7 +1111,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
         constexpr int kpl = BK * DP * 2, vpl = BK * DVC * 2;  // bytes of a plane
         const int kpad = kpl - kch * BK * 16, vpad = vpl - vch * BK * 16;
         for (int s = 0; s < stages; ++s) {
-            uint8_t* st = smem + s * L.stage_bytes;
+            uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
             for (int o = threadIdx.x * 16; o < kpad; o += kAttnTmThreads * 16) {
                 *reinterpret_cast<uint4*>(st + kch * BK * 16 + o) = z;
                 *reinterpret_cast<uint4*>(st + L.k_lo + kch * BK * 16 + o) = z;
@@ -1129,11 +1137,20 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
             constexpr uint32_t kbytes = BK * DP * 2;                     // a stored K plane tile
             const uint32_t kload = kch * BK * 16, vload = vch * BK * 16;  // its dims that are loaded
             const long long ktile0 = static_cast<long long>(batch * a.hk + khead) * a.ntk;
+            if constexpr (!kQt) {
+                // Both tiles' Q planes into shared memory, completing on tile 0's barrier.
+                mbar_arrive_expect_tx(tiles[0].q_full, ntile * 2 * L.q_plane);
+                for (int t = 0; t < ntile; ++t) {
+                    const uint8_t* qsrc = a.qs + (static_cast<long long>(batch * a.h + head) * a.ntq + qt0 + t) * L.q_plane;
+                    bulk_load(smem + 2 * t * L.q_plane, qsrc, L.q_plane, tiles[0].q_full);
+                    bulk_load(smem + (2 * t + 1) * L.q_plane, qsrc + a.q_plane, L.q_plane, tiles[0].q_full);
+                }
+            }
             int issued = 0;
             for (int j = 0; j < nblk; ++j) {
                 const int s = j % stages;
                 if (!mbar_wait(&kv_empty[s], ((j / stages) & 1) ^ 1, abort, a.err)) break;
-                uint8_t* st = smem + s * L.stage_bytes;
+                uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
                 mbar_arrive_expect_tx(&kv_full[s], 2 * kload + 2 * vload);
                 const uint8_t* kt = a.ks + (ktile0 + j) * kbytes;
                 const uint8_t* vt = a.vs + (ktile0 + j) * static_cast<long long>(BK) * a.dvs * 2 +
@@ -1145,6 +1162,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
                 ++issued;
             }
             if (*abort) {
+                if (!kQt) mbar_wait_quiet(tiles[0].q_full, 0, 100000000ull);
                 for (int j = (issued > stages ? issued - stages : 0); j < issued; ++j)
                     mbar_wait_quiet(&kv_full[j % stages], (j / stages) & 1, 100000000ull);
             }
@@ -1155,9 +1173,11 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
             constexpr uint32_t k_lbo = BK * 16;
             // Descriptors of stage 0; another stage's, and another k-step's, add their byte offset / 16 to
             // the start-address field (shared addresses stay below 256 KB, so the field does not carry).
-            const uint64_t dk0 = desc_noswizzle(base, k_lbo, 128);
+            const uint64_t dk0 = desc_noswizzle(base + L.stage0, k_lbo, 128);
+            constexpr uint32_t q_lbo = kAttnQ * 16;
+            const uint64_t dq0 = desc_noswizzle(base, q_lbo, 128);   // Q in shared memory: tile 0 hi
             bool ok = true;
-            for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(tiles[t].q_full, 0, abort, a.err);
+            for (int t = 0; t < (kQt ? ntile : 1) && ok; ++t) ok = mbar_wait(tiles[t].q_full, 0, abort, a.err);
             for (int j = 0; j < nblk && ok; ++j) {
                 if (!mbar_wait(&kv_full[j % stages], (j / stages) & 1, abort, a.err)) { ok = false; break; }
                 const uint64_t dk = dk0 + static_cast<uint64_t>(((j % stages) * L.stage_bytes) >> 4);
@@ -1170,18 +1190,33 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
                     tc_fence_after();
                     const uint32_t tb = tmem + 256 * t;
                     const uint32_t sb = tb + (j & 1) * BK;
-                    const uint32_t t_qh = tb + 2 * BK + DVC, t_ql = t_qh + DP / 2;
                     // The lo products (Q.K lo, Q lo.K, each carrying 2^11) first, then Q.K hi with the
                     // input scale 2^-11.
+                    if constexpr (kQt) {
+                        const uint32_t t_qh = tb + 2 * BK + DVC, t_ql = t_qh + DP / 2;
 #pragma unroll
-                    for (int kk = 0; kk < DP / 16; ++kk) {
-                        mma_f16_ta(sb, t_qh + kk * 8, dk + ((L.k_lo + kk * 2 * k_lbo) >> 4), id_s, kk > 0 ? 1u : 0u);
-                        mma_f16_ta(sb, t_ql + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
-                    }
+                        for (int kk = 0; kk < DP / 16; ++kk) {
+                            mma_f16_ta(sb, t_qh + kk * 8, dk + ((L.k_lo + kk * 2 * k_lbo) >> 4), id_s, kk > 0 ? 1u : 0u);
+                            mma_f16_ta(sb, t_ql + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                        }
 #pragma unroll
-                    for (int kk = 0; kk < DP / 16; ++kk) {
-                        if (kk == 0) mma_f16_ta_scale_lo(sb, t_qh, dk, id_s);
-                        else mma_f16_ta(sb, t_qh + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                        for (int kk = 0; kk < DP / 16; ++kk) {
+                            if (kk == 0) mma_f16_ta_scale_lo(sb, t_qh, dk, id_s);
+                            else mma_f16_ta(sb, t_qh + kk * 8, dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                        }
+                    } else {
+                        const uint64_t dqh = dq0 + ((2 * t * L.q_plane) >> 4), dql = dqh + (L.q_plane >> 4);
+#pragma unroll
+                        for (int kk = 0; kk < DP / 16; ++kk) {
+                            mma_f16(sb, dqh + ((kk * 2 * q_lbo) >> 4), dk + ((L.k_lo + kk * 2 * k_lbo) >> 4), id_s,
+                                    kk > 0 ? 1u : 0u);
+                            mma_f16(sb, dql + ((kk * 2 * q_lbo) >> 4), dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                        }
+#pragma unroll
+                        for (int kk = 0; kk < DP / 16; ++kk) {
+                            if (kk == 0) mma_f16_scale_lo(sb, dqh, dk, id_s);
+                            else mma_f16(sb, dqh + ((kk * 2 * q_lbo) >> 4), dk + ((kk * 2 * k_lbo) >> 4), id_s, 1u);
+                        }
                     }
                     mma_commit(&tiles[t].s_full[j & 1]);
                 }
@@ -1198,7 +1233,7 @@ __global__ void __launch_bounds__(kAttnTmThreads, 1) attention_tm_kernel(const A
             const AttnTmTile& T = tiles[t];
             const uint32_t tb = tmem + 256 * t;
             const uint32_t t_o = tb + 2 * BK;
-            const uint64_t dv0d = desc_noswizzle(base + L.v_hi, 128, BK * 16);
+            const uint64_t dv0d = desc_noswizzle(base + L.stage0 + L.v_hi, 128, BK * 16);
             constexpr uint32_t vlo = (L.v_lo - L.v_hi) >> 4;
             bool ok = true;
             for (int j = 0; j < nblk; ++j) {
@@ -1338,12 +1373,7 @@ int launch_attention_tm(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, c
 
 template <int DVC>
 int launch_attention_tm(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
-    switch (a.dp) {
-    case 16: return launch_attention_tm<16, DVC>(a, q, k, v, st);
-    case 32: return launch_attention_tm<32, DVC>(a, q, k, v, st);
-    case 48: return launch_attention_tm<48, DVC>(a, q, k, v, st);
-    default: return launch_attention_tm<64, DVC>(a, q, k, v, st);
-    }
+    return launch_attention_tm<DVC, DVC>(a, q, k, v, st);
 }
 
 // The two-warpgroup kernel when its S buffers and two output accumulators fit
@@ -1372,8 +1402,8 @@ int launch_wg(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_t
 // whose S double buffer and output accumulators fit tensor memory.
 template <int DVC>
 int launch_bk(AttnArgs& a, const sdb_tensor* q, const sdb_tensor* k, const sdb_tensor* v, cudaStream_t st) {
-    if constexpr (DVC <= 64) {
-        if (tuning().attention_wg == 2 && attention_tm_fits(a.dp, DVC)) return launch_attention_tm<DVC>(a, q, k, v, st);
+    if constexpr (attention_tm_fits(DVC, DVC)) {
+        if (tuning().attention_wg == 2 && a.dp == DVC) return launch_attention_tm<DVC>(a, q, k, v, st);
     }
     if (tuning().attention_wg) {
         bool taken = false;

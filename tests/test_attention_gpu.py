@@ -97,14 +97,16 @@ def test_attention_config3(cuda, lk, residual):
     assert err <= oracle.K_B200, f"error {err:.3g}"
 
 
-KERNEL_CASES = [c for c in ATTN_CASES if c[0] <= 64] + [(40, 4096, 4096, 8, 8, 1, np.float32)]
+KERNEL_CASES = [c for c in ATTN_CASES if c[0] <= 80] + [(40, 4096, 4096, 8, 8, 1, np.float32),
+                                                          (80, 1024, 1024, 8, 8, 2, np.float32)]
 
 
 @pytest.mark.parametrize("kernel", [2, 1, 0], ids=["tensor_memory_operands", "two_warpgroups", "pairs"])
 @pytest.mark.parametrize("case", KERNEL_CASES, ids=lambda c: f"d{c[0]}_q{c[1]}_k{c[2]}_h{c[3]}_{c[4]}_b{c[5]}")
 def test_attention_kernels(cuda, case, kernel):
-    """Each fused kernel (tuning attention_wg: 2 = Q and P in tensor memory, two CTAs an SM; 1 = two
-    softmax warpgroups; 0 = warp pairs) on the reference's cases of heads up to 64 dims."""
+    """Each fused kernel (tuning attention_wg: 2 = two query tiles a CTA, P (and for heads up to 64
+    dims Q) in tensor memory; 1 = two softmax warpgroups; 0 = warp pairs) on the reference's cases of
+    heads up to 80 dims."""
     import sdb
 
     before = sdb.get_tuning("attention_wg")
