@@ -171,11 +171,13 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Items run column tile fastest, so that the CTAs working at one time on a row tile's column
+    // tiles read its activations from DRAM once between them (the weights stay in L2).
     auto item_range = [&](int item, int& tm, int& tn, int& split, int& kb0, int& kb1) {
-        tm = item % args.tiles_m;
-        const int rest = item / args.tiles_m;
-        tn = rest % args.tiles_n;
-        split = rest / args.tiles_n;
+        tn = item % args.tiles_n;
+        const int rest = item / args.tiles_n;
+        tm = rest % args.tiles_m;
+        split = rest / args.tiles_m;
         kb0 = split * args.per_split;
         kb1 = min(args.kblocks, kb0 + args.per_split);
     };
