@@ -1288,6 +1288,7 @@ OPS = {
     "linear_8192x320x320": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 320),
     "linear_8192x320x1280": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 8192, 320, 1280),
     "linear_2048x640x640": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 2048, 640, 640),
+    "linear_65536x320x320": lambda torch, sdb, dev: _op_linear(torch, sdb, dev, 65536, 320, 320),
     "groupnorm_2x64x64x320": lambda torch, sdb, dev: _op_groupnorm(torch, sdb, dev, 2, 64, 320),
 }
 

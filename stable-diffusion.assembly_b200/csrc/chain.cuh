@@ -166,9 +166,10 @@ struct ChainRow {
 
 __device__ __forceinline__ void row_offsets(const Chain& c, ChainRow& r, int col_dim, long long j0, long long j1,
                                             long long j2) {
-    // j0..j2: the three row coordinates in ggml order without col_dim.
+    // j0..j2: the three row coordinates in ggml order without col_dim; only the chain's steps.
 #pragma unroll
     for (int s = 0; s < SDB_MAX_STEPS; ++s) {
+        if (s >= c.count) break;
         if (col_dim == 0)
             r.off[s] = j0 * c.nb[s][1] + j1 * c.nb[s][2] + j2 * c.nb[s][3];
         else
@@ -179,7 +180,9 @@ __device__ __forceinline__ void row_offsets(const Chain& c, ChainRow& r, int col
 // The chain over NVAL consecutive columns col0.. of one row, in place: one
 // step at a time over all the columns, so that a step's operand loads are
 // issued together (columns past col_max read column col_max; their results
-// are not stored).
+// are not stored).  An operand whose columns are consecutive floats (a bias,
+// a residual row) is read a float4 at a time when the run is in range and
+// aligned; else element by element.
 template <int COL_DIM, int NVAL>
 __device__ __forceinline__ void apply_chain_cols(const Chain& c, const ChainRow& r, float* v, long long col0,
                                                  long long col_max) {
@@ -193,8 +196,21 @@ __device__ __forceinline__ void apply_chain_cols(const Chain& c, const ChainRow&
             const float* base = c.operand[s] + r.off[s];
             const long long stride = c.nb[s][COL_DIM];
             float o[NVAL];
+            const float* run = base + col0 * stride;
+            if (NVAL % 4 == 0 && stride == 1 && col0 + NVAL - 1 <= col_max &&
+                (reinterpret_cast<uintptr_t>(run) & 15) == 0) {
 #pragma unroll
-            for (int j = 0; j < NVAL; ++j) o[j] = __ldg(base + min(col0 + j, col_max) * stride);
+                for (int j = 0; j < NVAL; j += 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(run + j));
+                    o[j] = f.x;
+                    o[j + 1] = f.y;
+                    o[j + 2] = f.z;
+                    o[j + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < NVAL; ++j) o[j] = __ldg(base + min(col0 + j, col_max) * stride);
+            }
             if (c.kind[s] == SDB_STEP_ADD) {
 #pragma unroll
                 for (int j = 0; j < NVAL; ++j) v[j] += o[j];

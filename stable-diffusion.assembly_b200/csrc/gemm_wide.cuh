@@ -333,8 +333,14 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
             const long long m = static_cast<long long>(tm) * kBM + row;
             const bool live = m < args.m;
             const long long mc = live ? m : args.m - 1;
-            const long long i1 = mc % args.rne1, rest = mc / args.rne1;
-            const long long i2 = rest % args.rne2, i3 = rest / args.rne2;
+            // The row's ggml coordinates: rows of a 2-D output are i1 itself (no division).
+            long long i1 = mc, i2 = 0, i3 = 0;
+            if (args.rne1 < args.m) {
+                const long long rest = mc / args.rne1;
+                i1 = mc - rest * args.rne1;
+                i2 = rest % args.rne2;
+                i3 = rest / args.rne2;
+            }
             ChainRow cr;
             row_offsets(args.chain, cr, 0, i1, i2, i3);
             float* yrow = args.y + i1 * args.ynb[1] + i2 * args.ynb[2] + i3 * args.ynb[3];
