@@ -242,7 +242,10 @@ int sdb_token_downsampling(int64_t width, int64_t height);
  * every call), todo, todo_tokens, bits (0, or 2..8: the linear layers of 256
  * rows or more as integer products, quant.cc), input_bits (2..8), group (32,
  * 64, 128 or 256), weight_group (1 per group, 0 per row), quantize (bit 1:
- * linear layers), block_n.  Returns SDB_INVALID on an unknown name or value. */
+ * linear layers), block_n (the GEMM tile width: 0 automatic, 128, 160, 192 or
+ * 256), gemm_fused (the linear layers' FP32 activations split inside the GEMM:
+ * 1 where that is faster, 2 always, 0 never).  Returns SDB_INVALID on an
+ * unknown name or value. */
 int sdb_set_tuning(const char *spec);
 int sdb_get_tuning(const char *name, int64_t *value);
 /* The device error word of the current device (kernel-reported: bit 0 a

@@ -124,6 +124,92 @@ __device__ __forceinline__ void add_old_box16(const float* y, long long ld, long
     __syncwarp();
 }
 
+// One output row of a linear-layer tile: where it goes and its chain operands.
+struct LinearRow {
+    bool live;         // inside the output
+    ChainRow cr;
+    float* yrow;
+};
+
+__device__ __forceinline__ LinearRow linear_row(const GemmArgs& args, int tm, int row) {
+    LinearRow r;
+    const long long m = static_cast<long long>(tm) * kBM + row;
+    r.live = m < args.m;
+    const long long mc = r.live ? m : args.m - 1;
+    // The row's ggml coordinates: rows of a 2-D output are i1 itself (no division).
+    long long i1 = mc, i2 = 0, i3 = 0;
+    if (args.rne1 < args.m) {
+        const long long rest = mc / args.rne1;
+        i1 = mc - rest * args.rne1;
+        i2 = rest % args.rne2;
+        i3 = rest / args.rne2;
+    }
+    row_offsets(args.chain, r.cr, 0, i1, i2, i3);
+    r.yrow = args.y + i1 * args.ynb[1] + i2 * args.ynb[2] + i3 * args.ynb[3];
+    return r;
+}
+
+// Sixteen output columns cb .. cb + 15 of a warp's 32 rows (rows tm * 128 +
+// q * 32 + lane) out of registers: the chain (bias, scale, residual, SiLU; a
+// gated product x * GELU(gate) after both halves' chains, `gate` holding the
+// gate half's sums) applied, stored by TMA (kStoreTma) or directly.
+template <bool GATED>
+__device__ __forceinline__ void store_linear_group(const GemmArgs& args, const CUtensorMap* ymap, const LinearRow& r,
+                                                   float* v, float* gate, long long cb, int tm, int q, int lane,
+                                                   uint8_t* box) {
+    if (GATED) {
+        apply_chain_cols<0, 16>(args.chain, r.cr, v, cb, args.n - 1);
+        apply_chain_cols<0, 16>(args.chain, r.cr, gate, args.n + cb, 2LL * args.n - 1);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] *= gelu(gate[j]);
+    } else {
+        if (args.chain.from_redirect) {
+            if (args.store == kStoreTma) {
+                add_old_box16(args.y, args.n, static_cast<long long>(tm) * kBM + q * 32, args.m, cb, args.n, box, lane,
+                              v);
+            } else {
+                float old[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) old[j] = r.yrow[min(cb + j, args.n - 1LL) * args.ynb[0]];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
+            }
+        }
+        apply_chain_cols<0, 16>(args.chain, r.cr, v, cb, args.n - 1);
+    }
+    if (args.store == kStoreTma) {
+        store_box16(ymap, box, lane, v, static_cast<int>(cb), tm * kBM + q * 32);
+    } else if (r.live) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (cb + j < args.n) r.yrow[(cb + j) * args.ynb[0]] = v[j];
+    }
+}
+
+// A finished linear-layer tile (or a split-K part of one) out of the sixteen
+// draining warps' registers: warp (q, part) holds rows q * 32 + lane, columns
+// colA .. colA + BN / 4 of the product (gated: BN / 8 of the x half, then the
+// matching BN / 8 of the gate half).  Split-K parts go to the partial sums
+// through `ymap` (the reduction applies the chain).
+template <bool GATED, int BN>
+__device__ __forceinline__ void store_linear_tile(const GemmArgs& args, const CUtensorMap* ymap, float* sum, int tm,
+                                                  int tn, int split, int q, int lane, int colA, uint8_t* box) {
+    constexpr int CPW = BN / 4;
+    if (args.ksplit > 1) {
+        const int prow = (split * args.tiles_m + tm) * kBM + q * 32;
+#pragma unroll
+        for (int c = 0; c < CPW; c += 16) store_box16(ymap, box, lane, sum + c, tn * BN + colA + c, prow);
+        return;
+    }
+    const LinearRow r = linear_row(args, tm, q * 32 + lane);
+    constexpr int NOUT = GATED ? CPW / 2 : CPW;     // output columns this warp writes
+    const long long ocol0 = GATED ? static_cast<long long>(tn) * (BN / 2) + colA : static_cast<long long>(tn) * BN + colA;
+#pragma unroll
+    for (int c = 0; c < NOUT; c += 16)
+        store_linear_group<GATED>(args, ymap, r, sum + c, GATED ? sum + CPW / 2 + c : nullptr, ocol0 + c, tm, q, lane,
+                                  box);
+}
+
 template <int MODE, bool GATED, int BN>
 __global__ void __launch_bounds__(kWideThreads, 1)
 gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
@@ -325,59 +411,8 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
 
         // ---- the tile's epilogue (the next item's products run meanwhile)
         const int row = q * 32 + lane;
-        if (args.ksplit > 1) {
-            const int prow = (split * args.tiles_m + tm) * kBM + q * 32;
-#pragma unroll
-            for (int c = 0; c < CPW; c += 16) store_box16(&ymap, box, lane, sum + c, tn * BN + colA + c, prow);
-        } else if (MODE == kModeLinear) {
-            const long long m = static_cast<long long>(tm) * kBM + row;
-            const bool live = m < args.m;
-            const long long mc = live ? m : args.m - 1;
-            // The row's ggml coordinates: rows of a 2-D output are i1 itself (no division).
-            long long i1 = mc, i2 = 0, i3 = 0;
-            if (args.rne1 < args.m) {
-                const long long rest = mc / args.rne1;
-                i1 = mc - rest * args.rne1;
-                i2 = rest % args.rne2;
-                i3 = rest / args.rne2;
-            }
-            ChainRow cr;
-            row_offsets(args.chain, cr, 0, i1, i2, i3);
-            float* yrow = args.y + i1 * args.ynb[1] + i2 * args.ynb[2] + i3 * args.ynb[3];
-            constexpr int NOUT = GATED ? CPW / 2 : CPW;     // output columns this warp writes
-            const long long ocol0 = GATED ? static_cast<long long>(tn) * (BN / 2) + colA : static_cast<long long>(tn) * BN + colA;
-#pragma unroll
-            for (int c = 0; c < NOUT; c += 16) {
-                float* v = sum + c;
-                const long long cb = ocol0 + c;
-                if (GATED) {
-                    apply_chain_cols<0, 16>(args.chain, cr, v, cb, args.n - 1);
-                    apply_chain_cols<0, 16>(args.chain, cr, sum + CPW / 2 + c, args.n + cb, 2LL * args.n - 1);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] *= gelu(sum[CPW / 2 + c + j]);
-                } else {
-                    if (args.chain.from_redirect) {
-                        if (args.store == kStoreTma) {
-                            add_old_box16(args.y, args.n, static_cast<long long>(tm) * kBM + q * 32, args.m, cb,
-                                          args.n, box, lane, v);
-                        } else {
-                            float old[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) old[j] = yrow[min(cb + j, args.n - 1LL) * args.ynb[0]];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] = old[j] + v[j];
-                        }
-                    }
-                    apply_chain_cols<0, 16>(args.chain, cr, v, cb, args.n - 1);
-                }
-                if (args.store == kStoreTma) {
-                    store_box16(&ymap, box, lane, v, static_cast<int>(cb), tm * kBM + q * 32);
-                } else if (live) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (cb + j < args.n) yrow[(cb + j) * args.ynb[0]] = v[j];
-                }
-            }
+        if (args.ksplit > 1 || MODE == kModeLinear) {
+            store_linear_tile<GATED, BN>(args, &ymap, sum, tm, tn, split, q, lane, colA, box);
         } else {
             const ConvPos p = conv_pos(g, tm, row);
             const int ox = p.ok ? p.ox : 0, oy = p.ok ? p.oy : 0, img = p.ok ? p.img : 0;

@@ -10,6 +10,7 @@
 
 #include "../../include/sdb.h"
 #include "gemm.cuh"
+#include "gemm_fused.cuh"
 #include "gemm_wide.cuh"
 #include "quant.cuh"
 #include "runtime.cuh"
@@ -241,6 +242,170 @@ bool mul_mat_shapes(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* 
     return true;
 }
 
+// ---- the fused-split linear GEMM (gemm_fused.cuh)
+
+// GroupNorm prologue for the fused path: the rows of x (an image's positions,
+// channels along the row) normalised into `out`, the same values the split
+// pre-pass reads through chain.cuh gn_in.  Four channels a thread.
+__global__ void gn_rows_kernel(const float* __restrict__ x, long long rows, int k, float* __restrict__ out,
+                               GnIn gn) {
+    const int q4 = k / 4;
+    const long long total = rows * q4;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = idx / q4;
+        const int c0 = static_cast<int>(idx - r * q4) * 4;
+        const long long img = r / gn.positions;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x + r * k + c0));
+        float4 o;
+        o.x = gn_in(gn, v.x, gn_coef(gn, c0, img));
+        o.y = gn_in(gn, v.y, gn_coef(gn, c0 + 1, img));
+        o.z = gn_in(gn, v.z, gn_coef(gn, c0 + 2, img));
+        o.w = gn_in(gn, v.w, gn_coef(gn, c0 + 3, img));
+        *reinterpret_cast<float4*>(out + r * k + c0) = o;
+    }
+}
+
+// The fused kernel's plan: the tile width (the product's columns a tile: 128,
+// 160 or 192) and the K split that minimise
+//   waves x (k-blocks of an item x a k-block's cost + an item's epilogue),
+// a k-block costing its operand bytes from L2 (x 32 KB, W 128 BN bytes) at
+// ~48 bytes a clock an SM, plus the split's partial sums.  Gated products are
+// not split.
+int plan_fused(GemmArgs& a, int64_t n, int tiles_m, int64_t m, bool gated) {
+    const int64_t cols = gated ? 2 * n : n;
+    const int sms = current_sm_count();
+    const int64_t forced = tuning().block_n;
+    int best_bn = 0, best_split = 1;
+    double best_cost = 0.0;
+    for (int bn : {192, 160, 128}) {
+        if ((forced == 128 || forced == 160 || forced == 192) && bn != forced) continue;
+        const int64_t tiles = tiles_m * ((cols + bn - 1) / bn);
+        const double kb_cost = (32768.0 + 128.0 * bn) / 48.0;
+        const int max_split = gated ? 1 : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(32, a.kblocks / 4)));
+        for (int split = 1; split <= max_split; ++split) {
+            const int per = (a.kblocks + split - 1) / split;
+            const int parts = (a.kblocks + per - 1) / per;
+            if (parts != split) continue;
+            const int64_t items = tiles * parts;
+            const int64_t waves = (items + sms - 1) / sms;
+            double cost = static_cast<double>(waves) * (per * kb_cost + 600.0);
+            if (parts > 1) cost += (2.0 * parts + 1.0) * static_cast<double>(m) * n * 4 / sms / 48.0;
+            if (best_bn == 0 || cost < best_cost * 0.98) {
+                best_bn = bn;
+                best_split = parts;
+                best_cost = cost;
+            }
+        }
+    }
+    a.per_split = (a.kblocks + best_split - 1) / best_split;
+    a.ksplit = best_split;
+    return best_bn;
+}
+
+template <bool GATED, int BN>
+int launch_fused_bn(const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& ymap, GemmArgs a,
+                    cudaStream_t st) {
+    using S = FusedShape<BN>;
+    auto kern = gemm_fused_kernel<GATED, BN>;
+    SDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes));
+    const long long items = static_cast<long long>(a.tiles_m) * a.tiles_n * a.ksplit;
+    if (items >= (1LL << 31)) return fail(SDB_NOT_SUPPORTED, "gemm: too many tiles");
+    a.items = static_cast<int>(items);
+    const int grid = static_cast<int>(std::min<long long>(items, current_sm_count()));
+    CUtensorMap pmap;
+    if (a.ksplit > 1) {
+        const long long rows = static_cast<long long>(a.ksplit) * a.tiles_m * kBM;
+        if (!store_map(&pmap, a.part, a.part_ld, rows, a.part_ld, 16))
+            return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the partial sums");
+    }
+    kern<<<grid, kFusedThreads, S::kSmemBytes, st>>>(xmap, wmap, a.ksplit > 1 ? pmap : ymap, a);
+    count_launch();
+    SDB_CUDA(cudaGetLastError());
+    if (a.ksplit > 1) return launch_reduce<kModeLinear>(a, st);
+    return SDB_OK;
+}
+
+int launch_fused(const CUtensorMap& xmap, const Packed& p, bool gated, int bn, const CUtensorMap& ymap,
+                 const GemmArgs& a, cudaStream_t st) {
+    if (gated) {
+        if (bn == 192) return launch_fused_bn<true, 192>(xmap, p.map96, ymap, a, st);
+        if (bn == 160) return launch_fused_bn<true, 160>(xmap, p.map80, ymap, a, st);
+        return launch_fused_bn<true, 128>(xmap, p.map64, ymap, a, st);
+    }
+    if (bn == 192) return launch_fused_bn<false, 192>(xmap, p.map192, ymap, a, st);
+    if (bn == 160) return launch_fused_bn<false, 160>(xmap, p.map160, ymap, a, st);
+    return launch_fused_bn<false, 128>(xmap, p.map128, ymap, a, st);
+}
+
+// Whether the fused kernel takes x: FP32 rows of K % 4 == 0 (TMA's 16-byte
+// row pitch), 16-byte aligned, at most 2^31 rows; with gemm_fused = 1 only
+// where it measured faster than the split pre-pass (plain products of
+// K <= 2560), with 2 always.
+bool fused_rows(const sdb_tensor* x, int64_t k, int64_t m, bool gated) {
+    const int64_t mode = tuning().gemm_fused;
+    if (mode == 0 || (mode == 1 && (gated || k > 2560))) return false;
+    return k % 4 == 0 && (reinterpret_cast<uintptr_t>(x->data) & 15) == 0 && m < (1LL << 31) && k < (1LL << 31);
+}
+
+// run_linear's body on the fused kernel: x (or, with a normalisation
+// prologue, x normalised into the workspace by the same kernels as the
+// separate GroupNorm / LayerNorm nodes) read as FP32 rows straight by TMA.
+int run_linear_fused(std::shared_ptr<Packed> p, size_t w_bytes, bool transient, const sdb_tensor* w,
+                     const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain, cudaStream_t st, bool gated,
+                     const GnIn* gn, const LnIn* ln, int64_t m, int64_t n, int64_t k) {
+    const int tiles = static_cast<int>((m + kBM - 1) / kBM);
+    GemmArgs a{};
+    a.m = static_cast<int>(m);
+    a.kblocks = static_cast<int>(p->kpad / kBK);
+    a.n = static_cast<int>(n);
+    a.b1_row = static_cast<int>(p->b1_row);
+    a.tiles_m = tiles;
+    a.rne1 = dst->ne[1];
+    a.rne2 = dst->ne[2];
+    set_out(a, dst, chain);
+    const int bn = plan_fused(a, n, tiles, m, gated);
+
+    // Workspace: a transient operand's packing, the normalised x (with a prologue), partial sums.
+    const size_t xn_bytes = (gn || ln) ? static_cast<size_t>(round_up(m * k * 4, 256)) : 0;
+    void* ws0 = nullptr;
+    if (int s = workspace(st, w_bytes + xn_bytes + partial_bytes(a.ksplit, tiles, gated ? 2 * n : n, bn), &ws0);
+        s != SDB_OK)
+        return s;
+    if (transient)
+        if (int s = pack_transient(w, n, k, ws0, st, p.get()); s != SDB_OK) return s;
+    uint8_t* ws = static_cast<uint8_t*>(ws0) + w_bytes;
+    set_partials(a, ws, xn_bytes, tiles, bn);
+    const float* xrows = static_cast<const float*>(x->data);
+    if (ln) {
+        sdb_tensor xn = *x;
+        xn.data = ws;
+        if (int s = sdb_norm(x, &xn, ln->eps, ln->chain, st); s != SDB_OK) return s;
+        xrows = reinterpret_cast<const float*>(ws);
+    } else if (gn) {
+        const long long total = m * (k / 4);
+        const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+        gn_rows_kernel<<<blocks, 256, 0, st>>>(xrows, m, static_cast<int>(k), reinterpret_cast<float*>(ws), *gn);
+        count_launch();
+        SDB_CUDA(cudaGetLastError());
+        xrows = reinterpret_cast<const float*>(ws);
+    }
+    CUtensorMap xmap;
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(k) * 4};
+    const uint32_t box[2] = {32, 128};
+    if (encode_tensor_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(xrows), dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for the activation rows");
+    CUtensorMap ymap{};
+    a.store = kStoreDirect;
+    if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ynb[0] == 1 && a.ynb[1] == n &&
+        store_map(&ymap, a.y, n, m, n, 16))
+        a.store = kStoreTma;
+    a.tiles_n = static_cast<int>(((gated ? 2 * n : n) + bn - 1) / bn);
+    return launch_fused(xmap, *p, gated, bn, ymap, a, st);
+}
+
 // transient: w is packed into the workspace on every call instead of being
 // kept by the store (an operand the graph writes between calls).
 int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, const sdb_chain* chain,
@@ -272,6 +437,8 @@ int run_linear(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst, 
     }
     const int wmode = gated ? kWeightGated : p->split ? kWeightSplit : kWeightHalf;
     const int tiles = static_cast<int>((m + kBM - 1) / kBM);
+    if (wmode != kWeightSplit && fused_rows(x, k, m, gated))
+        return run_linear_fused(p, w_bytes, transient, w, x, dst, chain, st, gated, gn, ln, m, n, k);
     const int kblocks = static_cast<int>(p->kpad / kBK);
 
     GemmArgs a{};

@@ -372,6 +372,12 @@ __device__ __forceinline__ void tmem_st32_bits(uint32_t addr, const uint32_t (&v
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st4_bits(uint32_t addr, const uint4& v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_st8_bits(uint32_t addr, const uint32_t (&v)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr), "r"(v[0]),
                  "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
@@ -404,6 +410,23 @@ __device__ __forceinline__ void split_weights2(float p0, float p1, uint32_t& hi,
     asm("mov.b64 %0, {%1, %1};" : "=l"(s) : "f"(-2048.0f));
     asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(s));
     asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.f16x2.f32 %0, b, a;\n\t}" : "=r"(lo) : "l"(d));
+}
+
+// split8 in fewer instructions (split_weights2's packed form, the same pairs):
+// returns true when a value rounds beyond FP16's range (its hi half is an
+// infinity or a NaN).  Values in (65504, 65520) round to 65504 and keep an
+// exact remainder, so they are not reported.
+__device__ __forceinline__ bool split8_packed(const float (&x)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+    uint32_t inf = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        split_weights2(x[2 * i], x[2 * i + 1], h[i], l[i]);
+        inf |= ((h[i] & 0x7c00u) == 0x7c00u) | ((h[i] & 0x7c000000u) == 0x7c000000u);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+    return inf != 0;
 }
 
 // Descriptor of an operand tile in the no-swizzle canonical layout: 8 x 16-byte

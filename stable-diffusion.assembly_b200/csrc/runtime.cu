@@ -51,6 +51,7 @@ int64_t* knob(Tuning& t, const std::string& name) {
     if (name == "quantize") return &t.quantize;
     if (name == "block_n") return &t.block_n;
     if (name == "attention_wg") return &t.attention_wg;
+    if (name == "gemm_fused") return &t.gemm_fused;
     return nullptr;
 }
 
@@ -61,9 +62,10 @@ bool valid(const std::string& name, int64_t v) {
     if (name == "group") return v == 32 || v == 64 || v == 128 || v == 256;
     if (name == "weight_group") return v == 0 || v == 1;
     if (name == "quantize") return v >= 0 && v <= 7;
-    if (name == "block_n") return v == 0 || v == 128 || v == 256;
+    if (name == "block_n") return v == 0 || v == 128 || v == 160 || v == 192 || v == 256;
     if (name == "todo") return v >= 1 && v <= 4;
     if (name == "attention_wg") return v >= 0 && v <= 2;
+    if (name == "gemm_fused") return v >= 0 && v <= 2;
     return v >= 0;
 }
 

@@ -33,8 +33,9 @@ struct Tuning {
     int64_t group = 64;          // numbers of k sharing a scale: 32, 64, 128 or 256
     int64_t weight_group = 1;    // the weights' scale per group: 1; per whole row: 0
     int64_t quantize = 7;        // with bits, what is quantized: 1 linear layers, 2 convolutions, 4 attention
-    int64_t block_n = 0;         // GEMM tile width: 0 automatic, 128 or 256
+    int64_t block_n = 0;         // GEMM tile width: 0 automatic; 128 or 256 (wide kernel), 128, 160 or 192 (fused kernel)
     int64_t attention_wg = 2;    // 2: Q and P in tensor memory, two query tiles a CTA, where it fits; 1: two-warpgroup; 0: the pair kernel
+    int64_t gemm_fused = 1;      // linear layers: 1 the activations split inside the GEMM (FP32 rows by TMA) where it pays; 2 always; 0 the split pre-pass
 };
 
 Tuning& tuning();

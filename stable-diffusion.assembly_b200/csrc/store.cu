@@ -239,9 +239,10 @@ void remember(const Key& key, const std::shared_ptr<Packed>& p) {
 int make_maps(Packed& p) {
     const uint64_t dims[2] = {static_cast<uint64_t>(p.kpad), static_cast<uint64_t>(p.rows_total)};
     const uint64_t strides[1] = {static_cast<uint64_t>(p.kpad) * 2};
-    for (int bn : {64, 128, 192, 256}) {
+    for (int bn : {64, 80, 96, 128, 160, 192, 256}) {
         const uint32_t box[2] = {64, static_cast<uint32_t>(bn)};
-        CUtensorMap* m = bn == 256 ? &p.map256 : bn == 192 ? &p.map192 : bn == 128 ? &p.map128 : &p.map64;
+        CUtensorMap* m = bn == 256 ? &p.map256 : bn == 192 ? &p.map192 : bn == 160 ? &p.map160
+                       : bn == 128 ? &p.map128 : bn == 96 ? &p.map96 : bn == 80 ? &p.map80 : &p.map64;
         const CUresult r = encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.data, dims, strides, box,
                                              CU_TENSOR_MAP_SWIZZLE_128B);
         if (r != CUDA_SUCCESS) return fail(SDB_CUDA_ERROR, "cuTensorMapEncodeTiled failed for packed weights");

@@ -51,6 +51,9 @@ struct Packed {
     int icp = 0;              // conv: channels per tap
     bool split = false;       // FP32 weights: hi rows then lo rows
     CUtensorMap map64{};      // box {64, 64}
+    CUtensorMap map80{};      // box {64, 80}
+    CUtensorMap map96{};      // box {64, 96}
+    CUtensorMap map160{};     // box {64, 160}
     CUtensorMap map128{};     // box {64, 128}
     CUtensorMap map192{};     // box {64, 192}
     CUtensorMap map256{};     // box {64, 256}

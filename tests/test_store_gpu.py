@@ -61,8 +61,9 @@ def test_store_forget(cuda, name):
 
 
 def test_store_reuses_packed_weights(cuda):
-    """A second call with the same weights packs nothing: the split of the
-    activations and the product (two launches), without the packing."""
+    """A second call with the same weights packs nothing: one launch, the
+    product (which splits its FP32 activations itself), without the packing;
+    with the split pre-pass (gemm_fused=0) two."""
     import sdb
 
     g = rng(4)
@@ -71,13 +72,20 @@ def test_store_reuses_packed_weights(cuda):
     sdb.mul_mat(w, x)
     n0 = sdb.launch_count()
     sdb.mul_mat(w, x)
-    assert sdb.launch_count() - n0 == 2
+    assert sdb.launch_count() - n0 == 1
+    sdb.set_tuning("gemm_fused=0")
+    try:
+        n0 = sdb.launch_count()
+        sdb.mul_mat(w, x)
+        assert sdb.launch_count() - n0 == 2
+    finally:
+        sdb.set_tuning("gemm_fused=1")
     entries, nbytes = sdb.store_stats()
     assert entries >= 1 and nbytes > 0
 
 
 def test_store_off_repacks(cuda):
-    """With store=0 every call packs anew (pack, split, product) and keeps nothing."""
+    """With store=0 every call packs anew (pack, product) and keeps nothing."""
     import sdb
 
     g = rng(5)
@@ -88,7 +96,7 @@ def test_store_off_repacks(cuda):
         before = sdb.store_stats()[0]
         n0 = sdb.launch_count()
         a = host(sdb.mul_mat(w, x))
-        assert sdb.launch_count() - n0 == 3
+        assert sdb.launch_count() - n0 == 2
         assert sdb.store_stats()[0] <= before
     finally:
         sdb.set_tuning("store=1")
