@@ -76,11 +76,14 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
     uint64_t* xempty = xfull + S::kXStages;   // every worker read its part
     uint64_t* wfull = xempty + S::kXStages;
     uint64_t* wempty = wfull + S::kWStages;   // the products completed
+    // The two buffers of A and of the accumulator need no "free again" barriers of their
+    // own: a worker splits k-block it + 1 into A buffer (it + 1) % 2 after it drained
+    // k-block it - 1, whose d_full says that the products that read that buffer are done;
+    // and every worker drained accumulator it % 2 (k-block it - 2) before it split k-block
+    // it, so a_full(it) also says that the accumulator is free.
     uint64_t* a_full = wempty + S::kWStages;  // [2] the workers wrote an A buffer
-    uint64_t* a_empty = a_full + 2;           // [2] its products completed
-    uint64_t* d_full = a_empty + 2;           // [2] an accumulator's products completed
-    uint64_t* d_empty = d_full + 2;           // [2] the workers drained it
-    uint64_t* drain = d_empty + 2;
+    uint64_t* d_full = a_full + 2;            // [2] an accumulator's products completed
+    uint64_t* drain = d_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -98,9 +101,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&a_full[b], kFusedWorkers);
-            mbar_init(&a_empty[b], 1);
             mbar_init(&d_full[b], 1);
-            mbar_init(&d_empty[b], kFusedWorkers);
         }
         mbar_init(drain, 1);
         *abort = 0;
@@ -145,7 +146,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                 item_range(item, tm, tn, split, kb0, kb1);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % stages;
-                    if (!mbar_wait(&emptyb[s], ((it / stages) & 1) ^ 1, abort, args.err)) { ok = false; break; }
+                    if (!mbar_wait_sleep(&emptyb[s], ((it / stages) & 1) ^ 1, abort, args.err)) { ok = false; break; }
                     if (is_x) {
                         mbar_arrive_expect_tx(&xfull[s], S::kXBytes);
                         uint8_t* st = smem + s * S::kXBytes;
@@ -176,9 +177,8 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             for (int it = 0; it < total_kb; ++it) {
                 const int s = it % S::kWStages, b = it & 1;
                 const uint32_t use = static_cast<uint32_t>(it >> 1) & 1u;
-                if (!mbar_wait(&wfull[s], (it / S::kWStages) & 1, abort, args.err) ||
-                    !mbar_wait(&a_full[b], use, abort, args.err) ||
-                    !mbar_wait(&d_empty[b], use ^ 1u, abort, args.err)) {
+                if (!mbar_wait_sleep(&wfull[s], (it / S::kWStages) & 1, abort, args.err) ||
+                    !mbar_wait_sleep(&a_full[b], use, abort, args.err)) {
                     ok = false;
                     break;
                 }
@@ -193,8 +193,6 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
 #pragma unroll
                 for (int kk = 1; kk < kBK / 16; ++kk)
                     mma_f16_ta(d, a + 8 * kk, desc_kmajor_sw128(b0 + kk * 32), idesc, 1u);
-                // d_full last: a worker that saw it knows the other two arrived.
-                mma_commit(&a_empty[b]);
                 mma_commit(&wempty[s]);
                 mma_commit(&d_full[b]);
             }
@@ -215,7 +213,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         constexpr int G = GATED ? BN / 32 : BN / 16;
         constexpr int NG = (G + 3) / 4;
         auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
-            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, args.err) ? 1 : 0) != 0;
+            return __all_sync(0xffffffffu, mbar_wait_sleep(bar, parity, abort, args.err) ? 1 : 0) != 0;
         };
         // The split of k-block number `it`: this thread's row, K 16 part .. + 15 of the block,
         // read from the stage's x boxes (128-byte swizzle: chunk c of row r at (c ^ r % 8) 16).
@@ -241,8 +239,6 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&xempty[s]);
-            if (!warp_wait(&a_empty[b], ((static_cast<uint32_t>(it) >> 1) & 1u) ^ 1u)) return false;
-            tc_fence_after();
             const uint32_t a = lane_addr + S::kACol + 64u * b + 8u * part;
             tmem_st4_bits(a, hv[0]);
             tmem_st4_bits(a + 4, hv[1]);
@@ -294,8 +290,16 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             }
         };
 
+        // Splits every k-block up to j not split yet.  A worker may split k-block j once it has
+        // seen d_full(j - 2) (the products that read A buffer j % 2 are done).
+        int next_split = 0;
+        auto split_upto = [&](int j) -> bool {
+            for (; next_split <= j && next_split < total_kb; ++next_split)
+                if (!split_block(next_split)) return false;
+            return true;
+        };
         int it = 0;
-        if (total_kb > 0) ok = split_block(0);
+        ok = split_upto(0);
         for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x) {
             int tm, tn, split, kb0, kb1;
             item_range(item, tm, tn, split, kb0, kb1);
@@ -305,14 +309,13 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
 #pragma unroll
                 for (int j = 0; j < (GATED ? 32 : 16); ++j) sum[i][j] = 0.0f;
             for (int kb = kb0; kb < kb1; ++kb, ++it) {
-                if (it + 1 < total_kb && !split_block(it + 1)) { ok = false; break; }
+                if (!split_upto(it + 1)) { ok = false; break; }
                 const int b = it & 1;
                 if (!warp_wait(&d_full[b], (static_cast<uint32_t>(it) >> 1) & 1u)) { ok = false; break; }
                 tc_fence_after();
                 drain_groups(lane_addr + S::kAccStride * b, sum);
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&d_empty[b]);
             }
             if (!ok) break;
             // ---- the tile's epilogue (the next item's first products run meanwhile)

@@ -340,11 +340,11 @@ int launch_fused(const CUtensorMap& xmap, const Packed& p, bool gated, int bn, c
 
 // Whether the fused kernel takes x: FP32 rows of K % 4 == 0 (TMA's 16-byte
 // row pitch), 16-byte aligned, at most 2^31 rows; with gemm_fused = 1 only
-// where it measured faster than the split pre-pass (plain products of
-// K <= 2560), with 2 always.
+// where it measured faster than the split pre-pass (plain products: the gated
+// ones keep the wide kernel's 256-column tiles), with 2 always.
 bool fused_rows(const sdb_tensor* x, int64_t k, int64_t m, bool gated) {
     const int64_t mode = tuning().gemm_fused;
-    if (mode == 0 || (mode == 1 && (gated || k > 2560))) return false;
+    if (mode == 0 || (mode == 1 && gated)) return false;
     return k % 4 == 0 && (reinterpret_cast<uintptr_t>(x->data) & 15) == 0 && m < (1LL << 31) && k < (1LL << 31);
 }
 

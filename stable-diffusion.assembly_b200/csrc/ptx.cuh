@@ -78,6 +78,22 @@ __device__ __forceinline__ bool mbar_try_wait2(uint64_t* b1, uint32_t p1, uint64
     return ok != 0;
 }
 
+// The same test, except that a thread whose phase is not complete yet is
+// suspended (until the phase completes, or at the latest after about
+// `hint_ns` nanoseconds) instead of returning at once: waiting warps then
+// take no issue slots from the warps that work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `parity` to complete.  Returns false when the kernel
 // is winding down: either another thread set *abort, or this wait ran past
 // kWaitLimitCycles SM clocks (about 2 s at the B200's clocks), in which case
@@ -97,6 +113,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                 if (err) atomicOr(err, kErrTimeout);
                 return false;
             }
+        }
+    }
+}
+
+// mbar_wait for kernels where many warps wait while others work: the waiting
+// thread is suspended between tests (at most ~20 us at a time, so that an
+// abort is seen soon) instead of testing in a loop that takes issue slots
+// from the working warps.  Waking takes longer than a test, so kernels whose
+// waits are short and few keep mbar_wait.
+constexpr uint32_t kSuspendHintNs = 20000;
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
+        if (*abort) return false;
+        if (clock64() - t0 > kWaitLimitCycles) {
+            *abort = 1;
+            if (err) atomicOr(err, kErrTimeout);
+            return false;
         }
     }
 }
