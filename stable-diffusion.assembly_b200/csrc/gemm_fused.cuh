@@ -177,8 +177,10 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             for (int it = 0; it < total_kb; ++it) {
                 const int s = it % S::kWStages, b = it & 1;
                 const uint32_t use = static_cast<uint32_t>(it >> 1) & 1u;
-                if (!mbar_wait_sleep(&wfull[s], (it / S::kWStages) & 1, abort, args.err) ||
-                    !mbar_wait_sleep(&a_full[b], use, abort, args.err)) {
+                // Tested in a loop, not suspended: a woken thread would start the products
+                // a few hundred clocks late.
+                if (!mbar_wait(&wfull[s], (it / S::kWStages) & 1, abort, args.err) ||
+                    !mbar_wait(&a_full[b], use, abort, args.err)) {
                     ok = false;
                     break;
                 }
