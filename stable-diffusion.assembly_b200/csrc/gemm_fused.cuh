@@ -219,7 +219,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         };
         // The split of k-block number `it`: this thread's row, K 16 part .. + 15 of the block,
         // read from the stage's x boxes (128-byte swizzle: chunk c of row r at (c ^ r % 8) 16).
-        bool over = false;
+        float amax = 0.0f;   // the largest |x| split: 65520 or more rounds to an FP16 infinity
         auto split_block = [&](int it) -> bool {
             const int s = it % S::kXStages, b = it & 1;
             if (!warp_wait(&xfull[s], (it / S::kXStages) & 1)) return false;
@@ -237,7 +237,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                     e[4 * j + 2] = __uint_as_float(w.z);
                     e[4 * j + 3] = __uint_as_float(w.w);
                 }
-                over |= split8_packed(e, hv[h], lv[h]);
+                split8_packed(e, hv[h], lv[h], amax);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&xempty[s]);
@@ -263,11 +263,8 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                     tmem_ld16(acc + 16 * gidx, a);
                     tmem_ld16(acc + BN / 2 + 16 * gidx, g);
                     tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        sum[i][j] += a[j];
-                        sum[i][16 + j] += g[j];
-                    }
+                    add16_packed(sum[i], a);
+                    add16_packed(sum[i] + 16, g);
                 }
             } else {
                 // Two groups' loads in flight at a time.
@@ -280,14 +277,8 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                     if (has0) tmem_ld16(acc + 16 * g0, a);
                     if (has1) tmem_ld16(acc + 16 * g1, c);
                     tmem_ld_wait();
-                    if (has0) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) sum[i][j] += a[j];
-                    }
-                    if (has1) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) sum[i + 1][j] += c[j];
-                    }
+                    if (has0) add16_packed(sum[i], a);
+                    if (has1) add16_packed(sum[i + 1], c);
                 }
             }
         };
@@ -341,7 +332,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                 }
             }
         }
-        if (over) atomicOr(args.err, kErrRange);
+        if (!(amax < 65520.0f) && amax == amax) atomicOr(args.err, kErrRange);
         if (lane == 0) bulk_wait_all();
         __syncwarp();
     }

@@ -449,21 +449,32 @@ __device__ __forceinline__ void split_weights2(float p0, float p1, uint32_t& hi,
     asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.f16x2.f32 %0, b, a;\n\t}" : "=r"(lo) : "l"(d));
 }
 
-// split8 in fewer instructions (split_weights2's packed form, the same pairs):
-// returns true when a value rounds beyond FP16's range (its hi half is an
-// infinity or a NaN).  Values in (65504, 65520) round to 65504 and keep an
-// exact remainder, so they are not reported.
-__device__ __forceinline__ bool split8_packed(const float (&x)[8], uint4& hi, uint4& lo) {
+// split8 in fewer instructions (split_weights2's packed form, the same pairs),
+// with the range check left to the caller: `amax` takes the largest |x| (a
+// value of 65520 or more rounds to an FP16 infinity).  NaNs pass the maximum
+// unseen; they reach the output as NaNs.
+__device__ __forceinline__ void split8_packed(const float (&x)[8], uint4& hi, uint4& lo, float& amax) {
     uint32_t h[4], l[4];
-    uint32_t inf = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         split_weights2(x[2 * i], x[2 * i + 1], h[i], l[i]);
-        inf |= ((h[i] & 0x7c00u) == 0x7c00u) | ((h[i] & 0x7c000000u) == 0x7c000000u);
+        amax = fmax3(amax, fabsf(x[2 * i]), fabsf(x[2 * i + 1]));
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
-    return inf != 0;
+}
+
+// sum[j] += v[j] for j < 16, two lanes of FP32 a packed add (add.rn.f32x2: each
+// lane rounded to nearest as a scalar add would be).
+__device__ __forceinline__ void add16_packed(float* sum, const float (&v)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        uint64_t sp, vp;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(sp) : "f"(sum[j]), "f"(sum[j + 1]));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(vp) : "f"(v[j]), "f"(v[j + 1]));
+        asm("add.rn.f32x2 %0, %0, %1;" : "+l"(sp) : "l"(vp));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(sum[j]), "=f"(sum[j + 1]) : "l"(sp));
+    }
 }
 
 // Descriptor of an operand tile in the no-swizzle canonical layout: 8 x 16-byte
