@@ -370,13 +370,11 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constan
                         float gpart[32];
                         tmem_ld32(lane_addr + S::kNHi * BN + b * BN + half * NV + c, gpart);
                         tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) gsum[c + j] += gpart[j];
+                        add_packed<32>(gsum + c, gpart);
                     } else {
                         tmem_ld_wait();
                     }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) sum[c + j] += part[j];
+                    add_packed<32>(sum + c, part);
                 }
                 tc_fence_before();
                 __syncwarp();

@@ -55,11 +55,13 @@ __device__ __forceinline__ void tmem_add(uint32_t addr, float* sum, float scale)
         tmem_ld16(addr + c, a);
         if (c + 16 < N) tmem_ld16(addr + c + 16, b);
         tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) sum[c + j] = fmaf(a[j], scale, sum[c + j]);
-        if (c + 16 < N) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) sum[c + 16 + j] = fmaf(b[j], scale, sum[c + 16 + j]);
+        // Packed: two columns an instruction (fma(v, 1, s) is s + v exactly).
+        if (scale == 1.0f) {
+            add_packed<16>(sum + c, a);
+            if (c + 16 < N) add_packed<16>(sum + c + 16, b);
+        } else {
+            fma_packed<16>(sum + c, a, scale);
+            if (c + 16 < N) fma_packed<16>(sum + c + 16, b, scale);
         }
     }
 }

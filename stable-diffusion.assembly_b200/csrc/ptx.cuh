@@ -464,15 +464,33 @@ __device__ __forceinline__ void split8_packed(const float (&x)[8], uint4& hi, ui
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// sum[j] += v[j] for j < 16, two lanes of FP32 a packed add (add.rn.f32x2: each
-// lane rounded to nearest as a scalar add would be).
-__device__ __forceinline__ void add16_packed(float* sum, const float (&v)[16]) {
+// sum[j] += v[j] for j < N (N even), two lanes of FP32 a packed add
+// (add.rn.f32x2: each lane rounded to nearest as a scalar add would be).
+template <int N>
+__device__ __forceinline__ void add_packed(float* sum, const float* v) {
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
+    for (int j = 0; j < N; j += 2) {
         uint64_t sp, vp;
         asm("mov.b64 %0, {%1, %2};" : "=l"(sp) : "f"(sum[j]), "f"(sum[j + 1]));
         asm("mov.b64 %0, {%1, %2};" : "=l"(vp) : "f"(v[j]), "f"(v[j + 1]));
         asm("add.rn.f32x2 %0, %0, %1;" : "+l"(sp) : "l"(vp));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(sum[j]), "=f"(sum[j + 1]) : "l"(sp));
+    }
+}
+
+__device__ __forceinline__ void add16_packed(float* sum, const float (&v)[16]) { add_packed<16>(sum, v); }
+
+// sum[j] = fma(v[j], scale, sum[j]) for j < N (N even), packed as add_packed.
+template <int N>
+__device__ __forceinline__ void fma_packed(float* sum, const float* v, float scale) {
+    uint64_t sc;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(sc) : "f"(scale));
+#pragma unroll
+    for (int j = 0; j < N; j += 2) {
+        uint64_t sp, vp;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(sp) : "f"(sum[j]), "f"(sum[j + 1]));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(vp) : "f"(v[j]), "f"(v[j + 1]));
+        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(sp) : "l"(vp), "l"(sc));
         asm("mov.b64 {%0, %1}, %2;" : "=f"(sum[j]), "=f"(sum[j + 1]) : "l"(sp));
     }
 }
