@@ -1008,12 +1008,17 @@ __device__ __forceinline__ void attention_tm_softmax(const AttnArgs& a, uint32_t
             for (int ch = 0; ch < OCH; ++ch)
                 tmem_ld16(t_o + lane_off + ch * 16, *reinterpret_cast<float(*)[16]>(oh + ch * 16));
             tmem_ld_wait();
+            // Packed: two dims an instruction, each rounded as the scalar form.
+            add_packed<DVC>(o, oh);
             if (factor != 1.0f) {
+                const uint64_t f2 = pack2(factor, factor);
 #pragma unroll
-                for (int i = 0; i < DVC; ++i) o[i] = (o[i] + oh[i]) * factor;
-            } else {
-#pragma unroll
-                for (int i = 0; i < DVC; ++i) o[i] += oh[i];
+                for (int i = 0; i < DVC; i += 2) {
+                    float x0, x1;
+                    unpack2(fmul2(pack2(o[i], o[i + 1]), f2), x0, x1);
+                    o[i] = x0;
+                    o[i + 1] = x1;
+                }
             }
         }
         tmem_st_wait();
