@@ -69,6 +69,31 @@ def test_layer_norm_chain(cuda):
     close(host(out), want)
 
 
+@pytest.mark.parametrize("shape", [
+    (1, 77, 320),    # two rows a warp, an odd row count (the last warp's second row empty)
+    (3, 5, 256),     # 15 rows of 256 (eight numbers a lane)
+    (2, 9, 384),     # rows of 384: the widest of the two-rows-a-warp form
+    (1, 7, 640),     # one row a warp, 20 numbers a lane
+    (1, 3, 1280),    # 40 numbers a lane
+    (1, 5, 200),     # a row that ends inside a lane's numbers
+    (1, 2, 1500),    # wider than the register forms: the shared-memory kernel
+])
+def test_layer_norm_row_forms(cuda, shape):
+    """Every LayerNorm row form against the oracle, with a canary output and a gamma/beta chain."""
+    import sdb
+
+    g = rng(sum(shape))
+    x = oracle.uniform(g, shape, 3.0) + np.float32(0.5)
+    c = shape[-1]
+    gamma = oracle.uniform(g, (c,), 1.0)
+    beta = oracle.uniform(g, (c,), 1.0)
+    out = canary_like(x.shape, cuda)
+    chain = sdb.Chain().mul(cuda_tensor(gamma, cuda)).add(cuda_tensor(beta, cuda))
+    sdb.norm(cuda_tensor(x, cuda), 1e-5, out=out, chain=chain)
+    want = oracle.apply_chain(oracle.norm_ref(x, 1e-5), [("mul", gamma), ("add", beta)])
+    close(host(out), want)
+
+
 def test_group_norm_matches_double(cuda):
     """The statistics in double: the result is within FP32 rounding of the exact normalisation."""
     import sdb
