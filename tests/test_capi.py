@@ -80,6 +80,26 @@ def test_tuning_parser(lib):
     assert "unknown" in sdb.load().sdb_last_error().decode() or "bad value" in sdb.load().sdb_last_error().decode()
 
 
+def test_tuning_gemm_knobs(lib):
+    """The linear layers' GEMM knobs: gemm_fused 0..2 and the fused kernel's tile widths 160 and 192."""
+    import sdb
+
+    sdb.load()
+    assert sdb.get_tuning("gemm_fused") == 1
+    try:
+        for v in (0, 2, 1):
+            sdb.set_tuning(f"gemm_fused={v}")
+            assert sdb.get_tuning("gemm_fused") == v
+        for v in (128, 160, 192, 256, 0):
+            sdb.set_tuning(f"block_n={v}")
+            assert sdb.get_tuning("block_n") == v
+        for bad in ("gemm_fused=3", "block_n=144"):
+            with pytest.raises(sdb.SdbError):
+                sdb.set_tuning(bad)
+    finally:
+        sdb.set_tuning("gemm_fused=1,block_n=0")
+
+
 def test_token_downsampling(lib):
     """hooks.cc:166-172: 1 unless todo >= 2 and the grid has todo_tokens tokens."""
     import sdb
