@@ -802,6 +802,36 @@ int conv2d_impl(const sdb_tensor* w, const sdb_tensor* x, const sdb_tensor* dst,
         return run_quantized_conv(w, x, dst, params, chain, st);
     }
     if (const int f = winograd_form(w, dst, params); f != 0) return run_winograd(f, w, x, dst, params, chain, st, gn);
+    // A 1x1 convolution at stride 1 without padding, channels-last in and out, is a linear
+    // layer over the image's positions (rows of IC channels in, rows of OC out, the same
+    // memory): it takes the linear layers' path, whose GEMM splits the rows itself.  The
+    // chain's operands are read in the output's (x, y, c, n) order; the linear view is
+    // (c, x, y, n).
+    const int64_t ic1 = x->ne[2], oc1 = w->ne[3];
+    if (tuning().gemm_fused != 0 && w->type == SDB_TYPE_F16 && w->ne[0] == 1 && w->ne[1] == 1 && params[0] == 1 &&
+        params[1] == 1 && params[2] == 0 && params[3] == 0 && w->nb[0] == 2 && w->nb[1] == 2 && w->nb[2] == 2 &&
+        w->nb[3] == 2 * ic1 && channels_last(x) && channels_last(dst) && !(chain && chain->redirect)) {
+        const int64_t W = x->ne[0], H = x->ne[1], N = x->ne[3];
+        sdb_tensor wl = *w, xl = *x, dl = *dst;
+        const int64_t wne[4] = {ic1, oc1, 1, 1}, wnb[4] = {2, 2 * ic1, 2 * ic1 * oc1, 2 * ic1 * oc1};
+        const int64_t xne[4] = {ic1, W, H, N}, xnb[4] = {4, 4 * ic1, 4 * ic1 * W, 4 * ic1 * W * H};
+        const int64_t dne[4] = {oc1, W, H, N}, dnb[4] = {4, 4 * oc1, 4 * oc1 * W, 4 * oc1 * W * H};
+        for (int d = 0; d < 4; ++d) {
+            wl.ne[d] = wne[d]; wl.nb[d] = wnb[d];
+            xl.ne[d] = xne[d]; xl.nb[d] = xnb[d];
+            dl.ne[d] = dne[d]; dl.nb[d] = dnb[d];
+        }
+        sdb_chain cl{};
+        if (chain) {
+            cl = *chain;
+            for (int s = 0; s < cl.count; ++s) {
+                const int64_t* nb = chain->steps[s].nb;
+                const int64_t perm[4] = {nb[2], nb[0], nb[1], nb[3]};
+                for (int d = 0; d < 4; ++d) cl.steps[s].nb[d] = perm[d];
+            }
+        }
+        return run_linear(&wl, &xl, &dl, chain ? &cl : nullptr, st, false, false, gn);
+    }
     if (gn && !channels_last(x))
         return fail(SDB_NOT_SUPPORTED, "sdb_conv2d: a GroupNorm prologue needs a channels-last image");
     const int64_t ic = x->ne[2], oc = w->ne[3];

@@ -129,3 +129,32 @@ def _config2_sequence(cuda, c, hw, form):
         zr = zr / (1 + np.exp(-zr))
         limit = max(limit, 1.5 * np.abs(zr - z).max())
     assert np.abs(got - z).max() <= limit
+
+
+@pytest.mark.parametrize("n,h,wd,ic,oc", [(2, 16, 16, 320, 640), (1, 9, 7, 36, 20), (3, 8, 8, 64, 30)])
+def test_conv1x1_channels_last_as_linear(cuda, n, h, wd, ic, oc):
+    """A 1x1 convolution over channels-last images (the UNet's skip and projection convolutions):
+    taken as a linear layer over the positions, with a per-channel bias, a residual in its own
+    channels-last memory and SiLU, against float64."""
+    import sdb
+    import torch
+
+    g = rng(ic + oc)
+    w = oracle.uniform(g, (oc, ic, 1, 1), 0.25, np.float16)
+    x = oracle.uniform(g, (n, ic, h, wd), 1.0)
+    b = oracle.uniform(g, (oc,), 1.0)
+    res = oracle.uniform(g, (n, oc, h, wd), 1.0)
+    xt = cuda_tensor(x, cuda).permute(0, 2, 3, 1).contiguous()
+    rt = cuda_tensor(res, cuda).permute(0, 2, 3, 1).contiguous()
+    out = torch.full((n, h, wd, oc), float("nan"), device=cuda)
+    chain = (sdb.Chain().add(cuda_tensor(b, cuda), sdb.channel_operand(None))
+             .add(rt, [oc, wd * oc, 1, h * wd * oc]).silu())
+    sdb.conv2d_nhwc(cuda_tensor(w, cuda), xt, (1, 1), (0, 0), (1, 1), out=out, chain=chain)
+    assert sdb.device_status(clear=True) == 0
+    got = host(out).transpose(0, 3, 1, 2)
+    exact, mag = oracle.conv2d_exact(w, x, (1, 1), (0, 0), (1, 1))
+    pre = exact + b.reshape(1, oc, 1, 1).astype(np.float64) + res.astype(np.float64)
+    want = pre / (1 + np.exp(-pre))
+    # SiLU's slope is at most 1.1: the pre-activation bound carries over.
+    err = oracle.metric(got, want, mag + np.abs(b.reshape(1, oc, 1, 1)) + np.abs(res))
+    assert err <= 1.1 * oracle.K_B200, f"error {err:.3g}"
