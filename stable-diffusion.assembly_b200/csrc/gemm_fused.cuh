@@ -332,7 +332,7 @@ gemm_fused_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                 }
             }
         }
-        if (!(amax < 65520.0f) && amax == amax) atomicOr(args.err, kErrRange);
+        if (amax >= 65520.0f) atomicOr(args.err, kErrRange);
         if (lane == 0) bulk_wait_all();
         __syncwarp();
     }
