@@ -1,9 +1,9 @@
 // The wide-tile tcgen05 GEMM: 128 rows x BN (up to 256) columns a tile, FP16
 // weights, for the linear layers, the gated GEGLU product and the direct
-// convolution.  The arithmetic and its precision protocol are gemm.cuh's (the
-// activation split x = hi + lo 2^-11; the hi product drained from tensor
-// memory every k-block into FP32 registers with round-to-nearest; the lo
-// product accumulated over the CTA's K); what changes is the shape of the work.
+// convolution.  The arithmetic: the activation split x = hi + lo 2^-11, each
+// k-block's hi W + (lo W) 2^-11 in one tensor-memory accumulator (the lo
+// products first, the first hi product scaling them as it adds), drained every
+// k-block into FP32 registers with round-to-nearest.
 //
 // Why wide.  Each kind::f16 MMA reads its A and B tiles from shared memory, and
 // TMA writes them there: at 128 x 128 a k-block moves ~112 KB through shared
@@ -11,14 +11,13 @@
 // ~900 cycles (measured: ~950), twice the tensor time.  At 128 x 256 the same
 // products cost ~160 KB per 2 x 128 x 256 x 64, ~1250 cycles for twice the work.
 //
-// Tensor memory then holds one hi buffer of BN columns and the lo accumulator
-// (BN columns at 256): the hi product of k-block kb is issued, then its lo
-// product, so that the epilogue drains hi(kb) while lo(kb) runs; hi(kb + 1)
-// waits for the drain.  Sixteen warps (four per tensor-memory lane quarter,
-// BN / 4 columns each) hold the running sums -- 18 or more warps would cap a
-// thread at 96 registers.  No warp is left over for the producers, so lane 0
-// of warp 0 also issues the TMA loads and lane 0 of warp 1 the MMAs, between
-// their own drains.
+// Tensor memory holds two such accumulators (columns 0 and 256), so the
+// products of k-block kb + 1 run while the warps drain kb.  Sixteen warps (four
+// per tensor-memory lane quarter, BN / 4 columns each) hold the running sums --
+// 18 or more warps would cap a thread at 96 registers.  No warp is left over
+// for the producers, so lane 0 of warp 0 also issues the TMA loads (after its
+// drain) and lane 0 of warp 1 the MMAs (of the next k-block, before its drain:
+// the issuing thread blocks while the tensor core takes them).
 #pragma once
 
 #include "gemm.cuh"
@@ -38,7 +37,7 @@ struct WideShape {
     static constexpr int kStagingBytes = kWideWarps * kBoxBytes;
     static constexpr int kBudget = 227 * 1024 - kStagingBytes - 1024 - 512;
     static constexpr int kStages = kBudget / kStageBytes >= 6 ? 6 : kBudget / kStageBytes;
-    static constexpr int kLoCol = 256;                        // hi at [0, BN), lo at [256, 256 + BN)
+    static constexpr int kLoCol = 256;                        // accumulators at [0, BN) and [256, 256 + BN)
     static constexpr int CPW = BN / 4;                        // accumulator columns a warp owns
     static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 + 512;
     static_assert(kStages >= 2, "too few stages");
@@ -223,11 +222,9 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     uint8_t* staging = smem + S::kStages * S::kStageBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(staging + S::kStagingBytes);
     uint64_t* empty = full + S::kStages;
-    uint64_t* hi_full = empty + S::kStages;
-    uint64_t* hi_empty = hi_full + 1;
-    uint64_t* lo_full = hi_empty + 1;
-    uint64_t* lo_empty = lo_full + 1;
-    uint64_t* drain = lo_empty + 1;
+    uint64_t* d_full = empty + S::kStages;   // [2] an accumulator's products completed
+    uint64_t* d_empty = d_full + 2;          // [2] every warp drained it
+    uint64_t* drain = d_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -242,10 +239,10 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(hi_full, 1);
-        mbar_init(hi_empty, kWideWarps);
-        mbar_init(lo_full, 1);
-        mbar_init(lo_empty, kWideWarps);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&d_full[b], 1);
+            mbar_init(&d_empty[b], kWideWarps);
+        }
         mbar_init(drain, 1);
         *abort = 0;
         fence_barrier_init();
@@ -321,25 +318,32 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
         return true;
     };
 
-    // ---- MMA issuer (warp 1, lane 0): hi then lo of k-block number `it`.
+    // ---- MMA issuer (warp 1, lane 0): k-block number m_it of the CTA's sequence into
+    // accumulator m_it % 2 (columns 0 and kLoCol): the lo products first into a fresh
+    // accumulator, then the hi products, the first of them scaling the lo sum by 2^-11
+    // (tcgen05.mma's scale of the input D), so that one accumulator holds the k-block's
+    // hi W + (lo W) 2^-11.  The issuing thread blocks while the tensor core takes the
+    // products, so it issues k-block kb + 1 before its warp drains kb: the products of
+    // kb + 1 run while every warp drains kb.
     constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
     int m_it = 0;  // k-blocks issued
-    auto issue_hi_lo = [&](int kb, int kb0) -> bool {
-        const int s = m_it % S::kStages;
+    auto issue_kblock = [&]() -> bool {
+        const int s = m_it % S::kStages, b = m_it & 1;
         if (!mbar_wait(&full[s], (m_it / S::kStages) & 1, abort, args.err)) return false;
-        if (!mbar_wait(hi_empty, (m_it & 1) ^ 1, abort, args.err)) return false;
+        if (!mbar_wait(&d_empty[b], ((static_cast<uint32_t>(m_it) >> 1) & 1u) ^ 1u, abort, args.err)) return false;
         tc_fence_after();
+        const uint32_t d = tmem + (b ? S::kLoCol : 0u);
         const uint32_t ahi = smem_u32(smem + s * S::kStageBytes), alo = ahi + S::kABytes;
         const uint32_t b0 = ahi + 2 * S::kABytes;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16(tmem, desc_kmajor_sw128(ahi + kk * 32), desc_kmajor_sw128(b0 + kk * 32), idesc, kk > 0 ? 1u : 0u);
-        mma_commit(hi_full);
+            mma_f16(d, desc_kmajor_sw128(alo + kk * 32), desc_kmajor_sw128(b0 + kk * 32), idesc, kk > 0 ? 1u : 0u);
+        mma_f16_scale_lo(d, desc_kmajor_sw128(ahi), desc_kmajor_sw128(b0), idesc);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16(tmem + S::kLoCol, desc_kmajor_sw128(alo + kk * 32), desc_kmajor_sw128(b0 + kk * 32), idesc,
-                    (kb > kb0 || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < kBK / 16; ++kk)
+            mma_f16(d, desc_kmajor_sw128(ahi + kk * 32), desc_kmajor_sw128(b0 + kk * 32), idesc, 1u);
         mma_commit(&empty[s]);
+        mma_commit(&d_full[b]);
         ++m_it;
         return true;
     };
@@ -350,14 +354,6 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     const int colA = GATED ? part * (CPW / 2) : part * CPW;
     const int colB = GATED ? BN / 2 + part * (CPW / 2) : 0;
 
-    // The first k-block of an item is issued once every warp has read the
-    // previous item's lo accumulator (lo_empty); issue_first(t) does that for
-    // the CTA's item number t.
-    auto issue_first = [&](int item, int t) -> bool {
-        int tm, tn, split, kb0, kb1;
-        item_range(item, tm, tn, split, kb0, kb1);
-        return mbar_wait(lo_empty, (t & 1) ^ 1, abort, args.err) && issue_hi_lo(kb0, kb0);
-    };
     // Waits every lane of the warp makes together; the verdict is the warp's.
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, args.err) ? 1 : 0) != 0;
@@ -366,50 +362,37 @@ gemm_wide_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     bool ok = true;
     if (warp == 0 && lane == 0)
         for (int i = 0; i < S::kStages && ok; ++i) ok = producer_next();
-    if (warp == 1 && lane == 0) ok = issue_first(blockIdx.x, 0);
+    if (warp == 1 && lane == 0 && total_kb > 0) ok = issue_kblock();
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    int e_it = 0, t = 0;
-    for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x, ++t) {
+    int e_it = 0;
+    for (int item = blockIdx.x; item < args.items && ok; item += gridDim.x) {
         int tm, tn, split, kb0, kb1;
         item_range(item, tm, tn, split, kb0, kb1);
         float sum[CPW];
 #pragma unroll
         for (int j = 0; j < CPW; ++j) sum[j] = 0.0f;
         for (int kb = kb0; kb < kb1 && ok; ++kb, ++e_it) {
-            if (!warp_wait(hi_full, e_it & 1)) { ok = false; break; }
+            bool lane_ok = true;
+            if (warp == 1 && lane == 0 && e_it + 1 < total_kb) lane_ok = issue_kblock();
+            if (__shfl_sync(0xffffffffu, lane_ok ? 1 : 0, 0) == 0) { ok = false; break; }
+            const int b = e_it & 1;
+            if (!warp_wait(&d_full[b], (static_cast<uint32_t>(e_it) >> 1) & 1u)) { ok = false; break; }
             tc_fence_after();
+            const uint32_t acc = lane_addr + (b ? S::kLoCol : 0u);
             if (GATED) {
-                tmem_add<CPW / 2>(lane_addr + colA, sum, 1.0f);
-                tmem_add<CPW / 2>(lane_addr + colB, sum + CPW / 2, 1.0f);
+                tmem_add<CPW / 2>(acc + colA, sum, 1.0f);
+                tmem_add<CPW / 2>(acc + colB, sum + CPW / 2, 1.0f);
             } else {
-                tmem_add<CPW>(lane_addr + colA, sum, 1.0f);
+                tmem_add<CPW>(acc + colA, sum, 1.0f);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(hi_empty);
-            bool lane_ok = true;
-            if (warp == 1 && lane == 0 && kb + 1 < kb1) lane_ok = issue_hi_lo(kb + 1, kb0);
-            if (warp == 0 && lane == 0) lane_ok = producer_next() && lane_ok;
-            ok = __shfl_sync(0xffffffffu, lane_ok ? 1 : 0, 0) != 0;
+            if (lane == 0) mbar_arrive(&d_empty[b]);
+            // k-block e_it's products are done, so its stage is free: the next load never waits.
+            if (warp == 0 && lane == 0) lane_ok = producer_next();
+            if (__shfl_sync(0xffffffffu, lane_ok ? 1 : 0, 0) == 0) { ok = false; break; }
         }
         if (!ok) break;
-        if (warp == 1 && lane == 0) mma_commit(lo_full);
-        __syncwarp();
-        if (!warp_wait(lo_full, t & 1)) { ok = false; break; }
-        tc_fence_after();
-        if (GATED) {
-            tmem_add<CPW / 2>(lane_addr + S::kLoCol + colA, sum, kLoUnscale);
-            tmem_add<CPW / 2>(lane_addr + S::kLoCol + colB, sum + CPW / 2, kLoUnscale);
-        } else {
-            tmem_add<CPW>(lane_addr + S::kLoCol + colA, sum, kLoUnscale);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(lo_empty);
-        // The next item's first products start before this warp's stores.
-        if (warp == 1 && lane == 0 && item + static_cast<int>(gridDim.x) < args.items)
-            ok = issue_first(item + gridDim.x, t + 1);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 
         // ---- the tile's epilogue (the next item's products run meanwhile)
         const int row = q * 32 + lane;
