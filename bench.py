@@ -171,7 +171,7 @@ class HotOps:
         for i, (tag, cv) in enumerate(zip("abc", self.convs)):
             c, hw = cv["c"], cv["hw"]
             flops = 2 * 9 * c * c * hw * hw
-            # 8x8: the weights' bytes bound it (SURVEY config 2c: 63 FLOP/B).
+            # 8x8: the weights' bytes bound it (about 63 FLOP a byte at 1280 channels).
             work, bound = (flops, "tensor") if hw > 8 else (c * c * 9 * 2 + 2 * c * hw * hw * 4, "hbm")
 
             def conv_gn(s, i=i, cv=cv):
