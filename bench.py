@@ -8,7 +8,7 @@ One process per GPU (torchrun for N > 1).  The default workload shards a fixed
 collective); the step time is the max over ranks, and rank 0 prints one JSON
 line.
 
-Workload "sd15_unet_step" (default): one sampler step of SD
+Workload "sd15_unet_step" (default; benchmark config 4): one sampler step of SD
 1.5 at 512 x 512 -- the UNet forward on the classifier-free-guidance batch of 2
 (latent 64 x 64, context 2 x 77 x 768; ~860M random-init FP16 weights) and the
 fused guidance (scale 7) + Euler update -- captured once as a CUDA graph and
@@ -17,7 +17,7 @@ steps/s.  A second, eager pass with CUDA events around every library call
 gives the step's per-class times and the roofline of the dominant class.
 Weights (1.7 GB) and activations exceed L2 every step.
 
-Workload "sd15_hot_ops" (--workload hot_ops): the BASELINE configs 1-3 op set.
+Workload "sd15_hot_ops" (--workload hot_ops): the benchmark configs 1-3 op set.
 
 The JSON line follows the driver contract: roofline of the dominant kernel
 class, clocks sampled during the timed region, an end-to-end number through
@@ -43,7 +43,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "stable-diffusion.assembly_b200"))
 
 HOT_WORKLOAD = "sd15_hot_ops"
-HOT_METRIC = "SD1.5 UNet hot-path op set (BASELINE configs 1-3) steps/s"
+HOT_METRIC = "SD1.5 UNet hot-path op set (benchmark configs 1-3) steps/s"
 HOT_UNIT = "steps/s"
 UNET_WORKLOAD = "sd15_unet_step"
 UNET_METRIC = ("UNet ms/step + VAE ms (SD1.5 512x512, CFG 7, Euler; the 8-image batch over the GPUs): whole-job "
@@ -51,7 +51,7 @@ UNET_METRIC = ("UNet ms/step + VAE ms (SD1.5 512x512, CFG 7, Euler; the 8-image 
                "job's UNet step")
 UNET_UNIT = "image-steps/s"
 SAMPLER_STEPS = 20
-IMAGES = 8        # batches of 8 images, sharded by image over 1/2/4/8 GPUs
+IMAGES = 8        # benchmark config 4: batches of 8 images, sharded by image over 1/2/4/8 GPUs
 
 
 # ---------------------------------------------------------------- peaks
@@ -161,7 +161,7 @@ class HotOps:
         self.ops = self._ops()
 
     def _ops(self):
-        """(name, work, bound, fn(set)) -- BASELINE configs 1-3, work in FLOPs (tensor) or the least bytes
+        """(name, work, bound, fn(set)) -- benchmark configs 1-3, work in FLOPs (tensor) or the least bytes
         moved (hbm), by the reference's convention (bench.cc:82-124, profile.cc:65-81)."""
         sdb = self.sdb
         ops = []
@@ -624,7 +624,7 @@ def run_reference(args) -> None:
 
 
 def hot_op_configs(torch, dev, reps: int = 30) -> dict:
-    """BASELINE configs 1-3 timed op by op on this GPU (CUDA-graph replays over three rotating input
+    """benchmark configs 1-3 timed op by op on this GPU (CUDA-graph replays over three rotating input
     sets larger than L2), each against its roofline: tensor-bound ops by the reference's FLOP count over
     the measured bf16 burst peak, memory-bound ones by their least bytes over the measured HBM copy rate
     (MEASURED_PEAKS.json)."""
@@ -944,7 +944,7 @@ def measure_vae(torch, dev, latent, barrier, max_over_ranks, reps: int = 5, conf
 
 
 def measure_sdxl(torch, dev, barrier, max_over_ranks, reps: int = 5) -> dict:
-    """One SDXL sampler step at 832 x 1216 (latent 152 x 104): the UNet forward on the
+    """One SDXL sampler step at 832 x 1216 (latent 152 x 104, benchmark config 5): the UNet forward on the
     classifier-free-guidance batch of 2 (context 2 x 77 x 2048, pooled text + size/crop conditioning
     2 x 2816, 2.57B random-init FP16 weights) and the guidance (scale 6) + ancestral Euler update (each
     step's fresh noise drawn before the timing), captured once and replayed; ms a step as the max over
@@ -1156,7 +1156,7 @@ def run_unet(args, torch, dev, dist, world, rank, local, barrier, max_over_ranks
     d2h = h_out.numel() * 4
     # The VAE decode of this rank's latents, captured once and replayed.
     vae_ms, vae_flops = measure_vae(torch, dev, sampler.x, barrier, max_over_ranks)
-    # The job's final latents to rank 0 (NCCL over NVLink): the gather BASELINE config 4's image sharding
+    # The job's final latents to rank 0 (NCCL over NVLink): the gather benchmark config 4's image sharding
     # ends with, timed on the device as the max over ranks.
     gather = None
     if dist is not None and world > 1:
@@ -1354,7 +1354,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["unet", "hot_ops"], default="unet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-sdxl", action="store_true", help="skip the SDXL step (BASELINE config 5) measured beside SD 1.5")
+    ap.add_argument("--no-sdxl", action="store_true", help="skip the SDXL step (benchmark config 5) measured beside SD 1.5")
     ap.add_argument("--cfg-split", action="store_true",
                     help="split classifier-free guidance over GPU pairs (needs an even number of ranks)")
     ap.add_argument("--op", choices=sorted(OPS), help="run one operation three times (profiler captures) and exit")

@@ -3,7 +3,7 @@
 Cases: the reference's (tests/ops_test.cc:925-938) -- SD 1.5's self- and
 cross-attention made smaller, heads of 80 and 160, the VAE's single head of
 512, dims and keys of no multiple of a panel with heads sharing keys, FP16
-keys and values -- and BASELINE config 3 (8 heads x 40, Lq = Lk = 4096 and
+keys and values -- and benchmark config 3 (8 heads x 40, Lq = Lk = 4096 and
 Lk = 77), with and without the residual add fused; heads wider than 160 dims
 (the VAE's 512) at full size, with shared FP16 keys and an odd width.  Q, K, V ~ U(-1, 1)
 (ops_test.cc:478-483); bound: the ops_test metric <= 1e-6.
@@ -92,7 +92,7 @@ def test_attention_wide_heads_take_no_chain(cuda):
 
 @pytest.mark.parametrize("lk,residual", [(4096, False), (77, False), (4096, True), (77, True)])
 def test_attention_config3(cuda, lk, residual):
-    """8 heads x 40, Lq = 4096, Q/K/V ~ N(0, 1), optional fused residual."""
+    """benchmark config 3: 8 heads x 40, Lq = 4096, Q/K/V ~ N(0, 1), optional fused residual."""
     err = run(cuda, 40, 4096, lk, 8, 8, 1, np.float32, seed=5, normal=True, residual=residual)
     assert err <= oracle.K_B200, f"error {err:.3g}"
 

@@ -3,7 +3,7 @@
 Cases: the reference's 13 (tests/ops_test.cc:801-819) -- the UNet's 3x3
 convolutions made smaller, 1x1, stride 2, odd edges, FP32 weights, a 5x3
 kernel with dilation -- each in every form the tuning offers (direct,
-F(2x2), F(4x4)), and the three BASELINE config 2 shapes.  Bound: the ops_test
+F(2x2), F(4x4)), and the three benchmark config 2 shapes.  Bound: the ops_test
 metric <= 1e-6.
 """
 from __future__ import annotations
@@ -59,7 +59,7 @@ def test_conv2d_direct(cuda, case):
     assert err <= oracle.K_B200, f"error {err:.3g}"
 
 
-# 3x3, stride 1, pad 1, FP16 weights N(0, 1/sqrt(9 Cin)),
+# benchmark config 2: 3x3, stride 1, pad 1, FP16 weights N(0, 1/sqrt(9 Cin)),
 # FP32 input N(0, 1), bias, then GroupNorm(32, eps 1e-5, gamma ~ N(1, 0.1),
 # beta ~ N(0, 0.1)), then SiLU.
 CONFIG2 = [(320, 64), (640, 32), (1280, 8)]

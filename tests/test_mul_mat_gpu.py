@@ -1,7 +1,7 @@
 """Parity of the linear layers (MUL_MAT, GEGLU) against the exact oracle.
 
 The cases are the reference's (tests/ops_test.cc:825-832 for mul_mat,
-:946-949 for the gated GELU) plus BASELINE config 1 (4096 x 320 -> 1280 with
+:946-949 for the gated GELU) plus benchmark config 1 (4096 x 320 -> 1280 with
 its bias).  Weights U(-0.25, 0.25), inputs U(-1, 1) (ops_test.cc:441-444);
 every output starts as the NaN canary.  The bound is the north star's: the
 ops_test metric (error / sum of |products|, against float64) <= 1e-6.
@@ -43,7 +43,7 @@ def test_mul_mat_reference_cases(cuda, k, n, m, batch, wtype):
 
 @pytest.mark.parametrize("block_n", [128, 256])
 def test_mul_mat_config1_bias(cuda, block_n):
-    """x N(0,1) [4096 x 320], W N(0, 0.02) FP16 [1280 x 320], bias N(0, 0.02)."""
+    """benchmark config 1: x N(0,1) [4096 x 320], W N(0, 0.02) FP16 [1280 x 320], bias N(0, 0.02)."""
     import sdb
 
     g = rng(1)

@@ -8,7 +8,7 @@ convolution (Winograd's input transform, or the split of a direct convolution's 
 results must equal the separate nodes' bit for bit; the separate nodes are held to the oracle by
 tests/test_norm_gpu.py and the convolution tests.  Checked here besides:
   * the statistics against the reference's single-precision mean and 1/sqrt(var + eps) (norm.cc:121-129);
-  * BASELINE config 2's shapes (conv 3x3 + bias -> GroupNorm 32 + SiLU -> the next conv) on the fused
+  * benchmark config 2's shapes (conv 3x3 + bias -> GroupNorm 32 + SiLU -> the next conv) on the fused
     path against the float64 exact result of the reference's sequence, within the convolution bound.
 """
 from __future__ import annotations
@@ -116,7 +116,7 @@ def test_mul_mat_normed_equals_separate_nodes(cuda, n, c, hw, silu):
 
 @pytest.mark.parametrize("c,hw", [(320, 64), (640, 32), (1280, 8)], ids=["2a", "2b", "2c"])
 def test_config2_block_fused_within_bound(cuda, c, hw):
-    """BASELINE config 2 as the UNet runs it: conv 3x3 + bias, GroupNorm(32, eps 1e-5, gamma ~ N(1, 0.1),
+    """benchmark config 2 as the UNet runs it: conv 3x3 + bias, GroupNorm(32, eps 1e-5, gamma ~ N(1, 0.1),
     beta ~ N(0, 0.1)) + SiLU applied as the next convolution reads it.  The result against float64:
     the exact second convolution of the oracle's GroupNorm + SiLU of the first's exact output, bounded
     as the convolution tests bound a single convolution (plus the first's error carried through)."""

@@ -31,7 +31,7 @@ def close(got, want, bound=oracle.K_FUSED_APART):
 @pytest.mark.parametrize("shape,groups,eps,silu", [
     ((2, 64, 20, 36), 32, 1e-6, True),     # ops_test.cc:1083-1094
     ((1, 30, 7, 13), 10, 1e-5, True),      # ops_test.cc:1095-1106 (rows of no multiple of eight)
-    ((1, 320, 64, 64), 32, 1e-5, True),    # BASELINE config 2a's GroupNorm
+    ((1, 320, 64, 64), 32, 1e-5, True),    # benchmark config 2a's GroupNorm
     ((1, 1280, 8, 8), 32, 1e-5, True),     # config 2c
 ])
 def test_group_norm_chain(cuda, shape, groups, eps, silu):

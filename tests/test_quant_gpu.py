@@ -136,7 +136,7 @@ def test_quantized_narrow_integers(cuda, bits, input_bits, k, n, wtype):
 
 
 def test_quantized_row_scales(cuda):
-    """weight_group=0: one scale for a whole row of k (BASELINE config 5's weights)."""
+    """weight_group=0: one scale for a whole row of k (benchmark config 5's weights)."""
     with tuned("bits=8,weight_group=0"):
         w, x, _, got = run_linear(cuda, 1280, 320, 300, 1, np.float16, seed=3)
     form = ref_forms.qmul_mat(w, x.reshape(-1, 1280), weight_groups=False).reshape(got.shape)

@@ -4,7 +4,7 @@ Cases: every 3x3, stride-1 case of the reference's conv list (ops_test.cc:801-81
 in both forms, with the position thresholds lowered so each takes Winograd; the
 chains the reference's fusion tests put after a Winograd convolution (bias and
 residual, residual in its own memory: ops_test.cc:976-1066); channels-last images;
-BASELINE config 2's shapes under the default tuning.
+benchmark config 2's shapes under the default tuning.
 
 Bounds (ops_test metric, error over the summed product magnitudes):
   F(2x2): <= 1e-6;
@@ -145,7 +145,7 @@ CONFIG2 = [(320, 64), (640, 32), (1280, 8)]
 
 @pytest.mark.parametrize("c,hw", CONFIG2, ids=lambda v: str(v))
 def test_winograd_config2_default(cuda, c, hw):
-    """BASELINE config 2 under the default tuning (Winograd where it is taken) with its bias."""
+    """benchmark config 2 under the default tuning (Winograd where it is taken) with its bias."""
     import sdb
 
     g = rng(20)
